@@ -1,0 +1,414 @@
+"""Benchmark of the B200 K-quant matmul path (one JSON line on rank 0).
+
+Default workload: BASELINE config 0 -- Q4_K x Q8_K GEMV, M=1, N=9728 rows, K=2560 (the FFN gate
+shape of a 4B model), synthetic seeded GGUF blocks.  One step = one dispatch: the fp16
+activation is quantized to Q8_K inside the kernel and the 9728 fp32 outputs are written.
+
+  value  : weight GB/s over all ranks with inputs resident in HBM (kq_gemm_multi_async, steps
+           captured in a CUDA graph, 24 rotating weight copies = 336 MB > 2x L2 so every step
+           streams its weights from HBM)
+  e2e    : the same metric through the reference-facing C ABI with host buffers
+           (kq_sdot_gemm_multi_dispatch: pinned fp16 input copied in, fp32 result copied out,
+           one blocking call per step)
+  roofline, cpu_baseline, clocks, gpu_launches: see DESIGN.md
+
+--config lm_head runs BASELINE config 1 (Q6_K LM head, N=151936, K=2560) with vocab rows
+sharded over the ranks and the logit slices all-gathered with NCCL.
+--impl reference times the reference engine's own CPU path (oracle/_ref, built from its
+sources) on this host on the same workload.
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config gemv|lm_head]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC_GEMV = "Q4_K GEMV weight GB/s (% B200 HBM peak)"
+METRIC_LM = "Q6_K LM-head GEMV weight GB/s (vocab-sharded, all-gathered)"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(key):
+    """DRAM bytes per launch of a kernel from the committed ncu summary (profiles/traffic.json)."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        d = json.load(f)
+    v = d.get(key)
+    return None if v is None else float(v["dram_bytes_per_launch"])
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.tmp is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.tmp.flush()
+        rows = []
+        with open(self.tmp.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def physical_gpu_index(local_rank):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+# ---------------------------------------------------------------------------- CPU baselines
+
+def cpu_reference_gemv(n_rows, k, gtype, seconds=10.0, max_steps=None, warmup=1):
+    """The reference engine's own CPU path (sdot_gemm_multi_dispatch on its 4-thread pinned pool,
+    turbo mode, scalar kernels on x86) over full GEMVs of the workload.
+    Returns (weight GB/s, steps, seconds per step, kind, cores, sample description)."""
+    from npu880_mtk_npu_llm_runtime_b200 import synth
+    from oracle.oracle import Reference, reference_available, Oracle
+    w = synth.gen_weights(gtype, n_rows, k, seed=1234)
+    x = synth.gen_activations(1, k, seed=1235)
+    wbytes = w.nbytes
+    if reference_available():
+        R = Reference()
+        R.init_pool()
+        dst = np.zeros((1, n_rows), np.float16)
+        R.turbo(True)
+        for _ in range(warmup):
+            R.dispatch(x, [(gtype, w, dst, None)])
+        t0 = time.perf_counter()
+        R.dispatch(x, [(gtype, w, dst, None)])
+        t1 = time.perf_counter() - t0
+        steps = max(2, int(seconds / max(t1, 1e-6)))
+        if max_steps:
+            steps = min(steps, max_steps)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            R.dispatch(x, [(gtype, w, dst, None)])
+        dt = time.perf_counter() - t0
+        R.turbo(False)
+        return (wbytes * steps / dt / 1e9, steps, dt / steps, "reference", R.pool_threads,
+                f"{steps} full GEMVs (N={n_rows}, K={k}) through the reference's sdot_gemm_multi_dispatch "
+                f"on its {R.pool_threads}-thread pool (scalar x86 kernels, turbo mode)")
+    O = Oracle()
+    act = O.quantize_q8k(x)
+    t0 = time.perf_counter()
+    O.gemm(gtype, w, k, act)
+    t1 = time.perf_counter() - t0
+    steps = max(1, int(seconds / max(t1, 1e-6)))
+    if max_steps:
+        steps = min(steps, max_steps)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        O.gemm(gtype, w, k, act)
+    dt = time.perf_counter() - t0
+    return (wbytes * steps / dt / 1e9, steps, dt / steps, "port", 1,
+            f"{steps} full GEMVs (N={n_rows}, K={k}) through the oracle's scalar C restatement, 1 thread")
+
+
+# ---------------------------------------------------------------------------- our arm
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import npu880_mtk_npu_llm_runtime_b200 as kq
+    from npu880_mtk_npu_llm_runtime_b200 import build as kqbuild, synth
+
+    kqbuild.build()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    ctx = kq.Context(local_rank)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream.cuda_stream)
+
+    if args.config == "gemv":
+        gtype, N, K = kq.TYPE_Q4_K, 9728, 2560
+        rows_local, row0 = N, 0
+        metric = METRIC_GEMV
+    else:
+        gtype, N, K = kq.TYPE_Q6_K, 151936, 2560
+        rows_local = (N + world - 1) // world
+        row0 = rank * rows_local
+        rows_local = max(0, min(N, row0 + rows_local) - row0)
+        metric = METRIC_LM
+    w_host = synth.gen_weights(gtype, N, K, seed=1234)[row0:row0 + rows_local]
+    x_host = synth.gen_activations(1, K, seed=1235)
+    wbytes = w_host.nbytes                      # GGUF bytes this rank streams per step
+    raw = torch.from_numpy(np.ascontiguousarray(w_host)).to(dev)
+    n_copies = max(2, math.ceil(2.6 * L2_BYTES / max(1, wbytes)))
+    Ws = [ctx.upload_device(raw, gtype, rows_local, K) for _ in range(n_copies)]
+    del raw
+    x = torch.from_numpy(x_host.view(np.uint16).copy()).to(dev)
+    out = torch.zeros((n_copies, rows_local), dtype=torch.float32, device=dev)
+    full = torch.zeros((N if args.config == "lm_head" else rows_local,), dtype=torch.float32, device=dev)
+    tasks = [ctx.make_tasks([dict(w=Ws[i], dst_f32=out[i:i + 1], dst_f32_stride=rows_local)])
+             for i in range(n_copies)]
+
+    def step(i):
+        ctx.gemm_multi_async(x, 1, K, tasks[i % n_copies])
+
+    gather_chunks = None
+    if args.config == "lm_head" and world > 1:
+        # every rank owns an equal slice (the last one padded) so all_gather_into_tensor applies
+        chunk = (N + world - 1) // world
+        gather_chunks = torch.zeros((world * chunk,), dtype=torch.float32, device=dev)
+        slice_buf = torch.zeros((chunk,), dtype=torch.float32, device=dev)
+
+    def step_with_gather(i):
+        step(i)
+        if gather_chunks is not None:
+            slice_buf[:rows_local].copy_(out[i % n_copies])
+            dist.all_gather_into_tensor(gather_chunks, slice_buf)
+
+    # warm-up (eager), also configures the kernels before capture
+    with torch.cuda.stream(stream):
+        for i in range(max(3, args.warmup)):
+            step_with_gather(i)
+    ctx.synchronize()
+    torch.cuda.synchronize(dev)
+
+    steps = args.steps
+    G = min(steps, 1000 if args.config == "gemv" else 50)
+    graph = None
+    if gather_chunks is None:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            ctx.set_stream(torch.cuda.current_stream(dev).cuda_stream)
+            for i in range(G):
+                step(i)
+        ctx.set_stream(stream.cuda_stream)
+        reps = max(1, math.ceil(steps / G))
+        steps = reps * G
+        with torch.cuda.stream(stream):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+    launches_per_step = 1
+
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(physical_gpu_index(local_rank)) as clk:
+        ev0.record(stream)
+        with torch.cuda.stream(stream):
+            if graph is not None:
+                for _ in range(reps):
+                    graph.replay()
+            else:
+                for i in range(steps):
+                    step_with_gather(i)
+        ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    dt_local = ev0.elapsed_time(ev1) / 1e3
+    t = torch.tensor([dt_local], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    clocks = clk.summary()
+
+    total_wbytes = torch.tensor([float(wbytes)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(total_wbytes, op=dist.ReduceOp.SUM)
+    value = float(total_wbytes.item()) * steps / dt / 1e9
+    ms_per_step = dt / steps * 1e3
+
+    # roofline of the GEMV kernel on this rank: algorithmic bytes per launch / launch duration
+    act_bytes = (K // 256) * 292            # Q8_K activation (SURVEY: 2,920 B at K=2560)
+    out_bytes = rows_local * 4
+    algo = wbytes + act_bytes + out_bytes
+    avg_launch_s = dt_local / (steps * launches_per_step)
+    achieved = algo / avg_launch_s / 1e9
+    peak, peak_kind = measured_peaks()
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+            "traffic": ncu_traffic("gemv_q4k_cfg0" if args.config == "gemv" else "gemv_q6k_lmhead"),
+            "algorithmic_bytes_per_launch": algo}
+
+    # e2e through the reference-facing C ABI with host buffers (rank-local, blocking calls)
+    e2e_steps = min(steps, args.e2e_steps)
+    xp = torch.from_numpy(x_host.view(np.uint16).copy()).pin_memory()
+    op = torch.zeros((1, rows_local), dtype=torch.float32).pin_memory()
+    xp_np = xp.numpy().view(np.float16)
+    op_np = op.numpy()
+    for i in range(3):
+        ctx.sdot_gemm_multi_dispatch(xp_np, [dict(w=Ws[i % n_copies], dst_f32=op_np)])
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(e2e_steps):
+        ctx.sdot_gemm_multi_dispatch(xp_np, [dict(w=Ws[i % n_copies], dst_f32=op_np)])
+    e1.record(stream)
+    e1.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = float(total_wbytes.item()) * e2e_steps / float(te.item()) / 1e9
+
+    result = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            v, st, sec, kind, cores, sample = cpu_reference_gemv(N if args.config == "gemv" else 24832, K, gtype,
+                                                               seconds=args.cpu_seconds)
+            cpu = {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample,
+                   "seconds_per_step": sec}
+        result = {
+            "metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": max(3, args.warmup), "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
+            "scaling": "weak" if args.config == "gemv" else "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded GGUF blocks per BASELINE distributions; activations N(0,1) -> fp16)",
+            "config": {"workload": ("config0: Q4_K x Q8_K GEMV M=1 N=9728 K=2560" if args.config == "gemv"
+                                    else "config1: Q6_K LM head M=1 N=151936 K=2560, vocab rows sharded, "
+                                         "NCCL all-gather of fp32 logit slices"),
+                       "m": 1, "n": N, "k": K, "weight_bytes_per_step_per_rank": wbytes,
+                       "l2": f"inputs larger than L2: {n_copies} rotating weight copies "
+                             f"({n_copies * wbytes / 2**20:.0f} MiB > 2x126 MB L2)",
+                       "parallelism": (f"replicas x{world}" if args.config == "gemv" else f"vocab-shard x{world}"),
+                       "timing": "CUDA graph of back-to-back dispatches (PDL), CUDA events on the launch stream"
+                                 if graph is not None else "eager launches + NCCL all-gather per step"},
+            "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "steps": e2e_steps,
+                    "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(rows_local * 4),
+                    "api": "kq_sdot_gemm_multi_dispatch (host buffers, blocking)"},
+            "gpu_launches": steps * launches_per_step,
+        }
+    for W in Ws:
+        W.free()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+# ---------------------------------------------------------------------------- reference arm
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    from npu880_mtk_npu_llm_runtime_b200 import synth
+    gtype = synth.TYPE_Q4_K if args.config == "gemv" else synth.TYPE_Q6_K
+    n_rows = 9728 if args.config == "gemv" else 151936
+    # each step is one full GEMV on the reference pool; the step count is capped so the whole
+    # arm ends within a few minutes
+    v, steps, sec, kind, cores, sample = cpu_reference_gemv(n_rows, 2560, gtype, seconds=args.ref_seconds,
+                                                           max_steps=args.steps, warmup=min(args.warmup, 3))
+    return {
+        "impl": "reference", "metric": METRIC_GEMV if args.config == "gemv" else METRIC_LM,
+        "value": round(v, 4), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 3),
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak" if args.config == "gemv" else "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded GGUF blocks per BASELINE distributions)",
+        "config": {"workload": "config0: Q4_K x Q8_K GEMV M=1 N=9728 K=2560" if args.config == "gemv"
+                   else "config1: Q6_K LM head M=1 N=151936 K=2560", "m": 1, "n": n_rows, "k": 2560},
+        "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300000)
+    ap.add_argument("--warmup", type=int, default=300)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["gemv", "lm_head"], default="gemv")
+    ap.add_argument("--e2e-steps", type=int, default=2000)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seconds", type=float, default=30.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = env_int("RANK", 0)
+    world = env_int("WORLD_SIZE", 1)
+    local_rank = env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+    else:
+        res = run_ours(args, rank, world, local_rank)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,371 @@
+// kq_act.cu -- activation quantizers, fused producers, weight repack and dequant for sm_100a.
+//
+// All of these are bandwidth-trivial next to the weight stream; they are written so that the
+// integer/byte outputs are bit-exact to the reference engine (src/v182_r22_breakthrough_engine.c):
+//   quantize_row_fp16_to_q8_k  ENG:925-990    -> quantize_kernel<Q8_K>
+//   quantize_row_fp16_to_q8_0  ENG:1016-1064  -> quantize_kernel<Q8_0>
+//   rmsnorm_fp16_rows_fast     ENG:4264-4314  -> rmsnorm_q8k_kernel (fp32 sum in tree order)
+//   swiglu_fp16_rows_fast      ENG:4326-4383  -> swiglu_q8k_kernel (CUDA expf)
+//   dequant_block_<type>       ENG:598-853    -> dequant_kernel
+#include "kq_common.cuh"
+#include "kq_internal.h"
+
+#include <algorithm>
+
+namespace kq {
+
+// Quantize the 256 values v[8*lane .. 8*lane+7] held by a warp to Q8_K and store a BlockQ8K.
+// v are fp32 copies of fp16 values (exact).
+__device__ __forceinline__ void warp_store_q8k(const float v[8], BlockQ8K *out, int lane) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    int q[8];
+    if (amax == 0.0f) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = 0;
+    } else {
+        const float inv = __fdiv_rn(127.0f, amax);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = max(-127, min(127, __float2int_rn(__fmul_rn(v[i], inv))));
+    }
+    uint32_t *w = reinterpret_cast<uint32_t *>(out);
+    w[1 + 2 * lane] = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) | ((uint32_t)(q[2] & 0xFF) << 16) |
+                      ((uint32_t)(q[3] & 0xFF) << 24);
+    w[2 + 2 * lane] = (uint32_t)(q[4] & 0xFF) | ((uint32_t)(q[5] & 0xFF) << 8) | ((uint32_t)(q[6] & 0xFF) << 16) |
+                      ((uint32_t)(q[7] & 0xFF) << 24);
+    int s = q[0] + q[1] + q[2] + q[3] + q[4] + q[5] + q[6] + q[7];
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if ((lane & 3) == 0) w[65 + (lane >> 2)] = (uint32_t)s;
+    if (lane == 0) out->d = (amax == 0.0f) ? 0.0f : __fdiv_rn(amax, 127.0f);
+}
+
+// Same for four Q8_0 blocks per 8 lanes: lanes 4j..4j+3 hold block j of the 256 values.
+__device__ __forceinline__ void warp_store_q80(const float v[8], BlockQ80 *out8, int lane) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    int q[8];
+    if (amax == 0.0f) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = 0;
+    } else {
+        const float inv = __fdiv_rn(127.0f, amax);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = max(-127, min(127, __float2int_rn(__fmul_rn(v[i], inv))));
+    }
+    const int j = lane >> 2, part = lane & 3;
+    uint32_t *w = reinterpret_cast<uint32_t *>(out8 + j);
+    w[1 + 2 * part] = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) | ((uint32_t)(q[2] & 0xFF) << 16) |
+                      ((uint32_t)(q[3] & 0xFF) << 24);
+    w[2 + 2 * part] = (uint32_t)(q[4] & 0xFF) | ((uint32_t)(q[5] & 0xFF) << 8) | ((uint32_t)(q[6] & 0xFF) << 16) |
+                      ((uint32_t)(q[7] & 0xFF) << 24);
+    if (part == 0) out8[j].d = (amax == 0.0f) ? 0.0f : __fdiv_rn(amax, 127.0f);
+}
+
+__device__ __forceinline__ void load8_f16(const __half *p, float v[8]) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        const uint4 raw = *reinterpret_cast<const uint4 *>(p);
+        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(h2[i]);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __half2float(p[i]);
+    }
+}
+
+// One warp per 256-value unit of one row.
+template <int TARGET>
+__global__ void __launch_bounds__(256) quantize_kernel(const __half *x, long long x_stride, int M, int K, void *out) {
+    const int nbu = K / 256;
+    const int unit = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (unit >= M * nbu) return;
+    const int m = unit / nbu, b = unit % nbu;
+    float v[8];
+    load8_f16(x + (size_t)m * x_stride + (size_t)b * 256 + 8 * lane, v);
+    if (TARGET == TYPE_Q8_0) {
+        warp_store_q80(v, reinterpret_cast<BlockQ80 *>(out) + (size_t)m * (K / 32) + 8 * b, lane);
+    } else {
+        warp_store_q8k(v, reinterpret_cast<BlockQ8K *>(out) + (size_t)m * nbu + b, lane);
+    }
+}
+
+cudaError_t launch_quantize(int target_type, const void *x, long long x_stride, int M, int K, void *out,
+                            cudaStream_t stream) {
+    const int units = M * (K / 256);
+    if (units == 0) return cudaSuccess;
+    const dim3 grid((units + 7) / 8), block(256);
+    if (target_type == TYPE_Q8_0)
+        quantize_kernel<TYPE_Q8_0><<<grid, block, 0, stream>>>(reinterpret_cast<const __half *>(x), x_stride, M, K, out);
+    else
+        quantize_kernel<TYPE_Q4_K><<<grid, block, 0, stream>>>(reinterpret_cast<const __half *>(x), x_stride, M, K, out);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ RMSNorm (+ Q8_K)
+
+// One CTA per row.  x_out = fp16((x * inv_rms) * gamma), inv_rms = 1 / sqrt(sum(x^2) / K + 1e-6)
+// with each operation rounded as in ENG:4291-4299; the fp32 sum of squares is a tree sum
+// (the reference's scalar loop adds sequentially, its NEON loop in eight lanes), so outputs
+// can differ from either in the last fp16 bit.
+__global__ void __launch_bounds__(256) rmsnorm_q8k_kernel(const __half *x, const __half *gamma, __half *out,
+                                                          BlockQ8K *q8k, int K) {
+    const int m = blockIdx.x;
+    const __half *xr = x + (size_t)m * K;
+    __half *yr = out + (size_t)m * K;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < K; i += 256) {
+        const float v = __half2float(xr[i]);
+        ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    __shared__ float red[8];
+    __shared__ float s_inv;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int i = 0; i < 8; ++i) t = __fadd_rn(t, red[i]);
+        const float inv_k = __fdiv_rn(1.0f, (float)K);
+        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(t, inv_k), 1.0e-6f)));
+    }
+    __syncthreads();
+    const float inv_rms = s_inv;
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nbu = K / 256;
+    for (int b = warp; b < nbu; b += 8) {
+        const int base = b * 256 + 8 * lane;
+        float v[8];
+        uint32_t packed[4];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            const float y0 = __fmul_rn(__fmul_rn(__half2float(xr[base + i]), inv_rms), __half2float(gamma[base + i]));
+            const float y1 =
+                __fmul_rn(__fmul_rn(__half2float(xr[base + i + 1]), inv_rms), __half2float(gamma[base + i + 1]));
+            const __half h0 = __float2half_rn(y0), h1 = __float2half_rn(y1);
+            v[i] = __half2float(h0);
+            v[i + 1] = __half2float(h1);
+            packed[i / 2] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+        }
+        if ((reinterpret_cast<uintptr_t>(yr + base) & 15) == 0) {
+            *reinterpret_cast<uint4 *>(yr + base) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) *reinterpret_cast<uint32_t *>(yr + base + 2 * i) = packed[i];
+        }
+        if (q8k) warp_store_q8k(v, q8k + (size_t)m * nbu + b, lane);
+    }
+}
+
+cudaError_t launch_rmsnorm_q8k(const void *x, const void *gamma, void *out, void *q8k, int M, int K,
+                               cudaStream_t stream, bool pdl) {
+    if (M == 0) return cudaSuccess;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(M);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, rmsnorm_q8k_kernel, reinterpret_cast<const __half *>(x),
+                              reinterpret_cast<const __half *>(gamma), reinterpret_cast<__half *>(out),
+                              reinterpret_cast<BlockQ8K *>(q8k), K);
+}
+
+// ------------------------------------------------------------------ SwiGLU (+ Q8_K)
+
+// One warp per 256-value unit: gate = fp16((g / (1 + exp(-g))) * u), ENG:4350-4356, then Q8_K
+// of the rounded values (ENG:4357).
+__global__ void __launch_bounds__(256) swiglu_q8k_kernel(__half *gate, const __half *up, BlockQ8K *q8k, int M, int N) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int nbu = N / 256;
+    const int unit = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (unit >= M * nbu) return;
+    const int m = unit / nbu, b = unit % nbu;
+    const size_t off = (size_t)m * N + (size_t)b * 256 + 8 * lane;
+    float g[8], u[8], v[8];
+    load8_f16(gate + off, g);
+    load8_f16(up + off, u);
+    uint32_t packed[4];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        const float y0 = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, expf(-g[i]))), u[i]);
+        const float y1 = __fmul_rn(__fdiv_rn(g[i + 1], __fadd_rn(1.0f, expf(-g[i + 1]))), u[i + 1]);
+        const __half h0 = __float2half_rn(y0), h1 = __float2half_rn(y1);
+        v[i] = __half2float(h0);
+        v[i + 1] = __half2float(h1);
+        packed[i / 2] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+    }
+    if ((reinterpret_cast<uintptr_t>(gate + off) & 15) == 0) {
+        *reinterpret_cast<uint4 *>(gate + off) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) *reinterpret_cast<uint32_t *>(gate + off + 2 * i) = packed[i];
+    }
+    if (q8k) warp_store_q8k(v, q8k + (size_t)m * nbu + b, lane);
+}
+
+cudaError_t launch_swiglu_q8k(void *gate, const void *up, void *q8k, int M, int N, cudaStream_t stream, bool pdl) {
+    const int units = M * (N / 256);
+    if (units == 0) return cudaSuccess;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((units + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, swiglu_q8k_kernel, reinterpret_cast<__half *>(gate),
+                              reinterpret_cast<const __half *>(up), reinterpret_cast<BlockQ8K *>(q8k), M, N);
+}
+
+// ------------------------------------------------------------------ weight repack
+
+// GGUF rows -> device layout (see kq_common.cuh).  One thread per device byte; runs once per
+// tensor at upload.
+__global__ void repack_kernel(int type, const uint8_t *gguf, uint8_t *dev, int rows, int K, size_t dev_rb) {
+    const size_t total = (size_t)rows * dev_rb;
+    const size_t nb = (type == TYPE_Q8_0) ? (size_t)K / 32 : (size_t)K / 256;
+    const size_t src_rb = nb * (size_t)block_bytes(type);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / dev_rb, o = i % dev_rb;
+        const uint8_t *src = gguf + r * src_rb;
+        uint8_t v = 0;
+        if (type == TYPE_Q6_K) {
+            if (o < nb * 208) {
+                v = src[(o / 208) * 210 + (o % 208)];
+            } else if (o < nb * 210) {
+                const size_t j = o - nb * 208;       // d plane: 2 bytes per block
+                v = src[(j / 2) * 210 + 208 + (j % 2)];
+            }
+        } else {  // Q8_0
+            if (o < (size_t)K) {
+                v = src[(o / 32) * 34 + 2 + (o % 32)];
+            } else if (o < (size_t)K + nb * 2) {
+                const size_t j = o - (size_t)K;
+                v = src[(j / 2) * 34 + (j % 2)];
+            }
+        }
+        dev[i] = v;
+    }
+}
+
+cudaError_t launch_repack(int type, const uint8_t *gguf, uint8_t *dev, int rows, int K, cudaStream_t stream) {
+    const size_t rb = dev_row_bytes(type, K);
+    if (type == TYPE_Q4_K || type == TYPE_Q5_K) {
+        return cudaMemcpyAsync(dev, gguf, (size_t)rows * rb, cudaMemcpyDeviceToDevice, stream);
+    }
+    const size_t total = (size_t)rows * rb;
+    const int threads = 256;
+    const int blocks = (int)std::min<size_t>((total + threads - 1) / threads, 148 * 64);
+    repack_kernel<<<blocks, threads, 0, stream>>>(type, gguf, dev, rows, K, rb);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ dequant to fp16
+
+// One thread per output value, from the device layout; same rounding sequence as the
+// reference's scalar dequant loops.
+__global__ void dequant_kernel(int type, const uint8_t *dev, size_t rb, int rows, int K, __half *out) {
+    const size_t total = (size_t)rows * K;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / K;
+        const int e = (int)(i % K);
+        const uint8_t *row = dev + r * rb;
+        float y;
+        if (type == TYPE_Q8_0) {
+            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(row + K + 2 * (e / 32)));
+            y = __fmul_rn(d, (float)(int8_t)row[e]);
+        } else if (type == TYPE_Q6_K) {
+            const int b = e / 256, w = e % 256;
+            const uint8_t *blk = row + (size_t)b * 208;
+            const int hh = w / 128, g = (w % 128) / 32, l = w % 32;
+            const uint8_t ql = blk[64 * hh + l + 32 * (g & 1)];
+            const uint8_t qh = blk[128 + 32 * hh + l];
+            const int lo = (g >= 2) ? (ql >> 4) : (ql & 0x0F);
+            const int q = (lo | (((qh >> (2 * g)) & 3) << 4)) - 32;
+            const int sc = (int)(int8_t)blk[192 + 8 * hh + 2 * g + (l >= 16)];
+            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(row + (size_t)(K / 256) * 208 + 2 * b));
+            y = __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
+        } else {
+            const int bbytes = (type == TYPE_Q4_K) ? 144 : 176;
+            const int b = e / 256, w = e % 256;
+            const uint8_t *blk = row + (size_t)b * bbytes;
+            const int c = w / 64, hi = (w % 64) / 32, l = w % 32;
+            const int j = 2 * c + hi;
+            const uint8_t *s = blk + 4;
+            int sc, mn;
+            if (j < 4) {
+                sc = s[j] & 63;
+                mn = s[j + 4] & 63;
+            } else {
+                sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+                mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+            }
+            const uint8_t *qs = (type == TYPE_Q4_K) ? blk + 16 : blk + 48;
+            int q = hi ? (qs[32 * c + l] >> 4) : (qs[32 * c + l] & 0x0F);
+            if (type == TYPE_Q5_K) q += ((blk[16 + l] >> j) & 1) ? 16 : 0;
+            const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
+            const float d = half_bits_to_float(dd), dmin = half_bits_to_float(dd >> 16);
+            y = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)mn));
+        }
+        out[i] = __float2half_rn(y);
+    }
+}
+
+cudaError_t launch_dequant(int type, const uint8_t *dev, size_t row_bytes, int rows, int K, void *out,
+                           cudaStream_t stream) {
+    const size_t total = (size_t)rows * K;
+    if (total == 0) return cudaSuccess;
+    const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 32);
+    dequant_kernel<<<blocks, 256, 0, stream>>>(type, dev, row_bytes, rows, K, reinterpret_cast<__half *>(out));
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ argmax keys -> (row, value)
+
+// keys[m] = (ordered value << 32) | (0xFFFFFFFF - index); index maps through ids when given.
+__global__ void argmax_finalize_kernel(const unsigned long long *keys, int M, const uint32_t *ids, uint32_t *toks,
+                                       float *vals) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m >= M) return;
+    const unsigned long long k = keys[m];
+    if (k == 0ull) {  // no row reported (empty list or a kernel that stopped early)
+        if (toks) toks[m] = 0xFFFFFFFFu;
+        if (vals) vals[m] = -INFINITY;
+        return;
+    }
+    const uint32_t o = (uint32_t)(k >> 32);
+    const uint32_t b = (o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o;
+    const uint32_t idx = 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
+    if (toks) toks[m] = ids ? ids[idx] : idx;
+    if (vals) vals[m] = __uint_as_float(b);
+}
+
+cudaError_t launch_argmax_finalize(const unsigned long long *keys, int M, const uint32_t *ids, uint32_t *toks,
+                                   float *vals, cudaStream_t stream) {
+    argmax_finalize_kernel<<<(M + 127) / 128, 128, 0, stream>>>(keys, M, ids, toks, vals);
+    return cudaGetLastError();
+}
+
+}  // namespace kq

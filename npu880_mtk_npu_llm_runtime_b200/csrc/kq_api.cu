@@ -1,0 +1,926 @@
+// kq_api.cu -- the C ABI of libkq (include/kq.h): contexts, device weights, dispatch.
+//
+// Host-side replacement of the engine's dispatch layer (sdot_gemm_multi_dispatch and its
+// pool, src/v182_r22_breakthrough_engine.c:3442-4262): argument validation, the
+// pre-quantized-input state, host<->device staging for the host-pointer entry points, and
+// the grouping of tasks into kernel launches.
+#include "kq_common.cuh"
+#include "kq_internal.h"
+#include "../../include/kq.h"
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+struct kq_weight {
+    uint32_t type;
+    int rows, cols;
+    size_t row_bytes;  // device layout
+    uint8_t *d;
+    size_t bytes;
+};
+
+namespace {
+
+struct DevBuf {
+    void *p = nullptr;
+    size_t cap = 0;
+};
+
+}  // namespace
+
+struct kq_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    int num_sms = 0;
+    int *d_status = nullptr;     // device-side error word
+    bool pdl = true;
+    bool inject_timeout = false;  // test hook: GEMV consumers wait on a barrier nothing completes
+    unsigned long long timeout_ns = 1000000000ull;
+    std::string err;
+
+    // scratch (grown on demand, freed at destroy)
+    DevBuf x, res, out16, out32, q8k_pending, q8k_cur, q80_cur, tmp, misc, keys;
+
+    // the engine's g_sdot_input state: pending pre-quantized Q8_K input (ENG:4184) and the
+    // current input rows for row-level calls (kept as fp16 on the device, quantized lazily)
+    bool pending = false;
+    int pending_M = 0, pending_K = 0;
+    int cur_M = 0, cur_K = 0;
+    bool cur_q8k_valid = false, cur_q80_valid = false, cur_x_valid = false;
+};
+
+namespace {
+
+int fail(kq_ctx *c, int code, const char *fmt, ...) {
+    if (c) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof buf, fmt, ap);
+        va_end(ap);
+        c->err = buf;
+    }
+    return code;
+}
+
+int cuda_fail(kq_ctx *c, cudaError_t e, const char *what) {
+    return fail(c, e == cudaErrorMemoryAllocation ? KQ_ERR_OUT_OF_MEMORY : KQ_ERR_CUDA, "%s: %s", what,
+                cudaGetErrorString(e));
+}
+
+#define KQ_CUDA(ctx, call)                                   \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call); \
+    } while (0)
+
+bool is_kquant(uint32_t t) { return t == KQ_TYPE_Q4_K || t == KQ_TYPE_Q5_K || t == KQ_TYPE_Q6_K; }
+bool supported(uint32_t t) { return is_kquant(t) || t == KQ_TYPE_Q8_0; }
+
+int ensure(kq_ctx *c, DevBuf &b, size_t bytes) {
+    if (b.cap >= bytes) return KQ_OK;
+    if (b.p) {
+        cudaStreamSynchronize(c->stream);
+        cudaFree(b.p);
+        b.p = nullptr;
+        b.cap = 0;
+    }
+    size_t cap = std::max<size_t>(bytes, 4096);
+    cap = (cap + 255) & ~(size_t)255;
+    cudaError_t e = cudaMalloc(&b.p, cap);
+    if (e != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(scratch)");
+    b.cap = cap;
+    return KQ_OK;
+}
+
+// Read and clear the device status word after the stream drained.
+int check_device_status(kq_ctx *c) {
+    int st = 0;
+    cudaError_t e = cudaMemcpyAsync(&st, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, e, "status readback");
+    if (st != kq::DEV_OK) {
+        cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream);
+        cudaStreamSynchronize(c->stream);
+        if (st == kq::DEV_ERR_TIMEOUT) return fail(c, KQ_ERR_TIMEOUT, "a device-side wait timed out");
+        return fail(c, KQ_ERR_CUDA, "device error code %d", st);
+    }
+    return KQ_OK;
+}
+
+int sync_and_check(kq_ctx *c) {
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, e, "cudaStreamSynchronize");
+    return check_device_status(c);
+}
+
+int validate_task(kq_ctx *c, const kq_task &t, int K) {
+    if (!t.w) return fail(c, KQ_ERR_INVALID_ARGUMENT, "task weight is NULL");
+    if (t.w->cols != K) return fail(c, KQ_ERR_SHAPE, "task weight has %d columns, input K = %d", t.w->cols, K);
+    if (t.rows < 0 || t.row_begin < 0 || (long long)t.row_begin + t.rows > t.w->rows)
+        return fail(c, KQ_ERR_SHAPE, "task rows [%d, %d) outside weight rows %d", t.row_begin, t.row_begin + t.rows,
+                    t.w->rows);
+    if (t.dst && t.dst_stride < (size_t)t.rows) return fail(c, KQ_ERR_INVALID_ARGUMENT, "dst_stride < rows");
+    if (t.residual && t.res_stride < (size_t)t.rows) return fail(c, KQ_ERR_INVALID_ARGUMENT, "res_stride < rows");
+    if (t.dst_f32 && t.dst_f32_stride < (size_t)t.rows)
+        return fail(c, KQ_ERR_INVALID_ARGUMENT, "dst_f32_stride < rows");
+    return KQ_OK;
+}
+
+int validate_mk(kq_ctx *c, int M, int K) {
+    if (M < 1 || M > KQ_MAX_M) return fail(c, KQ_ERR_SHAPE, "M = %d outside [1, %d]", M, KQ_MAX_M);
+    if (K < 256 || K > KQ_MAX_K || (K % 256) != 0)
+        return fail(c, KQ_ERR_SHAPE, "K = %d must be a positive multiple of 256 up to %d", K, KQ_MAX_K);
+    return KQ_OK;
+}
+
+// Run the tasks (device pointers) over input rows [0, M): fp16 x, or pre-quantized act_q8k /
+// act_q80.  Tasks of the same type share a launch; M is processed in tiles of up to 8 rows.
+struct GemvExtra {
+    int *dbg_sumi = nullptr, *dbg_summ = nullptr;
+    unsigned long long *argmax = nullptr;  // [M] keys
+    int argmax_f16 = 0;
+    const uint32_t *row_ids = nullptr;     // gather list for tasks[0]
+    int scatter = 0;
+};
+
+int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half *x, long long x_stride,
+             const void *act_q8k, const void *act_q80, const GemvExtra &ex = GemvExtra()) {
+    const int types[4] = {KQ_TYPE_Q4_K, KQ_TYPE_Q5_K, KQ_TYPE_Q6_K, KQ_TYPE_Q8_0};
+    for (int ti = 0; ti < 4; ++ti) {
+        const int type = types[ti];
+        std::vector<int> idx;
+        for (int i = 0; i < n; ++i)
+            if ((int)tasks[i].w->type == type && tasks[i].rows > 0) idx.push_back(i);
+        if (idx.empty()) continue;
+        const void *act = (type == KQ_TYPE_Q8_0) ? act_q80 : act_q8k;
+        if (!x && !act) return fail(c, KQ_ERR_NOT_READY, "no activation for type %d", type);
+        int m0 = 0;
+        while (m0 < M) {
+            int mt = std::min(8, M - m0);
+            kq::GemvLaunch L{};
+            L.type = type;
+            L.K = K;
+            L.row_bytes = tasks[idx[0]].w->row_bytes;
+            L.n_tasks = (int)idx.size();
+            for (int j = 0; j < L.n_tasks; ++j) {
+                const kq_task &t = tasks[idx[j]];
+                kq::GemvTaskHost &h = L.tasks[j];
+                h.w = t.w->d + (size_t)t.row_begin * t.w->row_bytes;
+                h.rows = t.rows;
+                h.dst = t.dst ? (void *)(t.dst + (size_t)m0 * t.dst_stride) : nullptr;
+                h.dst_stride = (long long)t.dst_stride;
+                h.res = t.residual ? (const void *)(t.residual + (size_t)m0 * t.res_stride) : nullptr;
+                h.res_stride = (long long)t.res_stride;
+                h.dst_f32 = t.dst_f32 ? t.dst_f32 + (size_t)m0 * t.dst_f32_stride : nullptr;
+                h.f32_stride = (long long)t.dst_f32_stride;
+                if (ex.dbg_sumi && idx[j] == 0) {
+                    const size_t bpr = (type == KQ_TYPE_Q8_0) ? (size_t)K / 32 : (size_t)K / 256;
+                    h.dbg_sumi = ex.dbg_sumi + (size_t)m0 * t.rows * bpr;
+                    h.dbg_summ = ex.dbg_summ + (size_t)m0 * t.rows * bpr;
+                }
+                if (ex.row_ids && idx[j] == 0) {
+                    h.w = t.w->d;
+                    h.row_ids = ex.row_ids;
+                    h.scatter = ex.scatter;
+                }
+                h.index_base = t.row_begin;
+            }
+            if (x) {
+                L.x = x + (size_t)m0 * x_stride;
+                L.x_stride = x_stride;
+            } else if (type == KQ_TYPE_Q8_0) {
+                L.act = reinterpret_cast<const kq::BlockQ80 *>(act) + (size_t)m0 * (K / 32);
+            } else {
+                L.act = reinterpret_cast<const kq::BlockQ8K *>(act) + (size_t)m0 * (K / 256);
+            }
+            L.M = mt;
+            L.status = c->d_status;
+            L.timeout_ns = c->timeout_ns;
+            L.pdl = c->pdl;
+            L.num_sms = c->num_sms;
+            L.argmax = ex.argmax ? ex.argmax + m0 : nullptr;
+            L.argmax_f16 = ex.argmax_f16;
+            L.inject_wait = c->inject_timeout ? 1 : 0;
+            cudaError_t e = kq::launch_gemv(L, c->stream);
+            if (e == cudaErrorInvalidConfiguration && mt > 1) {
+                // activation too large for shared memory at this tile: halve the tile
+                cudaGetLastError();
+                L.M = mt = std::max(1, mt / 2);
+                e = kq::launch_gemv(L, c->stream);
+            }
+            if (e != cudaSuccess) return cuda_fail(c, e, "gemv launch");
+            m0 += mt;
+        }
+    }
+    return KQ_OK;
+}
+
+void set_current_x(kq_ctx *c, int M, int K) {
+    c->cur_M = M;
+    c->cur_K = K;
+    c->cur_x_valid = true;
+    c->cur_q8k_valid = false;
+    c->cur_q80_valid = false;
+}
+
+// Make sure the current input is available quantized as `type` (Q8_K for K-quants, Q8_0).
+int current_act(kq_ctx *c, uint32_t type, const void **act) {
+    if (c->cur_M == 0) return fail(c, KQ_ERR_NOT_READY, "no current quantized input in the context");
+    const int M = c->cur_M, K = c->cur_K;
+    if (type == KQ_TYPE_Q8_0) {
+        if (!c->cur_q80_valid) {
+            if (!c->cur_x_valid) return fail(c, KQ_ERR_NOT_READY, "current input has no Q8_0 form");
+            int r = ensure(c, c->q80_cur, (size_t)M * (K / 32) * sizeof(kq::BlockQ80));
+            if (r) return r;
+            KQ_CUDA(c, kq::launch_quantize(KQ_TYPE_Q8_0, c->x.p, K, M, K, c->q80_cur.p, c->stream));
+            c->cur_q80_valid = true;
+        }
+        *act = c->q80_cur.p;
+    } else {
+        if (!c->cur_q8k_valid) {
+            if (!c->cur_x_valid) return fail(c, KQ_ERR_NOT_READY, "current input has no Q8_K form");
+            int r = ensure(c, c->q8k_cur, (size_t)M * (K / 256) * sizeof(kq::BlockQ8K));
+            if (r) return r;
+            KQ_CUDA(c, kq::launch_quantize(KQ_TYPE_Q4_K, c->x.p, K, M, K, c->q8k_cur.p, c->stream));
+            c->cur_q8k_valid = true;
+        }
+        *act = c->q8k_cur.p;
+    }
+    return KQ_OK;
+}
+
+int h2d(kq_ctx *c, DevBuf &b, const void *src, size_t bytes) {
+    int r = ensure(c, b, bytes);
+    if (r) return r;
+    KQ_CUDA(c, cudaMemcpyAsync(b.p, src, bytes, cudaMemcpyHostToDevice, c->stream));
+    return KQ_OK;
+}
+
+}  // namespace
+
+// =================================================================== library / context
+
+extern "C" const char *kq_version(void) { return "kq-b200 0.1 (sm_100a)"; }
+
+extern "C" const char *kq_status_string(int s) {
+    switch (s) {
+        case KQ_OK: return "ok";
+        case KQ_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case KQ_ERR_UNSUPPORTED_TYPE: return "unsupported type";
+        case KQ_ERR_SHAPE: return "shape error";
+        case KQ_ERR_CUDA: return "CUDA error";
+        case KQ_ERR_OUT_OF_MEMORY: return "out of device memory";
+        case KQ_ERR_NO_DEVICE: return "no CUDA device";
+        case KQ_ERR_TIMEOUT: return "device-side wait timed out";
+        case KQ_ERR_NOT_READY: return "no pending quantized input";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int kq_init(int device, kq_ctx **out) {
+    if (!out) return KQ_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return KQ_ERR_NO_DEVICE;
+    }
+    if (device < 0 || device >= n) return KQ_ERR_INVALID_ARGUMENT;
+    kq_ctx *c = new kq_ctx();
+    c->device = device;
+    if (cudaSetDevice(device) != cudaSuccess) {
+        delete c;
+        return KQ_ERR_CUDA;
+    }
+    cudaDeviceProp prop{};
+    cudaGetDeviceProperties(&prop, device);
+    c->num_sms = prop.multiProcessorCount;
+    if (prop.major < 10) {
+        delete c;
+        return KQ_ERR_NO_DEVICE;  // built for sm_100a only
+    }
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&c->d_status, sizeof(int)) != cudaSuccess ||
+        cudaMemset(c->d_status, 0, sizeof(int)) != cudaSuccess) {
+        if (c->stream) cudaStreamDestroy(c->stream);
+        delete c;
+        return KQ_ERR_CUDA;
+    }
+    c->own_stream = true;
+    *out = c;
+    return KQ_OK;
+}
+
+extern "C" int kq_destroy(kq_ctx *c) {
+    if (!c) return KQ_ERR_INVALID_ARGUMENT;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    for (DevBuf *b : {&c->x, &c->res, &c->out16, &c->out32, &c->q8k_pending, &c->q8k_cur, &c->q80_cur, &c->tmp,
+                      &c->misc, &c->keys})
+        if (b->p) cudaFree(b->p);
+    cudaFree(c->d_status);
+    if (c->own_stream) cudaStreamDestroy(c->stream);
+    delete c;
+    return KQ_OK;
+}
+
+extern "C" int kq_set_stream(kq_ctx *c, void *s) {
+    if (!c) return KQ_ERR_INVALID_ARGUMENT;
+    cudaStreamSynchronize(c->stream);
+    if (c->own_stream) cudaStreamDestroy(c->stream);
+    c->stream = reinterpret_cast<cudaStream_t>(s);
+    c->own_stream = false;
+    return KQ_OK;
+}
+
+extern "C" void *kq_get_stream(const kq_ctx *c) { return c ? (void *)c->stream : nullptr; }
+
+extern "C" int kq_synchronize(kq_ctx *c) {
+    if (!c) return KQ_ERR_INVALID_ARGUMENT;
+    cudaSetDevice(c->device);
+    return sync_and_check(c);
+}
+
+extern "C" const char *kq_last_error(const kq_ctx *c) { return c ? c->err.c_str() : "no context"; }
+
+extern "C" int kq_set_option(kq_ctx *c, const char *name, long long value) {
+    if (!c || !name) return KQ_ERR_INVALID_ARGUMENT;
+    if (!strcmp(name, "pdl")) {
+        c->pdl = value != 0;
+        return KQ_OK;
+    }
+    if (!strcmp(name, "inject_timeout")) {
+        c->inject_timeout = value != 0;
+        return KQ_OK;
+    }
+    if (!strcmp(name, "timeout_ms")) {
+        if (value <= 0) return fail(c, KQ_ERR_INVALID_ARGUMENT, "timeout_ms must be positive");
+        c->timeout_ns = (unsigned long long)value * 1000000ull;
+        return KQ_OK;
+    }
+    if (!strcmp(name, "timeout_us")) {
+        if (value <= 0) return fail(c, KQ_ERR_INVALID_ARGUMENT, "timeout_us must be positive");
+        c->timeout_ns = (unsigned long long)value * 1000ull;
+        return KQ_OK;
+    }
+    return fail(c, KQ_ERR_INVALID_ARGUMENT, "unknown option '%s'", name);
+}
+
+extern "C" uint64_t kq_row_bytes(uint32_t type, uint64_t k) {
+    // compute_ggml_bytes, ENG:364-374
+    switch (type) {
+        case KQ_TYPE_F32: return k * 4;
+        case KQ_TYPE_F16: return k * 2;
+        case KQ_TYPE_Q8_0: return (k / 32) * 34;
+        case KQ_TYPE_Q4_K: return (k / 256) * 144;
+        case KQ_TYPE_Q5_K: return (k / 256) * 176;
+        case KQ_TYPE_Q6_K: return (k / 256) * 210;
+        default: return 0;
+    }
+}
+
+// =================================================================== weights
+
+static int weight_create(kq_ctx *c, const void *src, bool src_on_device, uint32_t type, int rows, int cols,
+                         kq_weight **out) {
+    if (!c || !src || !out) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    if (!supported(type)) return fail(c, KQ_ERR_UNSUPPORTED_TYPE, "type %u is not Q4_K/Q5_K/Q6_K/Q8_0", type);
+    if (rows < 1) return fail(c, KQ_ERR_SHAPE, "rows = %d", rows);
+    if (cols < 256 || cols > KQ_MAX_K || cols % 256)
+        return fail(c, KQ_ERR_SHAPE, "cols = %d must be a positive multiple of 256 up to %d", cols, KQ_MAX_K);
+    cudaSetDevice(c->device);
+    const size_t gguf_bytes = (size_t)rows * kq_row_bytes(type, cols);
+    const size_t rb = kq::dev_row_bytes((int)type, cols);
+    kq_weight *w = new kq_weight();
+    w->type = type;
+    w->rows = rows;
+    w->cols = cols;
+    w->row_bytes = rb;
+    w->bytes = rb * rows;
+    cudaError_t e = cudaMalloc(&w->d, w->bytes);
+    if (e != cudaSuccess) {
+        delete w;
+        return cuda_fail(c, e, "cudaMalloc(weight)");
+    }
+    void *staging = nullptr;
+    const uint8_t *gsrc = reinterpret_cast<const uint8_t *>(src);
+    if (!src_on_device) {
+        if (type == KQ_TYPE_Q4_K || type == KQ_TYPE_Q5_K) {
+            e = cudaMemcpyAsync(w->d, src, gguf_bytes, cudaMemcpyHostToDevice, c->stream);
+        } else {
+            e = cudaMalloc(&staging, gguf_bytes);
+            if (e == cudaSuccess) e = cudaMemcpyAsync(staging, src, gguf_bytes, cudaMemcpyHostToDevice, c->stream);
+            if (e == cudaSuccess) e = kq::launch_repack((int)type, (const uint8_t *)staging, w->d, rows, cols, c->stream);
+        }
+    } else {
+        e = kq::launch_repack((int)type, gsrc, w->d, rows, cols, c->stream);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (staging) cudaFree(staging);
+    if (e != cudaSuccess) {
+        cudaFree(w->d);
+        delete w;
+        return cuda_fail(c, e, "weight upload");
+    }
+    *out = w;
+    return KQ_OK;
+}
+
+extern "C" int kq_weight_upload(kq_ctx *c, const void *b, uint32_t type, int rows, int cols, kq_weight **out) {
+    return weight_create(c, b, false, type, rows, cols, out);
+}
+
+extern "C" int kq_weight_upload_device(kq_ctx *c, const void *b, uint32_t type, int rows, int cols, kq_weight **out) {
+    return weight_create(c, b, true, type, rows, cols, out);
+}
+
+extern "C" int kq_weight_free(kq_ctx *c, kq_weight *w) {
+    if (!w) return KQ_ERR_INVALID_ARGUMENT;
+    if (c) {
+        cudaSetDevice(c->device);
+        cudaStreamSynchronize(c->stream);
+    }
+    cudaFree(w->d);
+    delete w;
+    return KQ_OK;
+}
+
+extern "C" int kq_weight_info(const kq_weight *w, uint32_t *type, int *rows, int *cols, uint64_t *device_bytes) {
+    if (!w) return KQ_ERR_INVALID_ARGUMENT;
+    if (type) *type = w->type;
+    if (rows) *rows = w->rows;
+    if (cols) *cols = w->cols;
+    if (device_bytes) *device_bytes = w->bytes;
+    return KQ_OK;
+}
+
+// =================================================================== activations
+
+extern "C" int kq_quantize_q8k_async(kq_ctx *c, const uint16_t *x, int M, int K, void *out) {
+    if (!c || !x || !out) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, K)) return r;
+    KQ_CUDA(c, kq::launch_quantize(KQ_TYPE_Q4_K, x, K, M, K, out, c->stream));
+    return KQ_OK;
+}
+
+extern "C" int kq_quantize_q8_0_async(kq_ctx *c, const uint16_t *x, int M, int K, void *out) {
+    if (!c || !x || !out) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, K)) return r;
+    KQ_CUDA(c, kq::launch_quantize(KQ_TYPE_Q8_0, x, K, M, K, out, c->stream));
+    return KQ_OK;
+}
+
+static int quantize_host(kq_ctx *c, int target, const uint16_t *x, int M, int K, void *out) {
+    if (!c || !x || !out) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, K)) return r;
+    cudaSetDevice(c->device);
+    const size_t ob = target == KQ_TYPE_Q8_0 ? (size_t)M * (K / 32) * sizeof(kq::BlockQ80)
+                                             : (size_t)M * (K / 256) * sizeof(kq::BlockQ8K);
+    if (int r = h2d(c, c->x, x, (size_t)M * K * 2)) return r;
+    if (int r = ensure(c, c->tmp, ob)) return r;
+    KQ_CUDA(c, kq::launch_quantize(target, c->x.p, K, M, K, c->tmp.p, c->stream));
+    KQ_CUDA(c, cudaMemcpyAsync(out, c->tmp.p, ob, cudaMemcpyDeviceToHost, c->stream));
+    set_current_x(c, M, K);
+    return sync_and_check(c);
+}
+
+extern "C" int kq_quantize_q8k(kq_ctx *c, const uint16_t *x, int M, int K, void *out) {
+    return quantize_host(c, KQ_TYPE_Q4_K, x, M, K, out);
+}
+
+extern "C" int kq_quantize_q8_0(kq_ctx *c, const uint16_t *x, int M, int K, void *out) {
+    return quantize_host(c, KQ_TYPE_Q8_0, x, M, K, out);
+}
+
+// =================================================================== matrix products
+
+static int validate_tasks(kq_ctx *c, const kq_task *tasks, int n, int K) {
+    if (!tasks || n < 1 || n > KQ_MAX_TASKS)
+        return fail(c, KQ_ERR_INVALID_ARGUMENT, "n_tasks = %d outside [1, %d]", n, KQ_MAX_TASKS);
+    for (int i = 0; i < n; ++i)
+        if (int r = validate_task(c, tasks[i], K)) return r;
+    return KQ_OK;
+}
+
+extern "C" int kq_gemm_multi_async(kq_ctx *c, const uint16_t *x, size_t x_stride, int M, int K, const kq_task *tasks,
+                                   int n) {
+    if (!c || !x) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, K)) return r;
+    if (int r = validate_tasks(c, tasks, n, K)) return r;
+    if (x_stride < (size_t)K) return fail(c, KQ_ERR_INVALID_ARGUMENT, "x_stride < K");
+    return run_gemv(c, tasks, n, M, K, reinterpret_cast<const __half *>(x), (long long)x_stride, nullptr, nullptr);
+}
+
+extern "C" int kq_gemm_multi_q8_async(kq_ctx *c, const void *q8k, const void *q80, int M, int K, const kq_task *tasks,
+                                      int n) {
+    if (!c) return KQ_ERR_INVALID_ARGUMENT;
+    if (int r = validate_mk(c, M, K)) return r;
+    if (int r = validate_tasks(c, tasks, n, K)) return r;
+    for (int i = 0; i < n; ++i) {
+        if (tasks[i].w->type == KQ_TYPE_Q8_0 && !q80) return fail(c, KQ_ERR_INVALID_ARGUMENT, "Q8_0 task needs act_q80");
+        if (tasks[i].w->type != KQ_TYPE_Q8_0 && !q8k) return fail(c, KQ_ERR_INVALID_ARGUMENT, "K-quant task needs act_q8k");
+    }
+    return run_gemv(c, tasks, n, M, K, nullptr, 0, q8k, q80);
+}
+
+extern "C" int kq_sdot_gemm_multi_dispatch(kq_ctx *c, const uint16_t *x, int M, int K, const kq_task *tasks, int n) {
+    if (!c || !x) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, K)) return r;
+    if (int r = validate_tasks(c, tasks, n, K)) return r;
+    cudaSetDevice(c->device);
+    // the pre-quantized flag is consumed by this call whatever happens (ENG:4205-4206)
+    const bool use_pending = c->pending && c->pending_M == M && c->pending_K == K;
+    c->pending = false;
+
+    if (int r = h2d(c, c->x, x, (size_t)M * K * 2)) return r;
+    // device staging of outputs and residuals, one contiguous [M][rows] slab per task
+    size_t o16 = 0, o32 = 0, ores = 0;
+    std::vector<size_t> off16(n), off32(n), offr(n);
+    for (int i = 0; i < n; ++i) {
+        off16[i] = o16;
+        o16 += tasks[i].dst ? (size_t)M * tasks[i].rows * 2 : 0;
+        off32[i] = o32;
+        o32 += tasks[i].dst_f32 ? (size_t)M * tasks[i].rows * 4 : 0;
+        offr[i] = ores;
+        ores += tasks[i].residual ? (size_t)M * tasks[i].rows * 2 : 0;
+    }
+    if (int r = ensure(c, c->out16, o16 + 16)) return r;
+    if (int r = ensure(c, c->out32, o32 + 16)) return r;
+    if (int r = ensure(c, c->res, ores + 16)) return r;
+    kq_task dt[KQ_MAX_TASKS];
+    for (int i = 0; i < n; ++i) {
+        dt[i] = tasks[i];
+        const size_t rows = (size_t)tasks[i].rows;
+        if (tasks[i].dst) {
+            dt[i].dst = reinterpret_cast<uint16_t *>((uint8_t *)c->out16.p + off16[i]);
+            dt[i].dst_stride = rows;
+        }
+        if (tasks[i].dst_f32) {
+            dt[i].dst_f32 = reinterpret_cast<float *>((uint8_t *)c->out32.p + off32[i]);
+            dt[i].dst_f32_stride = rows;
+        }
+        if (tasks[i].residual) {
+            uint16_t *rd = reinterpret_cast<uint16_t *>((uint8_t *)c->res.p + offr[i]);
+            KQ_CUDA(c, cudaMemcpy2DAsync(rd, rows * 2, tasks[i].residual, tasks[i].res_stride * 2, rows * 2, M,
+                                         cudaMemcpyHostToDevice, c->stream));
+            dt[i].residual = rd;
+            dt[i].res_stride = rows;
+        }
+    }
+    int r;
+    if (use_pending) {
+        // Q8_K already produced on the device; Q8_0 tasks still quantize x (ENG:4212-4216)
+        bool any_q80 = false;
+        for (int i = 0; i < n; ++i) any_q80 |= tasks[i].w->type == KQ_TYPE_Q8_0;
+        const void *q80 = nullptr;
+        if (any_q80) {
+            if ((r = ensure(c, c->q80_cur, (size_t)M * (K / 32) * sizeof(kq::BlockQ80)))) return r;
+            KQ_CUDA(c, kq::launch_quantize(KQ_TYPE_Q8_0, c->x.p, K, M, K, c->q80_cur.p, c->stream));
+            q80 = c->q80_cur.p;
+        }
+        r = run_gemv(c, dt, n, M, K, nullptr, 0, c->q8k_pending.p, q80);
+        // the pending Q8_K becomes the current input for row-level calls
+        std::swap(c->q8k_pending, c->q8k_cur);
+        c->cur_M = M;
+        c->cur_K = K;
+        c->cur_x_valid = true;
+        c->cur_q8k_valid = true;
+        c->cur_q80_valid = any_q80;
+    } else {
+        r = run_gemv(c, dt, n, M, K, reinterpret_cast<const __half *>(c->x.p), K, nullptr, nullptr);
+        set_current_x(c, M, K);
+    }
+    if (r) return r;
+    for (int i = 0; i < n; ++i) {
+        const size_t rows = (size_t)tasks[i].rows;
+        if (tasks[i].dst)
+            KQ_CUDA(c, cudaMemcpy2DAsync(tasks[i].dst, tasks[i].dst_stride * 2, dt[i].dst, rows * 2, rows * 2, M,
+                                         cudaMemcpyDeviceToHost, c->stream));
+        if (tasks[i].dst_f32)
+            KQ_CUDA(c, cudaMemcpy2DAsync(tasks[i].dst_f32, tasks[i].dst_f32_stride * 4, dt[i].dst_f32, rows * 4,
+                                         rows * 4, M, cudaMemcpyDeviceToHost, c->stream));
+    }
+    return sync_and_check(c);
+}
+
+// Row-level entry points over the current input.
+static int row_level(kq_ctx *c, const kq_weight *w, uint32_t row, int m0, int M, float *out) {
+    if (!c || !w || !out) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if ((int)row >= w->rows) return fail(c, KQ_ERR_SHAPE, "row %u >= rows %d", row, w->rows);
+    if (c->cur_M == 0) return fail(c, KQ_ERR_NOT_READY, "no current input");
+    if (w->cols != c->cur_K) return fail(c, KQ_ERR_SHAPE, "weight cols %d != current K %d", w->cols, c->cur_K);
+    if (m0 < 0 || M < 1 || m0 + M > c->cur_M) return fail(c, KQ_ERR_SHAPE, "token range outside current input");
+    cudaSetDevice(c->device);
+    const void *act = nullptr;
+    if (int r = current_act(c, w->type, &act)) return r;
+    if (int r = ensure(c, c->misc, (size_t)M * 4)) return r;
+    kq_task t{};
+    t.w = w;
+    t.row_begin = (int)row;
+    t.rows = 1;
+    t.dst_f32 = reinterpret_cast<float *>(c->misc.p);
+    t.dst_f32_stride = 1;
+    const int K = c->cur_K;
+    const void *a = (w->type == KQ_TYPE_Q8_0)
+                        ? (const void *)(reinterpret_cast<const kq::BlockQ80 *>(act) + (size_t)m0 * (K / 32))
+                        : (const void *)(reinterpret_cast<const kq::BlockQ8K *>(act) + (size_t)m0 * (K / 256));
+    int r = run_gemv(c, &t, 1, M, K, nullptr, 0, w->type == KQ_TYPE_Q8_0 ? nullptr : a,
+                     w->type == KQ_TYPE_Q8_0 ? a : nullptr);
+    if (r) return r;
+    KQ_CUDA(c, cudaMemcpyAsync(out, c->misc.p, (size_t)M * 4, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+extern "C" int kq_sdot_row_batch(kq_ctx *c, const kq_weight *w, uint32_t row, int M, float *out_sums) {
+    return row_level(c, w, row, 0, M, out_sums);
+}
+
+extern "C" int kq_eval_single_lm_row_dot(kq_ctx *c, const kq_weight *w, uint32_t row_idx, int m, float *out) {
+    return row_level(c, w, row_idx, m, 1, out);
+}
+
+extern "C" int kq_debug_block_sums_async(kq_ctx *c, const kq_weight *w, int row_begin, int rows, const void *act,
+                                         int M, int32_t *sumi, int32_t *summ, float *out_f32) {
+    if (!c || !w || !act || !sumi || !summ) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, w->cols)) return r;
+    kq_task t{};
+    t.w = w;
+    t.row_begin = row_begin;
+    t.rows = rows;
+    t.dst_f32 = out_f32;
+    t.dst_f32_stride = (size_t)rows;
+    if (int r = validate_task(c, t, w->cols)) return r;
+    const bool q80 = w->type == KQ_TYPE_Q8_0;
+    GemvExtra ex;
+    ex.dbg_sumi = sumi;
+    ex.dbg_summ = summ;
+    return run_gemv(c, &t, 1, M, w->cols, nullptr, 0, q80 ? nullptr : act, q80 ? act : nullptr, ex);
+}
+
+// =================================================================== producers
+
+extern "C" int kq_rmsnorm_q8k_async(kq_ctx *c, const uint16_t *x, const uint16_t *gamma, uint16_t *out, int M, int K,
+                                    void *q8k) {
+    if (!c || !x || !gamma || !out) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, K)) return r;
+    if (!q8k) {
+        if (int r = ensure(c, c->q8k_pending, (size_t)M * (K / 256) * sizeof(kq::BlockQ8K))) return r;
+        q8k = c->q8k_pending.p;
+        c->pending = true;
+        c->pending_M = M;
+        c->pending_K = K;
+    }
+    KQ_CUDA(c, kq::launch_rmsnorm_q8k(x, gamma, out, q8k, M, K, c->stream, c->pdl));
+    return KQ_OK;
+}
+
+extern "C" int kq_swiglu_q8k_async(kq_ctx *c, uint16_t *gate, const uint16_t *up, int M, int N, void *q8k) {
+    if (!c || !gate || !up) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, N)) return r;
+    if (!q8k) {
+        if (int r = ensure(c, c->q8k_pending, (size_t)M * (N / 256) * sizeof(kq::BlockQ8K))) return r;
+        q8k = c->q8k_pending.p;
+        c->pending = true;
+        c->pending_M = M;
+        c->pending_K = N;
+    }
+    KQ_CUDA(c, kq::launch_swiglu_q8k(gate, up, q8k, M, N, c->stream, c->pdl));
+    return KQ_OK;
+}
+
+extern "C" int kq_rmsnorm_fp16_rows(kq_ctx *c, const uint16_t *x_in, const uint16_t *gamma, uint16_t *x_out, int M,
+                                    int K) {
+    if (!c || !x_in || !gamma || !x_out) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, K)) return r;
+    cudaSetDevice(c->device);
+    const size_t xb = (size_t)M * K * 2;
+    if (int r = ensure(c, c->tmp, xb + (size_t)K * 2 + 16)) return r;
+    uint16_t *dx = reinterpret_cast<uint16_t *>(c->tmp.p);
+    uint16_t *dg = dx + (size_t)M * K;
+    KQ_CUDA(c, cudaMemcpyAsync(dx, x_in, xb, cudaMemcpyHostToDevice, c->stream));
+    KQ_CUDA(c, cudaMemcpyAsync(dg, gamma, (size_t)K * 2, cudaMemcpyHostToDevice, c->stream));
+    if (int r = ensure(c, c->x, xb)) return r;
+    if (int r = kq_rmsnorm_q8k_async(c, dx, dg, reinterpret_cast<uint16_t *>(c->x.p), M, K, nullptr)) return r;
+    KQ_CUDA(c, cudaMemcpyAsync(x_out, c->x.p, xb, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+extern "C" int kq_swiglu_fp16_rows(kq_ctx *c, uint16_t *gate, const uint16_t *up, int M, int N) {
+    if (!c || !gate || !up) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, N)) return r;
+    cudaSetDevice(c->device);
+    const size_t xb = (size_t)M * N * 2;
+    if (int r = ensure(c, c->tmp, xb)) return r;
+    if (int r = ensure(c, c->x, xb)) return r;
+    KQ_CUDA(c, cudaMemcpyAsync(c->x.p, gate, xb, cudaMemcpyHostToDevice, c->stream));
+    KQ_CUDA(c, cudaMemcpyAsync(c->tmp.p, up, xb, cudaMemcpyHostToDevice, c->stream));
+    if (int r = kq_swiglu_q8k_async(c, reinterpret_cast<uint16_t *>(c->x.p), reinterpret_cast<uint16_t *>(c->tmp.p), M,
+                                    N, nullptr))
+        return r;
+    KQ_CUDA(c, cudaMemcpyAsync(gate, c->x.p, xb, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+// =================================================================== FFN block
+
+extern "C" int kq_run_ffn_async(kq_ctx *c, const kq_weight *gate, const kq_weight *up, const kq_weight *down, int M,
+                                const uint16_t *x_in, const uint16_t *gamma, uint16_t *x_out) {
+    if (!c || !gate || !up || !down || !x_in || !gamma || !x_out)
+        return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    const int hidden = gate->cols, ffn = gate->rows;
+    if (up->cols != hidden || up->rows != ffn || down->cols != ffn || down->rows != hidden)
+        return fail(c, KQ_ERR_SHAPE, "FFN weights do not chain: gate %dx%d up %dx%d down %dx%d", gate->rows,
+                    gate->cols, up->rows, up->cols, down->rows, down->cols);
+    if (int r = validate_mk(c, M, hidden)) return r;
+    if (ffn % 256) return fail(c, KQ_ERR_SHAPE, "ffn dim %d not a multiple of 256", ffn);
+    // scratch: xn [M][hidden] fp16 | g [M][ffn] | u [M][ffn] | q8k(xn) | q8k(h) | q80 forms
+    const size_t xnb = (size_t)M * hidden * 2, gb = (size_t)M * ffn * 2;
+    const size_t qa = (size_t)M * (hidden / 256) * sizeof(kq::BlockQ8K);
+    const size_t qh = (size_t)M * (ffn / 256) * sizeof(kq::BlockQ8K);
+    const size_t qa0 = (size_t)M * (hidden / 32) * sizeof(kq::BlockQ80);
+    const size_t qh0 = (size_t)M * (ffn / 32) * sizeof(kq::BlockQ80);
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    const size_t total = al(xnb) + 2 * al(gb) + al(qa) + al(qh) + al(qa0) + al(qh0);
+    if (int r = ensure(c, c->misc, total)) return r;
+    uint8_t *base = reinterpret_cast<uint8_t *>(c->misc.p);
+    uint16_t *xn = reinterpret_cast<uint16_t *>(base);
+    uint16_t *g = reinterpret_cast<uint16_t *>(base + al(xnb));
+    uint16_t *u = reinterpret_cast<uint16_t *>(base + al(xnb) + al(gb));
+    void *q_a = base + al(xnb) + 2 * al(gb);
+    void *q_h = (uint8_t *)q_a + al(qa);
+    void *q_a0 = (uint8_t *)q_h + al(qh);
+    void *q_h0 = (uint8_t *)q_a0 + al(qa0);
+
+    // RMSNorm (+ Q8_K), ENG:8285
+    KQ_CUDA(c, kq::launch_rmsnorm_q8k(x_in, gamma, xn, q_a, M, hidden, c->stream, c->pdl));
+    const bool gu_q80 = gate->type == KQ_TYPE_Q8_0 || up->type == KQ_TYPE_Q8_0;
+    if (gu_q80) KQ_CUDA(c, kq::launch_quantize(KQ_TYPE_Q8_0, xn, hidden, M, hidden, q_a0, c->stream));
+    // gate / up, ENG:8287-8290
+    kq_task gu[2] = {};
+    gu[0].w = gate;
+    gu[0].rows = ffn;
+    gu[0].dst = g;
+    gu[0].dst_stride = ffn;
+    gu[1].w = up;
+    gu[1].rows = ffn;
+    gu[1].dst = u;
+    gu[1].dst_stride = ffn;
+    if (int r = run_gemv(c, gu, 2, M, hidden, nullptr, 0, q_a, gu_q80 ? q_a0 : nullptr)) return r;
+    // SwiGLU (+ Q8_K), ENG:8292
+    KQ_CUDA(c, kq::launch_swiglu_q8k(g, u, q_h, M, ffn, c->stream, c->pdl));
+    if (down->type == KQ_TYPE_Q8_0) KQ_CUDA(c, kq::launch_quantize(KQ_TYPE_Q8_0, g, ffn, M, ffn, q_h0, c->stream));
+    // down + residual, ENG:8294-8296
+    kq_task dn{};
+    dn.w = down;
+    dn.rows = hidden;
+    dn.dst = x_out;
+    dn.dst_stride = hidden;
+    dn.residual = x_in;
+    dn.res_stride = hidden;
+    return run_gemv(c, &dn, 1, M, ffn, nullptr, 0, q_h, down->type == KQ_TYPE_Q8_0 ? q_h0 : nullptr);
+}
+
+extern "C" int kq_run_ffn(kq_ctx *c, const kq_weight *gate, const kq_weight *up, const kq_weight *down, int M,
+                          const uint16_t *x_in, const uint16_t *gamma, uint16_t *x_out) {
+    if (!c || !gate || !x_in || !gamma || !x_out) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (M < 1 || M > KQ_MAX_M) return fail(c, KQ_ERR_SHAPE, "batch_len = %d", M);
+    cudaSetDevice(c->device);
+    const int hidden = gate->cols;
+    const size_t xb = (size_t)M * hidden * 2;
+    if (int r = ensure(c, c->x, 2 * xb + (size_t)hidden * 2 + 32)) return r;
+    uint16_t *dx = reinterpret_cast<uint16_t *>(c->x.p);
+    uint16_t *dy = dx + (size_t)M * hidden;
+    uint16_t *dg = dy + (size_t)M * hidden;
+    KQ_CUDA(c, cudaMemcpyAsync(dx, x_in, xb, cudaMemcpyHostToDevice, c->stream));
+    KQ_CUDA(c, cudaMemcpyAsync(dg, gamma, (size_t)hidden * 2, cudaMemcpyHostToDevice, c->stream));
+    if (int r = kq_run_ffn_async(c, gate, up, down, M, dx, dg, dy)) return r;
+    KQ_CUDA(c, cudaMemcpyAsync(x_out, dy, xb, cudaMemcpyDeviceToHost, c->stream));
+    c->cur_M = 0;  // the FFN leaves no current input behind
+    return sync_and_check(c);
+}
+
+// =================================================================== dequant
+
+extern "C" int kq_dequant_rows_async(kq_ctx *c, const kq_weight *w, int row_begin, int rows, uint16_t *dst) {
+    if (!c || !w || !dst) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (row_begin < 0 || rows < 0 || (long long)row_begin + rows > w->rows) return fail(c, KQ_ERR_SHAPE, "row range");
+    KQ_CUDA(c, kq::launch_dequant((int)w->type, w->d + (size_t)row_begin * w->row_bytes, w->row_bytes, rows, w->cols,
+                                  dst, c->stream));
+    return KQ_OK;
+}
+
+extern "C" int kq_dequant_rows(kq_ctx *c, const kq_weight *w, int row_begin, int rows, uint16_t *dst) {
+    if (!c || !w || !dst) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    cudaSetDevice(c->device);
+    const size_t b = (size_t)rows * w->cols * 2;
+    if (int r = ensure(c, c->tmp, b + 16)) return r;
+    if (int r = kq_dequant_rows_async(c, w, row_begin, rows, reinterpret_cast<uint16_t *>(c->tmp.p))) return r;
+    KQ_CUDA(c, cudaMemcpyAsync(dst, c->tmp.p, b, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+// =================================================================== LM head
+
+extern "C" int kq_lm_head_argmax_async(kq_ctx *c, const kq_weight *w, const uint16_t *x, int M, uint16_t *logits,
+                                       float *logits_f32, uint32_t *toks, float *vals) {
+    if (!c || !w || !x) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, w->cols)) return r;
+    if (int r = ensure(c, c->keys, (size_t)M * 8)) return r;
+    auto *keys = reinterpret_cast<unsigned long long *>(c->keys.p);
+    KQ_CUDA(c, cudaMemsetAsync(keys, 0, (size_t)M * 8, c->stream));
+    kq_task t{};
+    t.w = w;
+    t.rows = w->rows;
+    t.dst = logits;
+    t.dst_stride = (size_t)w->rows;
+    t.dst_f32 = logits_f32;
+    t.dst_f32_stride = (size_t)w->rows;
+    GemvExtra ex;
+    ex.argmax = keys;
+    ex.argmax_f16 = 1;  // the reference scans the fp16 logits the dispatch stored (ENG:9699-9707)
+    if (int r = run_gemv(c, &t, 1, M, w->cols, reinterpret_cast<const __half *>(x), w->cols, nullptr, nullptr, ex))
+        return r;
+    KQ_CUDA(c, kq::launch_argmax_finalize(keys, M, nullptr, toks, vals, c->stream));
+    return KQ_OK;
+}
+
+extern "C" int kq_lm_head_argmax(kq_ctx *c, const kq_weight *w, const uint16_t *x, int M, uint16_t *logits,
+                                 uint32_t *toks, float *vals) {
+    if (!c || !w || !x || !toks || !vals) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = validate_mk(c, M, w->cols)) return r;
+    cudaSetDevice(c->device);
+    const int K = w->cols, V = w->rows;
+    if (int r = h2d(c, c->x, x, (size_t)M * K * 2)) return r;
+    if (logits)
+        if (int r = ensure(c, c->out16, (size_t)M * V * 2)) return r;
+    if (int r = ensure(c, c->misc, (size_t)M * 8)) return r;
+    uint32_t *dt = reinterpret_cast<uint32_t *>(c->misc.p);
+    float *dv = reinterpret_cast<float *>(dt + M);
+    if (int r = kq_lm_head_argmax_async(c, w, reinterpret_cast<uint16_t *>(c->x.p), M,
+                                        logits ? reinterpret_cast<uint16_t *>(c->out16.p) : nullptr, nullptr, dt, dv))
+        return r;
+    set_current_x(c, M, K);
+    if (logits) KQ_CUDA(c, cudaMemcpyAsync(logits, c->out16.p, (size_t)M * V * 2, cudaMemcpyDeviceToHost, c->stream));
+    KQ_CUDA(c, cudaMemcpyAsync(toks, dt, (size_t)M * 4, cudaMemcpyDeviceToHost, c->stream));
+    KQ_CUDA(c, cudaMemcpyAsync(vals, dv, (size_t)M * 4, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+extern "C" int kq_eval_indexed_rows_argmax(kq_ctx *c, const kq_weight *w, const uint32_t *row_ids, int n_rows, int M,
+                                           uint16_t *logits_m1, uint32_t *top_toks, float *top_vals) {
+    if (!c || !w || !row_ids || !top_toks || !top_vals) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (n_rows <= 0 || M <= 0) return KQ_OK;  // ENG:9591
+    if (logits_m1 && M != 1) return fail(c, KQ_ERR_INVALID_ARGUMENT, "logits_m1 needs M == 1 (ENG:9569)");
+    if (c->cur_M == 0) return fail(c, KQ_ERR_NOT_READY, "no current input");
+    if (w->cols != c->cur_K || M > c->cur_M) return fail(c, KQ_ERR_SHAPE, "input shape mismatch");
+    for (int i = 0; i < n_rows; ++i)
+        if ((int)row_ids[i] >= w->rows) return fail(c, KQ_ERR_SHAPE, "row id %u >= rows %d", row_ids[i], w->rows);
+    cudaSetDevice(c->device);
+    const void *act = nullptr;
+    if (int r = current_act(c, w->type, &act)) return r;
+    const size_t idb = (size_t)n_rows * 4, kb = (size_t)M * 8;
+    if (int r = ensure(c, c->misc, idb + kb + (size_t)M * 8 + 64)) return r;
+    uint32_t *dids = reinterpret_cast<uint32_t *>(c->misc.p);
+    auto *keys = reinterpret_cast<unsigned long long *>((uint8_t *)c->misc.p + ((idb + 15) & ~(size_t)15));
+    uint32_t *dt = reinterpret_cast<uint32_t *>(keys + M);
+    float *dv = reinterpret_cast<float *>(dt + M);
+    KQ_CUDA(c, cudaMemcpyAsync(dids, row_ids, idb, cudaMemcpyHostToDevice, c->stream));
+    KQ_CUDA(c, cudaMemsetAsync(keys, 0, kb, c->stream));
+    kq_task t{};
+    t.w = w;
+    t.rows = n_rows;
+    if (logits_m1) {
+        if (int r = h2d(c, c->out16, logits_m1, (size_t)w->rows * 2)) return r;
+        t.dst = reinterpret_cast<uint16_t *>(c->out16.p);
+        t.dst_stride = (size_t)w->rows;
+    }
+    GemvExtra ex;
+    ex.argmax = keys;
+    ex.argmax_f16 = 0;  // the work item compares fp32 row results (ENG:9557-9571)
+    ex.row_ids = dids;
+    ex.scatter = 1;
+    const bool q80 = w->type == KQ_TYPE_Q8_0;
+    if (int r = run_gemv(c, &t, 1, M, w->cols, nullptr, 0, q80 ? nullptr : act, q80 ? act : nullptr, ex)) return r;
+    KQ_CUDA(c, kq::launch_argmax_finalize(keys, M, dids, dt, dv, c->stream));
+    std::vector<uint32_t> bt(M);
+    std::vector<float> bv(M);
+    KQ_CUDA(c, cudaMemcpyAsync(bt.data(), dt, (size_t)M * 4, cudaMemcpyDeviceToHost, c->stream));
+    KQ_CUDA(c, cudaMemcpyAsync(bv.data(), dv, (size_t)M * 4, cudaMemcpyDeviceToHost, c->stream));
+    if (logits_m1)
+        KQ_CUDA(c, cudaMemcpyAsync(logits_m1, c->out16.p, (size_t)w->rows * 2, cudaMemcpyDeviceToHost, c->stream));
+    if (int r = sync_and_check(c)) return r;
+    for (int m = 0; m < M; ++m) {  // merge into the running best, strict '>' (ENG:9606-9612)
+        if (bv[m] > top_vals[m]) {
+            top_vals[m] = bv[m];
+            top_toks[m] = bt[m];
+        }
+    }
+    return KQ_OK;
+}

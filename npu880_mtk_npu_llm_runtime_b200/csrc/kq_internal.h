@@ -1,0 +1,61 @@
+// kq_internal.h -- host-side declarations shared by the CUDA translation units of libkq.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace kq {
+
+// One matrix of a dispatch, device pointers, already offset to the task's first weight row.
+struct GemvTaskHost {
+    const uint8_t *w;
+    int rows;
+    void *dst;             // __half*
+    long long dst_stride;
+    const void *res;       // const __half*
+    long long res_stride;
+    float *dst_f32;
+    long long f32_stride;
+    int *dbg_sumi;         // [M][rows][blocks per row] or nullptr
+    int *dbg_summ;
+    const uint32_t *row_ids = nullptr;  // gather rows by id (device), or nullptr for contiguous rows
+    int scatter = 0;                    // outputs indexed by row id instead of local row
+    int index_base = 0;                 // argmax index of local row 0
+};
+
+struct GemvLaunch {
+    int type;
+    int K;
+    int M;
+    size_t row_bytes;          // device-layout row bytes
+    GemvTaskHost tasks[4];
+    int n_tasks;
+    // input: exactly one of x (fp16 [M][x_stride]), act (BlockQ8K[M][K/256] or BlockQ8_0_Fast[M][K/32])
+    const void *x;
+    long long x_stride;
+    const void *act;
+    int *status;
+    unsigned long long timeout_ns;
+    bool pdl;
+    int num_sms;
+    unsigned long long *argmax = nullptr;  // [M] packed keys (device), or nullptr
+    int argmax_f16 = 0;
+    int inject_wait = 0;  // failure-path test hook (see kq_set_option "inject_timeout")
+};
+
+// kq_gemv.cu
+cudaError_t launch_gemv(const GemvLaunch &L, cudaStream_t stream);
+
+// kq_act.cu
+cudaError_t launch_quantize(int target_type /*12 = Q8_K, 8 = Q8_0*/, const void *x, long long x_stride, int M, int K,
+                            void *out, cudaStream_t stream);
+cudaError_t launch_repack(int type, const uint8_t *gguf, uint8_t *dev, int rows, int K, cudaStream_t stream);
+cudaError_t launch_rmsnorm_q8k(const void *x, const void *gamma, void *out, void *q8k, int M, int K, cudaStream_t stream,
+                               bool pdl);
+cudaError_t launch_swiglu_q8k(void *gate, const void *up, void *q8k, int M, int N, cudaStream_t stream, bool pdl);
+cudaError_t launch_argmax_finalize(const unsigned long long *keys, int M, const uint32_t *ids, uint32_t *toks,
+                                   float *vals, cudaStream_t stream);
+cudaError_t launch_dequant(int type, const uint8_t *dev, size_t row_bytes, int rows, int K, void *out, cudaStream_t stream);
+
+}  // namespace kq
