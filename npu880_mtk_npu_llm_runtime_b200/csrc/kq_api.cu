@@ -332,7 +332,12 @@ extern "C" int kq_destroy(kq_ctx *c) {
 
 extern "C" int kq_set_stream(kq_ctx *c, void *s) {
     if (!c) return KQ_ERR_INVALID_ARGUMENT;
-    cudaStreamSynchronize(c->stream);
+    if (reinterpret_cast<cudaStream_t>(s) == c->stream) return KQ_OK;
+    // drain the previous stream unless it is being captured into a graph (a sync would end
+    // the capture); work captured there belongs to the graph, not to this context
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(c->stream, &cap);
+    if (cap == cudaStreamCaptureStatusNone) cudaStreamSynchronize(c->stream);
     if (c->own_stream) cudaStreamDestroy(c->stream);
     c->stream = reinterpret_cast<cudaStream_t>(s);
     c->own_stream = false;

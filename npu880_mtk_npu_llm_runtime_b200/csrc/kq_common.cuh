@@ -108,13 +108,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes or about
+// hint_ns passes, instead of spinning and taking issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase.  Gives up after timeout_ns of wall time, records
-// DEV_ERR_TIMEOUT in *status and returns false; never traps.
+// DEV_ERR_TIMEOUT in *status and returns false; never traps.  The clock is read every 16
+// suspended polls.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint64_t timeout_ns, int *status) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        for (int i = 0; i < 16; ++i)
+            if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
         if (global_timer_ns() - t0 > timeout_ns) {
             if (status) atomicExch(status, DEV_ERR_TIMEOUT);
             return false;

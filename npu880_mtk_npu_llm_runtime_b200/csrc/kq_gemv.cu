@@ -30,10 +30,8 @@
 
 namespace kq {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;
-constexpr int kMaxStages = 8;
+constexpr int kMaxWarps = 10;                  // consumer warps per CTA (W)
+constexpr int kMaxThreads = (kMaxWarps + 1) * 32;
 
 struct GemvTaskDev {
     const uint8_t *w;
@@ -60,10 +58,13 @@ struct GemvParams {
     int nbu;              // 256-value units per row
     int M;
     unsigned int row_bytes;
-    int rows_per_stage;
-    int n_stages;
+    int rows_per_stage;   // P * rows_per_sub
+    int rows_per_sub;
+    int subs_per_stage;   // P
+    int units_per_row;    // 256-value units (Q8_0: 32-value blocks)
+    int n_warps;          // consumer warps W
+    int n_stages;         // S
     unsigned int stage_bytes;
-    int terms_per_row;    // nbu (K-quants) or 8 * nbu (Q8_0)
     const __half *x;
     long long x_stride;
     const void *act;
@@ -72,7 +73,7 @@ struct GemvParams {
     unsigned long long *argmax;  // [M] packed (ordered value, ~index) keys, or nullptr
     int argmax_f16;              // compare the fp16-rounded results (the dispatch's stored logits)
     int inject_wait;             // failure test: consumers first wait on a barrier nothing arrives at
-    unsigned int off_act, off_terms, off_stages, off_bars;
+    unsigned int off_act, off_stages, off_bars;
 };
 
 // Total order on floats as unsigned keys: larger float -> larger key.
@@ -163,52 +164,59 @@ __device__ __forceinline__ void stage_act_from_q80(const BlockQ80 *src, ActUnit 
 }
 
 // ------------------------------------------------------------------ per-unit dot products
+//
+// A "unit" is 256 weight values of one row: one Q4_K/Q5_K/Q6_K super-block, or eight Q8_0
+// blocks; one lane computes a whole unit for all tokens, chunk by chunk (weights read from the
+// shared-memory stage once per chunk, tokens in the inner loop), keeping registers low.
+// Integer sums are exact; every fp32 term is formed with the reference's operation order and
+// written to term[j * MT + m] (j = 0 for K-quants, j = Q8_0 block for Q8_0).
 
-// Q4_K super-block (ENG:758-801 layout) x Q8_K, all tokens.  Integer sums are exact; the
-// fp32 term is dx * (d * sumi - dmin * summ) with each operation rounded separately
-// (eval_single_lm_row_dot, ENG:11025).
+// Q4_K (ENG:758-801): term = dx * (d * sumi - dmin * summ)  (ENG:11025).  High nibbles are
+// used in place (x16) and the factor is divided out exactly at the end.
 template <int MT>
-__device__ __forceinline__ void unit_q4k(const uint8_t *blk, const ActUnit *au, int nbu, int M, float *term,
-                                         int *dsumi, int *dsumm, long long dstride) {
+__device__ __forceinline__ void unit_q4k(const uint8_t *blk, const ActUnit *a0, int nbu, int M, float *term,
+                                         int *dsi, int *dsm, long long dstride) {
     const uint4 h = *reinterpret_cast<const uint4 *>(blk);
-    uint4 q[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = reinterpret_cast<const uint4 *>(blk + 16)[i];
-    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    // get_scale_min_k4 (ENG:743-749) for all eight sub-blocks at once
-    const uint32_t sc03 = h.y & 0x3F3F3F3Fu, mn03 = h.z & 0x3F3F3F3Fu;
+    const uint32_t sc03 = h.y & 0x3F3F3F3Fu;
     const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    int s16[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) s16[m] = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint4 qa = reinterpret_cast<const uint4 *>(blk + 16)[2 * c];
+        const uint4 qb = reinterpret_cast<const uint4 *>(blk + 16)[2 * c + 1];
+        const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        const uint32_t scw = (c < 2) ? sc03 : sc47;
+        const int s_lo = (int)byte_of(scw, 2 * (c & 1)), s_hi = (int)byte_of(scw, 2 * (c & 1) + 1);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            if (m < M) {
+                const uint4 *xv = reinterpret_cast<const uint4 *>(a0[(size_t)m * nbu].qs + 64 * c);
+                const uint4 x0 = xv[0], x1 = xv[1], x2 = xv[2], x3 = xv[3];
+                const uint32_t xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                const uint32_t xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+                // four independent dp4a chains per chunk
+                int dl0 = 0, dl1 = 0, dh0 = 0, dh1 = 0;
+#pragma unroll
+                for (int i = 0; i < 8; i += 2) {
+                    dl0 = dp4a_us(w[i] & 0x0F0F0F0Fu, (int)xl[i], dl0);
+                    dl1 = dp4a_us(w[i + 1] & 0x0F0F0F0Fu, (int)xl[i + 1], dl1);
+                    dh0 = dp4a_us(w[i] & 0xF0F0F0F0u, (int)xh[i], dh0);  // 16 x the high-nibble dot
+                    dh1 = dp4a_us(w[i + 1] & 0xF0F0F0F0u, (int)xh[i + 1], dh1);
+                }
+                s16[m] += s_lo * ((dl0 + dl1) << 4) + s_hi * (dh0 + dh1);
+            }
+        }
+    }
+    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    const uint32_t mn03 = h.z & 0x3F3F3F3Fu;
     const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
         if (m < M) {
-            const ActUnit *a = au + (size_t)m * nbu;
-            const uint4 *xv = reinterpret_cast<const uint4 *>(a->qs);
-            int sumi = 0;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint4 x0 = xv[4 * c + 0], x1 = xv[4 * c + 1], x2 = xv[4 * c + 2], x3 = xv[4 * c + 3];
-                const uint4 qa = q[2 * c], qb = q[2 * c + 1];
-                int dl = 0, dh = 0;
-                dl = dp4a_us(qa.x & 0x0F0F0F0Fu, (int)x0.x, dl);
-                dl = dp4a_us(qa.y & 0x0F0F0F0Fu, (int)x0.y, dl);
-                dl = dp4a_us(qa.z & 0x0F0F0F0Fu, (int)x0.z, dl);
-                dl = dp4a_us(qa.w & 0x0F0F0F0Fu, (int)x0.w, dl);
-                dl = dp4a_us(qb.x & 0x0F0F0F0Fu, (int)x1.x, dl);
-                dl = dp4a_us(qb.y & 0x0F0F0F0Fu, (int)x1.y, dl);
-                dl = dp4a_us(qb.z & 0x0F0F0F0Fu, (int)x1.z, dl);
-                dl = dp4a_us(qb.w & 0x0F0F0F0Fu, (int)x1.w, dl);
-                dh = dp4a_us((qa.x >> 4) & 0x0F0F0F0Fu, (int)x2.x, dh);
-                dh = dp4a_us((qa.y >> 4) & 0x0F0F0F0Fu, (int)x2.y, dh);
-                dh = dp4a_us((qa.z >> 4) & 0x0F0F0F0Fu, (int)x2.z, dh);
-                dh = dp4a_us((qa.w >> 4) & 0x0F0F0F0Fu, (int)x2.w, dh);
-                dh = dp4a_us((qb.x >> 4) & 0x0F0F0F0Fu, (int)x3.x, dh);
-                dh = dp4a_us((qb.y >> 4) & 0x0F0F0F0Fu, (int)x3.y, dh);
-                dh = dp4a_us((qb.z >> 4) & 0x0F0F0F0Fu, (int)x3.z, dh);
-                dh = dp4a_us((qb.w >> 4) & 0x0F0F0F0Fu, (int)x3.w, dh);
-                const uint32_t scw = (c < 2) ? sc03 : sc47;
-                sumi += (int)byte_of(scw, 2 * (c & 1)) * dl + (int)byte_of(scw, 2 * (c & 1) + 1) * dh;
-            }
+            const ActUnit *a = a0 + (size_t)m * nbu;
+            const int sumi = s16[m] >> 4;
             const int4 b0 = *reinterpret_cast<const int4 *>(a->aux);
             const int4 b1 = *reinterpret_cast<const int4 *>(a->aux + 4);
             const int summ = (int)byte_of(mn03, 0) * b0.x + (int)byte_of(mn03, 1) * b0.y +
@@ -217,54 +225,66 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *blk, const ActUnit *au, 
                              (int)byte_of(mn47, 2) * b1.z + (int)byte_of(mn47, 3) * b1.w;
             const float t = __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dmin, __int2float_rn(summ)));
             term[m] = __fmul_rn(a->d, t);
-            if (dsumi) {
-                dsumi[m * dstride] = sumi;
-                dsumm[m * dstride] = summ;
+            if (dsi) {
+                dsi[m * dstride] = sumi;
+                dsm[m * dstride] = summ;
             }
         }
     }
 }
 
-// Q5_K super-block (ENG:803-853 layout): the fifth bit of value l of chunk c is bit 2c (low
-// half) / 2c+1 (high half) of qh[l].
+// Q5_K (ENG:803-853): as Q4_K with the fifth bit of value l of chunk c in bit 2c (low half) /
+// 2c+1 (high half) of qh[l]  (ENG:11028-11062).
 template <int MT>
-__device__ __forceinline__ void unit_q5k(const uint8_t *blk, const ActUnit *au, int nbu, int M, float *term,
-                                         int *dsumi, int *dsumm, long long dstride) {
+__device__ __forceinline__ void unit_q5k(const uint8_t *blk, const ActUnit *a0, int nbu, int M, float *term,
+                                         int *dsi, int *dsm, long long dstride) {
     const uint4 h = *reinterpret_cast<const uint4 *>(blk);
     const uint4 qh0 = reinterpret_cast<const uint4 *>(blk + 16)[0];
     const uint4 qh1 = reinterpret_cast<const uint4 *>(blk + 16)[1];
-    uint4 q[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = reinterpret_cast<const uint4 *>(blk + 48)[i];
-    const uint32_t qhw[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
-    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    const uint32_t sc03 = h.y & 0x3F3F3F3Fu, mn03 = h.z & 0x3F3F3F3Fu;
+    const uint32_t hb[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
+    const uint32_t sc03 = h.y & 0x3F3F3F3Fu;
     const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-    const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    int s16[MT];
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-        if (m < M) {
-            const ActUnit *a = au + (size_t)m * nbu;
-            const uint4 *xv = reinterpret_cast<const uint4 *>(a->qs);
-            int sumi = 0;
+    for (int m = 0; m < MT; ++m) s16[m] = 0;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint4 x0 = xv[4 * c + 0], x1 = xv[4 * c + 1], x2 = xv[4 * c + 2], x3 = xv[4 * c + 3];
-                const uint32_t qw[8] = {q[2 * c].x, q[2 * c].y, q[2 * c].z, q[2 * c].w,
-                                        q[2 * c + 1].x, q[2 * c + 1].y, q[2 * c + 1].z, q[2 * c + 1].w};
+    for (int c = 0; c < 4; ++c) {
+        const uint4 qa = reinterpret_cast<const uint4 *>(blk + 48)[2 * c];
+        const uint4 qb = reinterpret_cast<const uint4 *>(blk + 48)[2 * c + 1];
+        const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        uint32_t wl[8], wh[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            wl[i] = (w[i] & 0x0F0F0F0Fu) | (((hb[i] >> (2 * c)) & 0x01010101u) << 4);
+            wh[i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((hb[i] >> (2 * c + 1)) & 0x01010101u) << 4);
+        }
+        const uint32_t scw = (c < 2) ? sc03 : sc47;
+        const int s_lo = (int)byte_of(scw, 2 * (c & 1)), s_hi = (int)byte_of(scw, 2 * (c & 1) + 1);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            if (m < M) {
+                const uint4 *xv = reinterpret_cast<const uint4 *>(a0[(size_t)m * nbu].qs + 64 * c);
+                const uint4 x0 = xv[0], x1 = xv[1], x2 = xv[2], x3 = xv[3];
                 const uint32_t xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
                 const uint32_t xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
                 int dl = 0, dh = 0;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const uint32_t wl = (qw[i] & 0x0F0F0F0Fu) | (((qhw[i] >> (2 * c)) & 0x01010101u) << 4);
-                    const uint32_t wh = ((qw[i] >> 4) & 0x0F0F0F0Fu) | (((qhw[i] >> (2 * c + 1)) & 0x01010101u) << 4);
-                    dl = dp4a_us(wl, (int)xl[i], dl);
-                    dh = dp4a_us(wh, (int)xh[i], dh);
+                    dl = dp4a_us(wl[i], (int)xl[i], dl);
+                    dh = dp4a_us(wh[i], (int)xh[i], dh);
                 }
-                const uint32_t scw = (c < 2) ? sc03 : sc47;
-                sumi += (int)byte_of(scw, 2 * (c & 1)) * dl + (int)byte_of(scw, 2 * (c & 1) + 1) * dh;
+                s16[m] += (s_lo * dl + s_hi * dh) << 4;
             }
+        }
+    }
+    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    const uint32_t mn03 = h.z & 0x3F3F3F3Fu;
+    const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        if (m < M) {
+            const ActUnit *a = a0 + (size_t)m * nbu;
+            const int sumi = s16[m] >> 4;
             const int4 b0 = *reinterpret_cast<const int4 *>(a->aux);
             const int4 b1 = *reinterpret_cast<const int4 *>(a->aux + 4);
             const int summ = (int)byte_of(mn03, 0) * b0.x + (int)byte_of(mn03, 1) * b0.y +
@@ -273,308 +293,332 @@ __device__ __forceinline__ void unit_q5k(const uint8_t *blk, const ActUnit *au, 
                              (int)byte_of(mn47, 2) * b1.z + (int)byte_of(mn47, 3) * b1.w;
             const float t = __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dmin, __int2float_rn(summ)));
             term[m] = __fmul_rn(a->d, t);
-            if (dsumi) {
-                dsumi[m * dstride] = sumi;
-                dsumm[m * dstride] = summ;
+            if (dsi) {
+                dsi[m * dstride] = sumi;
+                dsm[m * dstride] = summ;
             }
         }
     }
 }
 
-// Q6_K super-block, device layout [ql 128][qh 64][scales 16] (d passed separately).
-// Value e = 128h + 32g + l: low 4 bits from ql[64h + l + 32(g&1)] (high nibble when g >= 2),
-// bits 4-5 from qh[32h + l] >> 2g, minus 32; sub-block s = 8h + 2g + (l >= 16) (ENG:11065-11101).
-// sum (q - 32) x = sum q x - 32 * (sum of the 16 activation quants), all exact integers.
+// Q6_K, device block [ql 128][qh 64][scales 16] + d from the row's d plane (ENG:673-741).
+// Value e = 128h + 32g + l: low 4 bits in ql[64h + l + 32(g&1)] (>> 4 when g >= 2), bits 4-5 in
+// qh[32h + l] >> 2g, minus 32; sub-block s = 8h + 2g + (l >= 16) (ENG:11065-11101).
+// sum (q - 32) x = sum q x - 32 * (sum of the 16 activation quants, ActUnit.xsum16).
+// term = (d * dx) * sumi  (ENG:11100).  Processed per (h, 16-value half): 16 sub-block dots.
 template <int MT>
-__device__ __forceinline__ void unit_q6k(const uint8_t *blk, float d, const ActUnit *au, int nbu, int M,
-                                         float *term, int *dsumi, int *dsumm, long long dstride) {
-    uint32_t ql[32], qh[16];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const uint4 v = reinterpret_cast<const uint4 *>(blk)[i];
-        ql[4 * i] = v.x; ql[4 * i + 1] = v.y; ql[4 * i + 2] = v.z; ql[4 * i + 3] = v.w;
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint4 v = reinterpret_cast<const uint4 *>(blk + 128)[i];
-        qh[4 * i] = v.x; qh[4 * i + 1] = v.y; qh[4 * i + 2] = v.z; qh[4 * i + 3] = v.w;
-    }
+__device__ __forceinline__ void unit_q6k(const uint8_t *blk, float d, const ActUnit *a0, int nbu, int M, float *term,
+                                         int *dsi, int *dsm, long long dstride) {
     const uint4 scv = reinterpret_cast<const uint4 *>(blk + 192)[0];
     const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+    int sumi[MT];
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-        if (m < M) {
-            const ActUnit *a = au + (size_t)m * nbu;
-            const uint4 *xv = reinterpret_cast<const uint4 *>(a->qs);
-            int sumi = 0;
+    for (int m = 0; m < MT; ++m) sumi[m] = 0;
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
+    for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
-                for (int half16 = 0; half16 < 2; ++half16) {
-                    int dg[4] = {0, 0, 0, 0};
-                    const uint4 xg0 = xv[8 * hh + 0 + half16];
-                    const uint4 xg1 = xv[8 * hh + 2 + half16];
-                    const uint4 xg2 = xv[8 * hh + 4 + half16];
-                    const uint4 xg3 = xv[8 * hh + 6 + half16];
-                    const uint32_t x0[4] = {xg0.x, xg0.y, xg0.z, xg0.w};
-                    const uint32_t x1[4] = {xg1.x, xg1.y, xg1.z, xg1.w};
-                    const uint32_t x2[4] = {xg2.x, xg2.y, xg2.z, xg2.w};
-                    const uint32_t x3[4] = {xg3.x, xg3.y, xg3.z, xg3.w};
+        for (int half16 = 0; half16 < 2; ++half16) {
+            // 16 values l in [16 half16, 16 half16 + 16) of the four groups g of half hh
+            const uint4 b0 = *reinterpret_cast<const uint4 *>(blk + 64 * hh + 16 * half16);
+            const uint4 b1 = *reinterpret_cast<const uint4 *>(blk + 64 * hh + 32 + 16 * half16);
+            const uint4 hv = *reinterpret_cast<const uint4 *>(blk + 128 + 32 * hh + 16 * half16);
+            const uint32_t B0[4] = {b0.x, b0.y, b0.z, b0.w}, B1[4] = {b1.x, b1.y, b1.z, b1.w};
+            const uint32_t HB[4] = {hv.x, hv.y, hv.z, hv.w};
+            uint32_t q[4][4];
 #pragma unroll
-                    for (int ww = 0; ww < 4; ++ww) {
-                        const int w = 4 * half16 + ww;
-                        const uint32_t B0 = ql[16 * hh + w], B1 = ql[16 * hh + 8 + w], HB = qh[8 * hh + w];
-                        const uint32_t q0 = (B0 & 0x0F0F0F0Fu) | ((HB << 4) & 0x30303030u);
-                        const uint32_t q1 = (B1 & 0x0F0F0F0Fu) | ((HB << 2) & 0x30303030u);
-                        const uint32_t q2 = ((B0 >> 4) & 0x0F0F0F0Fu) | (HB & 0x30303030u);
-                        const uint32_t q3 = ((B1 >> 4) & 0x0F0F0F0Fu) | ((HB >> 2) & 0x30303030u);
-                        dg[0] = dp4a_us(q0, (int)x0[ww], dg[0]);
-                        dg[1] = dp4a_us(q1, (int)x1[ww], dg[1]);
-                        dg[2] = dp4a_us(q2, (int)x2[ww], dg[2]);
-                        dg[3] = dp4a_us(q3, (int)x3[ww], dg[3]);
-                    }
+            for (int k = 0; k < 4; ++k) {
+                q[0][k] = (B0[k] & 0x0F0F0F0Fu) | ((HB[k] << 4) & 0x30303030u);
+                q[1][k] = (B1[k] & 0x0F0F0F0Fu) | ((HB[k] << 2) & 0x30303030u);
+                q[2][k] = ((B0[k] >> 4) & 0x0F0F0F0Fu) | (HB[k] & 0x30303030u);
+                q[3][k] = ((B1[k] >> 4) & 0x0F0F0F0Fu) | ((HB[k] >> 2) & 0x30303030u);
+            }
+            int sc[4];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const int sidx = 8 * hh + 2 * g + half16;
+                sc[g] = (int)(int8_t)byte_of(scw[sidx >> 2], sidx & 3);
+            }
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                if (m < M) {
+                    const ActUnit *a = a0 + (size_t)m * nbu;
+                    const uint4 *xv = reinterpret_cast<const uint4 *>(a->qs);
+                    int acc = 0;
 #pragma unroll
                     for (int g = 0; g < 4; ++g) {
-                        const int s = 8 * hh + 2 * g + half16;
-                        const int sc = (int)(int8_t)byte_of(scw[s >> 2], s & 3);
-                        sumi += sc * (dg[g] - 32 * a->xsum16[s]);
+                        const uint4 x = xv[8 * hh + 2 * g + half16];
+                        int dot = dp4a_us(q[g][0], (int)x.x, 0);
+                        dot = dp4a_us(q[g][1], (int)x.y, dot);
+                        dot = dp4a_us(q[g][2], (int)x.z, dot);
+                        dot = dp4a_us(q[g][3], (int)x.w, dot);
+                        acc += sc[g] * (dot - 32 * a->xsum16[8 * hh + 2 * g + half16]);
                     }
+                    sumi[m] += acc;
                 }
-            }
-            term[m] = __fmul_rn(__fmul_rn(d, a->d), __int2float_rn(sumi));
-            if (dsumi) {
-                dsumi[m * dstride] = sumi;
-                dsumm[m * dstride] = 0;
             }
         }
     }
-}
-
-// Eight Q8_0 blocks (device layout: 256 int8 quants here, 8 fp16 scales in the row's d plane).
-// term j = (d_j * dx_j) * dot_j (sdot_row_q8_0_batch, ENG:3393-3407).  T = 8 terms per unit.
-template <int MT>
-__device__ __forceinline__ void unit_q80(const uint8_t *qs, const uint8_t *dptr, const ActUnit *au, int nbu, int M,
-                                         float *term /* [8][MT] */, int *dsumi, int *dsumm, long long dstride) {
-    uint4 q[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) q[i] = reinterpret_cast<const uint4 *>(qs)[i];
-    const uint4 dv = *reinterpret_cast<const uint4 *>(dptr);
-    const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
         if (m < M) {
-            const ActUnit *a = au + (size_t)m * nbu;
-            const uint4 *xv = reinterpret_cast<const uint4 *>(a->qs);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const uint4 xa = xv[2 * j], xb = xv[2 * j + 1];
-                const uint4 wa = q[2 * j], wb = q[2 * j + 1];
-                int dot = 0;
-                dot = dp4a_ss((int)wa.x, (int)xa.x, dot);
-                dot = dp4a_ss((int)wa.y, (int)xa.y, dot);
-                dot = dp4a_ss((int)wa.z, (int)xa.z, dot);
-                dot = dp4a_ss((int)wa.w, (int)xa.w, dot);
-                dot = dp4a_ss((int)wb.x, (int)xb.x, dot);
-                dot = dp4a_ss((int)wb.y, (int)xb.y, dot);
-                dot = dp4a_ss((int)wb.z, (int)xb.z, dot);
-                dot = dp4a_ss((int)wb.w, (int)xb.w, dot);
-                const float dwj = half_bits_to_float(dw[j >> 1] >> (16 * (j & 1)));
-                const float dxj = __int_as_float(a->aux[j]);
-                term[j * MT + m] = __fmul_rn(__fmul_rn(dwj, dxj), __int2float_rn(dot));
-                if (dsumi) {
-                    dsumi[m * dstride + j] = dot;
-                    dsumm[m * dstride + j] = 0;
-                }
+            const ActUnit *a = a0 + (size_t)m * nbu;
+            term[m] = __fmul_rn(__fmul_rn(d, a->d), __int2float_rn(sumi[m]));
+            if (dsi) {
+                dsi[m * dstride] = sumi[m];
+                dsm[m * dstride] = 0;
             }
         }
     }
 }
 
-// ------------------------------------------------------------------ stage iteration
+// One Q8_0 block of 32 values (device: int8 quants at 32 * j, fp16 scale in the row's d plane).
+// term = (d * dx) * dot  (sdot_row_q8_0_batch, ENG:3393-3407).  The activation block is
+// sub-block j & 7 of ActUnit j >> 3.
+template <int MT>
+__device__ __forceinline__ void unit_q80(const uint8_t *qs, const uint8_t *dptr, int j, const ActUnit *act, int nbu,
+                                         int M, float *term, int *dsi, int *dsm, long long dstride) {
+    const uint4 wa = reinterpret_cast<const uint4 *>(qs)[0];
+    const uint4 wb = reinterpret_cast<const uint4 *>(qs)[1];
+    const float dw = half_bits_to_float(*reinterpret_cast<const uint16_t *>(dptr));
+    const int au = j >> 3, sub = j & 7;
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        if (m < M) {
+            const ActUnit *a = act + (size_t)m * nbu + au;
+            const uint4 xa = reinterpret_cast<const uint4 *>(a->qs)[2 * sub];
+            const uint4 xb = reinterpret_cast<const uint4 *>(a->qs)[2 * sub + 1];
+            int dot = dp4a_ss((int)wa.x, (int)xa.x, 0);
+            dot = dp4a_ss((int)wa.y, (int)xa.y, dot);
+            dot = dp4a_ss((int)wa.z, (int)xa.z, dot);
+            dot = dp4a_ss((int)wa.w, (int)xa.w, dot);
+            dot = dp4a_ss((int)wb.x, (int)xb.x, dot);
+            dot = dp4a_ss((int)wb.y, (int)xb.y, dot);
+            dot = dp4a_ss((int)wb.z, (int)xb.z, dot);
+            dot = dp4a_ss((int)wb.w, (int)xb.w, dot);
+            term[m] = __fmul_rn(__fmul_rn(dw, __int_as_float(a->aux[sub])), __int2float_rn(dot));
+            if (dsi) {
+                dsi[m * dstride] = dot;
+                dsm[m * dstride] = 0;
+            }
+        }
+    }
+}
 
-// The CTA's rows are walked in stages of at most rows_per_stage consecutive rows of one task.
-struct StageCursor {
-    int g, g_end, t;
-};
+// ------------------------------------------------------------------ row -> task
 
-__device__ __forceinline__ bool next_stage(const GemvParams &p, StageCursor &c, int &t, int &r0, int &R) {
-    if (c.g >= c.g_end) return false;
-    while (c.t + 1 < p.n_tasks && c.g >= p.task[c.t + 1].row_start) ++c.t;
-    t = c.t;
-    r0 = c.g - p.task[t].row_start;
-    R = min(p.rows_per_stage, min(c.g_end - c.g, p.task[t].rows - r0));
-    c.g += R;
-    return true;
+// Index of the task owning concatenated row g (tasks are in ascending row_start order).
+__device__ __forceinline__ int task_of(const GemvParams &p, int g) {
+    int t = 0;
+#pragma unroll
+    for (int i = 1; i < 4; ++i) t += (i < p.n_tasks && g >= p.task[i].row_start) ? 1 : 0;
+    return t;
 }
 
 // ------------------------------------------------------------------ the kernel
+//
+// Each CTA owns a contiguous range [g_begin, g_end) of the dispatch's concatenated output rows
+// and walks it in stages of rows_per_stage rows; stage s starts at g_begin + s * rows_per_stage.
+// The producer warp (index W) streams stages into an S-slot ring: one cp.async.bulk per task
+// segment of the stage (>= 16 KB per stage in total; one copy per row for gathered rows).  A
+// stage holds P sub-stages of rows_per_sub rows (rows_per_sub * units-per-row <= 32, or one
+// row) and sub-stage q = s * P + part belongs to consumer warp q % W.  The warp waits on the
+// stage's full barrier, computes one unit per lane (a row longer than 32 units in passes), adds
+// each row's unit terms in unit order through shuffles into the row's leader lane (the
+// reference's `acc += term` sequence), arrives on the stage's empty barrier (P arrivals free the
+// slot) and writes the epilogue.  There is no CTA-wide barrier in the main loop.
+// (P * S) % W == 0: the previous use of the slot of a warp's next sub-stage was one of the
+// warp's own sub-stages, which it already waited for, so a waiter never runs two phases ahead
+// of a full barrier (where the parity test of mbarrier.try_wait.parity would pass on the wrong
+// phase).
 
 template <int TYPE, int MT>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kMaxThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    ActUnit *act = reinterpret_cast<ActUnit *>(smem + p.off_act);
-    float *terms = reinterpret_cast<float *>(smem + p.off_terms);
-    uint8_t *stages = smem + p.off_stages;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.off_bars);  // full[NS], empty[NS], dead
-    volatile int *flags = reinterpret_cast<volatile int *>(bars + 2 * kMaxStages + 1);  // [0] error, [1] issued
-
     __shared__ unsigned long long s_best[8];
+    __shared__ int s_abort, s_issued;
+
+    ActUnit *act = reinterpret_cast<ActUnit *>(smem + p.off_act);
+    uint8_t *ring = smem + p.off_stages;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.off_bars);  // full[S], empty[S], dead
+    const int S = p.n_stages, W = p.n_warps, P = p.subs_per_stage, RS = p.rows_per_sub;
+    const int RPS = p.rows_per_stage;
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int NS = p.n_stages;
-    if (tid < 8) s_best[tid] = 0ull;
 
-    // balanced contiguous row range of this CTA
     const long long tot = p.total_rows;
     const int g_begin = (int)(tot * blockIdx.x / gridDim.x);
     const int g_end = (int)(tot * (blockIdx.x + 1) / gridDim.x);
+    const int n_stages_cta = (g_end - g_begin + RPS - 1) / RPS;
 
+    if (tid < 8) s_best[tid] = 0ull;
     if (tid == 0) {
-        for (int s = 0; s < NS; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&bars[s]), 1);
-            mbar_init(smem_u32(&bars[kMaxStages + s]), 1);
+            mbar_init(smem_u32(&bars[S + s]), P);
         }
-        mbar_init(smem_u32(&bars[2 * kMaxStages]), 1);  // never arrived at (failure-path test)
-        flags[0] = 0;
-        flags[1] = 0;
+        mbar_init(smem_u32(&bars[2 * S]), 1);  // never arrived at (failure-path test)
+        s_abort = 0;
+        s_issued = 0;
         mbar_init_fence();
     }
     __syncthreads();
     pdl_launch_dependents();
 
-    int consumed = 0;
-    if (warp == kConsumerWarps) {
-        // ---------------- producer: weights do not depend on earlier kernels, start at once
+    if (warp == W) {
+        // ---------------- producer: the weight stream does not depend on earlier kernels
         if (lane == 0) {
             const uint64_t policy = l2_evict_first_policy();
-            StageCursor cur{g_begin, g_end, 0};
-            int t, r0, R, s = 0;
-            while (next_stage(p, cur, t, r0, R)) {
-                const int slot = s % NS;
-                if (s >= NS) {
-                    if (!mbar_wait_bounded(smem_u32(&bars[kMaxStages + slot]), ((s / NS) - 1) & 1, p.timeout_ns,
-                                           p.status))
+            int s = 0;
+            for (; s < n_stages_cta; ++s) {
+                const int slot = s % S;
+                if (s >= S) {
+                    if (!mbar_wait_bounded(smem_u32(&bars[S + slot]), ((s / S) - 1) & 1, p.timeout_ns, p.status)) {
+                        s_abort = 1;
                         break;
+                    }
                 }
-                const uint32_t bytes = (uint32_t)R * p.row_bytes;
+                const int a = g_begin + s * RPS, b = min(g_end, a + RPS);
                 const uint32_t full = smem_u32(&bars[slot]);
-                const uint32_t sdst = smem_u32(stages + (size_t)slot * p.stage_bytes);
-                mbar_arrive_expect_tx(full, bytes);
-                if (p.task[t].row_ids) {
-                    for (int i = 0; i < R; ++i)
-                        bulk_g2s(sdst + i * p.row_bytes, p.task[t].w + (size_t)p.task[t].row_ids[r0 + i] * p.row_bytes,
-                                 p.row_bytes, full, policy);
-                } else {
-                    bulk_g2s(sdst, p.task[t].w + (size_t)r0 * p.row_bytes, bytes, full, policy);
+                const uint32_t sdst = smem_u32(ring + (size_t)slot * p.stage_bytes);
+                mbar_arrive_expect_tx(full, (uint32_t)(b - a) * p.row_bytes);
+                int g = a;
+                while (g < b) {
+                    const int t = task_of(p, g);
+                    const int tend = min(b, p.task[t].row_start + p.task[t].rows);
+                    const int r0 = g - p.task[t].row_start;
+                    const uint32_t off = (uint32_t)(g - a) * p.row_bytes;
+                    if (p.task[t].row_ids) {
+                        for (int i = 0; i < tend - g; ++i)
+                            bulk_g2s(sdst + off + i * p.row_bytes,
+                                     p.task[t].w + (size_t)p.task[t].row_ids[r0 + i] * p.row_bytes, p.row_bytes, full,
+                                     policy);
+                    } else {
+                        bulk_g2s(sdst + off, p.task[t].w + (size_t)r0 * p.row_bytes, (uint32_t)(tend - g) * p.row_bytes,
+                                 full, policy);
+                    }
+                    g = tend;
                 }
-                ++s;
+                s_issued = s + 1;
             }
-            flags[1] = s;
         }
     } else {
         // ---------------- consumers
         pdl_wait();  // activations / residuals may come from the previous kernel
-        const int ctid = tid;
-        // stage the activation: one warp per (token, unit)
-        const int n_units = p.M * p.nbu;
-        for (int u = warp; u < n_units; u += kConsumerWarps) {
-            const int m = u / p.nbu, b = u % p.nbu;
+        const int nbu = p.nbu;
+        const int n_units = p.M * nbu;
+        for (int u = warp; u < n_units; u += W) {
+            const int m = u / nbu, b = u % nbu;
             ActUnit *a = act + u;
             if (p.x) {
                 const __half *xu = p.x + (size_t)m * p.x_stride + (size_t)b * 256;
-                const bool vec_ok = ((reinterpret_cast<uintptr_t>(xu) & 15) == 0);
-                stage_act_from_fp16<TYPE>(xu, vec_ok, a, lane);
+                stage_act_from_fp16<TYPE>(xu, (reinterpret_cast<uintptr_t>(xu) & 15) == 0, a, lane);
             } else if (TYPE == TYPE_Q8_0) {
                 stage_act_from_q80(reinterpret_cast<const BlockQ80 *>(p.act) + (size_t)m * (p.K / 32) + 8 * b, a, lane);
             } else {
-                stage_act_from_q8k(reinterpret_cast<const BlockQ8K *>(p.act) + (size_t)m * p.nbu + b, a, lane);
+                stage_act_from_q8k(reinterpret_cast<const BlockQ8K *>(p.act) + (size_t)m * nbu + b, a, lane);
             }
         }
-        if (p.inject_wait && ctid == 0) {
+        if (p.inject_wait && tid == 0) {
             // failure-path test: a wait whose barrier nothing completes must end by its time limit
-            flags[0] = mbar_wait_bounded(smem_u32(&bars[2 * kMaxStages]), 0, p.timeout_ns, p.status) ? 0 : 1;
+            if (!mbar_wait_bounded(smem_u32(&bars[2 * S]), 0, p.timeout_ns, p.status)) s_abort = 1;
         }
-        named_bar_sync(1, kConsumers);
-        const bool injected_failure = p.inject_wait && flags[0];
+        named_bar_sync(1, W * 32);
 
-        constexpr int T = (TYPE == TYPE_Q8_0) ? 8 : 1;
-        const int tpr = p.terms_per_row;  // nbu * T
-        StageCursor cur{g_begin, g_end, 0};
-        int t, r0, R;
-        while (!injected_failure && next_stage(p, cur, t, r0, R)) {
-            const int slot = consumed % NS;
-            if (ctid == 0) {
-                const bool ok = mbar_wait_bounded(smem_u32(&bars[slot]), (consumed / NS) & 1, p.timeout_ns, p.status);
-                flags[0] = ok ? 0 : 1;
+        const int upr = p.units_per_row;  // 256-value units (32-value blocks for Q8_0)
+        const int multi = (RS > 1);       // several whole rows per sub-stage
+        const int npass = multi ? 1 : (upr + 31) / 32;
+        const int lrow = multi ? lane / upr : 0;
+        const int lead = multi ? lrow * upr : 0;  // leader lane of this lane's row
+        const int n_sub = n_stages_cta * P;
+        for (int q = warp; q < n_sub; q += W) {
+            if (*reinterpret_cast<volatile int *>(&s_abort)) break;
+            const int sidx = q / P, part = q - sidx * P;
+            const int slot = sidx % S;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait_bounded(smem_u32(&bars[slot]), (sidx / S) & 1, p.timeout_ns, p.status) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) s_abort = 1;
+                break;
             }
-            named_bar_sync(1, kConsumers);
-            if (flags[0]) break;
-
+            const int a = g_begin + sidx * RPS;                 // first row of the stage
+            const int sR = max(0, min(RS, min(g_end, a + RPS) - (a + part * RS)));  // rows of this sub-stage
+            const int g = a + part * RS + min(lrow, max(sR - 1, 0));  // this lane's row (concatenated)
+            const int t = task_of(p, g);
             const GemvTaskDev &tk = p.task[t];
-            const uint8_t *sbase = stages + (size_t)slot * p.stage_bytes;
-            float *tb = terms + (size_t)(consumed & 1) * p.rows_per_stage * tpr * MT;
-            const int units = R * p.nbu;
-            for (int u = ctid; u < units; u += kConsumers) {
-                const int row = u / p.nbu, b = u % p.nbu;
-                const uint8_t *wrow = sbase + (size_t)row * p.row_bytes;
-                float *term = tb + ((size_t)row * tpr + (size_t)b * T) * MT;
-                int *dsi = nullptr, *dsm = nullptr;
-                long long dstride = 0;
-                if (tk.dbg_sumi) {
-                    const long long bpr = (long long)p.nbu * T;
-                    dstride = (long long)tk.rows * bpr;
-                    dsi = tk.dbg_sumi + (long long)(r0 + row) * bpr + (long long)b * T;
-                    dsm = tk.dbg_summ + (long long)(r0 + row) * bpr + (long long)b * T;
+            const int r = g - tk.row_start;                      // row within the task
+            const uint8_t *wrow = ring + (size_t)slot * p.stage_bytes + (size_t)(g - a) * p.row_bytes;
+            const int units = sR * upr;
+            const bool is_lead = multi ? (lane == lead && lane < units) : (lane == 0 && sR > 0);
+            float acc[MT];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+            for (int pass = 0; pass < npass; ++pass) {
+                const int b = multi ? lane - lead : 32 * pass + lane;
+                const bool valid = multi ? (lane < units) : (sR > 0 && b < upr);
+                const int cnt = multi ? upr : min(32, upr - 32 * pass);  // the row's units in this pass
+                float term[MT];
+#pragma unroll
+                for (int m = 0; m < MT; ++m) term[m] = 0.0f;
+                if (valid) {
+                    int *dsi = nullptr, *dsm = nullptr;
+                    long long dstride = 0;
+                    if (tk.dbg_sumi) {
+                        dstride = (long long)tk.rows * upr;
+                        const long long off = (long long)r * upr + b;
+                        dsi = tk.dbg_sumi + off;
+                        dsm = tk.dbg_summ + off;
+                    }
+                    if (TYPE == TYPE_Q4_K) {
+                        unit_q4k<MT>(wrow + 144 * b, act + b, nbu, p.M, term, dsi, dsm, dstride);
+                    } else if (TYPE == TYPE_Q5_K) {
+                        unit_q5k<MT>(wrow + 176 * b, act + b, nbu, p.M, term, dsi, dsm, dstride);
+                    } else if (TYPE == TYPE_Q6_K) {
+                        const float dq = half_bits_to_float(*reinterpret_cast<const uint16_t *>(wrow + 208 * nbu + 2 * b));
+                        unit_q6k<MT>(wrow + 208 * b, dq, act + b, nbu, p.M, term, dsi, dsm, dstride);
+                    } else {
+                        unit_q80<MT>(wrow + 32 * b, wrow + p.K + 2 * b, b, act, nbu, p.M, term, dsi, dsm, dstride);
+                    }
                 }
-                const ActUnit *au = act + b;
-                if (TYPE == TYPE_Q4_K) {
-                    unit_q4k<MT>(wrow + (size_t)b * 144, au, p.nbu, p.M, term, dsi, dsm, dstride);
-                } else if (TYPE == TYPE_Q5_K) {
-                    unit_q5k<MT>(wrow + (size_t)b * 176, au, p.nbu, p.M, term, dsi, dsm, dstride);
-                } else if (TYPE == TYPE_Q6_K) {
-                    const uint16_t dbits = *reinterpret_cast<const uint16_t *>(wrow + (size_t)p.nbu * 208 + 2 * b);
-                    unit_q6k<MT>(wrow + (size_t)b * 208, half_bits_to_float(dbits), au, p.nbu, p.M, term, dsi, dsm,
-                                 dstride);
-                } else {
-                    unit_q80<MT>(wrow + (size_t)b * 256, wrow + (size_t)p.K + (size_t)b * 16, au, p.nbu, p.M, term,
-                                 dsi, dsm, dstride);
+                // in-order sum of the row's unit terms into the leader (the reference's `acc += term`)
+#pragma unroll 4
+                for (int i = 0; i < cnt; ++i) {
+                    const int src = min(lead + i, 31);
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) acc[m] = __fadd_rn(acc[m], __shfl_sync(0xffffffffu, term[m], src));
                 }
             }
-            named_bar_sync(1, kConsumers);
-            if (ctid == 0) mbar_arrive(smem_u32(&bars[kMaxStages + slot]));  // stage buffer free again
-
-            // in-order block sums (the reference's `acc += term` sequence) + epilogue
-            for (int idx = ctid; idx < R * p.M; idx += kConsumers) {
-                const int row = idx % R, m = idx / R;
-                const float *tr = tb + (size_t)row * tpr * MT + m;
-                float acc = 0.0f;
-                for (int j = 0; j < tpr; ++j) acc = __fadd_rn(acc, tr[(size_t)j * MT]);
-                const int r = r0 + row;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&bars[S + slot]));  // P arrivals free the slot
+            if (is_lead) {
                 const size_t col = tk.scatter ? (size_t)tk.row_ids[r] : (size_t)r;
-                if (tk.dst_f32) tk.dst_f32[(size_t)m * tk.f32_stride + col] = acc;
-                if (tk.dst) {
-                    float v = acc;
-                    if (tk.res) v = __fadd_rn(v, __half2float(tk.res[(size_t)m * tk.res_stride + col]));
-                    tk.dst[(size_t)m * tk.dst_stride + col] = __float2half_rn(v);
-                }
-                if (p.argmax) {
-                    const float cmp = p.argmax_f16 ? __half2float(__float2half_rn(acc)) : acc;
-                    atomicMax(&s_best[m], argmax_key(cmp, (uint32_t)(tk.index_base + r)));
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    if (m < p.M) {
+                        if (tk.dst_f32) tk.dst_f32[(size_t)m * tk.f32_stride + col] = acc[m];
+                        if (tk.dst) {
+                            float v = acc[m];
+                            if (tk.res) v = __fadd_rn(v, __half2float(tk.res[(size_t)m * tk.res_stride + col]));
+                            tk.dst[(size_t)m * tk.dst_stride + col] = __float2half_rn(v);
+                        }
+                        if (p.argmax) {
+                            const float cmp = p.argmax_f16 ? __half2float(__float2half_rn(acc[m])) : acc[m];
+                            atomicMax(&s_best[m], argmax_key(cmp, (uint32_t)(tk.index_base + r)));
+                        }
+                    }
                 }
             }
-            ++consumed;
-        }
-        if (p.argmax) {
-            named_bar_sync(1, kConsumers);
-            if (ctid < p.M) atomicMax(&p.argmax[ctid], s_best[ctid]);
         }
     }
     __syncthreads();
-    // drain: copies issued but not consumed (only after an error) must land before exit;
-    // consumer thread 0 (tid 0) holds the consumed count
+    if (p.argmax && tid < p.M && !s_abort) atomicMax(&p.argmax[tid], s_best[tid]);
+    // drain: a slot's most recent copy must land before the CTA exits (matters only after an
+    // early stop); consumers never arrive on full barriers, so the last S issued stages are
+    // exactly the outstanding candidates
     if (tid == 0) {
-        const int issued = flags[1];
-        for (int s = consumed; s < issued; ++s) mbar_wait_bounded(smem_u32(&bars[s % NS]), (s / NS) & 1, p.timeout_ns, p.status);
+        const int issued = s_issued;
+        for (int s = max(0, issued - S); s < issued; ++s)
+            mbar_wait_bounded(smem_u32(&bars[s % S]), (s / S) & 1, p.timeout_ns, p.status);
     }
 }
 
@@ -583,50 +627,69 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
 namespace {
 
 struct Plan {
-    int rows_per_stage, n_stages, ctas_per_sm;
-    unsigned stage_bytes, off_act, off_terms, off_stages, off_bars, smem;
+    int rows_per_sub, subs, n_stages, n_warps, grid;
+    unsigned stage_bytes, off_act, off_stages, off_bars, smem;
 };
 
 unsigned align_up(unsigned v, unsigned a) { return (v + a - 1) / a * a; }
 
-Plan make_plan(int type, int K, int M, int MT, size_t row_bytes) {
+// Sub-stage = the rows one consumer warp handles at once: floor(32 / units-per-row) whole rows
+// (one unit per lane), or one row.  Stage = P sub-stages with P * sub_bytes >= 16 KB (smaller
+// bulk copies do not reach full HBM bandwidth).  One CTA per SM, W = 10 consumer warps, the
+// ring of S stages within ~100 KB so that the next kernel's CTA (programmatic dependent
+// launch) fits beside it and prefetches its weights; large activations take up to 220 KB.
+// (P * S) % W == 0 keeps every full-barrier wait within one phase (see the kernel).
+Plan make_plan(int type, int K, int M, size_t row_bytes, int total_rows, int num_sms) {
+    Plan pl{};
+    const int W = kMaxWarps;
     const int nbu = K / 256;
-    const int T = (type == TYPE_Q8_0) ? 8 : 1;
-    const unsigned act_bytes = align_up((unsigned)(M * nbu * (int)sizeof(ActUnit)), 128);
-    Plan best{};
-    // Prefer two CTAs per SM (next kernel's CTAs can start while this one drains); fall back to
-    // one CTA per SM with a deeper ring when the activation is large.
-    for (int ctas = 2; ctas >= 1; --ctas) {
-        const unsigned budget = (ctas == 2) ? 112 * 1024 : 220 * 1024;
-        unsigned stage = (unsigned)std::max<size_t>(row_bytes, (ctas == 2) ? 24576 : 32768);
-        int rps = (int)(stage / row_bytes);
-        stage = (unsigned)(rps * row_bytes);
-        for (int ns = (ctas == 2 ? 4 : 6); ns >= 2; --ns) {
-            const unsigned terms = align_up((unsigned)(2 * rps * nbu * T * MT * 4), 128);
-            const unsigned bars = (2 * kMaxStages + 1) * 8 + 16;
-            const unsigned total = act_bytes + terms + ns * align_up(stage, 128) + bars;
-            if (total <= budget) {
-                best.rows_per_stage = rps;
-                best.n_stages = ns;
-                best.ctas_per_sm = ctas;
-                best.stage_bytes = align_up(stage, 128);
-                best.off_act = 0;
-                best.off_terms = act_bytes;
-                best.off_stages = act_bytes + terms;
-                best.off_bars = best.off_stages + ns * best.stage_bytes;
-                best.smem = best.off_bars + bars;
-                return best;
+    const int upr = (type == TYPE_Q8_0) ? K / 32 : nbu;
+    const int rsub = upr <= 16 ? 32 / upr : 1;
+    const size_t sub_bytes = (size_t)rsub * row_bytes;
+    const unsigned act = align_up((unsigned)(M * nbu * (int)sizeof(ActUnit)), 128);
+    for (unsigned budget : {100u * 1024u, 220u * 1024u}) {
+        if (act + 1024 >= budget) continue;
+        const unsigned avail = budget - act - 1024;
+        // candidates (P, S) with (P * S) % W == 0, S >= 2, preferring the most bytes in flight
+        // with stages of at least 16 KB
+        int bestP = 0, bestS = 0;
+        size_t best_flight = 0;
+        for (int P = 1; P <= 2 * W; ++P) {
+            const size_t stage = align_up((unsigned)(P * sub_bytes), 128);
+            if (stage > 64 * 1024 && P > 1) break;
+            for (int S = 2; S <= 16; ++S) {
+                if ((P * S) % W) continue;
+                if ((size_t)S * stage > avail) break;
+                const size_t flight = (size_t)S * stage;
+                const bool big = stage >= 16 * 1024;
+                const bool best_big = best_flight && align_up((unsigned)(bestP * sub_bytes), 128) >= 16 * 1024;
+                if (!best_flight || (big && !best_big) || (big == best_big && flight > best_flight)) {
+                    bestP = P;
+                    bestS = S;
+                    best_flight = flight;
+                }
             }
         }
+        if (!best_flight) continue;
+        pl.rows_per_sub = rsub;
+        pl.subs = bestP;
+        pl.n_stages = bestS;
+        pl.n_warps = W;
+        pl.stage_bytes = align_up((unsigned)(bestP * sub_bytes), 128);
+        pl.off_act = 0;
+        pl.off_stages = act;
+        pl.off_bars = act + bestS * pl.stage_bytes;
+        pl.smem = pl.off_bars + (2 * bestS + 1) * 8;
+        const int rps = bestP * rsub;
+        const int ctas_per_sm = pl.smem <= 110 * 1024 ? 2 : 1;
+        pl.grid = std::max(1, std::min(ctas_per_sm * num_sms, (total_rows + rps - 1) / rps));
+        return pl;
     }
-    best.smem = 0;  // does not fit
-    return best;
+    return pl;  // smem 0: does not fit
 }
 
 template <int TYPE, int MT>
 cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
-    const Plan pl = make_plan(TYPE, L.K, L.M, MT, L.row_bytes);
-    if (pl.smem == 0) return cudaErrorInvalidConfiguration;
     GemvParams p{};
     int total = 0;
     for (int i = 0; i < L.n_tasks; ++i) {
@@ -649,16 +712,21 @@ cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
         total += h.rows;
     }
     if (total == 0) return cudaSuccess;
+    const Plan pl = make_plan(TYPE, L.K, L.M, L.row_bytes, total, L.num_sms);
+    if (pl.smem == 0) return cudaErrorInvalidConfiguration;
     p.n_tasks = L.n_tasks;
     p.total_rows = total;
     p.K = L.K;
     p.nbu = L.K / 256;
     p.M = L.M;
     p.row_bytes = (unsigned)L.row_bytes;
-    p.rows_per_stage = pl.rows_per_stage;
+    p.rows_per_stage = pl.subs * pl.rows_per_sub;
+    p.rows_per_sub = pl.rows_per_sub;
+    p.subs_per_stage = pl.subs;
+    p.units_per_row = (TYPE == TYPE_Q8_0) ? L.K / 32 : L.K / 256;
+    p.n_warps = pl.n_warps;
     p.n_stages = pl.n_stages;
     p.stage_bytes = pl.stage_bytes;
-    p.terms_per_row = p.nbu * ((TYPE == TYPE_Q8_0) ? 8 : 1);
     p.x = reinterpret_cast<const __half *>(L.x);
     p.x_stride = L.x_stride;
     p.act = L.act;
@@ -668,7 +736,6 @@ cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
     p.argmax_f16 = L.argmax_f16;
     p.inject_wait = L.inject_wait;
     p.off_act = pl.off_act;
-    p.off_terms = pl.off_terms;
     p.off_stages = pl.off_stages;
     p.off_bars = pl.off_bars;
 
@@ -688,10 +755,10 @@ cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
             have = 225 * 1024;
         }
     }
-    const int grid = std::max(1, std::min(total, pl.ctas_per_sm * L.num_sms));
+    const int grid = pl.grid;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3((pl.n_warps + 1) * 32);
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
