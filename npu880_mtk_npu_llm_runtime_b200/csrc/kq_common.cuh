@@ -121,14 +121,15 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 }
 
 // Bounded wait on an mbarrier phase.  Gives up after timeout_ns of wall time, records
-// DEV_ERR_TIMEOUT in *status and returns false; never traps.  The clock is read every 16
-// suspended polls.
+// DEV_ERR_TIMEOUT in *status and returns false; never traps.  Polls without a suspend hint
+// (a suspended thread wakes up later than a polling one, which costs latency on the critical
+// path of a short kernel) and reads the clock every 64 polls.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint64_t timeout_ns, int *status) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        for (int i = 0; i < 16; ++i)
-            if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
         if (global_timer_ns() - t0 > timeout_ns) {
             if (status) atomicExch(status, DEV_ERR_TIMEOUT);
             return false;

@@ -30,7 +30,7 @@
 
 namespace kq {
 
-constexpr int kMaxWarps = 10;                  // consumer warps per CTA (W)
+constexpr int kMaxWarps = 12;                  // consumer warps per CTA (W <= 12)
 constexpr int kMaxThreads = (kMaxWarps + 1) * 32;
 
 struct GemvTaskDev {
@@ -633,57 +633,84 @@ struct Plan {
 
 unsigned align_up(unsigned v, unsigned a) { return (v + a - 1) / a * a; }
 
-// Sub-stage = the rows one consumer warp handles at once: floor(32 / units-per-row) whole rows
-// (one unit per lane), or one row.  Stage = P sub-stages with P * sub_bytes >= 16 KB (smaller
-// bulk copies do not reach full HBM bandwidth).  One CTA per SM, W = 10 consumer warps, the
-// ring of S stages within ~100 KB so that the next kernel's CTA (programmatic dependent
-// launch) fits beside it and prefetches its weights; large activations take up to 220 KB.
-// (P * S) % W == 0 keeps every full-barrier wait within one phase (see the kernel).
+// Geometry of one launch.
+//  * Sub-stage = the rows one consumer warp handles at once: floor(32 / units-per-row) whole
+//    rows (one unit per lane), or one row.  Stage = P sub-stages, P * sub_bytes >= 16 KB
+//    (smaller bulk copies do not reach full HBM bandwidth).
+//  * Prefetch mode: when a CTA's whole share of rows fits in ~110 KB, one CTA per SM with a
+//    ring that holds all of it.  Its smem, registers and threads stay under half an SM, so the
+//    next kernel's CTA (programmatic dependent launch) is resident meanwhile and streams its
+//    own weights while this one computes; back-to-back small GEMVs then overlap their HBM
+//    traffic.
+//  * Throughput mode (larger matrices): two CTAs per SM, ring within ~100 KB each.
+//  * W consumer warps with (P * S) % W == 0, which keeps every full-barrier wait within one
+//    phase (see the kernel).
 Plan make_plan(int type, int K, int M, size_t row_bytes, int total_rows, int num_sms) {
     Plan pl{};
-    const int W = kMaxWarps;
     const int nbu = K / 256;
     const int upr = (type == TYPE_Q8_0) ? K / 32 : nbu;
     const int rsub = upr <= 16 ? 32 / upr : 1;
     const size_t sub_bytes = (size_t)rsub * row_bytes;
     const unsigned act = align_up((unsigned)(M * nbu * (int)sizeof(ActUnit)), 128);
-    for (unsigned budget : {100u * 1024u, 220u * 1024u}) {
-        if (act + 1024 >= budget) continue;
-        const unsigned avail = budget - act - 1024;
-        // candidates (P, S) with (P * S) % W == 0, S >= 2, preferring the most bytes in flight
-        // with stages of at least 16 KB
-        int bestP = 0, bestS = 0;
-        size_t best_flight = 0;
-        for (int P = 1; P <= 2 * W; ++P) {
-            const size_t stage = align_up((unsigned)(P * sub_bytes), 128);
-            if (stage > 64 * 1024 && P > 1) break;
-            for (int S = 2; S <= 16; ++S) {
-                if ((P * S) % W) continue;
-                if ((size_t)S * stage > avail) break;
-                const size_t flight = (size_t)S * stage;
-                const bool big = stage >= 16 * 1024;
-                const bool best_big = best_flight && align_up((unsigned)(bestP * sub_bytes), 128) >= 16 * 1024;
-                if (!best_flight || (big && !best_big) || (big == best_big && flight > best_flight)) {
-                    bestP = P;
-                    bestS = S;
-                    best_flight = flight;
-                }
-            }
-        }
-        if (!best_flight) continue;
+    int pmin = 1;
+    while ((size_t)pmin * sub_bytes < 16 * 1024 && pmin < 16) ++pmin;
+    auto smem_of = [&](int P, int S) {
+        return act + S * align_up((unsigned)(P * sub_bytes), 128) + (2 * S + 1) * 8 + 256;
+    };
+    auto fill = [&](int P, int S, int W, int ctas_per_sm) {
+        const unsigned stage = align_up((unsigned)(P * sub_bytes), 128);
+        const int rps = P * rsub;
         pl.rows_per_sub = rsub;
-        pl.subs = bestP;
-        pl.n_stages = bestS;
+        pl.subs = P;
+        pl.n_stages = S;
         pl.n_warps = W;
-        pl.stage_bytes = align_up((unsigned)(bestP * sub_bytes), 128);
+        pl.stage_bytes = stage;
         pl.off_act = 0;
         pl.off_stages = act;
-        pl.off_bars = act + bestS * pl.stage_bytes;
-        pl.smem = pl.off_bars + (2 * bestS + 1) * 8;
-        const int rps = bestP * rsub;
-        const int ctas_per_sm = pl.smem <= 110 * 1024 ? 2 : 1;
+        pl.off_bars = act + S * stage;
+        pl.smem = pl.off_bars + (2 * S + 1) * 8;
         pl.grid = std::max(1, std::min(ctas_per_sm * num_sms, (total_rows + rps - 1) / rps));
+    };
+    // candidates: P in [pmin, pmin + 4], W in [6, 12]; prefer more warps, then more bytes in flight
+    int bP = 0, bS = 0, bW = 0, bctas = 0;
+    size_t bflight = 0;
+    auto consider = [&](int P, int S, int W, int ctas) {
+        const size_t flight = (size_t)S * align_up((unsigned)(P * sub_bytes), 128);
+        if (W > bW || (W == bW && flight > bflight)) {
+            bP = P, bS = S, bW = W, bctas = ctas, bflight = flight;
+        }
+    };
+    // prefetch mode: the ring holds the CTA's whole share
+    for (int P = pmin; P <= pmin + 4; ++P) {
+        const int rps = P * rsub;
+        const int share_stages = ((total_rows + num_sms - 1) / num_sms + rps - 1) / rps;
+        for (int W = 12; W >= 6; --W)
+            for (int S = std::max(2, share_stages); S <= share_stages + W; ++S) {
+                if ((P * S) % W) continue;
+                if (smem_of(P, S) <= 110 * 1024) consider(P, S, W, 1);
+                break;
+            }
+    }
+    if (bW) {
+        fill(bP, bS, bW, bctas);
         return pl;
+    }
+    // throughput mode: two CTAs per SM within ~100 KB each, else one CTA with up to 220 KB
+    for (unsigned budget : {100u * 1024u, 220u * 1024u}) {
+        for (int P = pmin; P <= pmin + 4; ++P)
+            for (int W = 12; W >= 6; --W) {
+                int best = 0;
+                for (int S = 2; S <= 32; ++S) {
+                    if ((P * S) % W) continue;
+                    if (smem_of(P, S) > budget) break;
+                    best = S;
+                }
+                if (best) consider(P, best, W, budget <= 100 * 1024 ? 2 : 1);
+            }
+        if (bW) {
+            fill(bP, bS, bW, bctas);
+            return pl;
+        }
     }
     return pl;  // smem 0: does not fit
 }
