@@ -197,6 +197,23 @@ int kq_lm_head_argmax(kq_ctx *ctx, const kq_weight *w, const uint16_t *x, int M,
 int kq_lm_head_argmax_async(kq_ctx *ctx, const kq_weight *w, const uint16_t *x_dev, int M, uint16_t *logits_dev,
                             float *logits_f32_dev, uint32_t *top_toks_dev, float *top_vals_dev);
 
+/* LM-head argmax that allocates nothing.  No counterpart in the reference: an addition for
+ * callers that cannot allocate device memory when they call, such as a decode loop whose memory
+ * is fixed after start-up or that runs inside another runtime's allocator.  Same computation and
+ * results as kq_lm_head_argmax_async (fused GEMV over all rows of w, fp16 logits to logits_dev
+ * when not NULL, argmax of the fp16 logits to toks_dev / vals_dev), with no context: DEVICE
+ * pointers, enqueued on `stream` (a cudaStream_t; NULL = the default stream) of the current
+ * device.  Its only scratch is a static device array of KQ_NOALLOC_MAX_M argmax slots that every
+ * GPU which loads the library keeps until exit; M > KQ_NOALLOC_MAX_M returns KQ_ERR_SHAPE.  The
+ * first call on a device looks up that array's device address once (cudaGetSymbolAddress), so
+ * make the first call on each device before any stream capture.  All calls share the array and
+ * clear it on their stream at the start: calls that overlap on the GPU (different streams) race
+ * and must be serialised by the caller.  Device-side wait timeouts are not reported by this
+ * call. */
+#define KQ_NOALLOC_MAX_M 64
+int kq_lm_head_argmax_noalloc(const kq_weight *w, const uint16_t *x_dev, int M, uint16_t *logits_dev,
+                              uint32_t *top_toks_dev, float *top_vals_dev, void *stream);
+
 /* eval_indexed_ext_lm_rows_parallel (ENG:9581-9614, work item ENG:9473-9579): the rows listed
  * in row_ids against the context's current quantized input (M rows), fp32 comparison;
  * top_toks/top_vals [M] are updated in place when a row beats them (strict '>').

@@ -45,7 +45,7 @@ EXPORTS = (
     "kq_sdot_row_batch", "kq_eval_single_lm_row_dot", "kq_debug_block_sums_async",
     "kq_rmsnorm_fp16_rows", "kq_swiglu_fp16_rows", "kq_rmsnorm_q8k_async", "kq_swiglu_q8k_async",
     "kq_run_ffn", "kq_run_ffn_async",
-    "kq_lm_head_argmax", "kq_lm_head_argmax_async", "kq_eval_indexed_rows_argmax",
+    "kq_lm_head_argmax", "kq_lm_head_argmax_async", "kq_lm_head_argmax_noalloc", "kq_eval_indexed_rows_argmax",
     "kq_dequant_rows", "kq_dequant_rows_async",
 )
 
@@ -111,6 +111,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "kq_run_ffn_async": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp]),
         "kq_lm_head_argmax": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp]),
         "kq_lm_head_argmax_async": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp]),
+        "kq_lm_head_argmax_noalloc": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
         "kq_eval_indexed_rows_argmax": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
         "kq_dequant_rows": (_i, [_vp, _vp, _i, _i, _vp]),
         "kq_dequant_rows_async": (_i, [_vp, _vp, _i, _i, _vp]),

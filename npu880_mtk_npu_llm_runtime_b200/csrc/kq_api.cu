@@ -15,14 +15,6 @@
 #include <string>
 #include <vector>
 
-struct kq_weight {
-    uint32_t type;
-    int rows, cols;
-    size_t row_bytes;  // device layout
-    uint8_t *d;
-    size_t bytes;
-};
-
 namespace {
 
 struct DevBuf {

@@ -5,6 +5,15 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+// A GGUF tensor resident in HBM in this library's device layout (opaque kq_weight of kq.h).
+struct kq_weight {
+    uint32_t type;
+    int rows, cols;
+    size_t row_bytes;  // device layout
+    uint8_t *d;
+    size_t bytes;
+};
+
 namespace kq {
 
 // One matrix of a dispatch, device pointers, already offset to the task's first weight row.
