@@ -530,18 +530,20 @@ __global__ void __launch_bounds__(kMaxThreads, 2) gemv_kernel(const __grid_const
         const int lrow = multi ? lane / upr : 0;
         const int lead = multi ? lrow * upr : 0;  // leader lane of this lane's row
         const int n_sub = n_stages_cta * P;
+        // sub-stage q = sidx * P + part lives in ring slot sidx % S, phase (sidx / S) & 1; the
+        // counters advance by W sub-stages per iteration without integer division
+        int sidx = warp / P, part = warp - (warp / P) * P;
+        int slot = sidx % S, phase = (sidx / S) & 1;
+        int a = g_begin + sidx * RPS;  // first row of the stage
         for (int q = warp; q < n_sub; q += W) {
             if (*reinterpret_cast<volatile int *>(&s_abort)) break;
-            const int sidx = q / P, part = q - sidx * P;
-            const int slot = sidx % S;
             int ok = 1;
-            if (lane == 0) ok = mbar_wait_bounded(smem_u32(&bars[slot]), (sidx / S) & 1, p.timeout_ns, p.status) ? 1 : 0;
+            if (lane == 0) ok = mbar_wait_bounded(smem_u32(&bars[slot]), phase, p.timeout_ns, p.status) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) {
                 if (lane == 0) s_abort = 1;
                 break;
             }
-            const int a = g_begin + sidx * RPS;                 // first row of the stage
             const int sR = max(0, min(RS, min(g_end, a + RPS) - (a + part * RS)));  // rows of this sub-stage
             const int g = a + part * RS + min(lrow, max(sR - 1, 0));  // this lane's row (concatenated)
             const int t = task_of(p, g);
@@ -606,6 +608,16 @@ __global__ void __launch_bounds__(kMaxThreads, 2) gemv_kernel(const __grid_const
                             atomicMax(&s_best[m], argmax_key(cmp, (uint32_t)(tk.index_base + r)));
                         }
                     }
+                }
+            }
+            part += W;
+            while (part >= P) {
+                part -= P;
+                ++sidx;
+                a += RPS;
+                if (++slot == S) {
+                    slot = 0;
+                    phase ^= 1;
                 }
             }
         }
