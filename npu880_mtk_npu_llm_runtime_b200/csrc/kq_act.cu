@@ -241,91 +241,79 @@ cudaError_t launch_swiglu_q8k(void *gate, const void *up, void *q8k, int M, int 
 
 // ------------------------------------------------------------------ weight repack
 
-// GGUF rows -> device layout (see kq_common.cuh).  One thread per device byte; runs once per
-// tensor at upload.
-__global__ void repack_kernel(int type, const uint8_t *gguf, uint8_t *dev, int rows, int K, size_t dev_rb) {
-    const size_t total = (size_t)rows * dev_rb;
-    const size_t nb = (type == TYPE_Q8_0) ? (size_t)K / 32 : (size_t)K / 256;
-    const size_t src_rb = nb * (size_t)block_bytes(type);
+// GGUF rows -> row-group tiles (kq_common.cuh).  One thread per GGUF byte (the padding rows of
+// the last group were zeroed before); runs once per tensor at upload.
+__global__ void repack_kernel(int type, int nbu, const uint8_t *gguf, uint8_t *dev, int rows, size_t gguf_rb) {
+    const size_t total = (size_t)rows * gguf_rb;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const size_t r = i / dev_rb, o = i % dev_rb;
-        const uint8_t *src = gguf + r * src_rb;
-        uint8_t v = 0;
-        if (type == TYPE_Q6_K) {
-            if (o < nb * 208) {
-                v = src[(o / 208) * 210 + (o % 208)];
-            } else if (o < nb * 210) {
-                const size_t j = o - nb * 208;       // d plane: 2 bytes per block
-                v = src[(j / 2) * 210 + 208 + (j % 2)];
-            }
-        } else {  // Q8_0
-            if (o < (size_t)K) {
-                v = src[(o / 32) * 34 + 2 + (o % 32)];
-            } else if (o < (size_t)K + nb * 2) {
-                const size_t j = o - (size_t)K;
-                v = src[(j / 2) * 34 + (j % 2)];
-            }
-        }
-        dev[i] = v;
+        const int r = (int)(i / gguf_rb);
+        dev[tile_byte_offset(type, nbu, r, i - (size_t)r * gguf_rb)] = gguf[i];
     }
 }
 
 cudaError_t launch_repack(int type, const uint8_t *gguf, uint8_t *dev, int rows, int K, cudaStream_t stream) {
-    const size_t rb = dev_row_bytes(type, K);
-    if (type == TYPE_Q4_K || type == TYPE_Q5_K) {
-        return cudaMemcpyAsync(dev, gguf, (size_t)rows * rb, cudaMemcpyDeviceToDevice, stream);
-    }
+    cudaError_t e = cudaMemsetAsync(dev, 0, weight_bytes(type, rows, K), stream);
+    if (e != cudaSuccess) return e;
+    const size_t rb = (size_t)(K / 256) * unit_bytes(type);
     const size_t total = (size_t)rows * rb;
     const int threads = 256;
     const int blocks = (int)std::min<size_t>((total + threads - 1) / threads, 148 * 64);
-    repack_kernel<<<blocks, threads, 0, stream>>>(type, gguf, dev, rows, K, rb);
+    repack_kernel<<<blocks, threads, 0, stream>>>(type, K / 256, gguf, dev, rows, rb);
     return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ dequant to fp16
 
-// One thread per output value, from the device layout; same rounding sequence as the
-// reference's scalar dequant loops.
-__global__ void dequant_kernel(int type, const uint8_t *dev, size_t rb, int rows, int K, __half *out) {
+// GGUF byte ob of row r, read from the tiled tensor.
+__device__ __forceinline__ uint8_t gguf_byte(int type, int nbu, const uint8_t *t, int r, size_t ob) {
+    return t[tile_byte_offset(type, nbu, r, ob)];
+}
+
+// One thread per output value of rows [row_begin, row_begin + rows); same rounding sequence as
+// the reference's scalar dequant loops.
+__global__ void dequant_kernel(int type, const uint8_t *tiled, int row_begin, int rows, int K, __half *out) {
+    const int nbu = K / 256;
     const size_t total = (size_t)rows * K;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const size_t r = i / K;
+        const int r = row_begin + (int)(i / K);
         const int e = (int)(i % K);
-        const uint8_t *row = dev + r * rb;
         float y;
         if (type == TYPE_Q8_0) {
-            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(row + K + 2 * (e / 32)));
-            y = __fmul_rn(d, (float)(int8_t)row[e]);
+            const size_t b = (size_t)(e / 32) * 34;
+            const uint32_t db = gguf_byte(type, nbu, tiled, r, b) | ((uint32_t)gguf_byte(type, nbu, tiled, r, b + 1) << 8);
+            y = __fmul_rn(half_bits_to_float(db), (float)(int8_t)gguf_byte(type, nbu, tiled, r, b + 2 + e % 32));
         } else if (type == TYPE_Q6_K) {
-            const int b = e / 256, w = e % 256;
-            const uint8_t *blk = row + (size_t)b * 208;
+            const size_t b = (size_t)(e / 256) * 210;
+            const int w = e % 256;
             const int hh = w / 128, g = (w % 128) / 32, l = w % 32;
-            const uint8_t ql = blk[64 * hh + l + 32 * (g & 1)];
-            const uint8_t qh = blk[128 + 32 * hh + l];
+            const uint8_t ql = gguf_byte(type, nbu, tiled, r, b + 64 * hh + l + 32 * (g & 1));
+            const uint8_t qh = gguf_byte(type, nbu, tiled, r, b + 128 + 32 * hh + l);
             const int lo = (g >= 2) ? (ql >> 4) : (ql & 0x0F);
             const int q = (lo | (((qh >> (2 * g)) & 3) << 4)) - 32;
-            const int sc = (int)(int8_t)blk[192 + 8 * hh + 2 * g + (l >= 16)];
-            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(row + (size_t)(K / 256) * 208 + 2 * b));
-            y = __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
+            const int sc = (int)(int8_t)gguf_byte(type, nbu, tiled, r, b + 192 + 8 * hh + 2 * g + (l >= 16));
+            const uint32_t db = gguf_byte(type, nbu, tiled, r, b + 208) | ((uint32_t)gguf_byte(type, nbu, tiled, r, b + 209) << 8);
+            y = __fmul_rn(__fmul_rn(half_bits_to_float(db), (float)sc), (float)q);
         } else {
             const int bbytes = (type == TYPE_Q4_K) ? 144 : 176;
-            const int b = e / 256, w = e % 256;
-            const uint8_t *blk = row + (size_t)b * bbytes;
+            const size_t b = (size_t)(e / 256) * bbytes;
+            const int w = e % 256;
             const int c = w / 64, hi = (w % 64) / 32, l = w % 32;
             const int j = 2 * c + hi;
-            const uint8_t *s = blk + 4;
+            auto sb = [&](int k) { return (int)gguf_byte(type, nbu, tiled, r, b + 4 + k); };
             int sc, mn;
             if (j < 4) {
-                sc = s[j] & 63;
-                mn = s[j + 4] & 63;
+                sc = sb(j) & 63;
+                mn = sb(j + 4) & 63;
             } else {
-                sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
-                mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+                sc = (sb(j + 4) & 0x0F) | ((sb(j - 4) >> 6) << 4);
+                mn = (sb(j + 4) >> 4) | ((sb(j) >> 6) << 4);
             }
-            const uint8_t *qs = (type == TYPE_Q4_K) ? blk + 16 : blk + 48;
-            int q = hi ? (qs[32 * c + l] >> 4) : (qs[32 * c + l] & 0x0F);
-            if (type == TYPE_Q5_K) q += ((blk[16 + l] >> j) & 1) ? 16 : 0;
-            const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
+            const size_t qs = (type == TYPE_Q4_K) ? b + 16 : b + 48;
+            const uint8_t qb = gguf_byte(type, nbu, tiled, r, qs + 32 * c + l);
+            int q = hi ? (qb >> 4) : (qb & 0x0F);
+            if (type == TYPE_Q5_K) q += ((gguf_byte(type, nbu, tiled, r, b + 16 + l) >> j) & 1) ? 16 : 0;
+            uint32_t dd = 0;
+            for (int k = 0; k < 4; ++k) dd |= (uint32_t)gguf_byte(type, nbu, tiled, r, b + k) << (8 * k);
             const float d = half_bits_to_float(dd), dmin = half_bits_to_float(dd >> 16);
             y = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)mn));
         }
@@ -333,12 +321,12 @@ __global__ void dequant_kernel(int type, const uint8_t *dev, size_t rb, int rows
     }
 }
 
-cudaError_t launch_dequant(int type, const uint8_t *dev, size_t row_bytes, int rows, int K, void *out,
+cudaError_t launch_dequant(int type, const uint8_t *tiled, int row_begin, int rows, int K, void *out,
                            cudaStream_t stream) {
     const size_t total = (size_t)rows * K;
     if (total == 0) return cudaSuccess;
     const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 32);
-    dequant_kernel<<<blocks, 256, 0, stream>>>(type, dev, row_bytes, rows, K, reinterpret_cast<__half *>(out));
+    dequant_kernel<<<blocks, 256, 0, stream>>>(type, tiled, row_begin, rows, K, reinterpret_cast<__half *>(out));
     return cudaGetLastError();
 }
 

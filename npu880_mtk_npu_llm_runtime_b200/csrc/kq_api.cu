@@ -137,8 +137,8 @@ struct GemvExtra {
     int *dbg_sumi = nullptr, *dbg_summ = nullptr;
     unsigned long long *argmax = nullptr;  // [M] keys
     int argmax_f16 = 0;
-    const uint32_t *row_ids = nullptr;     // gather list for tasks[0]
-    int scatter = 0;
+    const uint32_t *out_ids = nullptr;     // tasks[0]: output column of local row r (device)
+    bool no_pdl = false;                   // the weights were written by the previous kernel
 };
 
 int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half *x, long long x_stride,
@@ -158,12 +158,12 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
             kq::GemvLaunch L{};
             L.type = type;
             L.K = K;
-            L.row_bytes = tasks[idx[0]].w->row_bytes;
             L.n_tasks = (int)idx.size();
             for (int j = 0; j < L.n_tasks; ++j) {
                 const kq_task &t = tasks[idx[j]];
                 kq::GemvTaskHost &h = L.tasks[j];
-                h.w = t.w->d + (size_t)t.row_begin * t.w->row_bytes;
+                h.w = t.w->d;
+                h.row_begin = t.row_begin;
                 h.rows = t.rows;
                 h.dst = t.dst ? (void *)(t.dst + (size_t)m0 * t.dst_stride) : nullptr;
                 h.dst_stride = (long long)t.dst_stride;
@@ -176,11 +176,7 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
                     h.dbg_sumi = ex.dbg_sumi + (size_t)m0 * t.rows * bpr;
                     h.dbg_summ = ex.dbg_summ + (size_t)m0 * t.rows * bpr;
                 }
-                if (ex.row_ids && idx[j] == 0) {
-                    h.w = t.w->d;
-                    h.row_ids = ex.row_ids;
-                    h.scatter = ex.scatter;
-                }
+                if (ex.out_ids && idx[j] == 0) h.out_ids = ex.out_ids;
                 h.index_base = t.row_begin;
             }
             if (x) {
@@ -194,7 +190,7 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
             L.M = mt;
             L.status = c->d_status;
             L.timeout_ns = c->timeout_ns;
-            L.pdl = c->pdl;
+            L.pdl = c->pdl && !ex.no_pdl;
             L.num_sms = c->num_sms;
             L.argmax = ex.argmax ? ex.argmax + m0 : nullptr;
             L.argmax_f16 = ex.argmax_f16;
@@ -301,6 +297,7 @@ extern "C" int kq_init(int device, kq_ctx **out) {
         cudaMalloc(&c->d_status, sizeof(int)) != cudaSuccess ||
         cudaMemset(c->d_status, 0, sizeof(int)) != cudaSuccess) {
         if (c->stream) cudaStreamDestroy(c->stream);
+        cudaFree(c->d_status);
         delete c;
         return KQ_ERR_CUDA;
     }
@@ -394,13 +391,12 @@ static int weight_create(kq_ctx *c, const void *src, bool src_on_device, uint32_
         return fail(c, KQ_ERR_SHAPE, "cols = %d must be a positive multiple of 256 up to %d", cols, KQ_MAX_K);
     cudaSetDevice(c->device);
     const size_t gguf_bytes = (size_t)rows * kq_row_bytes(type, cols);
-    const size_t rb = kq::dev_row_bytes((int)type, cols);
     kq_weight *w = new kq_weight();
     w->type = type;
     w->rows = rows;
     w->cols = cols;
-    w->row_bytes = rb;
-    w->bytes = rb * rows;
+    w->row_bytes = kq_row_bytes(type, cols);
+    w->bytes = kq::weight_bytes((int)type, rows, cols);
     cudaError_t e = cudaMalloc(&w->d, w->bytes);
     if (e != cudaSuccess) {
         delete w;
@@ -409,13 +405,9 @@ static int weight_create(kq_ctx *c, const void *src, bool src_on_device, uint32_
     void *staging = nullptr;
     const uint8_t *gsrc = reinterpret_cast<const uint8_t *>(src);
     if (!src_on_device) {
-        if (type == KQ_TYPE_Q4_K || type == KQ_TYPE_Q5_K) {
-            e = cudaMemcpyAsync(w->d, src, gguf_bytes, cudaMemcpyHostToDevice, c->stream);
-        } else {
-            e = cudaMalloc(&staging, gguf_bytes);
-            if (e == cudaSuccess) e = cudaMemcpyAsync(staging, src, gguf_bytes, cudaMemcpyHostToDevice, c->stream);
-            if (e == cudaSuccess) e = kq::launch_repack((int)type, (const uint8_t *)staging, w->d, rows, cols, c->stream);
-        }
+        e = cudaMalloc(&staging, gguf_bytes);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(staging, src, gguf_bytes, cudaMemcpyHostToDevice, c->stream);
+        if (e == cudaSuccess) e = kq::launch_repack((int)type, (const uint8_t *)staging, w->d, rows, cols, c->stream);
     } else {
         e = kq::launch_repack((int)type, gsrc, w->d, rows, cols, c->stream);
     }
@@ -808,8 +800,7 @@ extern "C" int kq_run_ffn(kq_ctx *c, const kq_weight *gate, const kq_weight *up,
 extern "C" int kq_dequant_rows_async(kq_ctx *c, const kq_weight *w, int row_begin, int rows, uint16_t *dst) {
     if (!c || !w || !dst) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
     if (row_begin < 0 || rows < 0 || (long long)row_begin + rows > w->rows) return fail(c, KQ_ERR_SHAPE, "row range");
-    KQ_CUDA(c, kq::launch_dequant((int)w->type, w->d + (size_t)row_begin * w->row_bytes, w->row_bytes, rows, w->cols,
-                                  dst, c->stream));
+    KQ_CUDA(c, kq::launch_dequant((int)w->type, w->d, row_begin, rows, w->cols, dst, c->stream));
     return KQ_OK;
 }
 
@@ -883,15 +874,23 @@ extern "C" int kq_eval_indexed_rows_argmax(kq_ctx *c, const kq_weight *w, const 
     const void *act = nullptr;
     if (int r = current_act(c, w->type, &act)) return r;
     const size_t idb = (size_t)n_rows * 4, kb = (size_t)M * 8;
-    if (int r = ensure(c, c->misc, idb + kb + (size_t)M * 8 + 64)) return r;
+    const size_t gb = kq::weight_bytes((int)w->type, n_rows, w->cols);
+    const size_t o_keys = (idb + 255) & ~(size_t)255, o_w = (o_keys + kb + (size_t)M * 8 + 255) & ~(size_t)255;
+    if (int r = ensure(c, c->misc, o_w + gb)) return r;
     uint32_t *dids = reinterpret_cast<uint32_t *>(c->misc.p);
-    auto *keys = reinterpret_cast<unsigned long long *>((uint8_t *)c->misc.p + ((idb + 15) & ~(size_t)15));
+    auto *keys = reinterpret_cast<unsigned long long *>((uint8_t *)c->misc.p + o_keys);
     uint32_t *dt = reinterpret_cast<uint32_t *>(keys + M);
     float *dv = reinterpret_cast<float *>(dt + M);
     KQ_CUDA(c, cudaMemcpyAsync(dids, row_ids, idb, cudaMemcpyHostToDevice, c->stream));
     KQ_CUDA(c, cudaMemsetAsync(keys, 0, kb, c->stream));
+    // the listed rows, gathered into a tiled tensor of n_rows rows
+    kq_weight gw = *w;
+    gw.rows = n_rows;
+    gw.d = (uint8_t *)c->misc.p + o_w;
+    gw.bytes = gb;
+    KQ_CUDA(c, kq::launch_gather_rows((int)w->type, w->cols, w->d, dids, n_rows, gw.d, c->stream));
     kq_task t{};
-    t.w = w;
+    t.w = &gw;
     t.rows = n_rows;
     if (logits_m1) {
         if (int r = h2d(c, c->out16, logits_m1, (size_t)w->rows * 2)) return r;
@@ -901,8 +900,8 @@ extern "C" int kq_eval_indexed_rows_argmax(kq_ctx *c, const kq_weight *w, const 
     GemvExtra ex;
     ex.argmax = keys;
     ex.argmax_f16 = 0;  // the work item compares fp32 row results (ENG:9557-9571)
-    ex.row_ids = dids;
-    ex.scatter = 1;
+    ex.out_ids = dids;
+    ex.no_pdl = true;
     const bool q80 = w->type == KQ_TYPE_Q8_0;
     if (int r = run_gemv(c, &t, 1, M, w->cols, nullptr, 0, q80 ? nullptr : act, q80 ? act : nullptr, ex)) return r;
     KQ_CUDA(c, kq::launch_argmax_finalize(keys, M, dids, dt, dv, c->stream));

@@ -1,14 +1,16 @@
 // kq_common.cuh -- shared device definitions of the B200 K-quant matmul path.
 //
-// Device weight layout (one contiguous row after another, every row 16-byte aligned so a
-// stage of consecutive rows is one cp.async.bulk copy):
-//   Q4_K : the GGUF bytes unchanged, 144 B per 256 values (16 B header + 128 B nibbles)
-//   Q5_K : the GGUF bytes unchanged, 176 B per 256 values
-//   Q6_K : per row [nb x 208 B: ql[128] qh[64] scales[16]] [nb x fp16 d] [pad to 16 B]
-//          (the GGUF block is ql, qh, scales, d = 210 B; d moves to a per-row plane so the
-//          208-byte remainder stays 16-byte aligned)
-//   Q8_0 : per row [K int8 quants] [K/32 x fp16 d] [pad to 16 B]
-// Activations are staged per (token, 256-value unit) in shared memory as kq::ActUnit.
+// Device weight layout: row-group tiles.  Rows are taken 16 at a time (the last group is
+// zero-padded); row group rg holds one tile per 256-value unit u = 0 .. K/256-1, stored
+// [rg][u][tile], so any run of consecutive tiles is one contiguous cp.async.bulk copy.  A tile
+// holds the unit's bytes of its 16 rows one row after another, each row 16-byte aligned at a
+// stride that is an odd multiple of 16 bytes (so 8 rows read at the same column fall in 8
+// different bank groups -- conflict-free per-row loads and ldmatrix):
+//   Q4_K  16 x 144 B GGUF blocks                                    (2304 B)
+//   Q5_K  16 x 176 B GGUF blocks                                    (2816 B)
+//   Q6_K  16 x 208 B (ql[128] qh[64] scales[16]), then 16 fp16 d     (3360 B)
+//   Q8_0  16 x 272 B: the eight fp16 d of the row's 8 blocks, then their 256 quants (4352 B)
+// tile_byte_offset() is the exact map from a GGUF byte to its place in a tile.
 #pragma once
 
 #include <cstddef>
@@ -41,32 +43,40 @@ struct BlockQ80 {
 };
 static_assert(sizeof(BlockQ80) == 36, "BlockQ8_0_Fast layout");
 
-// One token's 256 activation values in shared memory.  368 B = 23 x 16 B: consecutive units
-// start in different 16-byte bank groups, so lanes reading different units do not conflict.
-struct __align__(16) ActUnit {
-    int8_t qs[256];
-    int32_t aux[8];     // K-quants: bsum32[8] (sum of each 32 quants); Q8_0: fp32 d of each 32-block
-    int32_t xsum16[16]; // sum of each 16 quants (Q6_K's 16-value sub-blocks)
-    float d;            // K-quants: the Q8_K block scale
-    int32_t pad[3];
-};
-static_assert(sizeof(ActUnit) == 368, "ActUnit layout");
-
 __host__ __device__ constexpr int block_bytes(int type) {
     return type == TYPE_Q4_K ? 144 : type == TYPE_Q5_K ? 176 : type == TYPE_Q6_K ? 210 : type == TYPE_Q8_0 ? 34 : 0;
 }
 __host__ __device__ constexpr int block_elems(int type) { return type == TYPE_Q8_0 ? 32 : 256; }
 
-// bytes of one row in the device layout (K % 256 == 0)
-__host__ __device__ inline size_t dev_row_bytes(int type, int K) {
-    const size_t nbu = (size_t)K / 256;
-    switch (type) {
-        case TYPE_Q4_K: return nbu * 144;
-        case TYPE_Q5_K: return nbu * 176;
-        case TYPE_Q6_K: return (nbu * 210 + 15) & ~(size_t)15;
-        case TYPE_Q8_0: return ((size_t)K + (size_t)K / 32 * 2 + 15) & ~(size_t)15;
-        default: return 0;
+// GGUF bytes of 256 values (one tile row)
+__host__ __device__ constexpr int unit_bytes(int type) {
+    return type == TYPE_Q4_K ? 144 : type == TYPE_Q5_K ? 176 : type == TYPE_Q6_K ? 210 : type == TYPE_Q8_0 ? 272 : 0;
+}
+__host__ __device__ constexpr int tile_bytes(int type) { return 16 * unit_bytes(type); }
+
+// device bytes of a rows x K weight (K % 256 == 0)
+__host__ __device__ inline size_t weight_bytes(int type, int rows, int K) {
+    return (size_t)((rows + 15) / 16) * (size_t)(K / 256) * (size_t)tile_bytes(type);
+}
+
+// Offset in the tiled tensor of byte ob of GGUF row `row` (ob counts from the start of the
+// row's GGUF bytes).
+__host__ __device__ inline size_t tile_byte_offset(int type, int nbu, int row, size_t ob) {
+    const int rr = row & 15;
+    size_t u, off;
+    if (type == TYPE_Q8_0) {
+        const size_t blk = ob / 34, o = ob % 34;
+        u = blk / 8;
+        const size_t jj = blk % 8;
+        off = 272 * rr + (o < 2 ? 2 * jj + o : 16 + 32 * jj + (o - 2));
+    } else {
+        const int bb = unit_bytes(type);
+        u = ob / bb;
+        const size_t o = ob % bb;
+        if (type == TYPE_Q6_K) off = (o < 208) ? 208 * rr + o : 3328 + 2 * rr + (o - 208);
+        else off = (size_t)bb * rr + o;
     }
+    return ((size_t)(row >> 4) * nbu + u) * (size_t)tile_bytes(type) + off;
 }
 
 // ------------------------------------------------------------------ PTX helpers
@@ -164,18 +174,88 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// 4-way int8 dot products with 32-bit accumulate
-__device__ __forceinline__ int dp4a_us(uint32_t a_u8x4, int b_s8x4, int c) {
-    int d;
-    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a_u8x4), "r"(b_s8x4), "r"(c));
-    return d;
-}
-__device__ __forceinline__ int dp4a_ss(int a, int b, int c) { return __dp4a(a, b, c); }
-
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
     return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFFu)));
 }
 
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFFu; }
+
+// ------------------------------------------------------------------ integer MMA (mma.sync)
+// m16n8k32 and m16n8k16, 8-bit operands, int32 accumulate.  Fragments (lane = 4g + t):
+// A a0/a1 = rows g / g+8 at k-slots 4t..4t+3, a2/a3 the same rows at 16+4t..16+4t+3 (k32);
+// B b0 = k-slots 4t..4t+3 of column g, b1 = 16+4t..; D d0,d1 = row g, columns 2t, 2t+1,
+// d2,d3 = row g+8.  Which k a slot stands for is free as long as A and B agree.
+__device__ __forceinline__ void mma_k32_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1, int c0, int c1, int c2, int c3) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+}
+__device__ __forceinline__ void mma_k32_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void mma_k16_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0, int c0, int c1,
+                                             int c2, int c3) {
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+}
+
+__device__ __forceinline__ uint4 lds128(const void *p) { return *reinterpret_cast<const uint4 *>(p); }
+// ldmatrix: four (x4) / two (x2) 8x8 b16 matrices; lane i supplies the address of row i % 8 of
+// matrix i / 8; thread 4g+t receives bytes 4t..4t+3 of row g of each matrix.
+__device__ __forceinline__ uint4 ldsm_x4(uint32_t saddr) {
+    uint4 r;
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "r"(saddr));
+    return r;
+}
+__device__ __forceinline__ uint2 ldsm_x2(uint32_t saddr) {
+    uint2 r;
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(saddr));
+    return r;
+}
+// 4-way int8 dot products with 32-bit accumulate (u8 x s8, s8 x s8)
+__device__ __forceinline__ int dp4a_us(uint32_t a_u8x4, uint32_t b_s8x4, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a_u8x4), "r"(b_s8x4), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint2 lds64(const void *p) { return *reinterpret_cast<const uint2 *>(p); }
+
+// byte k of w, zero-extended / replicated into all four bytes
+__device__ __forceinline__ int ubyte(uint32_t w, int k) { return (int)__byte_perm(w, 0u, 0x4440u | (unsigned)k); }
+__device__ __forceinline__ uint32_t rep_byte(uint32_t w, int k) { return __byte_perm(w, 0u, 0x1111u * (unsigned)k); }
+// byte k of w sign-extended (prmt with the sign-replicate selector bit)
+__device__ __forceinline__ int sbyte(uint32_t w, int k) {
+    int r;
+    const unsigned sel = (unsigned)k | ((8u | (unsigned)k) * 0x1110u);
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
+    return r;
+}
+
+// Bounded wait until *p >= v (a shared-memory counter other warps advance).
+__device__ __forceinline__ bool wait_ge_bounded(const int *p, int v, uint64_t timeout_ns, int *status) {
+    const volatile int *vp = p;
+    if (*vp >= v) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        for (int i = 0; i < 64; ++i)
+            if (*vp >= v) return true;
+        if (global_timer_ns() - t0 > timeout_ns) {
+            if (status) atomicExch(status, DEV_ERR_TIMEOUT);
+            return false;
+        }
+    }
+}
 
 }  // namespace kq

@@ -1,24 +1,34 @@
-// kq_gemv.cu -- K-quant x Q8 matrix-vector / small-batch product for sm_100a.
+// kq_gemv.cu -- K-quant x Q8 matrix-vector / small-batch product (M <= 8 tokens) for sm_100a.
 //
 // Replaces the engine's NEON row kernels (sdot_4rows_<type>_m1 / _batch, sdot_row_<type>_batch,
 // src/v182_r22_breakthrough_engine.c:1226-3440) and its pinned work-stealing pool
-// (exec_sdot_job_work_stealing, ENG:3491-3619) for M <= 8 activation rows.
+// (exec_sdot_job_work_stealing, ENG:3491-3619).
 //
 // Design (HBM-bound: every weight byte is read once, activations are tiny):
-//  * Persistent-style grid, at most a few CTAs per SM.  CTA c owns a contiguous range of the
-//    dispatch's concatenated output rows (the reference's 64-row grains, ENG:3502, become
-//    one balanced range per CTA).
-//  * Warp 8 is the producer: one lane streams the CTA's rows through an NS-deep ring of
-//    shared-memory stages with cp.async.bulk (the TMA engine), one bulk copy per stage of
-//    whole consecutive rows, completion counted on an mbarrier, L2 evict-first.
-//  * Warps 0-7 are consumers.  Before the first stage they quantize the fp16 activation to
-//    Q8_K / Q8_0 in shared memory (bit-exact to quantize_row_fp16_to_q8_k, ENG:925-990) or copy
-//    a pre-quantized one.  Per stage, each thread takes whole 256-value units (one super-block,
-//    or eight Q8_0 blocks) and computes the exact integer sub-block sums with dp4a, then the
-//    fp32 block term with the reference's operation order.  After a consumer barrier the stage
-//    is released and one thread per (row, token) adds the block terms in block order -- the
-//    same fp32 sequence as the reference's `acc += term` loop, so results are bit-identical to
-//    the scalar reference -- and applies the epilogue (fp32 out, fp16 out, fp16 residual).
+//  * Weights are in the row-group tile layout of kq_common.cuh; the launch's tiles form one
+//    sequence (row group major), each CTA owning a contiguous range of it.
+//  * Warp W is the producer: one lane streams the CTA's tiles into shared-memory stages
+//    (>= 16 KB) with cp.async.bulk, completion counted on mbarriers, L2 evict-first.
+//  * Consumer warps 0..W-1 first stage the activation in shared memory (quantized to Q8_K /
+//    Q8_0 bit-exactly as quantize_row_fp16_to_q8_k / _q8_0, ENG:925-1064, or copied from a
+//    pre-quantized input).  Then they take work items round-robin and compute, for every
+//    (row, token), the exact integer sub-block sums and the fp32 block term with the
+//    reference's operation order into a term buffer:
+//      - M <= 2: dp4a, an item is a tile with two lanes per row; the two lanes of a row read
+//        different bank groups of the activation, shared by all rows (a broadcast);
+//      - M > 2: an item is a tile; integer MMAs (m16n8k32, Q6_K m16n8k16) with ldmatrix
+//        fragments give the sub-block dot products of all tokens at once.
+//  * Each (row, token) result is the sum of its block terms in block order -- the reference's
+//    `acc += term` sequence, so fp32 results equal the reference's bit for bit -- followed by
+//    the epilogue: fp32 out, fp16 out with optional fp16 residual, argmax keys.
+//  * Each CTA owns whole row groups and streams them through a ring of stages.  When the terms
+//    of its whole share fit in shared memory (small launches) the warps compute all items and
+//    fold everything after one barrier (and, when the ring holds the whole share, wait for the
+//    stages once); otherwise the warp that completes a row group folds it (shared-memory
+//    counters).
+//    Under half an SM per CTA, the next kernel's CTA (programmatic dependent launch, enabled
+//    once this CTA has staged its activation) prefetches its weights during this one's
+//    arithmetic.
 //  * Every wait is bounded (globaltimer); on timeout the kernel records DEV_ERR_TIMEOUT,
 //    drains its own copies in flight (bounded) and returns.
 #include "kq_common.cuh"
@@ -30,13 +40,21 @@
 
 namespace kq {
 
-constexpr int kMaxWarps = 12;                  // consumer warps per CTA (W <= 12)
-constexpr int kMaxThreads = (kMaxWarps + 1) * 32;
+constexpr int kMaxTermSlots = 32;
+
+// consumer warps: 15 for the dp4a kernels (M <= 2, 64 registers: two CTAs of 512 threads per
+// SM), 12 for the MMA kernels (72 registers)
+template <int MT>
+__host__ __device__ constexpr int warps_of() { return MT <= 2 ? 15 : 12; }
+template <int MT>
+__host__ __device__ constexpr int threads_of() { return (warps_of<MT>() + 1) * 32; }
 
 struct GemvTaskDev {
-    const uint8_t *w;
-    int rows;
-    int row_start;  // first row of this task in the concatenated row space
+    const uint8_t *w;  // tiled weight, row group 0 of the tensor
+    int rg_first;      // first row group of the task (row_begin / 16)
+    int n_rg;          // row groups of the task
+    int rg_start;      // first row group of the task in the launch's concatenated space
+    int row_begin, rows;
     __half *dst;
     long long dst_stride;
     const __half *res;
@@ -45,26 +63,24 @@ struct GemvTaskDev {
     long long f32_stride;
     int *dbg_sumi;
     int *dbg_summ;
-    const uint32_t *row_ids;  // gathered rows: stage row i is weight row row_ids[r0 + i]
-    int scatter;              // write dst/dst_f32 at column row_ids[r] instead of r
+    const uint32_t *out_ids;  // output column of local row r is out_ids[r] (else r)
     int index_base;           // argmax index of local row r is index_base + r
 };
 
 struct GemvParams {
     GemvTaskDev task[4];
     int n_tasks;
-    int total_rows;
+    int total_rg;
     int K;
-    int nbu;              // 256-value units per row
+    int nbu;               // 256-value units per row = tiles per row group
     int M;
-    unsigned int row_bytes;
-    int rows_per_stage;   // P * rows_per_sub
-    int rows_per_sub;
-    int subs_per_stage;   // P
-    int units_per_row;    // 256-value units (Q8_0: 32-value blocks)
-    int n_warps;          // consumer warps W
-    int n_stages;         // S
-    unsigned int stage_bytes;
+    unsigned tile_bytes;
+    int tiles_per_stage;   // T
+    int n_stages;          // S
+    int term_slots;        // TS (large launches)
+    int terms_per_rg;      // J: terms per (row, token) of a row group
+    int q80_exact;         // Q8_0: one term per 32-block (exact order); else one per tile
+    unsigned stage_bytes;
     const __half *x;
     long long x_stride;
     const void *act;
@@ -73,7 +89,7 @@ struct GemvParams {
     unsigned long long *argmax;  // [M] packed (ordered value, ~index) keys, or nullptr
     int argmax_f16;              // compare the fp16-rounded results (the dispatch's stored logits)
     int inject_wait;             // failure test: consumers first wait on a barrier nothing arrives at
-    unsigned int off_act, off_stages, off_bars;
+    unsigned off_x, off_dx, off_xs, off_terms, off_stages, off_bars;
 };
 
 // Total order on floats as unsigned keys: larger float -> larger key.
@@ -83,34 +99,49 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index
     return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - index);
 }
 
-// ------------------------------------------------------------------ activation staging
+// token-slot pitch of the dx / -32*xsum tables (mma reads of tokens 2t, 2t+1 stay inside)
+template <int MT>
+__device__ __forceinline__ constexpr int xpitch() { return MT < 2 ? 2 : MT; }
+template <int MT>
+__device__ __forceinline__ int tok_pair(int t) { return min(2 * t, xpitch<MT>() - 2); }
+template <int MT>
+__device__ __forceinline__ constexpr bool use_dp() { return MT <= 2; }
 
-// Quantize 256 fp16 values of one token into an ActUnit (one warp).  K-quant weights get the
-// Q8_K block (ENG:925-990); Q8_0 weights get eight Q8_0 blocks (ENG:1016-1064).
+// ------------------------------------------------------------------ activation staging
+//
+// Shared-memory activation of MT token slots (tokens >= M are never read for an output):
+//  * x, int8 quants.  dp4a items (M <= 2): per token nbu units of 320 bytes, value k of a unit
+//    at 80 (k / 64) + k % 64 (Q6_K: 160 (k / 128) + k % 128), so the four quarter-lanes of a
+//    row read four different bank groups.  MMA items: [tok][K + 16] (the pad puts the tokens of
+//    one ldmatrix in different bank groups).
+//  * dx: the Q8_K scale of (unit, token) at [u][tok] (Q8_0: the block scale at [u*8+j][tok]).
+//  * Q4_K/Q5_K: the block's bsum32[8] at [tok][u][8].
+//  * Q6_K: -32 * (sum of the 16 quants of sub-block s = 8h + 2g + l), dp4a: [u][2h+l][tok][g],
+//    MMA: [u][s][tok].
+
+__device__ __forceinline__ int sum_s8x4(uint32_t w) {
+    return (int)(int8_t)(w & 0xFF) + (int)(int8_t)((w >> 8) & 0xFF) + (int)(int8_t)((w >> 16) & 0xFF) +
+           (int)(int8_t)(w >> 24);
+}
+
+// Quantize 8 fp16 values per lane of one 256-value unit: Q8_K (per 256, ENG:925-990) or Q8_0
+// (per 32-value block = 4 lanes, ENG:1016-1064).  Returns the packed quants and the scale.
 template <int TYPE>
-__device__ __forceinline__ void stage_act_from_fp16(const __half *xu, bool vec_ok, ActUnit *a, int lane) {
+__device__ __forceinline__ void quantize_lane(const uint4 raw, uint32_t &lo, uint32_t &hi, float &d) {
     float v[8];
-    if (vec_ok) {
-        const uint4 raw = *reinterpret_cast<const uint4 *>(xu + 8 * lane);
-        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+    const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float2 f = __half22float2(h2[i]);
-            v[2 * i] = f.x;
-            v[2 * i + 1] = f.y;
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __half2float(xu[8 * lane + i]);
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h2[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
     }
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    // K-quants: max over the whole 256 (32 lanes); Q8_0: over each 32-value block (4 lanes)
-    const int span = (TYPE == TYPE_Q8_0) ? 4 : 32;
+    constexpr int span = (TYPE == TYPE_Q8_0) ? 4 : 32;
 #pragma unroll
     for (int o = 1; o < span; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-
     int q[8];
     if (amax == 0.0f) {
 #pragma unroll
@@ -118,343 +149,620 @@ __device__ __forceinline__ void stage_act_from_fp16(const __half *xu, bool vec_o
     } else {
         const float inv = __fdiv_rn(127.0f, amax);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            int t = __float2int_rn(__fmul_rn(v[i], inv));
-            q[i] = max(-127, min(127, t));
-        }
+        for (int i = 0; i < 8; ++i) q[i] = max(-127, min(127, __float2int_rn(__fmul_rn(v[i], inv))));
     }
-    const uint32_t lo = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) | ((uint32_t)(q[2] & 0xFF) << 16) |
-                        ((uint32_t)(q[3] & 0xFF) << 24);
-    const uint32_t hi = (uint32_t)(q[4] & 0xFF) | ((uint32_t)(q[5] & 0xFF) << 8) | ((uint32_t)(q[6] & 0xFF) << 16) |
-                        ((uint32_t)(q[7] & 0xFF) << 24);
-    *reinterpret_cast<uint2 *>(a->qs + 8 * lane) = make_uint2(lo, hi);
-    int s8 = q[0] + q[1] + q[2] + q[3] + q[4] + q[5] + q[6] + q[7];
-    const int s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
-    const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);
-    if ((lane & 1) == 0) a->xsum16[lane >> 1] = s16;
-    if (TYPE == TYPE_Q8_0) {
-        if ((lane & 3) == 0) a->aux[lane >> 2] = __float_as_int(amax == 0.0f ? 0.0f : __fdiv_rn(amax, 127.0f));
-    } else {
-        if ((lane & 3) == 0) a->aux[lane >> 2] = s32;
-        if (lane == 0) a->d = (amax == 0.0f) ? 0.0f : __fdiv_rn(amax, 127.0f);
-    }
+    lo = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) | ((uint32_t)(q[2] & 0xFF) << 16) |
+         ((uint32_t)(q[3] & 0xFF) << 24);
+    hi = (uint32_t)(q[4] & 0xFF) | ((uint32_t)(q[5] & 0xFF) << 8) | ((uint32_t)(q[6] & 0xFF) << 16) |
+         ((uint32_t)(q[7] & 0xFF) << 24);
+    d = (amax == 0.0f) ? 0.0f : __fdiv_rn(amax, 127.0f);
 }
 
-// Copy one pre-quantized BlockQ8K (292 B, 4-byte aligned) into an ActUnit (one warp).
-__device__ __forceinline__ void stage_act_from_q8k(const BlockQ8K *src, ActUnit *a, int lane) {
-    const uint32_t *w = reinterpret_cast<const uint32_t *>(src);
-    const uint32_t lo = w[1 + 2 * lane], hi = w[2 + 2 * lane];
-    *reinterpret_cast<uint2 *>(a->qs + 8 * lane) = make_uint2(lo, hi);
-    int s8 = 0;
+// Stage the M tokens' activation (consumer warps).  Loads of up to 4 units per warp are issued
+// before any is used, so the staging costs about one global-memory latency.
+template <int TYPE, int MT>
+__device__ __forceinline__ void stage_activation(const GemvParams &p, uint8_t *smem, int warp, int lane, int W) {
+    constexpr int XP = xpitch<MT>();
+    uint8_t *xq = smem + p.off_x;
+    float *dx = reinterpret_cast<float *>(smem + p.off_dx);
+    int *aux = reinterpret_cast<int *>(smem + p.off_xs);
+    const int nbu = p.nbu, n_units = p.M * nbu;
+    for (int i0 = warp; i0 < n_units; i0 += 4 * W) {
+        uint4 raw[4];
+        int bs[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) s8 += (int)(int8_t)byte_of(lo, i) + (int)(int8_t)byte_of(hi, i);
-    const int s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
-    if ((lane & 1) == 0) a->xsum16[lane >> 1] = s16;
-    if (lane < 8) a->aux[lane] = (int)w[65 + lane];
-    if (lane == 0) a->d = __int_as_float((int)w[0]);
-}
-
-// Copy eight pre-quantized BlockQ8_0_Fast (36 B each) into an ActUnit (one warp).
-__device__ __forceinline__ void stage_act_from_q80(const BlockQ80 *src, ActUnit *a, int lane) {
-    const int j = lane >> 2, part = lane & 3;
-    const uint32_t *w = reinterpret_cast<const uint32_t *>(src + j);
-    const uint32_t lo = w[1 + 2 * part], hi = w[2 + 2 * part];
-    *reinterpret_cast<uint2 *>(a->qs + 8 * lane) = make_uint2(lo, hi);
-    if (part == 0) a->aux[j] = (int)w[0];
-}
-
-// ------------------------------------------------------------------ per-unit dot products
-//
-// A "unit" is 256 weight values of one row: one Q4_K/Q5_K/Q6_K super-block, or eight Q8_0
-// blocks; one lane computes a whole unit for all tokens, chunk by chunk (weights read from the
-// shared-memory stage once per chunk, tokens in the inner loop), keeping registers low.
-// Integer sums are exact; every fp32 term is formed with the reference's operation order and
-// written to term[j * MT + m] (j = 0 for K-quants, j = Q8_0 block for Q8_0).
-
-// Q4_K (ENG:758-801): term = dx * (d * sumi - dmin * summ)  (ENG:11025).  High nibbles are
-// used in place (x16) and the factor is divided out exactly at the end.
-template <int MT>
-__device__ __forceinline__ void unit_q4k(const uint8_t *blk, const ActUnit *a0, int nbu, int M, float *term,
-                                         int *dsi, int *dsm, long long dstride) {
-    const uint4 h = *reinterpret_cast<const uint4 *>(blk);
-    const uint32_t sc03 = h.y & 0x3F3F3F3Fu;
-    const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-    int s16[MT];
+        for (int b = 0; b < 4; ++b) {
+            const int i = i0 + b * W;
+            raw[b] = make_uint4(0, 0, 0, 0);
+            bs[b] = 0;
+            if (i < n_units) {
+                const int m = i / nbu, u = i - (i / nbu) * nbu;
+                if (p.x) {
+                    const __half *xu = p.x + (size_t)m * p.x_stride + (size_t)u * 256 + 8 * lane;
+                    if ((reinterpret_cast<uintptr_t>(xu) & 15) == 0) {
+                        raw[b] = *reinterpret_cast<const uint4 *>(xu);
+                    } else {
+                        uint32_t hv[8];
 #pragma unroll
-    for (int m = 0; m < MT; ++m) s16[m] = 0;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        const uint4 qa = reinterpret_cast<const uint4 *>(blk + 16)[2 * c];
-        const uint4 qb = reinterpret_cast<const uint4 *>(blk + 16)[2 * c + 1];
-        const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-        const uint32_t scw = (c < 2) ? sc03 : sc47;
-        const int s_lo = (int)byte_of(scw, 2 * (c & 1)), s_hi = (int)byte_of(scw, 2 * (c & 1) + 1);
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-            if (m < M) {
-                const uint4 *xv = reinterpret_cast<const uint4 *>(a0[(size_t)m * nbu].qs + 64 * c);
-                const uint4 x0 = xv[0], x1 = xv[1], x2 = xv[2], x3 = xv[3];
-                const uint32_t xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                const uint32_t xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
-                // four independent dp4a chains per chunk
-                int dl0 = 0, dl1 = 0, dh0 = 0, dh1 = 0;
-#pragma unroll
-                for (int i = 0; i < 8; i += 2) {
-                    dl0 = dp4a_us(w[i] & 0x0F0F0F0Fu, (int)xl[i], dl0);
-                    dl1 = dp4a_us(w[i + 1] & 0x0F0F0F0Fu, (int)xl[i + 1], dl1);
-                    dh0 = dp4a_us(w[i] & 0xF0F0F0F0u, (int)xh[i], dh0);  // 16 x the high-nibble dot
-                    dh1 = dp4a_us(w[i + 1] & 0xF0F0F0F0u, (int)xh[i + 1], dh1);
+                        for (int k = 0; k < 8; ++k) hv[k] = reinterpret_cast<const uint16_t *>(xu)[k];
+                        raw[b] = make_uint4(hv[0] | (hv[1] << 16), hv[2] | (hv[3] << 16), hv[4] | (hv[5] << 16),
+                                            hv[6] | (hv[7] << 16));
+                    }
+                } else if (TYPE == TYPE_Q8_0) {
+                    // eight BlockQ8_0_Fast: lane takes quants 8(L%4)..+7 of block L/4 and its scale
+                    const uint32_t *w = reinterpret_cast<const uint32_t *>(
+                        reinterpret_cast<const BlockQ80 *>(p.act) + ((size_t)m * nbu + u) * 8 + (lane >> 2));
+                    raw[b] = make_uint4(w[1 + 2 * (lane & 3)], w[2 + 2 * (lane & 3)], w[0], 0);
+                } else {
+                    const uint32_t *w =
+                        reinterpret_cast<const uint32_t *>(reinterpret_cast<const BlockQ8K *>(p.act) + (size_t)m * nbu + u);
+                    raw[b] = make_uint4(w[1 + 2 * lane], w[2 + 2 * lane], w[0], 0);
+                    if (lane < 8) bs[b] = (int)w[65 + lane];  // bsum32 as stored (ENG:868-872)
                 }
-                s16[m] += s_lo * ((dl0 + dl1) << 4) + s_hi * (dh0 + dh1);
             }
         }
-    }
-    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    const uint32_t mn03 = h.z & 0x3F3F3F3Fu;
-    const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-        if (m < M) {
-            const ActUnit *a = a0 + (size_t)m * nbu;
-            const int sumi = s16[m] >> 4;
-            const int4 b0 = *reinterpret_cast<const int4 *>(a->aux);
-            const int4 b1 = *reinterpret_cast<const int4 *>(a->aux + 4);
-            const int summ = (int)byte_of(mn03, 0) * b0.x + (int)byte_of(mn03, 1) * b0.y +
-                             (int)byte_of(mn03, 2) * b0.z + (int)byte_of(mn03, 3) * b0.w +
-                             (int)byte_of(mn47, 0) * b1.x + (int)byte_of(mn47, 1) * b1.y +
-                             (int)byte_of(mn47, 2) * b1.z + (int)byte_of(mn47, 3) * b1.w;
-            const float t = __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dmin, __int2float_rn(summ)));
-            term[m] = __fmul_rn(a->d, t);
-            if (dsi) {
-                dsi[m * dstride] = sumi;
-                dsm[m * dstride] = summ;
+        for (int b = 0; b < 4; ++b) {
+            const int i = i0 + b * W;
+            if (i >= n_units) break;  // uniform across the warp
+            const int m = i / nbu, u = i - (i / nbu) * nbu;
+            uint32_t lo, hi;
+            float d;
+            if (p.x) {
+                quantize_lane<TYPE>(raw[b], lo, hi, d);
+            } else {
+                lo = raw[b].x;
+                hi = raw[b].y;
+                d = __uint_as_float(raw[b].z);
+            }
+            size_t xo;
+            if (!use_dp<MT>()) xo = (size_t)m * (p.K + 16) + 256 * u + 8 * lane;
+            else if (TYPE == TYPE_Q6_K) xo = (size_t)(m * nbu + u) * 320 + 160 * (lane >> 4) + 8 * (lane & 15);
+            else xo = (size_t)(m * nbu + u) * 320 + 80 * (lane >> 3) + 8 * (lane & 7);
+            *reinterpret_cast<uint2 *>(xq + xo) = make_uint2(lo, hi);
+            if (TYPE == TYPE_Q8_0) {
+                if ((lane & 3) == 0) dx[(u * 8 + (lane >> 2)) * XP + m] = d;
+            } else {
+                if (lane == 0) dx[u * XP + m] = d;
+            }
+            if (TYPE == TYPE_Q6_K) {
+                const int s8 = sum_s8x4(lo) + sum_s8x4(hi);
+                const int s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
+                if ((lane & 1) == 0) {
+                    const int s = lane >> 1, h = s >> 3, g = (s >> 1) & 3, l = s & 1;
+                    if (use_dp<MT>()) aux[((u * 4 + 2 * h + l) * MT + m) * 4 + g] = -32 * s16;
+                    else aux[(u * 16 + s) * XP + m] = -32 * s16;
+                }
+            } else if (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K) {
+                if (p.x) {
+                    int s = sum_s8x4(lo) + sum_s8x4(hi);
+                    s += __shfl_xor_sync(0xffffffffu, s, 1);
+                    s += __shfl_xor_sync(0xffffffffu, s, 2);
+                    if ((lane & 3) == 0) aux[(m * nbu + u) * 8 + (lane >> 2)] = s;
+                } else if (lane < 8) {
+                    aux[(m * nbu + u) * 8 + lane] = bs[b];
+                }
             }
         }
     }
 }
 
-// Q5_K (ENG:803-853): as Q4_K with the fifth bit of value l of chunk c in bit 2c (low half) /
-// 2c+1 (high half) of qh[l]  (ENG:11028-11062).
+// ------------------------------------------------------------------ per-item products
+//
+// A tile is 16 weight rows x 256 values of unit u (row-major, kq_common.cuh).  Each (row,
+// token) gets the fp32 block term with the reference's operation order, stored at
+// terms[j * 16 * MT + row * MT + token] (j = 0, or the Q8_0 block in exact mode).
+
+struct DbgOut {
+    int *si, *sm;       // [M][rows][blocks per row] (rows of the task), or si == nullptr
+    int r0;             // task-local row of tile row 0 (may be negative)
+    int rows;           // task rows
+    int bpr;            // blocks per row
+    int blk0;           // first block of the tile
+    int M;
+};
+
+__device__ __forceinline__ void dbg_put(const DbgOut &db, int rr, int tok, int blk, int si, int sm) {
+    const int r = db.r0 + rr;
+    if (tok < db.M && r >= 0 && r < db.rows) {
+        const size_t o = ((size_t)tok * db.rows + r) * db.bpr + db.blk0 + blk;
+        db.si[o] = si;
+        db.sm[o] = sm;
+    }
+}
+
 template <int MT>
-__device__ __forceinline__ void unit_q5k(const uint8_t *blk, const ActUnit *a0, int nbu, int M, float *term,
-                                         int *dsi, int *dsm, long long dstride) {
-    const uint4 h = *reinterpret_cast<const uint4 *>(blk);
-    const uint4 qh0 = reinterpret_cast<const uint4 *>(blk + 16)[0];
-    const uint4 qh1 = reinterpret_cast<const uint4 *>(blk + 16)[1];
-    const uint32_t hb[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
-    const uint32_t sc03 = h.y & 0x3F3F3F3Fu;
-    const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-    int s16[MT];
+__device__ __forceinline__ void store_terms4(float *terms, int lane, const float tm[4]) {
+    const int g = lane >> 2, t = lane & 3;
+    if (2 * t < MT) {
+        terms[g * MT + 2 * t] = tm[0];
+        terms[(g + 8) * MT + 2 * t] = tm[2];
+    }
+    if (2 * t + 1 < MT) {
+        terms[g * MT + 2 * t + 1] = tm[1];
+        terms[(g + 8) * MT + 2 * t + 1] = tm[3];
+    }
+}
+
+// ---- dp4a tiles (M <= 2): lane 2r + h takes half h of row r (two 64-value chunks).
+
+template <int TYPE, int MT>
+__device__ __forceinline__ void tile_q45k_dp(const uint8_t *tile, const uint8_t *xu, int XSD, const float *dxu,
+                                             const int *bsu, int nbu8, int lane, float *terms, const DbgOut &db) {
+    constexpr int RB = (TYPE == TYPE_Q4_K) ? 144 : 176, QS = (TYPE == TYPE_Q4_K) ? 16 : 48;
+    const int rr = lane >> 1, hf = lane & 1;
+    const uint8_t *row = tile + RB * rr;
+    const uint4 h = lds128(row);
+    const uint32_t sc = hf ? ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u)) : (h.y & 0x3F3F3F3Fu);
+    const uint32_t mn = hf ? (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3F3F3F3Fu);
+    uint32_t qh[8];
+    if (TYPE == TYPE_Q5_K) {
+        const uint4 a = lds128(row + 16), b = lds128(row + 32);
+        qh[0] = a.x, qh[1] = a.y, qh[2] = a.z, qh[3] = a.w, qh[4] = b.x, qh[5] = b.y, qh[6] = b.z, qh[7] = b.w;
+    }
+    int si[MT];
 #pragma unroll
-    for (int m = 0; m < MT; ++m) s16[m] = 0;
+    for (int m = 0; m < MT; ++m) si[m] = 0;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        const uint4 qa = reinterpret_cast<const uint4 *>(blk + 48)[2 * c];
-        const uint4 qb = reinterpret_cast<const uint4 *>(blk + 48)[2 * c + 1];
+    for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * hf + cc;
+        const uint4 qa = lds128(row + QS + 32 * c), qb = lds128(row + QS + 32 * c + 16);
         const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
         uint32_t wl[8], wh[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            wl[i] = (w[i] & 0x0F0F0F0Fu) | (((hb[i] >> (2 * c)) & 0x01010101u) << 4);
-            wh[i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((hb[i] >> (2 * c + 1)) & 0x01010101u) << 4);
+            if (TYPE == TYPE_Q4_K) {
+                wl[i] = w[i] & 0x0F0F0F0Fu;
+                wh[i] = w[i] & 0xF0F0F0F0u;  // 16 x the high nibble
+            } else {
+                wl[i] = (w[i] & 0x0F0F0F0Fu) | (((qh[i] >> (2 * c)) & 0x01010101u) << 4);
+                wh[i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * c + 1)) & 0x01010101u) << 4);
+            }
         }
-        const uint32_t scw = (c < 2) ? sc03 : sc47;
-        const int s_lo = (int)byte_of(scw, 2 * (c & 1)), s_hi = (int)byte_of(scw, 2 * (c & 1) + 1);
+        const int s_lo = ubyte(sc, 2 * cc), s_hi = ubyte(sc, 2 * cc + 1);
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-            if (m < M) {
-                const uint4 *xv = reinterpret_cast<const uint4 *>(a0[(size_t)m * nbu].qs + 64 * c);
-                const uint4 x0 = xv[0], x1 = xv[1], x2 = xv[2], x3 = xv[3];
-                const uint32_t xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                const uint32_t xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
-                int dl = 0, dh = 0;
+            const uint8_t *xm = xu + m * XSD + 80 * c;
+            const uint4 x0 = lds128(xm), x1 = lds128(xm + 16), x2 = lds128(xm + 32), x3 = lds128(xm + 48);
+            const uint32_t xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            const uint32_t xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+            int dl0 = 0, dl1 = 0, dh0 = 0, dh1 = 0;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    dl = dp4a_us(wl[i], (int)xl[i], dl);
-                    dh = dp4a_us(wh[i], (int)xh[i], dh);
-                }
-                s16[m] += (s_lo * dl + s_hi * dh) << 4;
+            for (int i = 0; i < 8; i += 2) {
+                dl0 = dp4a_us(wl[i], xl[i], dl0);
+                dl1 = dp4a_us(wl[i + 1], xl[i + 1], dl1);
+                dh0 = dp4a_us(wh[i], xh[i], dh0);
+                dh1 = dp4a_us(wh[i + 1], xh[i + 1], dh1);
             }
+            if (TYPE == TYPE_Q4_K) si[m] += s_lo * ((dl0 + dl1) << 4) + s_hi * (dh0 + dh1);
+            else si[m] += s_lo * (dl0 + dl1) + s_hi * (dh0 + dh1);
         }
     }
     const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    const uint32_t mn03 = h.z & 0x3F3F3F3Fu;
-    const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-        if (m < M) {
-            const ActUnit *a = a0 + (size_t)m * nbu;
-            const int sumi = s16[m] >> 4;
-            const int4 b0 = *reinterpret_cast<const int4 *>(a->aux);
-            const int4 b1 = *reinterpret_cast<const int4 *>(a->aux + 4);
-            const int summ = (int)byte_of(mn03, 0) * b0.x + (int)byte_of(mn03, 1) * b0.y +
-                             (int)byte_of(mn03, 2) * b0.z + (int)byte_of(mn03, 3) * b0.w +
-                             (int)byte_of(mn47, 0) * b1.x + (int)byte_of(mn47, 1) * b1.y +
-                             (int)byte_of(mn47, 2) * b1.z + (int)byte_of(mn47, 3) * b1.w;
-            const float t = __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dmin, __int2float_rn(summ)));
-            term[m] = __fmul_rn(a->d, t);
-            if (dsi) {
-                dsi[m * dstride] = sumi;
-                dsm[m * dstride] = summ;
-            }
+        const int4 b = *reinterpret_cast<const int4 *>(bsu + m * nbu8 + 4 * hf);
+        int sm = ubyte(mn, 0) * b.x + ubyte(mn, 1) * b.y + ubyte(mn, 2) * b.z + ubyte(mn, 3) * b.w;
+        const int sit = si[m] + __shfl_xor_sync(0xffffffffu, si[m], 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        if (hf == 0) {
+            const int sumi = (TYPE == TYPE_Q4_K) ? (sit >> 4) : sit;
+            terms[rr * MT + m] =
+                __fmul_rn(dxu[m], __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dmin, __int2float_rn(sm))));
+            if (db.si) dbg_put(db, rr, m, 0, sumi, sm);
         }
     }
 }
 
-// Q6_K, device block [ql 128][qh 64][scales 16] + d from the row's d plane (ENG:673-741).
-// Value e = 128h + 32g + l: low 4 bits in ql[64h + l + 32(g&1)] (>> 4 when g >= 2), bits 4-5 in
-// qh[32h + l] >> 2g, minus 32; sub-block s = 8h + 2g + (l >= 16) (ENG:11065-11101).
-// sum (q - 32) x = sum q x - 32 * (sum of the 16 activation quants, ActUnit.xsum16).
-// term = (d * dx) * sumi  (ENG:11100).  Processed per (h, 16-value half): 16 sub-block dots.
 template <int MT>
-__device__ __forceinline__ void unit_q6k(const uint8_t *blk, float d, const ActUnit *a0, int nbu, int M, float *term,
-                                         int *dsi, int *dsm, long long dstride) {
-    const uint4 scv = reinterpret_cast<const uint4 *>(blk + 192)[0];
-    const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
-    int sumi[MT];
+__device__ __forceinline__ void tile_q6k_dp(const uint8_t *tile, const uint8_t *xu, int XSD, const float *dxu,
+                                            const int *xsu, int lane, float *terms, const DbgOut &db) {
+    const int rr = lane >> 1, h = lane & 1;
+    const uint8_t *row = tile + 208 * rr;
+    const uint4 a0 = lds128(row + 64 * h), a1 = lds128(row + 64 * h + 16);
+    const uint4 b0 = lds128(row + 64 * h + 32), b1 = lds128(row + 64 * h + 48);
+    const uint4 q0 = lds128(row + 128 + 32 * h), q1 = lds128(row + 144 + 32 * h);
+    const uint2 scv = lds64(row + 192 + 8 * h);
+    const uint32_t A[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const uint32_t B[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const uint32_t H[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    int acc[MT];
 #pragma unroll
-    for (int m = 0; m < MT; ++m) sumi[m] = 0;
+    for (int m = 0; m < MT; ++m) acc[m] = 0;
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
+    for (int g = 0; g < 4; ++g) {
+        uint32_t q[8];
 #pragma unroll
-        for (int half16 = 0; half16 < 2; ++half16) {
-            // 16 values l in [16 half16, 16 half16 + 16) of the four groups g of half hh
-            const uint4 b0 = *reinterpret_cast<const uint4 *>(blk + 64 * hh + 16 * half16);
-            const uint4 b1 = *reinterpret_cast<const uint4 *>(blk + 64 * hh + 32 + 16 * half16);
-            const uint4 hv = *reinterpret_cast<const uint4 *>(blk + 128 + 32 * hh + 16 * half16);
-            const uint32_t B0[4] = {b0.x, b0.y, b0.z, b0.w}, B1[4] = {b1.x, b1.y, b1.z, b1.w};
-            const uint32_t HB[4] = {hv.x, hv.y, hv.z, hv.w};
-            uint32_t q[4][4];
+        for (int i = 0; i < 8; ++i) {
+            if (g == 0) q[i] = (A[i] & 0x0F0F0F0Fu) | ((H[i] << 4) & 0x30303030u);
+            else if (g == 1) q[i] = (B[i] & 0x0F0F0F0Fu) | ((H[i] << 2) & 0x30303030u);
+            else if (g == 2) q[i] = ((A[i] >> 4) & 0x0F0F0F0Fu) | (H[i] & 0x30303030u);
+            else q[i] = ((B[i] >> 4) & 0x0F0F0F0Fu) | ((H[i] >> 2) & 0x30303030u);
+        }
+        const uint32_t sw = (g < 2) ? scv.x : scv.y;
+        const int sc0 = sbyte(sw, 2 * (g & 1)), sc1 = sbyte(sw, 2 * (g & 1) + 1);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                q[0][k] = (B0[k] & 0x0F0F0F0Fu) | ((HB[k] << 4) & 0x30303030u);
-                q[1][k] = (B1[k] & 0x0F0F0F0Fu) | ((HB[k] << 2) & 0x30303030u);
-                q[2][k] = ((B0[k] >> 4) & 0x0F0F0F0Fu) | (HB[k] & 0x30303030u);
-                q[3][k] = ((B1[k] >> 4) & 0x0F0F0F0Fu) | ((HB[k] >> 2) & 0x30303030u);
-            }
-            int sc[4];
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-                const int sidx = 8 * hh + 2 * g + half16;
-                sc[g] = (int)(int8_t)byte_of(scw[sidx >> 2], sidx & 3);
-            }
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                if (m < M) {
-                    const ActUnit *a = a0 + (size_t)m * nbu;
-                    const uint4 *xv = reinterpret_cast<const uint4 *>(a->qs);
-                    int acc = 0;
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        const uint4 x = xv[8 * hh + 2 * g + half16];
-                        int dot = dp4a_us(q[g][0], (int)x.x, 0);
-                        dot = dp4a_us(q[g][1], (int)x.y, dot);
-                        dot = dp4a_us(q[g][2], (int)x.z, dot);
-                        dot = dp4a_us(q[g][3], (int)x.w, dot);
-                        acc += sc[g] * (dot - 32 * a->xsum16[8 * hh + 2 * g + half16]);
-                    }
-                    sumi[m] += acc;
-                }
-            }
+        for (int m = 0; m < MT; ++m) {
+            const uint8_t *xm = xu + m * XSD + 160 * h + 32 * g;
+            const uint4 x0 = lds128(xm), x1 = lds128(xm + 16);
+            // -32 * sums of sub-blocks 8h + 2g (quarter 2h) and 8h + 2g + 1 (quarter 2h + 1)
+            int d0 = xsu[((2 * h) * MT + m) * 4 + g], d1 = xsu[((2 * h + 1) * MT + m) * 4 + g];
+            d0 = dp4a_us(q[0], x0.x, d0);
+            d1 = dp4a_us(q[4], x1.x, d1);
+            d0 = dp4a_us(q[1], x0.y, d0);
+            d1 = dp4a_us(q[5], x1.y, d1);
+            d0 = dp4a_us(q[2], x0.z, d0);
+            d1 = dp4a_us(q[6], x1.z, d1);
+            d0 = dp4a_us(q[3], x0.w, d0);
+            d1 = dp4a_us(q[7], x1.w, d1);
+            acc[m] += sc0 * d0 + sc1 * d1;
         }
     }
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(tile + 3328 + 2 * rr));
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-        if (m < M) {
-            const ActUnit *a = a0 + (size_t)m * nbu;
-            term[m] = __fmul_rn(__fmul_rn(d, a->d), __int2float_rn(sumi[m]));
-            if (dsi) {
-                dsi[m * dstride] = sumi[m];
-                dsm[m * dstride] = 0;
-            }
+        const int a = acc[m] + __shfl_xor_sync(0xffffffffu, acc[m], 1);
+        if (h == 0) {
+            terms[rr * MT + m] = __fmul_rn(__fmul_rn(d, dxu[m]), __int2float_rn(a));
+            if (db.si) dbg_put(db, rr, m, 0, a, 0);
         }
     }
 }
 
-// One Q8_0 block of 32 values (device: int8 quants at 32 * j, fp16 scale in the row's d plane).
-// term = (d * dx) * dot  (sdot_row_q8_0_batch, ENG:3393-3407).  The activation block is
-// sub-block j & 7 of ActUnit j >> 3.
 template <int MT>
-__device__ __forceinline__ void unit_q80(const uint8_t *qs, const uint8_t *dptr, int j, const ActUnit *act, int nbu,
-                                         int M, float *term, int *dsi, int *dsm, long long dstride) {
-    const uint4 wa = reinterpret_cast<const uint4 *>(qs)[0];
-    const uint4 wb = reinterpret_cast<const uint4 *>(qs)[1];
-    const float dw = half_bits_to_float(*reinterpret_cast<const uint16_t *>(dptr));
-    const int au = j >> 3, sub = j & 7;
+__device__ __forceinline__ void tile_q80_dp(const uint8_t *tile, const uint8_t *xu, int XSD, const float *dxu,
+                                            int lane, float *terms, int exact, const DbgOut &db) {
+    constexpr int XP = xpitch<MT>();
+    const int rr = lane >> 1, h = lane & 1;
+    const uint8_t *row = tile + 272 * rr;
+    const uint2 dv = lds64(row + 8 * h);
+    float tv[4][MT];
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-        if (m < M) {
-            const ActUnit *a = act + (size_t)m * nbu + au;
-            const uint4 xa = reinterpret_cast<const uint4 *>(a->qs)[2 * sub];
-            const uint4 xb = reinterpret_cast<const uint4 *>(a->qs)[2 * sub + 1];
-            int dot = dp4a_ss((int)wa.x, (int)xa.x, 0);
-            dot = dp4a_ss((int)wa.y, (int)xa.y, dot);
-            dot = dp4a_ss((int)wa.z, (int)xa.z, dot);
-            dot = dp4a_ss((int)wa.w, (int)xa.w, dot);
-            dot = dp4a_ss((int)wb.x, (int)xb.x, dot);
-            dot = dp4a_ss((int)wb.y, (int)xb.y, dot);
-            dot = dp4a_ss((int)wb.z, (int)xb.z, dot);
-            dot = dp4a_ss((int)wb.w, (int)xb.w, dot);
-            term[m] = __fmul_rn(__fmul_rn(dw, __int_as_float(a->aux[sub])), __int2float_rn(dot));
-            if (dsi) {
-                dsi[m * dstride] = dot;
-                dsm[m * dstride] = 0;
-            }
+    for (int b = 0; b < 4; ++b) {
+        const int jj = 4 * h + b;
+        const uint4 w0 = lds128(row + 16 + 32 * jj), w1 = lds128(row + 32 + 32 * jj);
+        const float dw = half_bits_to_float(((b < 2) ? dv.x : dv.y) >> (16 * (b & 1)));
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            const uint8_t *xm = xu + m * XSD + 80 * (jj >> 1) + 32 * (jj & 1);
+            const uint4 x0 = lds128(xm), x1 = lds128(xm + 16);
+            int d0 = dp4a_ss(w0.x, x0.x, 0), d1 = dp4a_ss(w0.y, x0.y, 0);
+            d0 = dp4a_ss(w0.z, x0.z, d0);
+            d1 = dp4a_ss(w0.w, x0.w, d1);
+            d0 = dp4a_ss(w1.x, x1.x, d0);
+            d1 = dp4a_ss(w1.y, x1.y, d1);
+            d0 = dp4a_ss(w1.z, x1.z, d0);
+            d1 = dp4a_ss(w1.w, x1.w, d1);
+            const int dot = d0 + d1;
+            tv[b][m] = __fmul_rn(__fmul_rn(dw, dxu[jj * XP + m]), __int2float_rn(dot));
+            if (exact) terms[jj * 16 * MT + rr * MT + m] = tv[b][m];
+            if (db.si) dbg_put(db, rr, m, jj, dot, 0);
+        }
+    }
+    if (!exact) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) acc = __fadd_rn(acc, tv[b][m]);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, tv[b][m], 1));
+            if (h == 0) terms[rr * MT + m] = acc;
         }
     }
 }
 
-// ------------------------------------------------------------------ row -> task
+// ---- MMA tiles (M > 2)
 
-// Index of the task owning concatenated row g (tasks are in ascending row_start order).
-__device__ __forceinline__ int task_of(const GemvParams &p, int g) {
+// Q4_K / Q5_K with m16n8k32: per 64-value chunk c, one ldmatrix gives rows g, g+8 x bytes
+// 4t..4t+3 and 16+4t..16+4t+3 of qs[32c..32c+31] (low nibbles = sub-block 2c, high = 2c+1);
+// a second gives the activation of tokens 0..7 for both sub-blocks.  Mins are one more MMA
+// against each row's min replicated over the sub-block (sum_l m_j x_l = m_j * bsum_j).
+template <int TYPE, int MT>
+__device__ __forceinline__ void tile_q45k_mma(const uint8_t *tile, const int8_t *xu, int XS, const float *dxu,
+                                              int lane, float *terms, const DbgOut &db) {
+    constexpr int RB = (TYPE == TYPE_Q4_K) ? 144 : 176, QS = (TYPE == TYPE_Q4_K) ? 16 : 48;
+    const int g = lane >> 2, t = lane & 3, tp = tok_pair<MT>(t);
+    const uint4 h0 = lds128(tile + RB * g), h1 = lds128(tile + RB * (g + 8));
+    const uint32_t sc0[2] = {h0.y & 0x3F3F3F3Fu, (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u)};
+    const uint32_t sc1[2] = {h1.y & 0x3F3F3F3Fu, (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u)};
+    const uint32_t mn0[2] = {h0.z & 0x3F3F3F3Fu, ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u)};
+    const uint32_t mn1[2] = {h1.z & 0x3F3F3F3Fu, ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u)};
+    // ldmatrix row addresses: weight row (lane % 16), column half (lane / 16); token (lane % 8) % MT
+    const uint32_t wrow = smem_u32(tile + RB * (lane & 15) + 16 * (lane >> 4));
+    const uint32_t xrow = smem_u32(xu + (lane & 7 & (MT - 1)) * XS + 16 * (lane >> 3));
+    uint4 qh = make_uint4(0, 0, 0, 0);  // Q5_K: qh bytes 4t.. / 16+4t.. of rows g, g+8
+    if (TYPE == TYPE_Q5_K) qh = ldsm_x4(wrow + 16);
+    int slo[4] = {0, 0, 0, 0}, shi[4] = {0, 0, 0, 0}, mm[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint4 a = ldsm_x4(wrow + QS + 32 * c);  // row g lo4, row g+8 lo4, row g hi4, row g+8 hi4
+        const uint4 xb = ldsm_x4(xrow + 64 * c);      // sub-block 2c (b0, b1), sub-block 2c+1 (b0, b1)
+        const uint32_t av[4] = {a.x, a.y, a.z, a.w};
+        const uint32_t hv[4] = {qh.x, qh.y, qh.z, qh.w};
+        uint32_t al[4], ah[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (TYPE == TYPE_Q4_K) {
+                al[i] = av[i] & 0x0F0F0F0Fu;
+                ah[i] = av[i] & 0xF0F0F0F0u;  // 16 x the high nibble
+            } else {
+                al[i] = (av[i] & 0x0F0F0F0Fu) | (((hv[i] >> (2 * c)) & 0x01010101u) << 4);
+                ah[i] = ((av[i] >> 4) & 0x0F0F0F0Fu) | (((hv[i] >> (2 * c + 1)) & 0x01010101u) << 4);
+            }
+        }
+        int dl[4], dh[4];
+        mma_k32_u8s8(dl, al[0], al[1], al[2], al[3], xb.x, xb.y, 0, 0, 0, 0);
+        mma_k32_u8s8(dh, ah[0], ah[1], ah[2], ah[3], xb.z, xb.w, 0, 0, 0, 0);
+        const int k0 = 2 * (c & 1);
+        const uint32_t s0 = sc0[c >> 1], s1 = sc1[c >> 1];
+        const int a0l = ubyte(s0, k0), a0h = ubyte(s0, k0 + 1), a1l = ubyte(s1, k0), a1h = ubyte(s1, k0 + 1);
+        slo[0] += a0l * dl[0];
+        slo[1] += a0l * dl[1];
+        slo[2] += a1l * dl[2];
+        slo[3] += a1l * dl[3];
+        shi[0] += a0h * dh[0];
+        shi[1] += a0h * dh[1];
+        shi[2] += a1h * dh[2];
+        shi[3] += a1h * dh[3];
+        const uint32_t n0 = mn0[c >> 1], n1 = mn1[c >> 1];
+        const uint32_t r0l = rep_byte(n0, k0), r1l = rep_byte(n1, k0), r0h = rep_byte(n0, k0 + 1),
+                       r1h = rep_byte(n1, k0 + 1);
+        mma_k32_u8s8(mm, r0l, r1l, r0l, r1l, xb.x, xb.y, mm[0], mm[1], mm[2], mm[3]);
+        mma_k32_u8s8(mm, r0h, r1h, r0h, r1h, xb.z, xb.w, mm[0], mm[1], mm[2], mm[3]);
+    }
+    const float d0 = half_bits_to_float(h0.x), dm0 = half_bits_to_float(h0.x >> 16);
+    const float d1 = half_bits_to_float(h1.x), dm1 = half_bits_to_float(h1.x >> 16);
+    const float2 dxv = *reinterpret_cast<const float2 *>(dxu + tp);
+    float tm[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int sumi = (TYPE == TYPE_Q4_K) ? slo[e] + (shi[e] >> 4) : slo[e] + shi[e];
+        const float d = (e < 2) ? d0 : d1, dm = (e < 2) ? dm0 : dm1;
+        const float dxe = (e & 1) ? dxv.y : dxv.x;
+        tm[e] = __fmul_rn(dxe, __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dm, __int2float_rn(mm[e]))));
+        if (db.si) dbg_put(db, g + 8 * (e >> 1), 2 * t + (e & 1), 0, sumi, mm[e]);
+    }
+    store_terms4<MT>(terms, lane, tm);
+}
+
+// Q6_K with m16n8k16 per 16-value sub-block s = 8h + 2g' + hf: ldmatrix gives rows g, g+8 x
+// ql[64h + 16hf + 4t..+3] and ql[64h + 32 + 16hf + 4t..+3], another qh[32h + 16hf + 4t..+3];
+// the accumulator starts at -32 * (sum of the sub-block's activation quants).
+template <int MT>
+__device__ __forceinline__ void tile_q6k_mma(const uint8_t *tile, const int8_t *xu, int XS, const float *dxu,
+                                             const int *xsu, int lane, float *terms, const DbgOut &db) {
+    constexpr int XP = xpitch<MT>();
+    const int g = lane >> 2, t = lane & 3, tp = tok_pair<MT>(t);
+    const uint4 scA = lds128(tile + 208 * g + 192), scB = lds128(tile + 208 * (g + 8) + 192);
+    const uint32_t sa[4] = {scA.x, scA.y, scA.z, scA.w}, sb[4] = {scB.x, scB.y, scB.z, scB.w};
+    const uint32_t wrow = smem_u32(tile + 208 * (lane & 15));
+    const int col = 32 * (lane >> 4);  // matrices 2, 3: the qlB half
+    const uint32_t xrow = smem_u32(xu + (lane & 7 & (MT - 1)) * XS + 32 * (lane >> 3));
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int hq = 0; hq < 4; ++hq) {
+        const int h = hq >> 1, hf = hq & 1;
+        const uint4 qv = ldsm_x4(wrow + 64 * h + 16 * hf + col);  // qlA g, qlA g+8, qlB g, qlB g+8
+        const uint2 hv = ldsm_x2(wrow + 128 + 32 * h + 16 * hf);   // qh g, qh g+8 (lanes 0-15 give rows)
+        const uint4 xv = ldsm_x4(xrow + 128 * h + 16 * hf);        // g' = 0..3 (values 32g' apart)
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int gp = 0; gp < 4; ++gp) {
+            const uint32_t la = (gp & 1) ? qv.z : qv.x, lb = (gp & 1) ? qv.w : qv.y;
+            uint32_t qa, qb;
+            if (gp == 0) {
+                qa = (la & 0x0F0F0F0Fu) | ((hv.x << 4) & 0x30303030u);
+                qb = (lb & 0x0F0F0F0Fu) | ((hv.y << 4) & 0x30303030u);
+            } else if (gp == 1) {
+                qa = (la & 0x0F0F0F0Fu) | ((hv.x << 2) & 0x30303030u);
+                qb = (lb & 0x0F0F0F0Fu) | ((hv.y << 2) & 0x30303030u);
+            } else if (gp == 2) {
+                qa = ((la >> 4) & 0x0F0F0F0Fu) | (hv.x & 0x30303030u);
+                qb = ((lb >> 4) & 0x0F0F0F0Fu) | (hv.y & 0x30303030u);
+            } else {
+                qa = ((la >> 4) & 0x0F0F0F0Fu) | ((hv.x >> 2) & 0x30303030u);
+                qb = ((lb >> 4) & 0x0F0F0F0Fu) | ((hv.y >> 2) & 0x30303030u);
+            }
+            const int s = 8 * h + 2 * gp + hf;
+            const int2 ci = *reinterpret_cast<const int2 *>(xsu + s * XP + tp);
+            int D[4];
+            mma_k16_u8s8(D, qa, qb, xw[gp], ci.x, ci.y, ci.x, ci.y);
+            const int sA = sbyte(sa[s >> 2], s & 3), sB = sbyte(sb[s >> 2], s & 3);
+            acc[0] += sA * D[0];
+            acc[1] += sA * D[1];
+            acc[2] += sB * D[2];
+            acc[3] += sB * D[3];
+        }
+    }
+    const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t *>(tile + 3328 + 2 * g));
+    const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t *>(tile + 3328 + 2 * (g + 8)));
+    const float2 dxv = *reinterpret_cast<const float2 *>(dxu + tp);
+    float tm[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float d = (e < 2) ? d0 : d1, dxe = (e & 1) ? dxv.y : dxv.x;
+        tm[e] = __fmul_rn(__fmul_rn(d, dxe), __int2float_rn(acc[e]));
+        if (db.si) dbg_put(db, g + 8 * (e >> 1), 2 * t + (e & 1), 0, acc[e], 0);
+    }
+    store_terms4<MT>(terms, lane, tm);
+}
+
+// Q8_0 with m16n8k32 per 32-block (s8 x s8).
+template <int MT>
+__device__ __forceinline__ void tile_q80_mma(const uint8_t *tile, const int8_t *xu, int XS, const float *dxu,
+                                             int lane, float *terms, int exact, const DbgOut &db) {
+    constexpr int XP = xpitch<MT>();
+    const int g = lane >> 2, t = lane & 3, tp = tok_pair<MT>(t);
+    const uint4 dA = lds128(tile + 272 * g), dB = lds128(tile + 272 * (g + 8));
+    const uint32_t da[4] = {dA.x, dA.y, dA.z, dA.w}, dbv[4] = {dB.x, dB.y, dB.z, dB.w};
+    const uint32_t wrow = smem_u32(tile + 272 * (lane & 15) + 16 + 16 * (lane >> 4));
+    const uint32_t xrow = smem_u32(xu + (lane & 7 & (MT - 1)) * XS + 16 * (lane >> 3));
+    float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int jp = 0; jp < 4; ++jp) {
+        const uint4 xb = ldsm_x4(xrow + 64 * jp);  // block 2jp (b0, b1), block 2jp+1 (b0, b1)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int jj = 2 * jp + hh;
+            const uint4 a = ldsm_x4(wrow + 32 * jj);
+            int D[4];
+            mma_k32_s8s8(D, a.x, a.y, a.z, a.w, hh ? xb.z : xb.x, hh ? xb.w : xb.y);
+            const float wa = half_bits_to_float(da[jj >> 1] >> (16 * (jj & 1)));
+            const float wb = half_bits_to_float(dbv[jj >> 1] >> (16 * (jj & 1)));
+            const float2 dxv = *reinterpret_cast<const float2 *>(dxu + jj * XP + tp);
+            float tm[4];
+            tm[0] = __fmul_rn(__fmul_rn(wa, dxv.x), __int2float_rn(D[0]));
+            tm[1] = __fmul_rn(__fmul_rn(wa, dxv.y), __int2float_rn(D[1]));
+            tm[2] = __fmul_rn(__fmul_rn(wb, dxv.x), __int2float_rn(D[2]));
+            tm[3] = __fmul_rn(__fmul_rn(wb, dxv.y), __int2float_rn(D[3]));
+            if (exact) {
+                store_terms4<MT>(terms + jj * 16 * MT, lane, tm);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) part[e] = __fadd_rn(part[e], tm[e]);
+            }
+            if (db.si) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dbg_put(db, g + 8 * (e >> 1), 2 * t + (e & 1), jj, D[e], 0);
+            }
+        }
+    }
+    if (!exact) store_terms4<MT>(terms, lane, part);
+}
+
+// ------------------------------------------------------------------ row group -> task
+
+__device__ __forceinline__ int task_of_rg(const GemvParams &p, int rg) {
     int t = 0;
 #pragma unroll
-    for (int i = 1; i < 4; ++i) t += (i < p.n_tasks && g >= p.task[i].row_start) ? 1 : 0;
+    for (int i = 1; i < 4; ++i) t += (i < p.n_tasks && rg >= p.task[i].rg_start) ? 1 : 0;
     return t;
+}
+
+// Write the finished result of one (row, token).
+__device__ __forceinline__ void epilogue(const GemvParams &p, const GemvTaskDev &tk, int r, int tok, float acc,
+                                         unsigned long long *s_best) {
+    const size_t col = tk.out_ids ? (size_t)tk.out_ids[r] : (size_t)r;
+    if (tk.dst_f32) tk.dst_f32[(size_t)tok * tk.f32_stride + col] = acc;
+    if (tk.dst) {
+        float v = acc;
+        if (tk.res) v = __fadd_rn(v, __half2float(tk.res[(size_t)tok * tk.res_stride + col]));
+        tk.dst[(size_t)tok * tk.dst_stride + col] = __float2half_rn(v);
+    }
+    if (p.argmax) {
+        const float cmp = p.argmax_f16 ? __half2float(__float2half_rn(acc)) : acc;
+        atomicMax(&s_best[tok], argmax_key(cmp, (uint32_t)(tk.index_base + r)));
+    }
+}
+
+// One tile, terms into `tdst` (the unit's term row).
+template <int TYPE, int MT>
+__device__ __forceinline__ void compute_item(const GemvParams &p, const uint8_t *tile, int u,
+                                             const uint8_t *smem, int lane, float *tdst, const DbgOut &db) {
+    constexpr int XP = xpitch<MT>();
+    const uint8_t *xq = smem + p.off_x;
+    const float *dxt = reinterpret_cast<const float *>(smem + p.off_dx);
+    const int *aux = reinterpret_cast<const int *>(smem + p.off_xs);
+    const int nbu = p.nbu;
+    if (use_dp<MT>()) {
+        const int XSD = 320 * nbu;
+        const uint8_t *xu = xq + 320 * u;
+        if (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K)
+            tile_q45k_dp<TYPE, MT>(tile, xu, XSD, dxt + u * XP, aux + u * 8, nbu * 8, lane, tdst, db);
+        else if (TYPE == TYPE_Q6_K)
+            tile_q6k_dp<MT>(tile, xu, XSD, dxt + u * XP, aux + u * 16 * MT, lane, tdst, db);
+        else
+            tile_q80_dp<MT>(tile, xu, XSD, dxt + u * 8 * XP, lane, tdst, p.q80_exact, db);
+    } else {
+        const int XS = p.K + 16;
+        const int8_t *xu = reinterpret_cast<const int8_t *>(xq) + 256 * u;
+        if (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K)
+            tile_q45k_mma<TYPE, MT>(tile, xu, XS, dxt + u * XP, lane, tdst, db);
+        else if (TYPE == TYPE_Q6_K)
+            tile_q6k_mma<MT>(tile, xu, XS, dxt + u * XP, aux + u * 16 * XP, lane, tdst, db);
+        else
+            tile_q80_mma<MT>(tile, xu, XS, dxt + u * 8 * XP, lane, tdst, p.q80_exact, db);
+    }
+}
+
+__device__ __forceinline__ DbgOut make_dbg(const GemvParams &p, const GemvTaskDev &tk, int rg, int u, int is_q80) {
+    DbgOut db;
+    db.si = tk.dbg_sumi;
+    db.sm = tk.dbg_summ;
+    db.r0 = (tk.rg_first + rg - tk.rg_start) * 16 - tk.row_begin;
+    db.rows = tk.rows;
+    db.bpr = is_q80 ? p.nbu * 8 : p.nbu;
+    db.blk0 = is_q80 ? u * 8 : u;
+    db.M = p.M;
+    return db;
+}
+
+// Sum the block terms of one (row, token) of local row group lr in order and write it.
+template <int MT>
+__device__ __forceinline__ void fold_one(const GemvParams &p, const float *tb, int J, int e, int rg,
+                                         unsigned long long *s_best) {
+    const int rr = e / MT, tok = e - rr * MT;
+    const GemvTaskDev &tk = p.task[task_of_rg(p, rg)];
+    const int r = (tk.rg_first + rg - tk.rg_start) * 16 + rr - tk.row_begin;
+    if (tok >= p.M || r < 0 || r >= tk.rows) return;
+    constexpr int ST = 16 * MT;
+    float acc = 0.0f;
+    int j = 0;
+    for (; j + 4 <= J; j += 4) {
+        const float a0 = tb[(j + 0) * ST + e], a1 = tb[(j + 1) * ST + e];
+        const float a2 = tb[(j + 2) * ST + e], a3 = tb[(j + 3) * ST + e];
+        acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, a0), a1), a2), a3);
+    }
+    for (; j < J; ++j) acc = __fadd_rn(acc, tb[j * ST + e]);
+    epilogue(p, tk, r, tok, acc, s_best);
 }
 
 // ------------------------------------------------------------------ the kernel
 //
-// Each CTA owns a contiguous range [g_begin, g_end) of the dispatch's concatenated output rows
-// and walks it in stages of rows_per_stage rows; stage s starts at g_begin + s * rows_per_stage.
-// The producer warp (index W) streams stages into an S-slot ring: one cp.async.bulk per task
-// segment of the stage (>= 16 KB per stage in total; one copy per row for gathered rows).  A
-// stage holds P sub-stages of rows_per_sub rows (rows_per_sub * units-per-row <= 32, or one
-// row) and sub-stage q = s * P + part belongs to consumer warp q % W.  The warp waits on the
-// stage's full barrier, computes one unit per lane (a row longer than 32 units in passes), adds
-// each row's unit terms in unit order through shuffles into the row's leader lane (the
-// reference's `acc += term` sequence), arrives on the stage's empty barrier (P arrivals free the
-// slot) and writes the epilogue.  There is no CTA-wide barrier in the main loop.
-// (P * S) % W == 0: the previous use of the slot of a warp's next sub-stage was one of the
-// warp's own sub-stages, which it already waited for, so a waiter never runs two phases ahead
-// of a full barrier (where the parity test of mbarrier.try_wait.parity would pass on the wrong
-// phase).
+// CTA c owns row groups [rg_lo, rg_hi) = tiles [t0, t1) of the launch's tile sequence
+// (tile = rg * nbu + u).  Stage s holds local tiles [s*T, s*T + T) in ring slot s % S;
+// consumers wait for a stage to be issued before testing its full barrier (so the barrier's
+// phase parity refers to that stage) and arrive on its empty barrier when done with an item.
+// Warp w takes tiles w, w + W, ...
+//  SMALL: the terms of the whole share stay in shared memory (local row group lr at
+//         terms[lr * J ...]); all row groups are folded after a consumer barrier.
+//  !SMALL: terms of row group lr go to term slot lr % TS, use lr / TS; a writer waits until the
+//         slot's previous use is folded and the warp completing the row group folds it
+//         (monotonic shared-memory counters).
 
-template <int TYPE, int MT>
-__global__ void __launch_bounds__(kMaxThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
+template <int TYPE, int MT, bool SMALL>
+__global__ void __launch_bounds__(threads_of<MT>(), 2) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ unsigned long long s_best[8];
     __shared__ int s_abort, s_issued;
+    __shared__ int s_done[kMaxTermSlots], s_folded[kMaxTermSlots];
 
-    ActUnit *act = reinterpret_cast<ActUnit *>(smem + p.off_act);
     uint8_t *ring = smem + p.off_stages;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.off_bars);  // full[S], empty[S], dead
-    const int S = p.n_stages, W = p.n_warps, P = p.subs_per_stage, RS = p.rows_per_sub;
-    const int RPS = p.rows_per_stage;
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31;
+    float *terms = reinterpret_cast<float *>(smem + p.off_terms);
+    constexpr int IPT = 1;  // items per tile
+    const int S = p.n_stages, T = p.tiles_per_stage, TS = p.term_slots, J = p.terms_per_rg;
+    constexpr int W = warps_of<MT>();
+    const int nbu = p.nbu;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tstride = 16 * MT;  // floats per term row
 
-    const long long tot = p.total_rows;
-    const int g_begin = (int)(tot * blockIdx.x / gridDim.x);
-    const int g_end = (int)(tot * (blockIdx.x + 1) / gridDim.x);
-    const int n_stages_cta = (g_end - g_begin + RPS - 1) / RPS;
+    const int rg_lo = (int)((long long)p.total_rg * blockIdx.x / gridDim.x);
+    const int rg_hi = (int)((long long)p.total_rg * (blockIdx.x + 1) / gridDim.x);
+    const int t0 = rg_lo * nbu;
+    const int n_tiles = (rg_hi - rg_lo) * nbu;
+    const int n_stages_cta = (n_tiles + T - 1) / T;
 
     if (tid < 8) s_best[tid] = 0ull;
+    if (tid < kMaxTermSlots) {
+        s_done[tid] = 0;
+        s_folded[tid] = 0;
+    }
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&bars[s]), 1);
-            mbar_init(smem_u32(&bars[S + s]), P);
+            mbar_init(smem_u32(&bars[S + s]), T);
         }
         mbar_init(smem_u32(&bars[2 * S]), 1);  // never arrived at (failure-path test)
         s_abort = 0;
@@ -462,163 +770,159 @@ __global__ void __launch_bounds__(kMaxThreads, 2) gemv_kernel(const __grid_const
         mbar_init_fence();
     }
     __syncthreads();
-    pdl_launch_dependents();
 
+    // The next kernel in the stream may launch (programmatic dependent launch) once this CTA
+    // has staged its activation: its weight prefetch then overlaps this kernel's arithmetic
+    // instead of competing with this kernel's activation loads.
     if (warp == W) {
         // ---------------- producer: the weight stream does not depend on earlier kernels
+        const uint64_t policy = l2_evict_first_policy();
+        auto issue = [&](int s) {
+            const int slot = s % S;
+            const int a = s * T, b = min(n_tiles, a + T);
+            const uint32_t full = smem_u32(&bars[slot]);
+            const uint32_t sdst = smem_u32(ring + (size_t)slot * p.stage_bytes);
+            mbar_arrive_expect_tx(full, (uint32_t)(b - a) * p.tile_bytes);
+            int i = a;
+            while (i < b) {
+                const int tau = t0 + i, rg = tau / nbu;
+                const GemvTaskDev &tk = p.task[task_of_rg(p, rg)];
+                const int iend = min(b, (tk.rg_start + tk.n_rg) * nbu - t0);
+                const size_t src_tile = (size_t)(tk.rg_first - tk.rg_start) * nbu + tau;
+                bulk_g2s(sdst + (uint32_t)(i - a) * p.tile_bytes, tk.w + src_tile * p.tile_bytes,
+                         (uint32_t)(iend - i) * p.tile_bytes, full, policy);
+                i = iend;
+            }
+            *reinterpret_cast<volatile int *>(&s_issued) = s + 1;
+        };
+        const int first = min(S, n_stages_cta);  // stages that need no free slot
+        if (lane == 0)
+            for (int s = 0; s < first; ++s) issue(s);
+        __syncwarp();
+        __syncthreads();  // activation staged
+        pdl_launch_dependents();
         if (lane == 0) {
-            const uint64_t policy = l2_evict_first_policy();
-            int s = 0;
-            for (; s < n_stages_cta; ++s) {
-                const int slot = s % S;
-                if (s >= S) {
-                    if (!mbar_wait_bounded(smem_u32(&bars[S + slot]), ((s / S) - 1) & 1, p.timeout_ns, p.status)) {
-                        s_abort = 1;
-                        break;
-                    }
+            for (int s = first; s < n_stages_cta; ++s) {
+                if (!mbar_wait_bounded(smem_u32(&bars[S + s % S]), ((s / S) - 1) & 1, p.timeout_ns, p.status)) {
+                    s_abort = 1;
+                    break;
                 }
-                const int a = g_begin + s * RPS, b = min(g_end, a + RPS);
-                const uint32_t full = smem_u32(&bars[slot]);
-                const uint32_t sdst = smem_u32(ring + (size_t)slot * p.stage_bytes);
-                mbar_arrive_expect_tx(full, (uint32_t)(b - a) * p.row_bytes);
-                int g = a;
-                while (g < b) {
-                    const int t = task_of(p, g);
-                    const int tend = min(b, p.task[t].row_start + p.task[t].rows);
-                    const int r0 = g - p.task[t].row_start;
-                    const uint32_t off = (uint32_t)(g - a) * p.row_bytes;
-                    if (p.task[t].row_ids) {
-                        for (int i = 0; i < tend - g; ++i)
-                            bulk_g2s(sdst + off + i * p.row_bytes,
-                                     p.task[t].w + (size_t)p.task[t].row_ids[r0 + i] * p.row_bytes, p.row_bytes, full,
-                                     policy);
-                    } else {
-                        bulk_g2s(sdst + off, p.task[t].w + (size_t)r0 * p.row_bytes, (uint32_t)(tend - g) * p.row_bytes,
-                                 full, policy);
-                    }
-                    g = tend;
-                }
-                s_issued = s + 1;
+                issue(s);
             }
         }
     } else {
         // ---------------- consumers
         pdl_wait();  // activations / residuals may come from the previous kernel
-        const int nbu = p.nbu;
-        const int n_units = p.M * nbu;
-        for (int u = warp; u < n_units; u += W) {
-            const int m = u / nbu, b = u % nbu;
-            ActUnit *a = act + u;
-            if (p.x) {
-                const __half *xu = p.x + (size_t)m * p.x_stride + (size_t)b * 256;
-                stage_act_from_fp16<TYPE>(xu, (reinterpret_cast<uintptr_t>(xu) & 15) == 0, a, lane);
-            } else if (TYPE == TYPE_Q8_0) {
-                stage_act_from_q80(reinterpret_cast<const BlockQ80 *>(p.act) + (size_t)m * (p.K / 32) + 8 * b, a, lane);
-            } else {
-                stage_act_from_q8k(reinterpret_cast<const BlockQ8K *>(p.act) + (size_t)m * nbu + b, a, lane);
-            }
-        }
+        stage_activation<TYPE, MT>(p, smem, warp, lane, W);
         if (p.inject_wait && tid == 0) {
             // failure-path test: a wait whose barrier nothing completes must end by its time limit
             if (!mbar_wait_bounded(smem_u32(&bars[2 * S]), 0, p.timeout_ns, p.status)) s_abort = 1;
         }
-        named_bar_sync(1, W * 32);
+        __syncthreads();  // activation staged
+        pdl_launch_dependents();
 
-        const int upr = p.units_per_row;  // 256-value units (32-value blocks for Q8_0)
-        const int multi = (RS > 1);       // several whole rows per sub-stage
-        const int npass = multi ? 1 : (upr + 31) / 32;
-        const int lrow = multi ? lane / upr : 0;
-        const int lead = multi ? lrow * upr : 0;  // leader lane of this lane's row
-        const int n_sub = n_stages_cta * P;
-        // sub-stage q = sidx * P + part lives in ring slot sidx % S, phase (sidx / S) & 1; the
-        // counters advance by W sub-stages per iteration without integer division
-        int sidx = warp / P, part = warp - (warp / P) * P;
-        int slot = sidx % S, phase = (sidx / S) & 1;
-        int a = g_begin + sidx * RPS;  // first row of the stage
-        for (int q = warp; q < n_sub; q += W) {
-            if (*reinterpret_cast<volatile int *>(&s_abort)) break;
+        // tile walk: tile i advances by W; stage/slot/phase, unit and row group incremental.  In a
+        // SMALL launch whose ring holds the whole share every stage was issued before the
+        // barrier above: wait for all of them once instead of per tile.
+        constexpr int TSTEP = W;
+        const bool all_in = SMALL && n_stages_cta <= S;
+        if (all_in) {
             int ok = 1;
-            if (lane == 0) ok = mbar_wait_bounded(smem_u32(&bars[slot]), phase, p.timeout_ns, p.status) ? 1 : 0;
+            if (lane == 0)
+                for (int s2 = 0; s2 < n_stages_cta && ok; ++s2)
+                    ok = mbar_wait_bounded(smem_u32(&bars[s2]), 0, p.timeout_ns, p.status);
             ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) {
-                if (lane == 0) s_abort = 1;
-                break;
+            if (!ok && lane == 0) s_abort = 1;
+        }
+        int i = warp;
+        int tt = i, sg = 0, slot = 0, ph = 0;
+        while (tt >= T) {
+            tt -= T;
+            ++sg;
+            if (++slot == S) {
+                slot = 0;
+                ph ^= 1;
             }
-            const int sR = max(0, min(RS, min(g_end, a + RPS) - (a + part * RS)));  // rows of this sub-stage
-            const int g = a + part * RS + min(lrow, max(sR - 1, 0));  // this lane's row (concatenated)
-            const int t = task_of(p, g);
-            const GemvTaskDev &tk = p.task[t];
-            const int r = g - tk.row_start;                      // row within the task
-            const uint8_t *wrow = ring + (size_t)slot * p.stage_bytes + (size_t)(g - a) * p.row_bytes;
-            const int units = sR * upr;
-            const bool is_lead = multi ? (lane == lead && lane < units) : (lane == 0 && sR > 0);
-            float acc[MT];
-#pragma unroll
-            for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
-            for (int pass = 0; pass < npass; ++pass) {
-                const int b = multi ? lane - lead : 32 * pass + lane;
-                const bool valid = multi ? (lane < units) : (sR > 0 && b < upr);
-                const int cnt = multi ? upr : min(32, upr - 32 * pass);  // the row's units in this pass
-                float term[MT];
-#pragma unroll
-                for (int m = 0; m < MT; ++m) term[m] = 0.0f;
-                if (valid) {
-                    int *dsi = nullptr, *dsm = nullptr;
-                    long long dstride = 0;
-                    if (tk.dbg_sumi) {
-                        dstride = (long long)tk.rows * upr;
-                        const long long off = (long long)r * upr + b;
-                        dsi = tk.dbg_sumi + off;
-                        dsm = tk.dbg_summ + off;
-                    }
-                    if (TYPE == TYPE_Q4_K) {
-                        unit_q4k<MT>(wrow + 144 * b, act + b, nbu, p.M, term, dsi, dsm, dstride);
-                    } else if (TYPE == TYPE_Q5_K) {
-                        unit_q5k<MT>(wrow + 176 * b, act + b, nbu, p.M, term, dsi, dsm, dstride);
-                    } else if (TYPE == TYPE_Q6_K) {
-                        const float dq = half_bits_to_float(*reinterpret_cast<const uint16_t *>(wrow + 208 * nbu + 2 * b));
-                        unit_q6k<MT>(wrow + 208 * b, dq, act + b, nbu, p.M, term, dsi, dsm, dstride);
-                    } else {
-                        unit_q80<MT>(wrow + 32 * b, wrow + p.K + 2 * b, b, act, nbu, p.M, term, dsi, dsm, dstride);
-                    }
+        }
+        int u = i, lr = 0;
+        while (u >= nbu) {
+            u -= nbu;
+            ++lr;
+        }
+        int ts = lr % TS, use = lr / TS;
+        const int JU = (TYPE == TYPE_Q8_0 && p.q80_exact) ? 8 : 1;  // terms per unit
+        for (; i < n_tiles; i += TSTEP) {
+            if (*reinterpret_cast<volatile int *>(&s_abort)) break;
+            if (!all_in) {
+                int ok = 1;
+                if (lane == 0) {
+                    ok = wait_ge_bounded(&s_issued, sg + 1, p.timeout_ns, p.status) &&
+                         mbar_wait_bounded(smem_u32(&bars[slot]), ph, p.timeout_ns, p.status) &&
+                         (SMALL || wait_ge_bounded(&s_folded[ts], use, p.timeout_ns, p.status));
                 }
-                // in-order sum of the row's unit terms into the leader (the reference's `acc += term`)
-#pragma unroll 4
-                for (int i = 0; i < cnt; ++i) {
-                    const int src = min(lead + i, 31);
-#pragma unroll
-                    for (int m = 0; m < MT; ++m) acc[m] = __fadd_rn(acc[m], __shfl_sync(0xffffffffu, term[m], src));
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) {
+                    if (lane == 0) s_abort = 1;
+                    break;
                 }
             }
+            const uint8_t *tile = ring + slot * p.stage_bytes + tt * p.tile_bytes;
+            const int rg = rg_lo + lr;
+            const GemvTaskDev &tk = p.task[task_of_rg(p, rg)];
+            DbgOut db;
+            db.si = nullptr;
+            if (tk.dbg_sumi) db = make_dbg(p, tk, rg, u, TYPE == TYPE_Q8_0);
+            float *tdst = terms + ((SMALL ? lr : ts) * J + u * JU) * tstride;
+            compute_item<TYPE, MT>(p, tile, u, smem, lane, tdst, db);
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&bars[S + slot]));  // P arrivals free the slot
-            if (is_lead) {
-                const size_t col = tk.scatter ? (size_t)tk.row_ids[r] : (size_t)r;
-#pragma unroll
-                for (int m = 0; m < MT; ++m) {
-                    if (m < p.M) {
-                        if (tk.dst_f32) tk.dst_f32[(size_t)m * tk.f32_stride + col] = acc[m];
-                        if (tk.dst) {
-                            float v = acc[m];
-                            if (tk.res) v = __fadd_rn(v, __half2float(tk.res[(size_t)m * tk.res_stride + col]));
-                            tk.dst[(size_t)m * tk.dst_stride + col] = __float2half_rn(v);
-                        }
-                        if (p.argmax) {
-                            const float cmp = p.argmax_f16 ? __half2float(__float2half_rn(acc[m])) : acc[m];
-                            atomicMax(&s_best[m], argmax_key(cmp, (uint32_t)(tk.index_base + r)));
-                        }
+            if (SMALL) {
+                if (!all_in && lane == 0) mbar_arrive(smem_u32(&bars[S + slot]));  // T arrivals free the slot
+            } else {
+                int last = 0;
+                if (lane == 0) {
+                    mbar_arrive(smem_u32(&bars[S + slot]));
+                    __threadfence_block();
+                    last = (atomicAdd(&s_done[ts], 1) == (use + 1) * nbu - 1);
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    // fold the row group: block terms in order, then the epilogue
+                    __threadfence_block();
+                    const float *tb = terms + ts * J * tstride;
+                    for (int e = lane; e < 16 * MT; e += 32) fold_one<MT>(p, tb, J, e, rg, s_best);
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence_block();
+                        *reinterpret_cast<volatile int *>(&s_folded[ts]) = use + 1;
                     }
                 }
             }
-            part += W;
-            while (part >= P) {
-                part -= P;
-                ++sidx;
-                a += RPS;
+            tt += TSTEP;
+            while (tt >= T) {
+                tt -= T;
+                ++sg;
                 if (++slot == S) {
                     slot = 0;
-                    phase ^= 1;
+                    ph ^= 1;
                 }
+            }
+            u += TSTEP;
+            while (u >= nbu) {
+                u -= nbu;
+                ++lr;
+                if (++ts == TS) {
+                    ts = 0;
+                    ++use;
+                }
+            }
+        }
+        if (SMALL) {
+            // ---------------- fold all row groups of the share
+            named_bar_sync(1, W * 32);
+            const int n_lr = rg_hi - rg_lo, E = 16 * MT;
+            for (int idx = tid; idx < n_lr * E; idx += W * 32) {
+                const int l = idx / E, e = idx - l * E;
+                fold_one<MT>(p, terms + (size_t)l * J * tstride, J, e, rg_lo + l, s_best);
             }
         }
     }
@@ -639,104 +943,108 @@ __global__ void __launch_bounds__(kMaxThreads, 2) gemv_kernel(const __grid_const
 namespace {
 
 struct Plan {
-    int rows_per_sub, subs, n_stages, n_warps, grid;
-    unsigned stage_bytes, off_act, off_stages, off_bars, smem;
+    int small, T, S, TS, J, q80_exact, grid;
+    unsigned stage_bytes, off_x, off_dx, off_xs, off_terms, off_stages, off_bars, smem;
 };
 
 unsigned align_up(unsigned v, unsigned a) { return (v + a - 1) / a * a; }
 
-// Geometry of one launch.
-//  * Sub-stage = the rows one consumer warp handles at once: floor(32 / units-per-row) whole
-//    rows (one unit per lane), or one row.  Stage = P sub-stages, P * sub_bytes >= 16 KB
-//    (smaller bulk copies do not reach full HBM bandwidth).
-//  * Prefetch mode: when a CTA's whole share of rows fits in ~110 KB, one CTA per SM with a
-//    ring that holds all of it.  Its smem, registers and threads stay under half an SM, so the
-//    next kernel's CTA (programmatic dependent launch) is resident meanwhile and streams its
-//    own weights while this one computes; back-to-back small GEMVs then overlap their HBM
-//    traffic.
-//  * Throughput mode (larger matrices): two CTAs per SM, ring within ~100 KB each.
-//  * W consumer warps with (P * S) % W == 0, which keeps every full-barrier wait within one
-//    phase (see the kernel).
-Plan make_plan(int type, int K, int M, size_t row_bytes, int total_rows, int num_sms) {
+// Geometry of one launch (MT token slots).
+//  * Stage = T tiles, >= 16 KB (smaller bulk copies do not reach full HBM bandwidth).
+//  * Whole row groups per CTA.  One CTA per SM (two when each has plenty of work) within
+//    ~110 KB of shared memory, so a second CTA -- this kernel's or the next one's -- fits beside
+//    it, else one with up to 220 KB.  The ring takes what is left after the activation and the
+//    term buffers, up to the CTA's whole share.
+//  * SMALL (dp4a only) when the terms of the whole share fit: fold after one barrier.  Else term
+//    slots cover the row groups that can be in flight (ring tiles / nbu + 2).
+//  * Q8_0 keeps one term per 32-block (the reference's exact order) when that fits, else one
+//    per tile.
+Plan make_plan(int type, int K, int MT, int total_rg, int num_sms, int n_warps) {
     Plan pl{};
     const int nbu = K / 256;
-    const int upr = (type == TYPE_Q8_0) ? K / 32 : nbu;
-    const int rsub = upr <= 16 ? 32 / upr : 1;
-    const size_t sub_bytes = (size_t)rsub * row_bytes;
-    const unsigned act = align_up((unsigned)(M * nbu * (int)sizeof(ActUnit)), 128);
-    int pmin = 1;
-    while ((size_t)pmin * sub_bytes < 16 * 1024 && pmin < 16) ++pmin;
-    auto smem_of = [&](int P, int S) {
-        return act + S * align_up((unsigned)(P * sub_bytes), 128) + (2 * S + 1) * 8 + 256;
-    };
-    auto fill = [&](int P, int S, int W, int ctas_per_sm) {
-        const unsigned stage = align_up((unsigned)(P * sub_bytes), 128);
-        const int rps = P * rsub;
-        pl.rows_per_sub = rsub;
-        pl.subs = P;
-        pl.n_stages = S;
-        pl.n_warps = W;
-        pl.stage_bytes = stage;
-        pl.off_act = 0;
-        pl.off_stages = act;
-        pl.off_bars = act + S * stage;
-        pl.smem = pl.off_bars + (2 * S + 1) * 8;
-        pl.grid = std::max(1, std::min(ctas_per_sm * num_sms, (total_rows + rps - 1) / rps));
-    };
-    // candidates: P in [pmin, pmin + 4], W in [6, 12]; prefer more warps, then more bytes in flight
-    int bP = 0, bS = 0, bW = 0, bctas = 0;
-    size_t bflight = 0;
-    auto consider = [&](int P, int S, int W, int ctas) {
-        const size_t flight = (size_t)S * align_up((unsigned)(P * sub_bytes), 128);
-        if (W > bW || (W == bW && flight > bflight)) {
-            bP = P, bS = S, bW = W, bctas = ctas, bflight = flight;
-        }
-    };
-    // prefetch mode: the ring holds the CTA's whole share
-    for (int P = pmin; P <= pmin + 4; ++P) {
-        const int rps = P * rsub;
-        const int share_stages = ((total_rows + num_sms - 1) / num_sms + rps - 1) / rps;
-        for (int W = 12; W >= 6; --W)
-            for (int S = std::max(2, share_stages); S <= share_stages + W; ++S) {
-                if ((P * S) % W) continue;
-                if (smem_of(P, S) <= 110 * 1024) consider(P, S, W, 1);
-                break;
-            }
-    }
-    if (bW) {
-        fill(bP, bS, bW, bctas);
-        return pl;
-    }
-    // throughput mode: two CTAs per SM within ~100 KB each, else one CTA with up to 220 KB
-    for (unsigned budget : {100u * 1024u, 220u * 1024u}) {
-        for (int P = pmin; P <= pmin + 4; ++P)
-            for (int W = 12; W >= 6; --W) {
-                int best = 0;
-                for (int S = 2; S <= 32; ++S) {
-                    if ((P * S) % W) continue;
-                    if (smem_of(P, S) > budget) break;
-                    best = S;
+    const unsigned TB = (unsigned)tile_bytes(type);
+    const int XP = MT < 2 ? 2 : MT;
+    const bool dp = MT <= 2;
+    const unsigned x_bytes = align_up((unsigned)(dp ? MT * 320 * nbu : MT * (K + 16)), 128);
+    const unsigned dx_bytes = align_up((unsigned)(nbu * (type == TYPE_Q8_0 ? 8 : 1) * XP * 4), 128);
+    const unsigned xs_bytes = (type == TYPE_Q6_K)   ? align_up((unsigned)(nbu * 16 * (dp ? MT : XP) * 4), 128)
+                              : (type == TYPE_Q8_0) ? 0
+                                                    : align_up((unsigned)(MT * nbu * 8 * 4), 128);
+    const unsigned fixed = x_bytes + dx_bytes + xs_bytes;
+    const int T = std::max(1, (int)((16384 + TB - 1) / TB));
+    const unsigned stage = align_up(T * TB, 128);
+    for (unsigned budget : {110u * 1024u, 220u * 1024u}) {
+        for (int ctas : {2, 1}) {
+            if (ctas == 2 && budget > 110u * 1024u) continue;
+            const int grid = std::max(1, std::min(total_rg, ctas * num_sms));
+            const int rg_cta = (total_rg + grid - 1) / grid;
+            if (ctas == 2 && rg_cta * nbu < 8 * n_warps) continue;  // small shares: one CTA, room for the next kernel's
+            const int stages_cta = (rg_cta * nbu + T - 1) / T;
+            for (int small = dp ? 1 : 0; small >= 0; --small) {
+                for (int exact = (type == TYPE_Q8_0) ? 1 : 0; exact >= 0; --exact) {
+                    const int J = (type == TYPE_Q8_0 && exact) ? 8 * nbu : nbu;
+                    for (int S = std::min(stages_cta, 32); S >= 1; --S) {
+                        const int TS = small ? rg_cta
+                                             : std::min(std::min(rg_cta, kMaxTermSlots), (S * T + nbu - 1) / nbu + 2);
+                        const unsigned term_bytes = align_up((unsigned)(TS * J * 16 * MT * 4), 128);
+                        const unsigned total = fixed + term_bytes + S * stage + (2 * S + 1) * 8;
+                        if (total > budget) continue;
+                        if (S < std::min(stages_cta, 2)) break;  // a ring needs two slots unless one stage is all
+                        pl.small = small;
+                        pl.T = T;
+                        pl.S = S;
+                        pl.TS = small ? 1 : TS;
+                        pl.J = J;
+                        pl.q80_exact = (type == TYPE_Q8_0) ? exact : 0;
+                        pl.grid = grid;
+                        pl.stage_bytes = stage;
+                        pl.off_x = 0;
+                        pl.off_dx = x_bytes;
+                        pl.off_xs = x_bytes + dx_bytes;
+                        pl.off_terms = fixed;
+                        pl.off_stages = fixed + term_bytes;
+                        pl.off_bars = pl.off_stages + S * stage;
+                        pl.smem = pl.off_bars + (2 * S + 1) * 8;
+                        return pl;
+                    }
                 }
-                if (best) consider(P, best, W, budget <= 100 * 1024 ? 2 : 1);
             }
-        if (bW) {
-            fill(bP, bS, bW, bctas);
-            return pl;
         }
     }
     return pl;  // smem 0: does not fit
 }
 
+template <typename Kern>
+cudaError_t configure_smem(Kern kern) {
+    static std::mutex mu;
+    static std::unordered_map<int, std::unordered_map<const void *, bool>> configured;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    bool &done = configured[dev][reinterpret_cast<const void *>(kern)];
+    if (!done) {
+        // plans stay below 221 KB of dynamic shared memory; 225 KB leaves room for the kernel's
+        // static shared words within the 227 KB per-block limit
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024);
+        if (e != cudaSuccess) return e;
+        done = true;
+    }
+    return cudaSuccess;
+}
+
 template <int TYPE, int MT>
 cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
     GemvParams p{};
-    int total = 0;
+    int total_rg = 0;
     for (int i = 0; i < L.n_tasks; ++i) {
         const GemvTaskHost &h = L.tasks[i];
         GemvTaskDev &d = p.task[i];
         d.w = h.w;
+        d.row_begin = h.row_begin;
         d.rows = h.rows;
-        d.row_start = total;
+        d.rg_first = h.row_begin / 16;
+        d.n_rg = h.rows > 0 ? (h.row_begin + h.rows - 1) / 16 - d.rg_first + 1 : 0;
+        d.rg_start = total_rg;
         d.dst = reinterpret_cast<__half *>(h.dst);
         d.dst_stride = h.dst_stride;
         d.res = reinterpret_cast<const __half *>(h.res);
@@ -745,26 +1053,24 @@ cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
         d.f32_stride = h.f32_stride;
         d.dbg_sumi = h.dbg_sumi;
         d.dbg_summ = h.dbg_summ;
-        d.row_ids = h.row_ids;
-        d.scatter = h.scatter;
+        d.out_ids = h.out_ids;
         d.index_base = h.index_base;
-        total += h.rows;
+        total_rg += d.n_rg;
     }
-    if (total == 0) return cudaSuccess;
-    const Plan pl = make_plan(TYPE, L.K, L.M, L.row_bytes, total, L.num_sms);
+    if (total_rg == 0) return cudaSuccess;
+    const Plan pl = make_plan(TYPE, L.K, MT, total_rg, L.num_sms, warps_of<MT>());
     if (pl.smem == 0) return cudaErrorInvalidConfiguration;
     p.n_tasks = L.n_tasks;
-    p.total_rows = total;
+    p.total_rg = total_rg;
     p.K = L.K;
     p.nbu = L.K / 256;
     p.M = L.M;
-    p.row_bytes = (unsigned)L.row_bytes;
-    p.rows_per_stage = pl.subs * pl.rows_per_sub;
-    p.rows_per_sub = pl.rows_per_sub;
-    p.subs_per_stage = pl.subs;
-    p.units_per_row = (TYPE == TYPE_Q8_0) ? L.K / 32 : L.K / 256;
-    p.n_warps = pl.n_warps;
-    p.n_stages = pl.n_stages;
+    p.tile_bytes = (unsigned)tile_bytes(TYPE);
+    p.tiles_per_stage = pl.T;
+    p.n_stages = pl.S;
+    p.term_slots = pl.TS;
+    p.terms_per_rg = pl.J;
+    p.q80_exact = pl.q80_exact;
     p.stage_bytes = pl.stage_bytes;
     p.x = reinterpret_cast<const __half *>(L.x);
     p.x_stride = L.x_stride;
@@ -774,30 +1080,18 @@ cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
     p.argmax = L.argmax;
     p.argmax_f16 = L.argmax_f16;
     p.inject_wait = L.inject_wait;
-    p.off_act = pl.off_act;
+    p.off_x = pl.off_x;
+    p.off_dx = pl.off_dx;
+    p.off_xs = pl.off_xs;
+    p.off_terms = pl.off_terms;
     p.off_stages = pl.off_stages;
     p.off_bars = pl.off_bars;
 
-    auto kern = gemv_kernel<TYPE, MT>;
-    static std::mutex mu;
-    static std::unordered_map<int, unsigned> configured;  // device -> smem size set
-    int dev = 0;
-    cudaGetDevice(&dev);
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        unsigned &have = configured[dev];
-        if (have < pl.smem) {
-            // plans stay below 221 KB of dynamic shared memory; 225 KB leaves room for the
-            // kernel's static shared words within the 227 KB per-block limit
-            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024);
-            if (e != cudaSuccess) return e;
-            have = 225 * 1024;
-        }
-    }
-    const int grid = pl.grid;
+    auto kern = pl.small ? gemv_kernel<TYPE, MT, true> : gemv_kernel<TYPE, MT, false>;
+    if (cudaError_t e = configure_smem(kern)) return e;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3((pl.n_warps + 1) * 32);
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(threads_of<MT>());
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -816,6 +1110,20 @@ cudaError_t launch_type(const GemvLaunch &L, cudaStream_t stream) {
     return launch_t<TYPE, 8>(L, stream);
 }
 
+// ------------------------------------------------------------------ gathered rows
+
+// Copy weight rows ids[0..n) into a fresh tiled tensor (row i of dst = row ids[i] of src), so a
+// row-id list runs through the same GEMV kernel.  One thread per GGUF byte of a row.
+__global__ void gather_rows_kernel(int type, int nbu, const uint8_t *src, const uint32_t *ids, int n, uint8_t *dst,
+                                   size_t gguf_row_bytes) {
+    const size_t total = (size_t)n * gguf_row_bytes;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / gguf_row_bytes);
+        const size_t ob = i - (size_t)r * gguf_row_bytes;
+        dst[tile_byte_offset(type, nbu, r, ob)] = src[tile_byte_offset(type, nbu, (int)ids[r], ob)];
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_gemv(const GemvLaunch &L, cudaStream_t stream) {
@@ -827,6 +1135,18 @@ cudaError_t launch_gemv(const GemvLaunch &L, cudaStream_t stream) {
         case TYPE_Q8_0: return launch_type<TYPE_Q8_0>(L, stream);
         default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_gather_rows(int type, int K, const uint8_t *src, const uint32_t *ids, int n, uint8_t *dst,
+                               cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    const size_t rb = (size_t)(K / 256) * unit_bytes(type);
+    cudaError_t e = cudaMemsetAsync(dst, 0, weight_bytes(type, n, K), stream);
+    if (e != cudaSuccess) return e;
+    const size_t total = (size_t)n * rb;
+    const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
+    gather_rows_kernel<<<blocks, 256, 0, stream>>>(type, K / 256, src, ids, n, dst, rb);
+    return cudaGetLastError();
 }
 
 }  // namespace kq

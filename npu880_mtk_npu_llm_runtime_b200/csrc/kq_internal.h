@@ -5,22 +5,24 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
-// A GGUF tensor resident in HBM in this library's device layout (opaque kq_weight of kq.h).
+// A GGUF tensor resident in HBM in this library's row-group tile layout (opaque kq_weight of
+// kq.h; layout in kq_common.cuh).
 struct kq_weight {
     uint32_t type;
     int rows, cols;
-    size_t row_bytes;  // device layout
-    uint8_t *d;
+    size_t row_bytes;  // GGUF bytes per row (compute_ggml_bytes)
+    uint8_t *d;        // tiled tensor, ceil(rows / 16) * 16 rows
     size_t bytes;
 };
 
 namespace kq {
 
-// One matrix of a dispatch, device pointers, already offset to the task's first weight row.
+// One matrix of a dispatch: weight rows [row_begin, row_begin + rows) of a tiled tensor.
 struct GemvTaskHost {
-    const uint8_t *w;
+    const uint8_t *w;      // tiled tensor (row group 0), device
+    int row_begin;
     int rows;
-    void *dst;             // __half*
+    void *dst;             // __half*, output column r = local row r (or out_ids[r])
     long long dst_stride;
     const void *res;       // const __half*
     long long res_stride;
@@ -28,16 +30,14 @@ struct GemvTaskHost {
     long long f32_stride;
     int *dbg_sumi;         // [M][rows][blocks per row] or nullptr
     int *dbg_summ;
-    const uint32_t *row_ids = nullptr;  // gather rows by id (device), or nullptr for contiguous rows
-    int scatter = 0;                    // outputs indexed by row id instead of local row
-    int index_base = 0;                 // argmax index of local row 0
+    const uint32_t *out_ids = nullptr;  // device; output column of local row r
+    int index_base = 0;                 // argmax index of local row r
 };
 
 struct GemvLaunch {
     int type;
     int K;
-    int M;
-    size_t row_bytes;          // device-layout row bytes
+    int M;                     // 1..8
     GemvTaskHost tasks[4];
     int n_tasks;
     // input: exactly one of x (fp16 [M][x_stride]), act (BlockQ8K[M][K/256] or BlockQ8_0_Fast[M][K/32])
@@ -55,6 +55,9 @@ struct GemvLaunch {
 
 // kq_gemv.cu
 cudaError_t launch_gemv(const GemvLaunch &L, cudaStream_t stream);
+// rows ids[0..n) of a tiled tensor -> a new tiled tensor of n rows (weight_bytes(type, n, K))
+cudaError_t launch_gather_rows(int type, int K, const uint8_t *src, const uint32_t *ids, int n, uint8_t *dst,
+                               cudaStream_t stream);
 
 // kq_act.cu
 cudaError_t launch_quantize(int target_type /*12 = Q8_K, 8 = Q8_0*/, const void *x, long long x_stride, int M, int K,
@@ -65,6 +68,6 @@ cudaError_t launch_rmsnorm_q8k(const void *x, const void *gamma, void *out, void
 cudaError_t launch_swiglu_q8k(void *gate, const void *up, void *q8k, int M, int N, cudaStream_t stream, bool pdl);
 cudaError_t launch_argmax_finalize(const unsigned long long *keys, int M, const uint32_t *ids, uint32_t *toks,
                                    float *vals, cudaStream_t stream);
-cudaError_t launch_dequant(int type, const uint8_t *dev, size_t row_bytes, int rows, int K, void *out, cudaStream_t stream);
+cudaError_t launch_dequant(int type, const uint8_t *tiled, int row_begin, int rows, int K, void *out, cudaStream_t stream);
 
 }  // namespace kq

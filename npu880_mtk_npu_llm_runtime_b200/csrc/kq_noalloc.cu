@@ -74,10 +74,10 @@ extern "C" int kq_lm_head_argmax_noalloc(const kq_weight *w, const uint16_t *x_d
         L.type = (int)w->type;
         L.K = K;
         L.M = mt;
-        L.row_bytes = w->row_bytes;
         L.n_tasks = 1;
         kq::GemvTaskHost &h = L.tasks[0];
         h.w = w->d;
+        h.row_begin = 0;
         h.rows = w->rows;
         h.dst = logits_dev ? (void *)(logits_dev + (size_t)m0 * w->rows) : nullptr;
         h.dst_stride = w->rows;
