@@ -36,7 +36,7 @@ struct kq_ctx {
     std::string err;
 
     // scratch (grown on demand, freed at destroy)
-    DevBuf x, res, out16, out32, q8k_pending, q8k_cur, q80_cur, tmp, misc, keys;
+    DevBuf x, res, out16, out32, q8k_pending, q8k_cur, q80_cur, tmp, misc, keys, tcpack;
 
     // the engine's g_sdot_input state: pending pre-quantized Q8_K input (ENG:4184) and the
     // current input rows for row-level calls (kept as fp16 on the device, quantized lazily)
@@ -152,6 +152,37 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
         if (idx.empty()) continue;
         const void *act = (type == KQ_TYPE_Q8_0) ? act_q80 : act_q8k;
         if (!x && !act) return fail(c, KQ_ERR_NOT_READY, "no activation for type %d", type);
+        if (M > 8 && !ex.dbg_sumi && !ex.argmax && !ex.out_ids) {
+            // many tokens: the tensor-core kernel (activation packed into the context's buffer)
+            kq::TcLaunch T{};
+            T.type = type;
+            T.K = K;
+            T.M = M;
+            T.n_tasks = (int)idx.size();
+            for (int j = 0; j < T.n_tasks; ++j) {
+                const kq_task &t = tasks[idx[j]];
+                kq::GemvTaskHost &h = T.tasks[j];
+                h.w = t.w->d;
+                h.row_begin = t.row_begin;
+                h.rows = t.rows;
+                h.dst = t.dst;
+                h.dst_stride = (long long)t.dst_stride;
+                h.res = t.residual;
+                h.res_stride = (long long)t.res_stride;
+                h.dst_f32 = t.dst_f32;
+                h.f32_stride = (long long)t.dst_f32_stride;
+            }
+            T.x = x;
+            T.x_stride = x_stride;
+            T.act = x ? nullptr : act;
+            T.scratch_bytes = kq::tc_scratch_bytes(type, M, K);
+            if (int r = ensure(c, c->tcpack, T.scratch_bytes)) return r;
+            T.scratch = c->tcpack.p;
+            T.status = c->d_status;
+            T.timeout_ns = c->timeout_ns;
+            if (cudaError_t e = kq::launch_gemm_tc(T, c->stream)) return cuda_fail(c, e, "tensor-core gemm launch");
+            continue;
+        }
         int m0 = 0;
         while (m0 < M) {
             int mt = std::min(8, M - m0);
@@ -311,7 +342,7 @@ extern "C" int kq_destroy(kq_ctx *c) {
     cudaSetDevice(c->device);
     cudaStreamSynchronize(c->stream);
     for (DevBuf *b : {&c->x, &c->res, &c->out16, &c->out32, &c->q8k_pending, &c->q8k_cur, &c->q80_cur, &c->tmp,
-                      &c->misc, &c->keys})
+                      &c->misc, &c->keys, &c->tcpack})
         if (b->p) cudaFree(b->p);
     cudaFree(c->d_status);
     if (c->own_stream) cudaStreamDestroy(c->stream);

@@ -1,0 +1,572 @@
+// kq_gemm_tc.cu -- K-quant x Q8_K matrix product for many tokens (prefill, tree verify, batched
+// decode) on the 5th-generation tensor cores (tcgen05.mma kind::i8, accumulators in TMEM).
+//
+// Replaces the engine's batch row kernels (sdot_4rows_<type>_batch, ENG:1336-3106, the SMMLA
+// paths) for M > 8 activation rows.  Results equal the reference's bit for bit: every integer
+// sub-block sum is exact, and each (row, token) adds the fp32 block terms in block order.
+//
+// The reference's block arithmetic, sumi = sum_j sc_j * dot_j with 6-bit per-(row, sub-block)
+// scales, does not map onto one int8 MMA (sc * q needs 10-12 bits).  It is split into pieces
+// that fit a byte, each one MMA over the whole 256-value super-block, recombined exactly in the
+// epilogue:
+//   Q4_K / Q5_K   sc = 8 sh + sl:  A0 = q * sh, A1 = q * sl (u8), A2 = the row's min m_j over
+//                 its sub-block (u8);  sumi = 8 D0 + D1, summ = D2 (= sum_j m_j * bsum_j)
+//   Q6_K          q = 16 q2 + 4 q1 + q0 (2-bit pieces): A_i = sc * q_i (s8), A3 = sc (s8);
+//                 sumi = 16 D2 + 4 D1 + D0 - 32 D3  (= sum_s sc_s * sum_l (q_l - 32) x_l)
+//   Q8_0          A = the quants (s8); one MMA per 32-value block into its own accumulator
+// D_i are int32 per (row, token) in TMEM.
+//
+// CTA: 128 weight rows (8 row groups) x BN tokens, all of K.  Warps 0-3 (one thread per row =
+// TMEM lane) build the A operands of a super-block from the quantized tiles, thread 0 issues
+// the MMAs, and the same warps run the epilogue of the previous super-block while the tensor
+// core works (two TMEM accumulator buffers).  Warp 4 streams weight tiles, the activation tile
+// (pre-packed in the MMA's K-major layout) and its scales through an S-stage ring with
+// cp.async.bulk.  Every wait is bounded.
+#include "kq_common.cuh"
+#include "kq_internal.h"
+
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
+namespace kq {
+
+namespace {
+
+constexpr int kTcRows = 128;
+constexpr int kTcThreads = 5 * 32;
+
+template <int TYPE>
+struct TcCfg {
+    static constexpr int BN = (TYPE == TYPE_Q8_0) ? 32 : 64;                   // tokens per CTA
+    static constexpr int NA = (TYPE == TYPE_Q8_0) ? 1 : (TYPE == TYPE_Q6_K) ? 4 : 3;  // A operands
+    static constexpr int NACC = (TYPE == TYPE_Q8_0) ? 8 : NA;                  // accumulators per buffer
+    static constexpr int S = (TYPE == TYPE_Q6_K) ? 2 : (TYPE == TYPE_Q8_0) ? 4 : 3;   // ring stages
+    static constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;                      // scales per token and unit
+    static constexpr unsigned B_BYTES = BN * 256;
+    static constexpr unsigned W_BYTES = 8u * (unsigned)tile_bytes(TYPE);
+    static constexpr unsigned DX_BYTES = BN * DX * 4;
+    static constexpr unsigned STAGE = B_BYTES + W_BYTES + DX_BYTES;            // multiple of 16
+    static constexpr unsigned A_BYTES = NA * 32768u;
+    static constexpr unsigned SMEM = A_BYTES + S * STAGE + 1024;
+};
+
+struct TcParams {
+    const uint8_t *w;          // tiled weight tensor (row group 0)
+    int rg_first;              // first row group of the task
+    int row_begin, rows;       // output rows = weight rows [row_begin, row_begin + rows)
+    int K, nbu, M;
+    int n_tok_tiles;           // tiles of BN tokens in the packed activation
+    const uint8_t *act;        // packed activation: [token tile][unit][BN * 256] K-major
+    const float *dx;           // [token tile][unit][BN * DX] scales
+    __half *dst;
+    long long dst_stride;
+    const __half *res;
+    long long res_stride;
+    float *dst_f32;
+    long long f32_stride;
+    int *status;
+    unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    // K-major, no swizzle: ((8 rows, n), 2 x 16 B) : ((16 B, SBO), LBO); sm100 descriptor version 1
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// byte offset of (row, k) in a K-major operand of 256 bytes per row: [row/8][k/16][row%8][k%16]
+__device__ __forceinline__ uint32_t canon256(int row, int kc16) { return (row >> 3) * 2048 + kc16 * 128 + (row & 7) * 16; }
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// per-byte negation of bytes in [0, 128]
+__device__ __forceinline__ uint32_t neg_bytes(uint32_t v) { return (0x80808080u - v) ^ 0x80808080u; }
+// bytes of t (each 0..3) times a signed scale in [-32, 31], as int8
+__device__ __forceinline__ uint32_t smul_bytes(uint32_t t, int sc) {
+    const uint32_t u = t * (uint32_t)(sc < 0 ? -sc : sc);
+    return sc < 0 ? neg_bytes(u) : u;
+}
+
+// ---- A operands of one super-block for row r (thread r), from the row's tile bytes.
+// Also returns what the epilogue needs of the row: d (and dmin).
+
+template <int TYPE>
+__device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, uint8_t *A, int r, float &d0, float &d1) {
+    if (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K) {
+        constexpr int RB = (TYPE == TYPE_Q4_K) ? 144 : 176, QS = (TYPE == TYPE_Q4_K) ? 16 : 48;
+        const uint8_t *row = tile + RB * rr;
+        const uint4 h = lds128(row);
+        d0 = half_bits_to_float(h.x);
+        d1 = half_bits_to_float(h.x >> 16);
+        const uint32_t sc[2] = {h.y & 0x3F3F3F3Fu, (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u)};
+        const uint32_t mn[2] = {h.z & 0x3F3F3F3Fu, ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u)};
+        uint32_t qh[8];
+        if (TYPE == TYPE_Q5_K) {
+            const uint4 a = lds128(row + 16), b = lds128(row + 32);
+            qh[0] = a.x, qh[1] = a.y, qh[2] = a.z, qh[3] = a.w, qh[4] = b.x, qh[5] = b.y, qh[6] = b.z, qh[7] = b.w;
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint4 qa = lds128(row + QS + 32 * c), qb = lds128(row + QS + 32 * c + 16);
+            const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+            for (int hi = 0; hi < 2; ++hi) {
+                const int j = 2 * c + hi;  // sub-block
+                const int s = ubyte(sc[j >> 2], j & 3), m = ubyte(mn[j >> 2], j & 3);
+                const uint32_t sh = (uint32_t)(s >> 3), sl = (uint32_t)(s & 7), mrep = 0x01010101u * (uint32_t)m;
+                uint32_t q[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    q[i] = hi ? ((w[i] >> 4) & 0x0F0F0F0Fu) : (w[i] & 0x0F0F0F0Fu);
+                    if (TYPE == TYPE_Q5_K) q[i] |= ((qh[i] >> j) & 0x01010101u) << 4;
+                }
+#pragma unroll
+                for (int h16 = 0; h16 < 2; ++h16) {  // two 16-byte chunks of the 32-value sub-block
+                    const uint32_t o = canon256(r, 2 * j + h16);
+                    const uint32_t *qq = q + 4 * h16;
+                    *reinterpret_cast<uint4 *>(A + o) = make_uint4(qq[0] * sh, qq[1] * sh, qq[2] * sh, qq[3] * sh);
+                    *reinterpret_cast<uint4 *>(A + 32768 + o) = make_uint4(qq[0] * sl, qq[1] * sl, qq[2] * sl, qq[3] * sl);
+                    *reinterpret_cast<uint4 *>(A + 65536 + o) = make_uint4(mrep, mrep, mrep, mrep);
+                }
+            }
+        }
+    } else if (TYPE == TYPE_Q6_K) {
+        const uint8_t *row = tile + 208 * rr;
+        d0 = half_bits_to_float(*reinterpret_cast<const uint16_t *>(tile + 3328 + 2 * rr));
+        d1 = 0.0f;
+        const uint4 s0 = lds128(row + 192);
+        const uint32_t scw[4] = {s0.x, s0.y, s0.z, s0.w};
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                // values 128hh + 32g + 16hf + i, i < 16, for g = 0..3 (sub-block s = 8hh + 2g + hf)
+                const uint4 A4 = lds128(row + 64 * hh + 16 * hf), B4 = lds128(row + 64 * hh + 32 + 16 * hf);
+                const uint4 H4 = lds128(row + 128 + 32 * hh + 16 * hf);
+                const uint32_t av[4] = {A4.x, A4.y, A4.z, A4.w}, bv[4] = {B4.x, B4.y, B4.z, B4.w};
+                const uint32_t hv[4] = {H4.x, H4.y, H4.z, H4.w};
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    const int s = 8 * hh + 2 * g + hf;
+                    const int sc = sbyte(scw[s >> 2], s & 3);
+                    uint32_t q[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        if (g == 0) q[i] = (av[i] & 0x0F0F0F0Fu) | ((hv[i] << 4) & 0x30303030u);
+                        else if (g == 1) q[i] = (bv[i] & 0x0F0F0F0Fu) | ((hv[i] << 2) & 0x30303030u);
+                        else if (g == 2) q[i] = ((av[i] >> 4) & 0x0F0F0F0Fu) | (hv[i] & 0x30303030u);
+                        else q[i] = ((bv[i] >> 4) & 0x0F0F0F0Fu) | ((hv[i] >> 2) & 0x30303030u);
+                    }
+                    const uint32_t o = canon256(r, s);  // sub-block s = 16-byte chunk s
+                    uint32_t p0[4], p1[4], p2[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        p0[i] = smul_bytes(q[i] & 0x03030303u, sc);
+                        p1[i] = smul_bytes((q[i] >> 2) & 0x03030303u, sc);
+                        p2[i] = smul_bytes((q[i] >> 4) & 0x03030303u, sc);
+                    }
+                    const uint32_t srep = 0x01010101u * (uint32_t)(sc & 0xFF);
+                    *reinterpret_cast<uint4 *>(A + o) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
+                    *reinterpret_cast<uint4 *>(A + 32768 + o) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+                    *reinterpret_cast<uint4 *>(A + 65536 + o) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
+                    *reinterpret_cast<uint4 *>(A + 98304 + o) = make_uint4(srep, srep, srep, srep);
+                }
+            }
+        }
+    } else {  // Q8_0: row = eight fp16 d, then 256 quants; the scales are read by the caller
+        const uint8_t *row = tile + 272 * rr;
+        d0 = d1 = 0.0f;
+#pragma unroll
+        for (int kc = 0; kc < 16; ++kc) *reinterpret_cast<uint4 *>(A + canon256(r, kc)) = lds128(row + 16 + 16 * kc);
+    }
+}
+
+// ------------------------------------------------------------------ the kernel
+
+template <int TYPE>
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ TcParams p) {
+    using C = TcCfg<TYPE>;
+    constexpr int BN = C::BN, NA = C::NA, NACC = C::NACC, S = C::S;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ uint64_t bar_full[S], bar_empty[S], bar_mma[2];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort;
+
+    uint8_t *A = smem;                      // NA operands of 32 KB
+    uint8_t *ring = smem + C::A_BYTES;      // S stages: B | weights | dx
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tok_tile = blockIdx.x, row_tile = blockIdx.y;
+    const int nbu = p.nbu;
+    const int rg0 = p.rg_first + 8 * row_tile;                         // first row group of the CTA
+    const int rg_end = (p.row_begin + p.rows - 1) / 16 + 1;            // past the task's last row group
+    const int n_rg = min(8, rg_end - rg0);
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(&bar_full[s]), 1);
+            mbar_init(smem_u32(&bar_empty[s]), 1);
+        }
+        mbar_init(smem_u32(&bar_mma[0]), 1);
+        mbar_init(smem_u32(&bar_mma[1]), 1);
+        s_abort = 0;
+        mbar_init_fence();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&s_tmem)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    if (warp == 4) {
+        // ---------------- producer
+        if (lane == 0) {
+            const uint64_t policy = l2_evict_first_policy();
+            for (int b = 0; b < nbu; ++b) {
+                const int st = b % S;
+                if (b >= S && !mbar_wait_bounded(smem_u32(&bar_empty[st]), ((b / S) - 1) & 1, p.timeout_ns, p.status)) {
+                    s_abort = 1;
+                    break;
+                }
+                const uint32_t full = smem_u32(&bar_full[st]);
+                uint8_t *sb = ring + (size_t)st * C::STAGE;
+                mbar_arrive_expect_tx(full, C::B_BYTES + (uint32_t)n_rg * (uint32_t)tile_bytes(TYPE) + C::DX_BYTES);
+                const size_t tix = (size_t)tok_tile * nbu + b;
+                bulk_g2s(smem_u32(sb), p.act + tix * C::B_BYTES, C::B_BYTES, full, policy);
+                for (int g = 0; g < n_rg; ++g)
+                    bulk_g2s(smem_u32(sb + C::B_BYTES + g * tile_bytes(TYPE)),
+                             p.w + ((size_t)(rg0 + g) * nbu + b) * tile_bytes(TYPE), tile_bytes(TYPE), full, policy);
+                bulk_g2s(smem_u32(sb + C::B_BYTES + C::W_BYTES), p.dx + tix * (BN * C::DX), C::DX_BYTES, full, policy);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- rows: A operands, MMA issue (thread 0), epilogue
+        const int r = tid;            // weight row within the CTA = TMEM lane
+        const int g = r >> 4, rr = r & 15;
+        float acc[BN];
+#pragma unroll
+        for (int m = 0; m < BN; ++m) acc[m] = 0.0f;
+        float dpp[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // per buffer: d, dmin (Q8_0: block scales, packed)
+        uint32_t dqq[2][2] = {{0u, 0u}, {0u, 0u}};
+        const uint32_t idesc = (2u << 4) | ((TYPE == TYPE_Q6_K || TYPE == TYPE_Q8_0) ? (1u << 7) : 0u) | (1u << 10) |
+                               ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+        const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+
+        // epilogue of super-block e (its accumulators in buffer e & 1, scales in stage e % S)
+        auto epilogue = [&](int e) {
+            const int buf = e & 1;
+            const float *dxs = reinterpret_cast<const float *>(ring + (size_t)(e % S) * C::STAGE + C::B_BYTES + C::W_BYTES);
+            const uint32_t tb = tmem + lane_base + (uint32_t)(buf * 256);
+#pragma unroll
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                if (TYPE == TYPE_Q8_0) {
+                    const uint32_t dw4[4] = {__float_as_uint(dpp[buf][0]), __float_as_uint(dpp[buf][1]), dqq[buf][0], dqq[buf][1]};
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        uint32_t D[16];
+                        tmem_ld16(tb + (uint32_t)(jj * BN + c0), D);
+                        tmem_wait_ld();
+                        const float dw = half_bits_to_float(dw4[jj >> 1] >> (16 * (jj & 1)));
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float t = __fmul_rn(__fmul_rn(dw, dxs[(c0 + i) * 8 + jj]), __int2float_rn((int)D[i]));
+                            acc[c0 + i] = __fadd_rn(acc[c0 + i], t);
+                        }
+                    }
+                } else {
+                    uint32_t D[NA][16];
+#pragma unroll
+                    for (int a = 0; a < NA; ++a) tmem_ld16(tb + (uint32_t)(a * BN + c0), D[a]);
+                    tmem_wait_ld();
+                    const float d = dpp[buf][0], dmin = dpp[buf][1];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float dx = dxs[c0 + i];
+                        float t;
+                        if (TYPE == TYPE_Q6_K) {
+                            const int sumi = 16 * (int)D[2][i] + 4 * (int)D[1][i] + (int)D[0][i] - 32 * (int)D[3][i];
+                            t = __fmul_rn(__fmul_rn(d, dx), __int2float_rn(sumi));
+                        } else {
+                            const int sumi = 8 * (int)D[0][i] + (int)D[1][i];
+                            const int summ = (int)D[2][i];
+                            t = __fmul_rn(dx, __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dmin, __int2float_rn(summ))));
+                        }
+                        acc[c0 + i] = __fadd_rn(acc[c0 + i], t);
+                    }
+                }
+            }
+            tc_fence_before();
+        };
+
+        // Waits record a failure in s_abort; every warp reads it after the next barrier, so all
+        // four leave the loop together.
+        for (int b = 0; b <= nbu; ++b) {
+            if (b < nbu) {
+                const int st = b % S;
+                int ok = 1;
+                if (lane == 0) {
+                    ok = mbar_wait_bounded(smem_u32(&bar_full[st]), (b / S) & 1, p.timeout_ns, p.status) &&
+                         (b < 1 || mbar_wait_bounded(smem_u32(&bar_mma[(b - 1) & 1]), ((b - 1) >> 1) & 1, p.timeout_ns,
+                                                     p.status));
+                    if (!ok) s_abort = 1;
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (ok) {
+                    // A operands of super-block b (the MMAs of b - 1 have finished reading A)
+                    const uint8_t *tile = ring + (size_t)st * C::STAGE + C::B_BYTES + (size_t)min(g, n_rg - 1) * tile_bytes(TYPE);
+                    float d0, d1;
+                    prep_row<TYPE>(tile, rr, A, r, d0, d1);
+                    if (TYPE == TYPE_Q8_0) {
+                        const uint4 dv = lds128(tile + 272 * rr);
+                        dpp[b & 1][0] = __uint_as_float(dv.x);
+                        dpp[b & 1][1] = __uint_as_float(dv.y);
+                        dqq[b & 1][0] = dv.z;
+                        dqq[b & 1][1] = dv.w;
+                    } else {
+                        dpp[b & 1][0] = d0;
+                        dpp[b & 1][1] = d1;
+                    }
+                }
+                fence_async_smem();
+                tc_fence_before();
+                named_bar_sync(1, 128);
+                tc_fence_after();
+                if (*reinterpret_cast<volatile int *>(&s_abort)) break;
+                if (tid == 0) {
+                    const uint32_t sa = smem_u32(A), sbm = smem_u32(ring + (size_t)st * C::STAGE);
+                    const uint32_t td = tmem + (uint32_t)((b & 1) * 256);
+                    if (TYPE == TYPE_Q8_0) {
+                        for (int jj = 0; jj < 8; ++jj)
+                            tc_mma(td + (uint32_t)(jj * BN), umma_desc(sa + 256 * jj, 128, 2048),
+                                   umma_desc(sbm + 256 * jj, 128, 2048), idesc, 0);
+                    } else {
+                        for (int a = 0; a < NA; ++a)
+                            for (int ks = 0; ks < 8; ++ks)
+                                tc_mma(td + (uint32_t)(a * BN), umma_desc(sa + a * 32768 + 256 * ks, 128, 2048),
+                                       umma_desc(sbm + 256 * ks, 128, 2048), idesc, ks > 0);
+                    }
+                    tc_commit(smem_u32(&bar_mma[b & 1]));
+                }
+            }
+            if (b >= 1) {
+                // epilogue of b - 1 overlaps the MMAs of b
+                const int e = b - 1;
+                int ok = 1;
+                if (lane == 0) {
+                    ok = mbar_wait_bounded(smem_u32(&bar_mma[e & 1]), (e >> 1) & 1, p.timeout_ns, p.status);
+                    if (!ok) s_abort = 1;
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                tc_fence_after();
+                if (ok) epilogue(e);
+                named_bar_sync(1, 128);  // the stage of e (its dx, weights, B) is no longer read
+                if (*reinterpret_cast<volatile int *>(&s_abort)) break;
+                if (tid == 0) mbar_arrive(smem_u32(&bar_empty[e % S]));
+            }
+        }
+        // results: row r, tokens tok_tile * BN + m
+        const int row = rg0 * 16 + r;  // weight row
+        const int lr = row - p.row_begin;                                 // task-local row
+        if (!s_abort && r < n_rg * 16 && lr >= 0 && lr < p.rows) {
+#pragma unroll
+            for (int m = 0; m < BN; ++m) {
+                const int tok = tok_tile * BN + m;
+                if (tok >= p.M) break;
+                if (p.dst_f32) p.dst_f32[(size_t)tok * p.f32_stride + lr] = acc[m];
+                if (p.dst) {
+                    float v = acc[m];
+                    if (p.res) v = __fadd_rn(v, __half2float(p.res[(size_t)tok * p.res_stride + lr]));
+                    p.dst[(size_t)tok * p.dst_stride + lr] = __float2half_rn(v);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    // drain: copies in flight must land before the CTA exits (only after an early stop)
+    if (tid == kTcRows) {
+        for (int b = max(0, nbu - S); b < nbu; ++b)
+            mbar_wait_bounded(smem_u32(&bar_full[b % S]), (b / S) & 1, p.timeout_ns, p.status);
+    }
+}
+
+// ------------------------------------------------------------------ activation packing
+//
+// x fp16 [M][K] -> Q8_K (quantize_row_fp16_to_q8_k, ENG:925-990) or Q8_0 per 32 (ENG:1016-1064),
+// written as the MMA's B operand: [token tile][unit][BN tokens x 256 bytes, K-major canonical]
+// plus the scales [token tile][unit][token][DX].  Tokens past M are zero.  One warp per (token,
+// unit); lane L holds values 8L .. 8L+7.
+
+template <int TYPE>
+__global__ void pack_act_kernel(const __half *x, long long x_stride, const void *act, int M, int K, int n_tok_tiles,
+                                uint8_t *out, float *dx) {
+    constexpr int BN = TcCfg<TYPE>::BN, DX = TcCfg<TYPE>::DX;
+    const int nbu = K / 256;
+    const int lane = threadIdx.x & 31;
+    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+    for (long long wi = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+         wi < (long long)n_tok_tiles * BN * nbu; wi += warps) {
+        const int m = (int)(wi / nbu), u = (int)(wi % nbu);
+        uint32_t lo = 0, hi = 0;
+        float d = 0.0f;
+        if (m < M) {
+            if (x) {
+                const __half *xu = x + (size_t)m * x_stride + (size_t)u * 256 + 8 * lane;
+                float v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = __half2float(xu[i]);
+                float amax = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+                constexpr int span = (TYPE == TYPE_Q8_0) ? 4 : 32;
+#pragma unroll
+                for (int o = 1; o < span; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                int q[8];
+                if (amax == 0.0f) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) q[i] = 0;
+                } else {
+                    const float inv = __fdiv_rn(127.0f, amax);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) q[i] = max(-127, min(127, __float2int_rn(__fmul_rn(v[i], inv))));
+                }
+                lo = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) | ((uint32_t)(q[2] & 0xFF) << 16) |
+                     ((uint32_t)(q[3] & 0xFF) << 24);
+                hi = (uint32_t)(q[4] & 0xFF) | ((uint32_t)(q[5] & 0xFF) << 8) | ((uint32_t)(q[6] & 0xFF) << 16) |
+                     ((uint32_t)(q[7] & 0xFF) << 24);
+                d = (amax == 0.0f) ? 0.0f : __fdiv_rn(amax, 127.0f);
+            } else if (TYPE == TYPE_Q8_0) {
+                const uint32_t *w = reinterpret_cast<const uint32_t *>(reinterpret_cast<const BlockQ80 *>(act) +
+                                                                       ((size_t)m * nbu + u) * 8 + (lane >> 2));
+                lo = w[1 + 2 * (lane & 3)];
+                hi = w[2 + 2 * (lane & 3)];
+                d = __uint_as_float(w[0]);
+            } else {
+                const uint32_t *w =
+                    reinterpret_cast<const uint32_t *>(reinterpret_cast<const BlockQ8K *>(act) + (size_t)m * nbu + u);
+                lo = w[1 + 2 * lane];
+                hi = w[2 + 2 * lane];
+                d = __uint_as_float(w[0]);
+            }
+        }
+        const int tt = m / BN, mm = m % BN;
+        const size_t tix = (size_t)tt * nbu + u;
+        uint8_t *o = out + tix * (BN * 256) + (mm >> 3) * 2048 + (lane >> 1) * 128 + (mm & 7) * 16 + 8 * (lane & 1);
+        *reinterpret_cast<uint2 *>(o) = make_uint2(lo, hi);
+        if (TYPE == TYPE_Q8_0) {
+            if ((lane & 3) == 0) dx[tix * (BN * DX) + mm * DX + (lane >> 2)] = d;
+        } else {
+            if (lane == 0) dx[tix * BN + mm] = d;
+        }
+    }
+}
+
+template <int TYPE>
+cudaError_t launch_tc_t(const TcLaunch &L, cudaStream_t stream) {
+    using C = TcCfg<TYPE>;
+    const int nbu = L.K / 256;
+    const int n_tok_tiles = (L.M + C::BN - 1) / C::BN;
+    const size_t need = (size_t)n_tok_tiles * nbu * (C::B_BYTES + C::DX_BYTES);
+    if (L.scratch_bytes < need) return cudaErrorInvalidValue;
+    uint8_t *act = reinterpret_cast<uint8_t *>(L.scratch);
+    float *dx = reinterpret_cast<float *>(act + (size_t)n_tok_tiles * nbu * C::B_BYTES);
+    {
+        const long long items = (long long)n_tok_tiles * C::BN * nbu;
+        const int blocks = (int)std::min<long long>((items + 7) / 8, 148 * 16);
+        pack_act_kernel<TYPE><<<blocks, 256, 0, stream>>>(reinterpret_cast<const __half *>(L.x), L.x_stride, L.act,
+                                                           L.M, L.K, n_tok_tiles, act, dx);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    static std::mutex mu;
+    static std::unordered_map<int, bool> configured;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!configured[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+            if (e != cudaSuccess) return e;
+            configured[dev] = true;
+        }
+    }
+    for (int i = 0; i < L.n_tasks; ++i) {
+        const GemvTaskHost &h = L.tasks[i];
+        if (h.rows <= 0) continue;
+        TcParams p{};
+        p.w = h.w;
+        p.rg_first = h.row_begin / 16;
+        p.row_begin = h.row_begin;
+        p.rows = h.rows;
+        p.K = L.K;
+        p.nbu = nbu;
+        p.M = L.M;
+        p.n_tok_tiles = n_tok_tiles;
+        p.act = act;
+        p.dx = dx;
+        p.dst = reinterpret_cast<__half *>(h.dst);
+        p.dst_stride = h.dst_stride;
+        p.res = reinterpret_cast<const __half *>(h.res);
+        p.res_stride = h.res_stride;
+        p.dst_f32 = h.dst_f32;
+        p.f32_stride = h.f32_stride;
+        p.status = L.status;
+        p.timeout_ns = L.timeout_ns;
+        const int n_rg = (h.row_begin + h.rows - 1) / 16 - p.rg_first + 1;
+        dim3 grid(n_tok_tiles, (n_rg + 7) / 8);
+        gemm_tc_kernel<TYPE><<<grid, kTcThreads, C::SMEM, stream>>>(p);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace
+
+size_t tc_scratch_bytes(int type, int M, int K) {
+    const int nbu = K / 256;
+    auto need = [&](int bn, int dxn) { return (size_t)((M + bn - 1) / bn) * nbu * ((size_t)bn * 256 + (size_t)bn * dxn * 4); };
+    return type == TYPE_Q8_0 ? need(32, 8) : need(64, 1);
+}
+
+cudaError_t launch_gemm_tc(const TcLaunch &L, cudaStream_t stream) {
+    if (L.M < 1 || L.K % 256) return cudaErrorInvalidValue;
+    switch (L.type) {
+        case TYPE_Q4_K: return launch_tc_t<TYPE_Q4_K>(L, stream);
+        case TYPE_Q5_K: return launch_tc_t<TYPE_Q5_K>(L, stream);
+        case TYPE_Q6_K: return launch_tc_t<TYPE_Q6_K>(L, stream);
+        case TYPE_Q8_0: return launch_tc_t<TYPE_Q8_0>(L, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace kq

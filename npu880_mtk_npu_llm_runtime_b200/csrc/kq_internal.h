@@ -53,9 +53,30 @@ struct GemvLaunch {
     int inject_wait = 0;  // failure-path test hook (see kq_set_option "inject_timeout")
 };
 
+// Many-token product on the tensor cores (kq_gemm_tc.cu): tasks of one type, the input as fp16
+// x or pre-quantized act (as in GemvLaunch), packed into `scratch` (tc_scratch_bytes) first.
+struct TcLaunch {
+    int type;
+    int K;
+    int M;
+    GemvTaskHost tasks[4];
+    int n_tasks;
+    const void *x;
+    long long x_stride;
+    const void *act;
+    void *scratch;
+    size_t scratch_bytes;
+    int *status;
+    unsigned long long timeout_ns;
+};
+
 // kq_gemv.cu
 cudaError_t launch_gemv(const GemvLaunch &L, cudaStream_t stream);
 // rows ids[0..n) of a tiled tensor -> a new tiled tensor of n rows (weight_bytes(type, n, K))
+// kq_gemm_tc.cu
+size_t tc_scratch_bytes(int type, int M, int K);
+cudaError_t launch_gemm_tc(const TcLaunch &L, cudaStream_t stream);
+
 cudaError_t launch_gather_rows(int type, int K, const uint8_t *src, const uint32_t *ids, int n, uint8_t *dst,
                                cudaStream_t stream);
 
