@@ -79,7 +79,9 @@ const char *kq_last_error(const kq_ctx *ctx);
  * "timeout_ms" / "timeout_us" -- limit of every device-side wait (default 1000 ms);
  * "inject_timeout" -- failure-path test: matrix-product kernels first wait on a barrier that
  * nothing completes, so the wait runs out, the kernel returns early and the call reports
- * KQ_ERR_TIMEOUT (default 0). */
+ * KQ_ERR_TIMEOUT (default 0);
+ * "gemm_path" -- products of more than 8 activation rows: 0 chooses by a cost model, 1 always
+ * the tensor-core kernel (tcgen05), 2 always the GEMV kernel in tiles of 8 rows (default 0). */
 int kq_set_option(kq_ctx *ctx, const char *name, long long value);
 
 /* compute_ggml_bytes / ggml_row_bytes (ENG:364-374, ENG:3940): bytes of one GGUF row of k

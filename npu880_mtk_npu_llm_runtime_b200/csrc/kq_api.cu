@@ -29,6 +29,7 @@ struct kq_ctx {
     cudaStream_t stream = nullptr;
     bool own_stream = false;
     int num_sms = 0;
+    int gemm_path = 0;           // M > 8: 0 auto, 1 tensor cores, 2 GEMV in tiles of 8 tokens
     int *d_status = nullptr;     // device-side error word
     bool pdl = true;
     bool inject_timeout = false;  // test hook: GEMV consumers wait on a barrier nothing completes
@@ -152,7 +153,24 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
         if (idx.empty()) continue;
         const void *act = (type == KQ_TYPE_Q8_0) ? act_q80 : act_q8k;
         if (!x && !act) return fail(c, KQ_ERR_NOT_READY, "no activation for type %d", type);
-        if (M > 8 && !ex.dbg_sumi && !ex.argmax && !ex.out_ids) {
+        // M > 8: the tensor-core kernel, unless tiles of 8 tokens through the GEMV are expected to
+        // be faster.  Its CTAs (128 rows x 64 tokens) walk K serially, ~2.7 us per 256-value unit;
+        // the GEMV streams the weights once per 8 tokens at ~4 TB/s plus ~3 us per launch.
+        bool use_tc = M > 8 && !ex.dbg_sumi && !ex.argmax && !ex.out_ids;
+        if (use_tc) {
+            long long rows = 0;
+            double wbytes = 0.0;
+            for (int j : idx) {
+                rows += tasks[j].rows;
+                wbytes += (double)tasks[j].rows * (double)tasks[j].w->row_bytes;
+            }
+            const int bn = (type == KQ_TYPE_Q8_0) ? 32 : 64;
+            const long long ctas = ((M + bn - 1) / bn) * ((rows + 127) / 128);
+            const double t_tc = (double)((ctas + c->num_sms - 1) / c->num_sms) * (K / 256) * 2.7e-6;
+            const double t_gemv = (double)((M + 7) / 8) * (wbytes / 4.0e12 + 3.0e-6);
+            use_tc = c->gemm_path == 1 || (c->gemm_path == 0 && t_tc <= t_gemv);
+        }
+        if (use_tc) {
             // many tokens: the tensor-core kernel (activation packed into the context's buffer)
             kq::TcLaunch T{};
             T.type = type;
@@ -387,6 +405,11 @@ extern "C" int kq_set_option(kq_ctx *c, const char *name, long long value) {
     if (!strcmp(name, "timeout_ms")) {
         if (value <= 0) return fail(c, KQ_ERR_INVALID_ARGUMENT, "timeout_ms must be positive");
         c->timeout_ns = (unsigned long long)value * 1000000ull;
+        return KQ_OK;
+    }
+    if (!strcmp(name, "gemm_path")) {
+        if (value < 0 || value > 2) return fail(c, KQ_ERR_INVALID_ARGUMENT, "gemm_path must be 0, 1 or 2");
+        c->gemm_path = (int)value;
         return KQ_OK;
     }
     if (!strcmp(name, "timeout_us")) {

@@ -16,10 +16,11 @@
 //   Q8_0          A = the quants (s8); one MMA per 32-value block into its own accumulator
 // D_i are int32 per (row, token) in TMEM.
 //
-// CTA: 128 weight rows (8 row groups) x BN tokens, all of K.  Warps 0-3 (one thread per row =
-// TMEM lane) build the A operands of a super-block from the quantized tiles, thread 0 issues
-// the MMAs, and the same warps run the epilogue of the previous super-block while the tensor
-// core works (two TMEM accumulator buffers).  Warp 4 streams weight tiles, the activation tile
+// CTA: 128 weight rows (8 row groups) x BN tokens, all of K.  Warps 0-7 (two per TMEM lane
+// quadrant: each thread half of one row's values, then half of its tokens) build the A operands
+// of a super-block from the quantized tiles, thread 0 issues the MMAs, and the same warps run
+// the epilogue of the previous super-block while the tensor core works (two TMEM accumulator
+// buffers).  Warp 8 streams weight tiles, the activation tile
 // (pre-packed in the MMA's K-major layout) and its scales through an S-stage ring with
 // cp.async.bulk.  Every wait is bounded.
 #include "kq_common.cuh"
@@ -34,7 +35,8 @@ namespace kq {
 namespace {
 
 constexpr int kTcRows = 128;
-constexpr int kTcThreads = 5 * 32;
+constexpr int kTcCompute = 256;  // 8 warps: two per TMEM lane quadrant, each half a row / half the tokens
+constexpr int kTcThreads = kTcCompute + 32;
 
 template <int TYPE>
 struct TcCfg {
@@ -97,6 +99,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -110,11 +123,11 @@ __device__ __forceinline__ uint32_t smul_bytes(uint32_t t, int sc) {
     return sc < 0 ? neg_bytes(u) : u;
 }
 
-// ---- A operands of one super-block for row r (thread r), from the row's tile bytes.
-// Also returns what the epilogue needs of the row: d (and dmin).
+// ---- A operands of one super-block: half hs (values 128 hs .. 128 hs + 127) of row r, from the
+// row's tile bytes.  Also returns what the epilogue needs of the row: d (and dmin).
 
 template <int TYPE>
-__device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, uint8_t *A, int r, float &d0, float &d1) {
+__device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, int hs, uint8_t *A, int r, float &d0, float &d1) {
     if (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K) {
         constexpr int RB = (TYPE == TYPE_Q4_K) ? 144 : 176, QS = (TYPE == TYPE_Q4_K) ? 16 : 48;
         const uint8_t *row = tile + RB * rr;
@@ -128,14 +141,16 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, uint8_t *A
             const uint4 a = lds128(row + 16), b = lds128(row + 32);
             qh[0] = a.x, qh[1] = a.y, qh[2] = a.z, qh[3] = a.w, qh[4] = b.x, qh[5] = b.y, qh[6] = b.z, qh[7] = b.w;
         }
+        const uint32_t scw = hs ? sc[1] : sc[0], mnw = hs ? mn[1] : mn[0];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int cc = 0; cc < 2; ++cc) {
+            const int c = 2 * hs + cc;
             const uint4 qa = lds128(row + QS + 32 * c), qb = lds128(row + QS + 32 * c + 16);
             const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
             for (int hi = 0; hi < 2; ++hi) {
                 const int j = 2 * c + hi;  // sub-block
-                const int s = ubyte(sc[j >> 2], j & 3), m = ubyte(mn[j >> 2], j & 3);
+                const int s = ubyte(scw, 2 * cc + hi), m = ubyte(mnw, 2 * cc + hi);
                 const uint32_t sh = (uint32_t)(s >> 3), sl = (uint32_t)(s & 7), mrep = 0x01010101u * (uint32_t)m;
                 uint32_t q[8];
 #pragma unroll
@@ -159,8 +174,8 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, uint8_t *A
         d1 = 0.0f;
         const uint4 s0 = lds128(row + 192);
         const uint32_t scw[4] = {s0.x, s0.y, s0.z, s0.w};
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
+        {
+            const int hh = hs;
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 // values 128hh + 32g + 16hf + i, i < 16, for g = 0..3 (sub-block s = 8hh + 2g + hf)
@@ -171,7 +186,7 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, uint8_t *A
 #pragma unroll
                 for (int g = 0; g < 4; ++g) {
                     const int s = 8 * hh + 2 * g + hf;
-                    const int sc = sbyte(scw[s >> 2], s & 3);
+                    const int sc = sbyte(hh ? scw[2 + (g >> 1)] : scw[g >> 1], 2 * (g & 1) + hf);
                     uint32_t q[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -200,7 +215,10 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, uint8_t *A
         const uint8_t *row = tile + 272 * rr;
         d0 = d1 = 0.0f;
 #pragma unroll
-        for (int kc = 0; kc < 16; ++kc) *reinterpret_cast<uint4 *>(A + canon256(r, kc)) = lds128(row + 16 + 16 * kc);
+        for (int k = 0; k < 8; ++k) {
+            const int kc = 8 * hs + k;
+            *reinterpret_cast<uint4 *>(A + canon256(r, kc)) = lds128(row + 16 + 16 * kc);
+        }
     }
 }
 
@@ -209,7 +227,7 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, uint8_t *A
 template <int TYPE>
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ TcParams p) {
     using C = TcCfg<TYPE>;
-    constexpr int BN = C::BN, NA = C::NA, NACC = C::NACC, S = C::S;
+    constexpr int BN = C::BN, NA = C::NA, S = C::S;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     __shared__ uint64_t bar_full[S], bar_empty[S], bar_mma[2];
@@ -244,7 +262,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
-    if (warp == 4) {
+    if (warp == kTcCompute / 32) {
         // ---------------- producer
         if (lane == 0) {
             const uint64_t policy = l2_evict_first_policy();
@@ -267,66 +285,68 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         }
         __syncwarp();
     } else {
-        // ---------------- rows: A operands, MMA issue (thread 0), epilogue
-        const int r = tid;            // weight row within the CTA = TMEM lane
+        // ---------------- rows: A operands, MMA issue (thread 0), epilogue.  Warp w covers TMEM
+        // lanes / rows 32 (w % 4) .. +31 and half w / 4 of each row's values (A operands) and of
+        // the tokens (epilogue).
+        constexpr int BH = BN / 2;
+        const int quad = warp & 3, hs = warp >> 2;
+        const int r = 32 * quad + lane;  // weight row within the CTA = TMEM lane
         const int g = r >> 4, rr = r & 15;
-        float acc[BN];
+        float acc[BH];
 #pragma unroll
-        for (int m = 0; m < BN; ++m) acc[m] = 0.0f;
+        for (int m = 0; m < BH; ++m) acc[m] = 0.0f;
         float dpp[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // per buffer: d, dmin (Q8_0: block scales, packed)
         uint32_t dqq[2][2] = {{0u, 0u}, {0u, 0u}};
         const uint32_t idesc = (2u << 4) | ((TYPE == TYPE_Q6_K || TYPE == TYPE_Q8_0) ? (1u << 7) : 0u) | (1u << 10) |
                                ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
-        const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+        const uint32_t lane_base = ((uint32_t)(32 * quad) << 16) + (uint32_t)(hs * BH);
 
         // epilogue of super-block e (its accumulators in buffer e & 1, scales in stage e % S)
         auto epilogue = [&](int e) {
             const int buf = e & 1;
-            const float *dxs = reinterpret_cast<const float *>(ring + (size_t)(e % S) * C::STAGE + C::B_BYTES + C::W_BYTES);
+            const float *dxs = reinterpret_cast<const float *>(ring + (size_t)(e % S) * C::STAGE + C::B_BYTES + C::W_BYTES) +
+                               hs * BH * C::DX;
             const uint32_t tb = tmem + lane_base + (uint32_t)(buf * 256);
+            if (TYPE == TYPE_Q8_0) {
+                const uint32_t dw4[4] = {__float_as_uint(dpp[buf][0]), __float_as_uint(dpp[buf][1]), dqq[buf][0], dqq[buf][1]};
 #pragma unroll
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                if (TYPE == TYPE_Q8_0) {
-                    const uint32_t dw4[4] = {__float_as_uint(dpp[buf][0]), __float_as_uint(dpp[buf][1]), dqq[buf][0], dqq[buf][1]};
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj) {
-                        uint32_t D[16];
-                        tmem_ld16(tb + (uint32_t)(jj * BN + c0), D);
-                        tmem_wait_ld();
-                        const float dw = half_bits_to_float(dw4[jj >> 1] >> (16 * (jj & 1)));
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float t = __fmul_rn(__fmul_rn(dw, dxs[(c0 + i) * 8 + jj]), __int2float_rn((int)D[i]));
-                            acc[c0 + i] = __fadd_rn(acc[c0 + i], t);
-                        }
-                    }
-                } else {
-                    uint32_t D[NA][16];
-#pragma unroll
-                    for (int a = 0; a < NA; ++a) tmem_ld16(tb + (uint32_t)(a * BN + c0), D[a]);
+                for (int jj = 0; jj < 8; ++jj) {
+                    uint32_t D[16];
+                    tmem_ld16(tb + (uint32_t)(jj * BN), D);
                     tmem_wait_ld();
-                    const float d = dpp[buf][0], dmin = dpp[buf][1];
+                    const float dw = half_bits_to_float(dw4[jj >> 1] >> (16 * (jj & 1)));
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const float dx = dxs[c0 + i];
-                        float t;
-                        if (TYPE == TYPE_Q6_K) {
-                            const int sumi = 16 * (int)D[2][i] + 4 * (int)D[1][i] + (int)D[0][i] - 32 * (int)D[3][i];
-                            t = __fmul_rn(__fmul_rn(d, dx), __int2float_rn(sumi));
-                        } else {
-                            const int sumi = 8 * (int)D[0][i] + (int)D[1][i];
-                            const int summ = (int)D[2][i];
-                            t = __fmul_rn(dx, __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dmin, __int2float_rn(summ))));
-                        }
-                        acc[c0 + i] = __fadd_rn(acc[c0 + i], t);
+                        const float t = __fmul_rn(__fmul_rn(dw, dxs[i * 8 + jj]), __int2float_rn((int)D[i]));
+                        acc[i] = __fadd_rn(acc[i], t);
                     }
+                }
+            } else {
+                uint32_t D[NA][32];
+#pragma unroll
+                for (int a = 0; a < NA; ++a) tmem_ld32(tb + (uint32_t)(a * BN), D[a]);
+                tmem_wait_ld();
+                const float d = dpp[buf][0], dmin = dpp[buf][1];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float dx = dxs[i];
+                    float t;
+                    if (TYPE == TYPE_Q6_K) {
+                        const int sumi = 16 * (int)D[2][i] + 4 * (int)D[1][i] + (int)D[0][i] - 32 * (int)D[3][i];
+                        t = __fmul_rn(__fmul_rn(d, dx), __int2float_rn(sumi));
+                    } else {
+                        const int sumi = 8 * (int)D[0][i] + (int)D[1][i];
+                        const int summ = (int)D[2][i];
+                        t = __fmul_rn(dx, __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dmin, __int2float_rn(summ))));
+                    }
+                    acc[i] = __fadd_rn(acc[i], t);
                 }
             }
             tc_fence_before();
         };
 
         // Waits record a failure in s_abort; every warp reads it after the next barrier, so all
-        // four leave the loop together.
+        // eight leave the loop together.
         for (int b = 0; b <= nbu; ++b) {
             if (b < nbu) {
                 const int st = b % S;
@@ -342,7 +362,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                     // A operands of super-block b (the MMAs of b - 1 have finished reading A)
                     const uint8_t *tile = ring + (size_t)st * C::STAGE + C::B_BYTES + (size_t)min(g, n_rg - 1) * tile_bytes(TYPE);
                     float d0, d1;
-                    prep_row<TYPE>(tile, rr, A, r, d0, d1);
+                    prep_row<TYPE>(tile, rr, hs, A, r, d0, d1);
                     if (TYPE == TYPE_Q8_0) {
                         const uint4 dv = lds128(tile + 272 * rr);
                         dpp[b & 1][0] = __uint_as_float(dv.x);
@@ -356,7 +376,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 }
                 fence_async_smem();
                 tc_fence_before();
-                named_bar_sync(1, 128);
+                named_bar_sync(1, kTcCompute);
                 tc_fence_after();
                 if (*reinterpret_cast<volatile int *>(&s_abort)) break;
                 if (tid == 0) {
@@ -386,18 +406,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 tc_fence_after();
                 if (ok) epilogue(e);
-                named_bar_sync(1, 128);  // the stage of e (its dx, weights, B) is no longer read
+                named_bar_sync(1, kTcCompute);  // the stage of e (its dx, weights, B) is no longer read
                 if (*reinterpret_cast<volatile int *>(&s_abort)) break;
                 if (tid == 0) mbar_arrive(smem_u32(&bar_empty[e % S]));
             }
         }
-        // results: row r, tokens tok_tile * BN + m
-        const int row = rg0 * 16 + r;  // weight row
-        const int lr = row - p.row_begin;                                 // task-local row
+        // results: row r, tokens tok_tile * BN + hs * BH + m
+        const int row = rg0 * 16 + r;     // weight row
+        const int lr = row - p.row_begin;  // task-local row
         if (!s_abort && r < n_rg * 16 && lr >= 0 && lr < p.rows) {
 #pragma unroll
-            for (int m = 0; m < BN; ++m) {
-                const int tok = tok_tile * BN + m;
+            for (int m = 0; m < BH; ++m) {
+                const int tok = tok_tile * BN + hs * BH + m;
                 if (tok >= p.M) break;
                 if (p.dst_f32) p.dst_f32[(size_t)tok * p.f32_stride + lr] = acc[m];
                 if (p.dst) {
@@ -413,7 +433,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     tc_fence_after();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
     // drain: copies in flight must land before the CTA exits (only after an early stop)
-    if (tid == kTcRows) {
+    if (tid == kTcCompute) {
         for (int b = max(0, nbu - S); b < nbu; ++b)
             mbar_wait_bounded(smem_u32(&bar_full[b % S]), (b / S) & 1, p.timeout_ns, p.status);
     }

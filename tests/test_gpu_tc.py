@@ -16,6 +16,15 @@ from conftest import bits, to_dev
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True)
+def force_tensor_cores(kqctx):
+    """pin the tensor-core path (the default chooses by a cost model)"""
+    kqctx.set_option("gemm_path", 1)
+    yield
+    kqctx.set_option("gemm_path", 0)
+
+
 TYPES = [kq.TYPE_Q4_K, kq.TYPE_Q5_K, kq.TYPE_Q6_K, kq.TYPE_Q8_0]
 
 
@@ -95,3 +104,24 @@ def test_tc_ffn_down_shape(kqctx, oracle):
         W.free()
     ref = oracle.gemm(gtype, w, K, act)
     assert np.array_equal(bits(got), bits(ref)), f"max |diff| {np.abs(got - ref).max()}"
+
+
+@pytest.mark.parametrize("path", [0, 2])
+def test_other_paths_agree(kqctx, oracle, path):
+    """the cost-model choice and the forced GEMV tiles give the same bits for M > 8"""
+    import torch
+    kqctx.set_option("gemm_path", path)
+    gtype, M, rows, K = kq.TYPE_Q4_K, 20, 200, 2560
+    w = synth.gen_weights(gtype, rows, K, seed=1600)
+    x = synth.gen_activations(M, K, seed=1601)
+    act = oracle.act_for(gtype, x)
+    W = kqctx.upload(w, gtype, rows, K)
+    try:
+        out = torch.full((M, rows), float("nan"), dtype=torch.float32, device="cuda")
+        kqctx.gemm_multi_q8_async(to_dev(act), None, M, K, [dict(w=W, dst_f32=out)])
+        kqctx.synchronize()
+        got = out.cpu().numpy()
+    finally:
+        W.free()
+    ref = oracle.gemm(gtype, w, K, act)
+    assert np.array_equal(bits(got), bits(ref))
