@@ -39,6 +39,7 @@ sys.path.insert(0, ROOT)
 METRIC_GEMV = "Q4_K GEMV weight GB/s (% B200 HBM peak)"
 METRIC_LM = "Q6_K LM-head GEMV weight GB/s (vocab-sharded, all-gathered)"
 L2_BYTES = 126 * 1024 * 1024
+STEPS_DEFAULT = 300000
 
 
 def env_int(name, default):
@@ -362,11 +363,335 @@ def run_ours(args, rank, world, local_rank):
     return result
 
 
+# ---------------------------------------------------------------------------- stack configs
+
+METRIC_FFN = "tree-verify FFN block weight GB/s (Q4_K gate/up, Q6_K down)"
+METRIC_PREFILL = "prefill GEMM TOPS (36-layer Q4_K_M stack, int8 tensor cores)"
+METRIC_DECODE = "batched decode tok/s (64 sequences, 36-layer Q5_K/Q8_0 stack + sharded LM head)"
+
+HIDDEN, FFN_DIM, Q_DIM, KV_DIM, VOCAB = 2560, 9728, 4096, 1024, 151936
+
+
+def stack_layout(kind):
+    """(name, type, rows, K) of one layer: SURVEY/BASELINE config 3 (Q4_K_M) or config 4 (Q5_K/Q8_0)."""
+    from npu880_mtk_npu_llm_runtime_b200 import synth as sy
+    if kind == "prefill":
+        a, b = sy.TYPE_Q4_K, sy.TYPE_Q6_K
+        return [("q", a, Q_DIM, HIDDEN), ("k", a, KV_DIM, HIDDEN), ("v", b, KV_DIM, HIDDEN), ("o", a, HIDDEN, Q_DIM),
+                ("gate", a, FFN_DIM, HIDDEN), ("up", a, FFN_DIM, HIDDEN), ("down", b, HIDDEN, FFN_DIM)]
+    a, b = sy.TYPE_Q5_K, sy.TYPE_Q8_0
+    return [("q", a, Q_DIM, HIDDEN), ("k", b, KV_DIM, HIDDEN), ("v", b, KV_DIM, HIDDEN), ("o", a, HIDDEN, Q_DIM),
+            ("gate", a, FFN_DIM, HIDDEN), ("up", a, FFN_DIM, HIDDEN), ("down", b, HIDDEN, FFN_DIM)]
+
+
+def time_device(stream, step, steps, warmup, gpu_index, graph=True, world=1):
+    """Run `step(i)` warmup + steps times; the timed steps are captured in a CUDA graph when asked.
+    Returns (seconds for `steps` steps, clock summary)."""
+    import torch
+    import torch.distributed as dist
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            step(i)
+    torch.cuda.synchronize()
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(steps):
+                step(i)
+        with torch.cuda.stream(stream):
+            g.replay()
+        torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(gpu_index) as clk:
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            if g is not None:
+                g.replay()
+            else:
+                for i in range(steps):
+                    step(i)
+        e1.record(stream)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del g
+    return float(t.item()), clk.summary()
+
+
+def run_stack(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import npu880_mtk_npu_llm_runtime_b200 as kq
+    from npu880_mtk_npu_llm_runtime_b200 import build as kqbuild, synth
+
+    kqbuild.build()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    ctx = kq.Context(local_rank)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream.cuda_stream)
+    gpu = physical_gpu_index(local_rank)
+    peak_hbm, peak_kind = measured_peaks()
+    result = None
+
+    def qact(x16_dev, M, K, gtype):
+        if gtype == synth.TYPE_Q8_0:
+            q = torch.zeros(kq.q8_0_bytes(M, K), dtype=torch.uint8, device=dev)
+            ctx.quantize_q8_0_async(x16_dev, M, K, q)
+            return None, q
+        q = torch.zeros(kq.q8k_bytes(M, K), dtype=torch.uint8, device=dev)
+        ctx.quantize_q8k_async(x16_dev, M, K, q)
+        return q, None
+
+    if args.config == "ffn":
+        # config 2: RMSNorm -> {gate, up} Q4_K -> SwiGLU -> down Q6_K + residual, M draft tokens
+        M = args.m or 8
+        per_set = [synth.gen_weights(synth.TYPE_Q4_K, FFN_DIM, HIDDEN, 2001), synth.gen_weights(synth.TYPE_Q4_K, FFN_DIM, HIDDEN, 2002),
+                   synth.gen_weights(synth.TYPE_Q6_K, HIDDEN, FFN_DIM, 2003)]
+        wbytes = sum(w.nbytes for w in per_set)
+        n_sets = max(2, math.ceil(2.2 * L2_BYTES / wbytes))
+        sets = [(ctx.upload(per_set[0], synth.TYPE_Q4_K, FFN_DIM, HIDDEN), ctx.upload(per_set[1], synth.TYPE_Q4_K, FFN_DIM, HIDDEN),
+                 ctx.upload(per_set[2], synth.TYPE_Q6_K, HIDDEN, FFN_DIM)) for _ in range(n_sets)]
+        x16 = synth.gen_activations(M, HIDDEN, 2004)
+        gamma = (synth.gen_gamma(HIDDEN, 2005) * np.float16(0.1)).astype(np.float16)
+        x = torch.from_numpy(x16.view(np.uint16).copy()).to(dev)
+        gm = torch.from_numpy(gamma.view(np.uint16).copy()).to(dev)
+        out = torch.zeros((M, HIDDEN), dtype=torch.float16, device=dev)
+
+        def step(i):
+            g_, u_, d_ = sets[i % n_sets]
+            ctx.run_ffn_async(g_, u_, d_, M, x, gm, out)
+
+        steps = args.steps
+        dt, clocks = time_device(stream, step, steps, max(3, args.warmup), gpu)
+        value = wbytes * steps / dt / 1e9
+        ops = 2.0 * M * (2 * FFN_DIM * HIDDEN + HIDDEN * FFN_DIM)
+        # e2e: the blocking C-ABI call with host buffers
+        xp = np.ascontiguousarray(x16)
+        for _ in range(2):
+            ctx.run_ffn(sets[0][0], sets[0][1], sets[0][2], xp, gamma)
+        e2e_steps = min(steps, 200)
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            g_, u_, d_ = sets[i % n_sets]
+            ctx.run_ffn(g_, u_, d_, xp, gamma)
+        e2e_dt = time.perf_counter() - t0
+        cpu = None
+        if not args.no_cpu_baseline:
+            from oracle.oracle import Oracle
+            O = Oracle()
+            t0 = time.perf_counter()
+            O.ffn(per_set[0], synth.TYPE_Q4_K, per_set[1], synth.TYPE_Q4_K, per_set[2], synth.TYPE_Q6_K, HIDDEN, FFN_DIM, x16, gamma)
+            sec = time.perf_counter() - t0
+            cpu = {"value": round(wbytes / sec / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                   "sample": f"1 FFN block at M={M} through the oracle's C restatement of the reference's SDOT "
+                             f"FFN sequence (ENG:8283-8298; its dispatch limit K <= 9216 excludes down, K = 9728)",
+                   "seconds_per_step": sec}
+        result = {
+            "metric": METRIC_FFN, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": max(3, args.warmup), "ms_per_step": round(dt / steps * 1e3, 6), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded GGUF blocks per BASELINE distributions; activations N(0,1) -> fp16)",
+            "config": {"workload": f"config2: tree-verify FFN block M={M}, hidden 2560, intermediate 9728",
+                       "m": M, "weight_bytes_per_step": wbytes, "tops": round(ops * steps / dt / 1e12, 3),
+                       "l2": f"{n_sets} rotating weight sets ({n_sets * wbytes / 2**20:.0f} MiB > 2x126 MB L2)",
+                       "parallelism": f"replicas x{world}",
+                       "timing": "CUDA graph of back-to-back kq_run_ffn_async steps, CUDA events"},
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak_hbm, "unit": "GB/s",
+                         "frac": round(value / peak_hbm, 4), "peak_source": peak_kind, "traffic": None},
+            "cpu_baseline": cpu, "clocks": clocks,
+            "e2e": {"value": round(wbytes * e2e_steps / e2e_dt / 1e9, 2), "unit": "GB/s", "steps": e2e_steps,
+                    "h2d_bytes_per_step": int(x16.nbytes + gamma.nbytes), "d2h_bytes_per_step": int(x16.nbytes),
+                    "api": "kq_run_ffn (host buffers, blocking)"},
+            "gpu_launches": steps * 5,
+        }
+        for st_ in sets:
+            for w_ in st_:
+                w_.free()
+
+    elif args.config == "prefill":
+        # config 3: every GEMM of a 36-layer Q4_K_M stack at M tokens (activations pre-quantized)
+        M = args.m or 2048
+        L = args.layers
+        layout = stack_layout("prefill")
+        host = {n: synth.gen_weights(t, r, k, 3000 + i) for i, (n, t, r, k) in enumerate(layout)}
+        layers = [{n: ctx.upload(host[n], t, r, k) for (n, t, r, k) in layout} for _ in range(L)]
+        acts = {}
+        for K_ in (HIDDEN, Q_DIM, FFN_DIM):
+            x16 = torch.from_numpy(synth.gen_activations(M, K_, 3100 + K_).view(np.uint16).copy()).to(dev)
+            acts[K_] = qact(x16, M, K_, synth.TYPE_Q4_K)[0]
+        outs = {n: torch.zeros((M, r), dtype=torch.float16, device=dev) for (n, t, r, k) in layout}
+        groups = [(["q", "k", "v"], HIDDEN), (["o"], Q_DIM), (["gate", "up"], HIDDEN), (["down"], FFN_DIM)]
+        task_sets = [[(ctx.make_tasks([dict(w=lay[n], dst=outs[n]) for n in names]), K_) for names, K_ in groups]
+                     for lay in layers]
+
+        def step(i):
+            for ts in task_sets:
+                for tasks, K_ in ts:
+                    ctx.gemm_multi_q8_async(acts[K_], None, M, K_, tasks)
+
+        steps = args.steps
+        dt, clocks = time_device(stream, step, steps, max(3, args.warmup), gpu, graph=False)
+        ops = 2.0 * M * sum(r * k for (_, _, r, k) in layout) * L
+        value = ops * steps / dt / 1e12
+        peak_int8 = 2.0 * measured_bf16()
+        cpu = None
+        if not args.no_cpu_baseline:
+            from oracle.oracle import Reference, reference_available, Oracle
+            rows_s, Ms = 256, 32
+            w_s = host["gate"][:rows_s]
+            act_s = Oracle().quantize_q8k(synth.gen_activations(Ms, HIDDEN, 3200))
+            if reference_available():
+                R = Reference()
+                t0 = time.perf_counter()
+                R.gemm(synth.TYPE_Q4_K, w_s, HIDDEN, act_s)
+                sec = time.perf_counter() - t0
+                kind, smp = "reference", (f"{rows_s} gate rows x {Ms} tokens through the reference's own row "
+                                          f"kernels (sdot_row_q4_k_batch, scalar x86), 1 thread")
+            else:
+                O = Oracle()
+                t0 = time.perf_counter()
+                O.gemm(synth.TYPE_Q4_K, w_s, HIDDEN, act_s)
+                sec = time.perf_counter() - t0
+                kind, smp = "port", f"{rows_s} gate rows x {Ms} tokens through the oracle, 1 thread"
+            cpu = {"value": round(2.0 * rows_s * HIDDEN * Ms / sec / 1e12, 6), "unit": "TOPS", "cores": 1,
+                   "kind": kind, "sample": smp}
+        result = {
+            "metric": METRIC_PREFILL, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": steps,
+            "warmup": max(3, args.warmup), "ms_per_step": round(dt / steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded GGUF blocks per BASELINE distributions; activations N(0,1) -> Q8_K)",
+            "config": {"workload": f"config3: prefill GEMMs of a {L}-layer Q4_K_M stack (q/k/o/gate/up Q4_K, v/down Q6_K) at M={M}",
+                       "m": M, "layers": L, "ops_per_step": ops,
+                       "l2": f"inputs larger than L2: {L} layers x {sum(h.nbytes for h in host.values()) / 2**20:.0f} MiB of weights",
+                       "parallelism": f"replicas x{world}",
+                       "timing": "eager launches of all layers per step, CUDA events"},
+            "roofline": {"bound": "tensor", "achieved": round(value, 2), "peak": round(peak_int8, 1), "unit": "TOPS",
+                         "frac": round(value / peak_int8, 4),
+                         "peak_source": "2 x measured dense bf16 TF/s (int8 runs at twice the bf16 rate)",
+                         "traffic": None},
+            "cpu_baseline": cpu, "clocks": clocks, "e2e": None,
+            "gpu_launches": steps * L * 7 * 2,
+        }
+        for lay in layers:
+            for w_ in lay.values():
+                w_.free()
+
+    else:
+        # config 4: 64 sequences, one token each per step, split over the ranks; every rank runs the
+        # 36-layer stack for its rows, then the hidden rows are all-gathered, each rank computes its
+        # vocabulary slice of the LM head for all 64 rows, and the per-row argmax keys are all-gathered
+        SEQ = 64
+        L = args.layers
+        Mr = SEQ // world
+        layout = stack_layout("decode")
+        host = {n: synth.gen_weights(t, r, k, 4000 + i) for i, (n, t, r, k) in enumerate(layout)}
+        layers = [{n: ctx.upload(host[n], t, r, k) for (n, t, r, k) in layout} for _ in range(L)]
+        vchunk = (VOCAB + world - 1) // world
+        v0 = rank * vchunk
+        vrows = max(0, min(VOCAB, v0 + vchunk) - v0)
+        lm = ctx.upload(synth.gen_weights(synth.TYPE_Q6_K, VOCAB, HIDDEN, 4100)[v0:v0 + vrows], synth.TYPE_Q6_K, vrows, HIDDEN)
+        acts = {}
+        for K_ in (HIDDEN, Q_DIM, FFN_DIM):
+            x16 = torch.from_numpy(synth.gen_activations(Mr, K_, 4200 + K_ + rank).view(np.uint16).copy()).to(dev)
+            acts[K_] = (qact(x16, Mr, K_, synth.TYPE_Q5_K)[0], qact(x16, Mr, K_, synth.TYPE_Q8_0)[1])
+        outs = {n: torch.zeros((Mr, r), dtype=torch.float16, device=dev) for (n, t, r, k) in layout}
+        groups = [(["q", "k", "v"], HIDDEN), (["o"], Q_DIM), (["gate", "up"], HIDDEN), (["down"], FFN_DIM)]
+        task_sets = [[(ctx.make_tasks([dict(w=lay[n], dst=outs[n]) for n in names]), K_) for names, K_ in groups]
+                     for lay in layers]
+        hid = torch.from_numpy(synth.gen_activations(Mr, HIDDEN, 4300 + rank).view(np.uint16).copy()).to(dev)
+        hid_all = torch.zeros((SEQ, HIDDEN), dtype=torch.int16, device=dev)
+        toks = torch.zeros((SEQ,), dtype=torch.int32, device=dev)
+        vals = torch.zeros((SEQ,), dtype=torch.float32, device=dev)
+        pair = torch.zeros((SEQ, 2), dtype=torch.float32, device=dev)
+        pair_all = torch.zeros((world, SEQ, 2), dtype=torch.float32, device=dev)
+
+        def step(i):
+            for ts in task_sets:
+                for tasks, K_ in ts:
+                    ctx.gemm_multi_q8_async(acts[K_][0], acts[K_][1], Mr, K_, tasks)
+            if world > 1:
+                dist.all_gather_into_tensor(hid_all, hid.view(torch.int16))
+            else:
+                hid_all.copy_(hid.view(torch.int16))
+            ctx.lm_head_argmax_async(lm, hid_all, SEQ, None, None, toks, vals)
+            if world > 1:
+                pair[:, 0] = vals
+                pair[:, 1] = (toks + v0).float()
+                dist.all_gather_into_tensor(pair_all, pair)
+
+        steps = args.steps
+        dt, clocks = time_device(stream, step, steps, max(3, args.warmup), gpu, graph=False, world=world)
+        value = SEQ * steps / dt
+        wbytes = sum(h.nbytes for h in host.values()) * L + lm.device_bytes
+        cpu = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            from oracle.oracle import Oracle
+            O = Oracle()
+            rows_s, Ms = 128, 8
+            t_layer = 0.0
+            for (n, t, r, k) in layout:
+                a_ = O.act_for(t, synth.gen_activations(Ms, k, 4400))
+                t0 = time.perf_counter()
+                O.gemm(t, host[n][:rows_s], k, a_)
+                t_layer += (time.perf_counter() - t0) * r / rows_s
+            cpu = {"value": round(Ms / (t_layer * L), 4), "unit": "tok/s", "cores": 1, "kind": "port",
+                   "sample": f"first {rows_s} rows of each matrix of one layer at {Ms} tokens through the oracle "
+                             f"(1 thread), scaled to full rows and {L} layers; LM head not included"}
+        if rank == 0:
+            result = {
+                "metric": METRIC_DECODE, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
+                "warmup": max(3, args.warmup), "ms_per_step": round(dt / steps * 1e3, 4), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic (seeded GGUF blocks per BASELINE distributions; activations N(0,1))",
+                "config": {"workload": f"config4: {SEQ} sequences x 1 token, {L}-layer stack (q/o/gate/up Q5_K, "
+                                       f"k/v/down Q8_0) + Q6_K LM head {VOCAB}x{HIDDEN} vocab-sharded",
+                           "rows_per_rank": Mr, "layers": L, "weight_bytes_per_step_per_rank": wbytes,
+                           "parallelism": f"batch-split x{world}, LM head vocab-split + NCCL all-gathers",
+                           "timing": "eager launches per step, CUDA events, max over ranks"},
+                "roofline": {"bound": "hbm", "achieved": round(wbytes * steps / dt / 1e9, 1), "peak": peak_hbm,
+                             "unit": "GB/s", "frac": round(wbytes * steps / dt / 1e9 / peak_hbm, 4),
+                             "peak_source": peak_kind, "traffic": None},
+                "cpu_baseline": cpu, "clocks": clocks, "e2e": None,
+                "gpu_launches": None,
+            }
+        for lay in layers:
+            for w_ in lay.values():
+                w_.free()
+        lm.free()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def measured_bf16():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"])
+    return 1590.0
+
+
 # ---------------------------------------------------------------------------- reference arm
 
 def run_reference(args, rank, world):
     if rank != 0:
         return None
+    if args.config not in ("gemv", "lm_head"):
+        return {"impl": "reference", "unavailable": "the reference arm times configs 0 and 1; the stack configs carry "
+                                                   "their CPU sample in cpu_baseline"}
     from npu880_mtk_npu_llm_runtime_b200 import synth
     gtype = synth.TYPE_Q4_K if args.config == "gemv" else synth.TYPE_Q6_K
     n_rows = 9728 if args.config == "gemv" else 151936
@@ -390,10 +715,12 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300000)
+    ap.add_argument("--steps", type=int, default=STEPS_DEFAULT)
     ap.add_argument("--warmup", type=int, default=300)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["gemv", "lm_head"], default="gemv")
+    ap.add_argument("--config", choices=["gemv", "lm_head", "ffn", "prefill", "decode"], default="gemv")
+    ap.add_argument("--m", type=int, default=0, help="tokens (ffn: 8/16/32/64, prefill: 512/2048)")
+    ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=30.0)
@@ -404,6 +731,11 @@ def main():
     local_rank = env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
         res = run_reference(args, rank, world)
+    elif args.config in ("ffn", "prefill", "decode"):
+        if args.steps == STEPS_DEFAULT:  # the GEMV default is far too many steps for a whole block or stack
+            args.steps = {"ffn": 2000, "prefill": 3, "decode": 20}[args.config]
+            args.warmup = min(args.warmup, 3)
+        res = run_stack(args, rank, world, local_rank)
     else:
         res = run_ours(args, rank, world, local_rank)
     if rank == 0 and res is not None:
