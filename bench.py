@@ -184,7 +184,7 @@ def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
     import npu880_mtk_npu_llm_runtime_b200 as kq
-    from npu880_mtk_npu_llm_runtime_b200 import build as kqbuild, synth
+    from npu880_mtk_npu_llm_runtime_b200 import build as kqbuild, shard, synth
 
     kqbuild.build()
     torch.cuda.set_device(local_rank)
@@ -203,9 +203,7 @@ def run_ours(args, rank, world, local_rank):
         metric = METRIC_GEMV
     else:
         gtype, N, K = kq.TYPE_Q6_K, 151936, 2560
-        rows_local = (N + world - 1) // world
-        row0 = rank * rows_local
-        rows_local = max(0, min(N, row0 + rows_local) - row0)
+        row0, rows_local = shard.vocab_slice(rank, world, N)
         metric = METRIC_LM
     w_host = synth.gen_weights(gtype, N, K, seed=1234)[row0:row0 + rows_local]
     x_host = synth.gen_activations(1, K, seed=1235)
@@ -429,7 +427,7 @@ def run_stack(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
     import npu880_mtk_npu_llm_runtime_b200 as kq
-    from npu880_mtk_npu_llm_runtime_b200 import build as kqbuild, synth
+    from npu880_mtk_npu_llm_runtime_b200 import build as kqbuild, shard, synth
 
     kqbuild.build()
     torch.cuda.set_device(local_rank)
@@ -597,9 +595,7 @@ def run_stack(args, rank, world, local_rank):
         layout = stack_layout("decode")
         host = {n: synth.gen_weights(t, r, k, 4000 + i) for i, (n, t, r, k) in enumerate(layout)}
         layers = [{n: ctx.upload(host[n], t, r, k) for (n, t, r, k) in layout} for _ in range(L)]
-        vchunk = (VOCAB + world - 1) // world
-        v0 = rank * vchunk
-        vrows = max(0, min(VOCAB, v0 + vchunk) - v0)
+        v0, vrows = shard.vocab_slice(rank, world, VOCAB)
         lm = ctx.upload(synth.gen_weights(synth.TYPE_Q6_K, VOCAB, HIDDEN, 4100)[v0:v0 + vrows], synth.TYPE_Q6_K, vrows, HIDDEN)
         acts = {}
         for K_ in (HIDDEN, Q_DIM, FFN_DIM):
@@ -610,7 +606,7 @@ def run_stack(args, rank, world, local_rank):
         task_sets = [[(ctx.make_tasks([dict(w=lay[n], dst=outs[n]) for n in names]), K_) for names, K_ in groups]
                      for lay in layers]
         hid = torch.from_numpy(synth.gen_activations(Mr, HIDDEN, 4300 + rank).view(np.uint16).copy()).to(dev)
-        hid_all = torch.zeros((SEQ, HIDDEN), dtype=torch.int16, device=dev)
+        hid_all = torch.zeros((SEQ, HIDDEN), dtype=torch.float16, device=dev)
         toks = torch.zeros((SEQ,), dtype=torch.int32, device=dev)
         vals = torch.zeros((SEQ,), dtype=torch.float32, device=dev)
         pair = torch.zeros((SEQ, 2), dtype=torch.float32, device=dev)
@@ -621,9 +617,9 @@ def run_stack(args, rank, world, local_rank):
                 for tasks, K_ in ts:
                     ctx.gemm_multi_q8_async(acts[K_][0], acts[K_][1], Mr, K_, tasks)
             if world > 1:
-                dist.all_gather_into_tensor(hid_all, hid.view(torch.int16))
+                dist.all_gather_into_tensor(hid_all, hid.view(torch.float16))
             else:
-                hid_all.copy_(hid.view(torch.int16))
+                hid_all.copy_(hid.view(torch.float16))
             ctx.lm_head_argmax_async(lm, hid_all, SEQ, None, None, toks, vals)
             if world > 1:
                 pair[:, 0] = vals

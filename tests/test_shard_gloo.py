@@ -1,0 +1,92 @@
+"""Vocabulary-sharded LM head on two CPU ranks (torch.distributed gloo): every rank computes the
+logits of its slice with the oracle, reduces it to per-row (value, row) pairs and the pairs are
+all-gathered and merged.  The result must equal the single-process scan of the whole vocabulary
+(the reference's first-maximal-row rule), including a tie planted across the slice boundary."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from npu880_mtk_npu_llm_runtime_b200 import shard, synth
+
+
+def test_vocab_slices_cover_exactly():
+    for vocab in (1, 7, 151936):
+        for world in (1, 2, 3, 4, 8):
+            spans = [shard.vocab_slice(r, world, vocab) for r in range(world)]
+            covered = []
+            for first, n in spans:
+                covered.extend(range(first, first + n))
+            assert covered == list(range(vocab))
+
+
+def test_merge_argmax_rules():
+    vals = np.array([[1.0, 5.0, -np.inf], [3.0, 5.0, 2.0]], np.float32)
+    rows = np.array([[10, 20, -1], [30, 7, 40]], np.int64)
+    r, v = shard.merge_argmax(vals, rows)
+    assert r.tolist() == [30, 7, 40] and v.tolist() == [3.0, 5.0, 2.0]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    from oracle.oracle import Oracle
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        V, K, M = 200, 256, 3
+        w = synth.gen_weights(synth.TYPE_Q6_K, V, K, seed=61)
+        x = synth.gen_activations(M, K, seed=62)
+        O = Oracle()
+        act = O.quantize_q8k(x)
+        first, n = shard.vocab_slice(rank, world, V)
+        logits = O.gemm(synth.TYPE_Q6_K, w[first:first + n], K, act)  # [M, n] fp32
+        if rank == 1:
+            logits[0, 0] = 1e9  # a tie with rank 0 below: the smaller global row must win
+        if rank == 0:
+            logits[0, n - 1] = 1e9
+        i = logits.argmax(axis=1)  # first maximal row of the slice
+        vals = torch.from_numpy(logits[np.arange(M), i].astype(np.float32))
+        rows = torch.from_numpy((i + first).astype(np.int64))
+        r, v = shard.gather_argmax_torch(vals, rows)
+        q.put((rank, r.tolist(), v.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_lm_head_gloo():
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    got = [q.get(timeout=10) for _ in range(world)]
+    # the single-process scan of the whole vocabulary with the same planted values
+    from oracle.oracle import Oracle
+    V, K, M = 200, 256, 3
+    w = synth.gen_weights(synth.TYPE_Q6_K, V, K, seed=61)
+    O = Oracle()
+    act = O.quantize_q8k(synth.gen_activations(M, K, seed=62))
+    full = O.gemm(synth.TYPE_Q6_K, w, K, act)
+    half = shard.vocab_slice(1, world, V)[0]
+    full[0, half] = 1e9
+    full[0, half - 1] = 1e9
+    ref_rows = full.argmax(axis=1).tolist()
+    ref_vals = full[np.arange(M), full.argmax(axis=1)].tolist()
+    for _, r, v in got:
+        assert r == ref_rows and np.allclose(v, ref_vals, rtol=0, atol=0)
