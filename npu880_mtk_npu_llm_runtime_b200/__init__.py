@@ -232,9 +232,16 @@ class Context:
     def sdot_gemm_multi_dispatch(self, x16: np.ndarray, tasks):
         """sdot_gemm_multi_dispatch (ENG:4188) with host arrays.  tasks: list of dicts with keys
         w (Weight), dst (fp16 [M, stride] or None), residual (fp16 or None), dst_f32 (fp32 or None),
-        row_begin (default 0), rows (default w.rows).  Outputs are written in place."""
+        row_begin (default 0), rows (default w.rows), or an array made once by make_host_tasks for
+        calls that repeat.  Outputs are written in place."""
         x16 = np.ascontiguousarray(x16, dtype=np.float16)
         M, K = x16.shape
+        arr = tasks if isinstance(tasks, C.Array) else self.make_host_tasks(tasks)
+        self.check(self.L.kq_sdot_gemm_multi_dispatch(self.handle, _hp(x16), M, K, arr, len(arr)))
+
+    @staticmethod
+    def make_host_tasks(tasks):
+        """kq_task array over HOST arrays (the arrays must outlive every call that uses it)"""
         arr = (Task * len(tasks))()
         for i, t in enumerate(tasks):
             w = t["w"]
@@ -246,7 +253,7 @@ class Context:
                 if a is not None:
                     setattr(arr[i], key, _hp(a))
                     setattr(arr[i], skey, a.shape[1])
-        self.check(self.L.kq_sdot_gemm_multi_dispatch(self.handle, _hp(x16), M, K, arr, len(tasks)))
+        return arr
 
     def sdot_row_batch(self, w: Weight, row: int, M: int) -> np.ndarray:
         out = np.zeros(M, dtype=np.float32)

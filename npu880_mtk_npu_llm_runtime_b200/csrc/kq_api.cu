@@ -31,6 +31,7 @@ struct kq_ctx {
     int num_sms = 0;
     int gemm_path = 0;           // M > 8: 0 auto, 1 tensor cores, 2 GEMV in tiles of 8 tokens
     int *d_status = nullptr;     // device-side error word
+    int *h_status = nullptr;     // pinned host copy of it, read after the blocking calls' one sync
     bool pdl = true;
     bool inject_timeout = false;  // test hook: GEMV consumers wait on a barrier nothing completes
     unsigned long long timeout_ns = 1000000000ull;
@@ -91,26 +92,26 @@ int ensure(kq_ctx *c, DevBuf &b, size_t bytes) {
     return KQ_OK;
 }
 
-// Read and clear the device status word after the stream drained.
-int check_device_status(kq_ctx *c) {
-    int st = 0;
-    cudaError_t e = cudaMemcpyAsync(&st, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
-    if (e != cudaSuccess) return cuda_fail(c, e, "status readback");
-    if (st != kq::DEV_OK) {
-        cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream);
-        cudaStreamSynchronize(c->stream);
-        if (st == kq::DEV_ERR_TIMEOUT) return fail(c, KQ_ERR_TIMEOUT, "a device-side wait timed out");
-        return fail(c, KQ_ERR_CUDA, "device error code %d", st);
-    }
-    return KQ_OK;
+// Read and clear the device status word after the stream drained (blocking calls copy it into
+// pinned host memory on their stream first, so one synchronize covers the work and the status).
+int status_result(kq_ctx *c) {
+    const int st = *c->h_status;
+    if (st == kq::DEV_OK) return KQ_OK;
+    *c->h_status = kq::DEV_OK;
+    cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream);
+    cudaStreamSynchronize(c->stream);
+    if (st == kq::DEV_ERR_TIMEOUT) return fail(c, KQ_ERR_TIMEOUT, "a device-side wait timed out");
+    return fail(c, KQ_ERR_CUDA, "device error code %d", st);
 }
 
-int sync_and_check(kq_ctx *c) {
-    cudaError_t e = cudaStreamSynchronize(c->stream);
-    if (e != cudaSuccess) return cuda_fail(c, e, "cudaStreamSynchronize");
-    return check_device_status(c);
+int check_device_status(kq_ctx *c) {
+    cudaError_t e = cudaMemcpyAsync(c->h_status, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, e, "status readback");
+    return status_result(c);
 }
+
+int sync_and_check(kq_ctx *c) { return check_device_status(c); }
 
 int validate_task(kq_ctx *c, const kq_task &t, int K) {
     if (!t.w) return fail(c, KQ_ERR_INVALID_ARGUMENT, "task weight is NULL");
@@ -292,6 +293,14 @@ int current_act(kq_ctx *c, uint32_t type, const void **act) {
     return KQ_OK;
 }
 
+// Strided row copy; one linear copy when the rows are contiguous on both sides (cheaper to issue).
+cudaError_t copy_rows(void *dst, size_t dpitch, const void *src, size_t spitch, size_t width, size_t height,
+                      cudaMemcpyKind kind, cudaStream_t s) {
+    if (height == 1 || (dpitch == width && spitch == width))
+        return cudaMemcpyAsync(dst, src, width * height, kind, s);
+    return cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, kind, s);
+}
+
 int h2d(kq_ctx *c, DevBuf &b, const void *src, size_t bytes) {
     int r = ensure(c, b, bytes);
     if (r) return r;
@@ -344,9 +353,11 @@ extern "C" int kq_init(int device, kq_ctx **out) {
     }
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&c->d_status, sizeof(int)) != cudaSuccess ||
-        cudaMemset(c->d_status, 0, sizeof(int)) != cudaSuccess) {
+        cudaMemset(c->d_status, 0, sizeof(int)) != cudaSuccess ||
+        cudaMallocHost(&c->h_status, sizeof(int)) != cudaSuccess) {
         if (c->stream) cudaStreamDestroy(c->stream);
         cudaFree(c->d_status);
+        if (c->h_status) cudaFreeHost(c->h_status);
         delete c;
         return KQ_ERR_CUDA;
     }
@@ -363,6 +374,7 @@ extern "C" int kq_destroy(kq_ctx *c) {
                       &c->misc, &c->keys, &c->tcpack})
         if (b->p) cudaFree(b->p);
     cudaFree(c->d_status);
+    cudaFreeHost(c->h_status);
     if (c->own_stream) cudaStreamDestroy(c->stream);
     delete c;
     return KQ_OK;
@@ -611,7 +623,7 @@ extern "C" int kq_sdot_gemm_multi_dispatch(kq_ctx *c, const uint16_t *x, int M, 
         }
         if (tasks[i].residual) {
             uint16_t *rd = reinterpret_cast<uint16_t *>((uint8_t *)c->res.p + offr[i]);
-            KQ_CUDA(c, cudaMemcpy2DAsync(rd, rows * 2, tasks[i].residual, tasks[i].res_stride * 2, rows * 2, M,
+            KQ_CUDA(c, copy_rows(rd, rows * 2, tasks[i].residual, tasks[i].res_stride * 2, rows * 2, M,
                                          cudaMemcpyHostToDevice, c->stream));
             dt[i].residual = rd;
             dt[i].res_stride = rows;
@@ -644,10 +656,10 @@ extern "C" int kq_sdot_gemm_multi_dispatch(kq_ctx *c, const uint16_t *x, int M, 
     for (int i = 0; i < n; ++i) {
         const size_t rows = (size_t)tasks[i].rows;
         if (tasks[i].dst)
-            KQ_CUDA(c, cudaMemcpy2DAsync(tasks[i].dst, tasks[i].dst_stride * 2, dt[i].dst, rows * 2, rows * 2, M,
+            KQ_CUDA(c, copy_rows(tasks[i].dst, tasks[i].dst_stride * 2, dt[i].dst, rows * 2, rows * 2, M,
                                          cudaMemcpyDeviceToHost, c->stream));
         if (tasks[i].dst_f32)
-            KQ_CUDA(c, cudaMemcpy2DAsync(tasks[i].dst_f32, tasks[i].dst_f32_stride * 4, dt[i].dst_f32, rows * 4,
+            KQ_CUDA(c, copy_rows(tasks[i].dst_f32, tasks[i].dst_f32_stride * 4, dt[i].dst_f32, rows * 4,
                                          rows * 4, M, cudaMemcpyDeviceToHost, c->stream));
     }
     return sync_and_check(c);
