@@ -11,8 +11,9 @@
 // epilogue:
 //   Q4_K / Q5_K   sc = 8 sh + sl:  A0 = q * sh, A1 = q * sl (u8), A2 = the row's min m_j over
 //                 its sub-block (u8);  sumi = 8 D0 + D1, summ = D2 (= sum_j m_j * bsum_j)
-//   Q6_K          q = 16 q2 + 4 q1 + q0 (2-bit pieces): A_i = sc * q_i (s8), A3 = sc (s8);
-//                 sumi = 16 D2 + 4 D1 + D0 - 32 D3  (= sum_s sc_s * sum_l (q_l - 32) x_l)
+//   Q6_K          q - 32 = 8 qa + qb (qa in -4..3, qb in 0..7), sc = 16 sh + sl (sh in -8..7,
+//                 sl in 0..15; any int8 scale): A0 = sl qb, A1 = sl qa, A2 = sh qb, A3 = sh qa
+//                 (s8); sumi = D0 + 8 D1 + 16 D2 + 128 D3  (= sum_s sc_s * sum_l (q_l - 32) x_l)
 //   Q8_0          A = the quants (s8); one MMA per 32-value block into its own accumulator
 // D_i are int32 per (row, token) in TMEM.
 //
@@ -115,12 +116,20 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// per-byte negation of bytes in [0, 128]
-__device__ __forceinline__ uint32_t neg_bytes(uint32_t v) { return (0x80808080u - v) ^ 0x80808080u; }
-// bytes of t (each 0..3) times a signed scale in [-32, 31], as int8
-__device__ __forceinline__ uint32_t smul_bytes(uint32_t t, int sc) {
-    const uint32_t u = t * (uint32_t)(sc < 0 ? -sc : sc);
-    return sc < 0 ? neg_bytes(u) : u;
+// per-byte a - b as int8, for bytes a in [0, 127] and b in [0, 128] (no borrow crosses a byte)
+__device__ __forceinline__ uint32_t sub_bytes(uint32_t a, uint32_t b) { return ((a | 0x80808080u) - b) ^ 0x80808080u; }
+// Q6_K operand bytes of one word of four 6-bit quants q: (q - 32) * sc split as in the header,
+// for any int8 scale sc.  All products stay within int8 (|A| <= 105).
+__device__ __forceinline__ void q6_pieces(uint32_t q, int sc, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
+    const uint32_t qb = q & 0x07070707u, qa4 = (q >> 3) & 0x07070707u;  // qa4 = qa + 4
+    const uint32_t sl = (uint32_t)(sc & 15);
+    const int sh = sc >> 4;
+    const uint32_t ash = (uint32_t)(sh < 0 ? -sh : sh);
+    a0 = qb * sl;
+    a1 = sub_bytes(qa4 * sl, 0x01010101u * (4u * sl));
+    const uint32_t pb = qb * ash, pa = qa4 * ash, r4 = 0x01010101u * (4u * ash);
+    a2 = sh < 0 ? sub_bytes(0u, pb) : pb;                        // sh * qb
+    a3 = sh < 0 ? sub_bytes(r4, pa) : sub_bytes(pa, r4);         // sh * qa = |sh| (4 - qa4) or |sh| (qa4 - 4)
 }
 
 // ---- A operands of one super-block: half hs (values 128 hs .. 128 hs + 127) of row r, from the
@@ -196,18 +205,13 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, int hs, ui
                         else q[i] = ((bv[i] >> 4) & 0x0F0F0F0Fu) | ((hv[i] >> 2) & 0x30303030u);
                     }
                     const uint32_t o = canon256(r, s);  // sub-block s = 16-byte chunk s
-                    uint32_t p0[4], p1[4], p2[4];
+                    uint32_t p0[4], p1[4], p2[4], p3[4];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        p0[i] = smul_bytes(q[i] & 0x03030303u, sc);
-                        p1[i] = smul_bytes((q[i] >> 2) & 0x03030303u, sc);
-                        p2[i] = smul_bytes((q[i] >> 4) & 0x03030303u, sc);
-                    }
-                    const uint32_t srep = 0x01010101u * (uint32_t)(sc & 0xFF);
+                    for (int i = 0; i < 4; ++i) q6_pieces(q[i], sc, p0[i], p1[i], p2[i], p3[i]);
                     *reinterpret_cast<uint4 *>(A + o) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
                     *reinterpret_cast<uint4 *>(A + 32768 + o) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
                     *reinterpret_cast<uint4 *>(A + 65536 + o) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
-                    *reinterpret_cast<uint4 *>(A + 98304 + o) = make_uint4(srep, srep, srep, srep);
+                    *reinterpret_cast<uint4 *>(A + 98304 + o) = make_uint4(p3[0], p3[1], p3[2], p3[3]);
                 }
             }
         }
@@ -332,7 +336,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                     const float dx = dxs[i];
                     float t;
                     if (TYPE == TYPE_Q6_K) {
-                        const int sumi = 16 * (int)D[2][i] + 4 * (int)D[1][i] + (int)D[0][i] - 32 * (int)D[3][i];
+                        const int sumi = (int)D[0][i] + 8 * (int)D[1][i] + 16 * (int)D[2][i] + 128 * (int)D[3][i];
                         t = __fmul_rn(__fmul_rn(d, dx), __int2float_rn(sumi));
                     } else {
                         const int sumi = 8 * (int)D[0][i] + (int)D[1][i];

@@ -43,6 +43,11 @@ def _scale_f16(rng: np.random.Generator, n: int) -> np.ndarray:
     return np.abs(rng.normal(0.0, 1e-3, size=n)).astype(np.float16).view(np.uint8).reshape(n, 2)
 
 
+def _int8_draw(rng: np.random.Generator, span: tuple[int, int], shape) -> np.ndarray:
+    """int8 values uniform in [lo, hi) as bytes (hi <= 128)."""
+    return rng.integers(span[0], span[1], size=shape, dtype=np.int8).view(np.uint8)
+
+
 def pack_scale_min_k4(sc: np.ndarray, mn: np.ndarray) -> np.ndarray:
     """Inverse of get_scale_min_k4 (ENG:743-749): pack eight 6-bit scales and eight 6-bit mins
     per super-block into 12 bytes.  sc, mn: uint8 [..., 8] with values 0..63."""
@@ -57,8 +62,12 @@ def pack_scale_min_k4(sc: np.ndarray, mn: np.ndarray) -> np.ndarray:
     return out
 
 
-def gen_weights(gtype: int, rows: int, k: int, seed: int) -> np.ndarray:
-    """rows x k weights of GGUF type gtype as raw row-major block bytes: uint8[rows, row_bytes]."""
+def gen_weights(gtype: int, rows: int, k: int, seed: int, q6_scales: tuple[int, int] = (-32, 32),
+                q8_quants: tuple[int, int] = (-127, 128)) -> np.ndarray:
+    """rows x k weights of GGUF type gtype as raw row-major block bytes: uint8[rows, row_bytes].
+    q6_scales / q8_quants: [lo, hi) of the Q6_K sub-block scales and the Q8_0 quants; the
+    defaults are the benchmark distributions, (-128, 128) covers every value a GGUF file can hold
+    (the reference's Q6_K quantizer maps each block's largest scale to -128)."""
     if k % BLOCK_ELEMS[gtype]:
         raise ValueError(f"k={k} is not a multiple of the {TYPE_NAMES[gtype]} block size")
     rng = np.random.default_rng(seed)
@@ -76,11 +85,11 @@ def gen_weights(gtype: int, rows: int, k: int, seed: int) -> np.ndarray:
             blk[:, 16:176] = rng.integers(0, 256, size=(nb, 160), dtype=np.uint8)
     elif gtype == TYPE_Q6_K:
         blk[:, 0:192] = rng.integers(0, 256, size=(nb, 192), dtype=np.uint8)
-        blk[:, 192:208] = rng.integers(-32, 32, size=(nb, 16), dtype=np.int8).view(np.uint8)
+        blk[:, 192:208] = _int8_draw(rng, q6_scales, (nb, 16))
         blk[:, 208:210] = _scale_f16(rng, nb)
     elif gtype == TYPE_Q8_0:
         blk[:, 0:2] = _scale_f16(rng, nb)
-        blk[:, 2:34] = rng.integers(-127, 128, size=(nb, 32), dtype=np.int8).view(np.uint8)
+        blk[:, 2:34] = _int8_draw(rng, q8_quants, (nb, 32))
     else:
         raise ValueError(f"unsupported type {gtype}")
     return blk.reshape(rows, row_bytes(gtype, k))

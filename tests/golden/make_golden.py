@@ -65,6 +65,22 @@ def main() -> None:
                                                        act=act.view(np.uint8).reshape(M, -1),
                                                        out=out, lm_out=lm, dequant=deq)
 
+    # every value a GGUF file can hold: Q6_K scales over all of int8 (the reference's Q6_K
+    # quantizer maps each block's largest scale to -128) and Q8_0 quants including -128
+    for name, t, kw in [("q6_k_full", TYPE_Q6_K, dict(q6_scales=(-128, 128))),
+                        ("q8_0_full", TYPE_Q8_0, dict(q8_quants=(-128, 128)))]:
+        rows, K, M, seed = 16, 768, 3, 13
+        w = synth.gen_weights(t, rows, K, seed=1000 * t + seed, **kw)
+        x = edge_activations(M, K, seed=seed)
+        act = R.quantize_q8_0(x) if t == TYPE_Q8_0 else R.quantize_q8k(x)
+        out = R.gemm(t, w, K, act)
+        lm = np.array([R.lm_row_dot(t, w, K, act, r, 0) for r in range(rows)], dtype=np.float32) \
+            if t != TYPE_Q8_0 else np.zeros(0, np.float32)
+        deq = R.dequant(t, w, K)
+        cases[f"dot_{name}_{rows}x{K}_m{M}"] = dict(type=np.int32(t), K=np.int32(K), w=w, x=x,
+                                                   act=act.view(np.uint8).reshape(M, -1),
+                                                   out=out, lm_out=lm, dequant=deq)
+
     # sdot_gemm_multi_dispatch: two tasks sharing one input, fp16 output, residual on task 0
     K, M = 512, 3
     x = synth.gen_activations(M, K, 21)

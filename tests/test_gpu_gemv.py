@@ -44,6 +44,32 @@ def test_gemv_bitexact(kqctx, oracle, gtype, M, K):
     assert np.array_equal(bits(got), bits(ref)), f"max |diff| {np.abs(got - ref).max()}"
 
 
+FULL_RANGE = {kq.TYPE_Q6_K: dict(q6_scales=(-128, 128)), kq.TYPE_Q8_0: dict(q8_quants=(-128, 128))}
+
+
+@pytest.mark.parametrize("gtype", sorted(FULL_RANGE), ids=lambda t: synth.TYPE_NAMES[t])
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 9, 40])
+@pytest.mark.parametrize("path", [0, 1, 2])
+def test_full_range_values_bitexact(kqctx, oracle, gtype, M, path):
+    """Q6_K scales over all of int8 (real Q6_K blocks always hold -128 or 127: the quantizer maps
+    each block's largest scale there) and Q8_0 quants including -128, on every M > 8 path"""
+    if path and M <= 8:
+        pytest.skip("the M > 8 path choice does not apply")
+    rows, K = 150, 1024
+    w = synth.gen_weights(gtype, rows, K, seed=70 + M, **FULL_RANGE[gtype])
+    x = synth.gen_activations(M, K, seed=71 + M)
+    act = oracle.act_for(gtype, x)
+    kqctx.set_option("gemm_path", path)
+    W = kqctx.upload(w, gtype, rows, K)
+    try:
+        got = run_q8(kqctx, W, gtype, act, M, K, rows)
+    finally:
+        W.free()
+        kqctx.set_option("gemm_path", 0)
+    ref = oracle.gemm(gtype, w, K, act)
+    assert np.array_equal(bits(got), bits(ref)), f"max |diff| {np.abs(got - ref).max()}"
+
+
 @pytest.mark.parametrize("gtype", TYPES, ids=lambda t: synth.TYPE_NAMES[t])
 def test_block_sums_bitexact(kqctx, oracle, gtype):
     """per-super-block integer intermediates (sumi, summ) equal the reference's locals"""

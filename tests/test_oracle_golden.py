@@ -24,7 +24,7 @@ DOT_FILES = golden_files("dot_")
 
 
 def test_fixtures_present():
-    assert len(DOT_FILES) == 8, "golden fixtures missing: run tests/golden/make_golden.py"
+    assert len(DOT_FILES) == 10, "golden fixtures missing: run tests/golden/make_golden.py"
 
 
 @pytest.mark.parametrize("path", DOT_FILES, ids=[os.path.basename(p)[:-4] for p in DOT_FILES])
