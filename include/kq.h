@@ -81,7 +81,9 @@ const char *kq_last_error(const kq_ctx *ctx);
  * nothing completes, so the wait runs out, the kernel returns early and the call reports
  * KQ_ERR_TIMEOUT (default 0);
  * "gemm_path" -- products of more than 8 activation rows: 0 chooses by a cost model, 1 always
- * the tensor-core kernel (tcgen05), 2 always the GEMV kernel in tiles of 8 rows (default 0). */
+ * the weight-row-major tensor-core kernel (tcgen05; weight rows as the MMA's A operand), 2 always
+ * the GEMV kernel in tiles of 8 rows, 3 always the token-major tensor-core kernel (activation
+ * tokens as A in tensor memory, row groups spread over all SMs) (default 0). */
 int kq_set_option(kq_ctx *ctx, const char *name, long long value);
 
 /* compute_ggml_bytes / ggml_row_bytes (ENG:364-374, ENG:3940): bytes of one GGUF row of k

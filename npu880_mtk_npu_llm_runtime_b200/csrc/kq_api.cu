@@ -154,23 +154,36 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
         if (idx.empty()) continue;
         const void *act = (type == KQ_TYPE_Q8_0) ? act_q80 : act_q8k;
         if (!x && !act) return fail(c, KQ_ERR_NOT_READY, "no activation for type %d", type);
-        // M > 8: the tensor-core kernel, unless tiles of 8 tokens through the GEMV are expected to
-        // be faster.  Its CTAs (128 rows x 64 tokens) walk K serially, ~2.7 us per 256-value unit;
-        // the GEMV streams the weights once per 8 tokens at ~4 TB/s plus ~3 us per launch.
-        bool use_tc = M > 8 && !ex.dbg_sumi && !ex.argmax && !ex.out_ids;
-        if (use_tc) {
-            long long rows = 0;
+        // M > 8: one of two tensor-core kernels or GEMV tiles of 8 tokens, by a cost model fitted
+        // to B200 timings of the FFN and attention shapes (M = 9..512):
+        //  * weight-row-major tensor-core kernel (kq_gemm_tc.cu, 128 rows x 64 tokens per CTA,
+        //    all of K serially): ~2.8 us per 256-value unit (Q6_K ~4.2 us) per wave of CTAs;
+        //  * token-major kernel (row groups spread over all SMs): ~3.5 us per item (a unit of
+        //    up to 4 row groups, Q6_K 3) per wave;
+        //  * GEMV tiles: the weights streamed once per 8 tokens at ~1 TB/s plus ~5 us a launch.
+        int tc_kernel = 0;  // 0 GEMV tiles, 1 row-major, 3 token-major
+        if (M > 8 && !ex.dbg_sumi && !ex.argmax && !ex.out_ids) {
+            long long rows = 0, rgs = 0;
             double wbytes = 0.0;
             for (int j : idx) {
                 rows += tasks[j].rows;
+                rgs += (tasks[j].row_begin + tasks[j].rows - 1) / 16 - tasks[j].row_begin / 16 + 1;
                 wbytes += (double)tasks[j].rows * (double)tasks[j].w->row_bytes;
             }
+            const int nbu = K / 256, sms = c->num_sms;
             const int bn = (type == KQ_TYPE_Q8_0) ? 32 : 64;
-            const long long ctas = ((M + bn - 1) / bn) * ((rows + 127) / 128);
-            const double t_tc = (double)((ctas + c->num_sms - 1) / c->num_sms) * (K / 256) * 2.7e-6;
-            const double t_gemv = (double)((M + 7) / 8) * (wbytes / 4.0e12 + 3.0e-6);
-            use_tc = c->gemm_path == 1 || (c->gemm_path == 0 && t_tc <= t_gemv);
+            const long long ctas1 = ((M + bn - 1) / bn) * ((rows + 127) / 128);
+            const double t1 = (double)((ctas1 + sms - 1) / sms) * nbu * (type == KQ_TYPE_Q6_K ? 4.2e-6 : 2.8e-6);
+            const int n_tb = (M + 127) / 128, g = (type == KQ_TYPE_Q6_K) ? 3 : (type == KQ_TYPE_Q8_0) ? 1 : 4;
+            const int rgmax = (type == KQ_TYPE_Q6_K) ? 6 : 8;
+            const long long gx = std::min<long long>(rgs, std::max<long long>((sms + n_tb - 1) / n_tb, (rgs + rgmax - 1) / rgmax));
+            const long long rg_cta = (rgs + gx - 1) / gx;
+            const double t3 = (double)((gx * n_tb + sms - 1) / sms) * nbu * ((rg_cta + g - 1) / g) * 3.5e-6;
+            const double tg = (double)((M + 7) / 8) * (wbytes / 1.0e12 + 5.0e-6);
+            if (c->gemm_path == 1 || c->gemm_path == 3) tc_kernel = c->gemm_path;
+            else if (c->gemm_path == 0) tc_kernel = (tg <= std::min(t1, t3)) ? 0 : (t1 <= t3 ? 1 : 3);
         }
+        const bool use_tc = tc_kernel != 0;
         if (use_tc) {
             // many tokens: the tensor-core kernel (activation packed into the context's buffer)
             kq::TcLaunch T{};
@@ -194,12 +207,15 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
             T.x = x;
             T.x_stride = x_stride;
             T.act = x ? nullptr : act;
-            T.scratch_bytes = kq::tc_scratch_bytes(type, M, K);
+            const bool tc2 = tc_kernel == 3;
+            T.scratch_bytes = tc2 ? kq::tc2_scratch_bytes(type, M, K) : kq::tc_scratch_bytes(type, M, K);
             if (int r = ensure(c, c->tcpack, T.scratch_bytes)) return r;
             T.scratch = c->tcpack.p;
             T.status = c->d_status;
             T.timeout_ns = c->timeout_ns;
-            if (cudaError_t e = kq::launch_gemm_tc(T, c->stream)) return cuda_fail(c, e, "tensor-core gemm launch");
+            T.num_sms = c->num_sms;
+            if (cudaError_t e = tc2 ? kq::launch_gemm_tc2(T, c->stream) : kq::launch_gemm_tc(T, c->stream))
+                return cuda_fail(c, e, "tensor-core gemm launch");
             continue;
         }
         int m0 = 0;
@@ -420,7 +436,7 @@ extern "C" int kq_set_option(kq_ctx *c, const char *name, long long value) {
         return KQ_OK;
     }
     if (!strcmp(name, "gemm_path")) {
-        if (value < 0 || value > 2) return fail(c, KQ_ERR_INVALID_ARGUMENT, "gemm_path must be 0, 1 or 2");
+        if (value < 0 || value > 3) return fail(c, KQ_ERR_INVALID_ARGUMENT, "gemm_path must be 0..3");
         c->gemm_path = (int)value;
         return KQ_OK;
     }

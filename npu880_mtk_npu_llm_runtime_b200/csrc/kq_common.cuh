@@ -147,6 +147,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     }
 }
 
+// Bounded wait that sleeps between polls (suspend-time hint): for kernels whose roles wait on one
+// another most of the time, so that waiting warps leave the issue slots to the working ones.
+__device__ __forceinline__ bool mbar_wait_bounded_sleep(uint32_t bar, uint32_t parity, uint64_t timeout_ns,
+                                                        int *status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        for (int i = 0; i < 8; ++i)
+            if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
+        if (global_timer_ns() - t0 > timeout_ns) {
+            if (status) atomicExch(status, DEV_ERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
 // 1-D bulk copy global -> shared (TMA engine), completion counted on an mbarrier.
 // dst, src and bytes must be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,

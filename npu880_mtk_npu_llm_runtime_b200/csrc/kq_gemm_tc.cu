@@ -135,7 +135,7 @@ __device__ __forceinline__ void q6_pieces(uint32_t q, int sc, uint32_t &a0, uint
 // ---- A operands of one super-block: half hs (values 128 hs .. 128 hs + 127) of row r, from the
 // row's tile bytes.  Also returns what the epilogue needs of the row: d (and dmin).
 
-template <int TYPE>
+template <int TYPE, unsigned OPS = 32768u>
 __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, int hs, uint8_t *A, int r, float &d0, float &d1) {
     if (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K) {
         constexpr int RB = (TYPE == TYPE_Q4_K) ? 144 : 176, QS = (TYPE == TYPE_Q4_K) ? 16 : 48;
@@ -172,8 +172,8 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, int hs, ui
                     const uint32_t o = canon256(r, 2 * j + h16);
                     const uint32_t *qq = q + 4 * h16;
                     *reinterpret_cast<uint4 *>(A + o) = make_uint4(qq[0] * sh, qq[1] * sh, qq[2] * sh, qq[3] * sh);
-                    *reinterpret_cast<uint4 *>(A + 32768 + o) = make_uint4(qq[0] * sl, qq[1] * sl, qq[2] * sl, qq[3] * sl);
-                    *reinterpret_cast<uint4 *>(A + 65536 + o) = make_uint4(mrep, mrep, mrep, mrep);
+                    *reinterpret_cast<uint4 *>(A + OPS + o) = make_uint4(qq[0] * sl, qq[1] * sl, qq[2] * sl, qq[3] * sl);
+                    *reinterpret_cast<uint4 *>(A + 2 * OPS + o) = make_uint4(mrep, mrep, mrep, mrep);
                 }
             }
         }
@@ -209,9 +209,9 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, int hs, ui
 #pragma unroll
                     for (int i = 0; i < 4; ++i) q6_pieces(q[i], sc, p0[i], p1[i], p2[i], p3[i]);
                     *reinterpret_cast<uint4 *>(A + o) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
-                    *reinterpret_cast<uint4 *>(A + 32768 + o) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
-                    *reinterpret_cast<uint4 *>(A + 65536 + o) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
-                    *reinterpret_cast<uint4 *>(A + 98304 + o) = make_uint4(p3[0], p3[1], p3[2], p3[3]);
+                    *reinterpret_cast<uint4 *>(A + OPS + o) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+                    *reinterpret_cast<uint4 *>(A + 2 * OPS + o) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
+                    *reinterpret_cast<uint4 *>(A + 3 * OPS + o) = make_uint4(p3[0], p3[1], p3[2], p3[3]);
                 }
             }
         }
@@ -574,12 +574,626 @@ cudaError_t launch_tc_t(const TcLaunch &L, cudaStream_t stream) {
     return cudaSuccess;
 }
 
+
+// ================================================================== token-major kernel
+//
+// For up to 128 tokens per CTA the roles are swapped: the activation quants of one 256-value
+// unit are the MMA's A operand (M = 128 token lanes, written to tensor memory with tcgen05.st,
+// 64 columns), and the byte-split weight operands of a group of G row groups are the B operand
+// in shared memory (N = G x NOP x 16 rows, K-major).  A CTA owns a contiguous range of row groups
+// (like the GEMV) and walks the units in order, so every (row, token) adds its block terms in
+// block order in the registers of the thread that owns the token's lane.
+//
+// Items i = (unit u, group of G row groups) in unit-major order flow through four roles:
+//   warp 12    producer: activation unit u (quants + scales) and the group's weight tiles (cp.async.bulk)
+//   warps 8-11 build the B operand of item i (one row group each; Q8_0 items round-robin)
+//   warp 13    issues the item's MMAs (converged warp, one elected lane) and commits
+//   warps 0-7  write activation units into TMEM (0-3, one lane quadrant each) and run the
+//              epilogue: warp w reads lane quadrant w % 4 for the row groups c of the chunk with
+//              c % 2 == w / 4.
+// One MMA accumulator chain per item: N = 192 (Q4_K/Q5_K 4 x 48, Q6_K 3 x 64) keeps the tensor
+// core near its peak rate; Q8_0 items are one row group with eight independent 32-block chains.
+// TMEM: columns [0, 128) two activation buffers, [128, 512) SD item accumulators.
+
+template <int TYPE>
+struct Tc2Cfg {
+    static constexpr int NOP = (TYPE == TYPE_Q6_K) ? 4 : (TYPE == TYPE_Q8_0) ? 1 : 3;
+    static constexpr int G = (TYPE == TYPE_Q6_K) ? 3 : (TYPE == TYPE_Q8_0) ? 1 : 4;  // row groups per item
+    static constexpr int NMMA = (TYPE == TYPE_Q8_0) ? 16 : G * NOP * 16;              // N of one MMA
+    static constexpr int NCOL = (TYPE == TYPE_Q8_0) ? 128 : NMMA;                     // D columns per item
+    static constexpr int SD = 384 / NCOL;                                             // accumulator slots (2, Q8_0 3)
+    static constexpr int SB = SD;                                                     // B operand slots
+    static constexpr int SH = 4;                                                      // header slots
+    static constexpr int RGMAX_C = (TYPE == TYPE_Q6_K) ? 6 : 8;                      // row groups per chunk
+    static constexpr unsigned BSLOT = (unsigned)(G * NOP) * 4096u;                    // 16 rows x 256 B per operand
+    static constexpr unsigned HDR = (unsigned)G * 256u;                               // per-row scales of an item
+    static constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;
+    static constexpr int SW = 4, SA = 2;
+    static constexpr unsigned TB = (unsigned)tile_bytes(TYPE);
+    static constexpr unsigned WSLOT = (unsigned)G * TB;
+    static constexpr unsigned AROW = 272u;  // padded token row: conflict-free 16-byte reads
+    static constexpr unsigned AQ = 128u * AROW;
+    static constexpr unsigned ASLOT = AQ + 128u * DX * 4u;
+    static constexpr unsigned OFF_H = SB * BSLOT;
+    static constexpr unsigned OFF_A = OFF_H + SH * HDR;
+    static constexpr unsigned OFF_W = OFF_A + SA * ASLOT;
+    static constexpr unsigned SMEM = OFF_W + SW * WSLOT + 1024;
+    // b_fmt: Q5_K operands reach 217 (u8), all others fit s8; a_fmt s8 (activation quants)
+    static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | ((TYPE == TYPE_Q5_K) ? 0u : (1u << 10)) |
+                                      ((uint32_t)(NMMA >> 3) << 17) | ((128u >> 4) << 24);
+};
+constexpr int kTc2Threads = 14 * 32;
+
+struct Tc2Task {
+    const uint8_t *w;
+    int rg_first, rg_start, n_rg;  // tiled row group of the task's first row, its first launch row group, count
+    int row_begin, rows;
+    __half *dst;
+    long long dst_stride;
+    const __half *res;
+    long long res_stride;
+    float *dst_f32;
+    long long f32_stride;
+};
+
+struct Tc2Params {
+    Tc2Task task[4];
+    int n_tasks, total_rg, nbu, M;
+    const uint8_t *act;  // [token block][unit][128][AROW]
+    const float *dx;     // [token block][unit][128][DX]
+    int *status;
+    unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ int tc2_task_of(const Tc2Params &p, int rg) {
+    int t = 0;
+#pragma unroll
+    for (int i = 1; i < 4; ++i) t += (i < p.n_tasks && rg >= p.task[i].rg_start) ? 1 : 0;
+    return t;
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// one lane of a converged warp (the MMA is issued by a single thread; converged issue keeps its
+// operands in uniform registers)
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile("{ .reg .pred P; elect.sync _|P, 0xffffffff; selp.u32 %0, 1, 0, P; }" : "=r"(pred));
+    return pred != 0;
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_constant__ Tc2Params p) {
+    using C = Tc2Cfg<TYPE>;
+    constexpr int SB = C::SB, SD = C::SD, SH = C::SH, SW = C::SW, SA = C::SA, G = C::G, NOP = C::NOP, RGM = C::RGMAX_C;
+    constexpr bool COOP = G > 1;  // prep warps share an item (one row group each)
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ uint64_t w_full[SW], w_empty[SW], a_full_s[SA], a_empty_s[SA], t_full[2], t_empty[2];
+    __shared__ uint64_t b_full[SB], b_empty[SB], d_full[SD], d_free[SD], h_free[SH];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tb = blockIdx.y, nbu = p.nbu;
+    const int Mb = min(128, p.M - 128 * tb);  // tokens of this block
+    const int rg_lo = (int)((long long)p.total_rg * blockIdx.x / gridDim.x);
+    const int rg_hi = (int)((long long)p.total_rg * (blockIdx.x + 1) / gridDim.x);
+    const int n_chunks = (rg_hi - rg_lo + RGM - 1) / RGM;
+
+    if (tid == 0) {
+        for (int s = 0; s < SW; ++s) {
+            mbar_init(smem_u32(&w_full[s]), 1);
+            mbar_init(smem_u32(&w_empty[s]), COOP ? 4 : 1);
+        }
+        for (int s = 0; s < SA; ++s) {
+            mbar_init(smem_u32(&a_full_s[s]), 1);
+            mbar_init(smem_u32(&a_empty_s[s]), 8);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(smem_u32(&t_full[s]), 4);
+            mbar_init(smem_u32(&t_empty[s]), 1);
+        }
+        for (int s = 0; s < SB; ++s) {
+            mbar_init(smem_u32(&b_full[s]), COOP ? 4 : 1);
+            mbar_init(smem_u32(&b_empty[s]), 1);
+        }
+        for (int s = 0; s < SD; ++s) {
+            mbar_init(smem_u32(&d_full[s]), 1);
+            mbar_init(smem_u32(&d_free[s]), 8);
+        }
+        for (int s = 0; s < SH; ++s) mbar_init(smem_u32(&h_free[s]), 8);
+        s_abort = 0;
+        mbar_init_fence();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&s_tmem)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    volatile int *abort_flag = &s_abort;
+    // bounded wait; a timeout stops every role (each checks the flag before its next wait)
+    auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {
+        if (*abort_flag) return false;
+        if (!mbar_wait_bounded_sleep(smem_u32(bar), parity, p.timeout_ns, p.status)) {
+            *abort_flag = 1;
+            return false;
+        }
+        return true;
+    };
+    // chunk ch: row groups [g0, g0 + ng), items of ceil(ng / G) groups per unit
+    auto chunk_of = [&](int ch, int &g0, int &ng) {
+        g0 = rg_lo + ch * RGM;
+        ng = min(RGM, rg_hi - g0);
+    };
+
+    if (warp == 12) {
+        // ---------------- producer.  Activation units run one unit ahead of the weight tiles, so
+        // the epilogue warps, which load unit u + 1 into TMEM before the items of unit u, never wait
+        // on tiles that wait on them.
+        if (lane == 0) {
+            const uint64_t policy = l2_evict_first_policy();
+            auto issue_act = [&](int gunit, int u) -> bool {
+                const int as = gunit % SA;
+                if (!wait(&a_empty_s[as], ((gunit / SA) & 1) ^ 1)) return false;
+                const uint32_t qb = (uint32_t)Mb * C::AROW, db = ((uint32_t)Mb * C::DX * 4u + 15u) & ~15u;
+                uint8_t *slot = smem + C::OFF_A + (size_t)as * C::ASLOT;
+                mbar_arrive_expect_tx(smem_u32(&a_full_s[as]), qb + db);
+                const size_t blk = (size_t)tb * nbu + u;
+                bulk_g2s(smem_u32(slot), p.act + blk * C::AQ, qb, smem_u32(&a_full_s[as]), policy);
+                bulk_g2s(smem_u32(slot + C::AQ), p.dx + blk * 128 * C::DX, db, smem_u32(&a_full_s[as]), policy);
+                return true;
+            };
+            int i = 0, gu = 0;
+            for (int ch = 0; ch < n_chunks && !*abort_flag; ++ch) {
+                int g0, ng;
+                chunk_of(ch, g0, ng);
+                const int ni = (ng + G - 1) / G;
+                if (!issue_act(gu, 0)) break;
+                for (int u = 0; u < nbu && !*abort_flag; ++u, ++gu) {
+                    if (u + 1 < nbu && !issue_act(gu + 1, u + 1)) break;
+                    for (int j = 0; j < ni; ++j, ++i) {
+                        const int ws = i % SW;
+                        if (!wait(&w_empty[ws], ((i / SW) & 1) ^ 1)) break;
+                        const int gn = min(G, ng - j * G);
+                        mbar_arrive_expect_tx(smem_u32(&w_full[ws]), (uint32_t)gn * C::TB);
+                        for (int gi = 0; gi < gn; ++gi) {
+                            const int rg = g0 + j * G + gi;
+                            const Tc2Task &tk = p.task[tc2_task_of(p, rg)];
+                            const size_t tile = (size_t)(tk.rg_first + rg - tk.rg_start) * nbu + u;
+                            bulk_g2s(smem_u32(smem + C::OFF_W + (size_t)ws * C::WSLOT + (size_t)gi * C::TB),
+                                     tk.w + tile * C::TB, C::TB, smem_u32(&w_full[ws]), policy);
+                        }
+                    }
+                }
+            }
+        }
+    } else if (warp >= 8 && warp < 12) {
+        // ---------------- B operands
+        // lanes 0-15 take the first half of rows 0-15, lanes 16-31 the second half: the 16-byte
+        // stores of 8 consecutive lanes then land in 8 different bank groups
+        const int pw = warp - 8, rr = lane & 15, hs = lane >> 4;
+        int i = 0;
+        for (int ch = 0; ch < n_chunks && !*abort_flag; ++ch) {
+            int g0, ng;
+            chunk_of(ch, g0, ng);
+            const int ni = (ng + G - 1) / G;
+            for (int u = 0; u < nbu && !*abort_flag; ++u) {
+                for (int j = 0; j < ni; ++j, ++i) {
+                    if (!COOP && (i & 3) != pw) continue;
+                    const int ws = i % SW, sb = i % SB, sh = i % SH;
+                    int ok = 1;
+                    if (lane == 0)
+                        ok = wait(&w_full[ws], (i / SW) & 1) && wait(&b_empty[sb], ((i / SB) & 1) ^ 1) &&
+                             wait(&h_free[sh], ((i / SH) & 1) ^ 1);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) break;
+                    const int gi = COOP ? pw : 0;
+                    if (gi < min(G, ng - j * G)) {
+                        const uint8_t *tile = smem + C::OFF_W + (size_t)ws * C::WSLOT + (size_t)gi * C::TB;
+                        uint8_t *B = smem + (size_t)sb * C::BSLOT + (size_t)gi * NOP * 4096;
+                        float d0, d1;
+                        prep_row<TYPE, 4096u>(tile, rr, hs, B, rr, d0, d1);
+                        if (hs == 0) {
+                            uint8_t *h = smem + C::OFF_H + (size_t)sh * C::HDR + (size_t)gi * 256;
+                            if (TYPE == TYPE_Q8_0) *reinterpret_cast<uint4 *>(h + 16 * rr) = lds128(tile + 272 * rr);
+                            else *reinterpret_cast<float2 *>(h + 8 * rr) = make_float2(d0, d1);
+                        }
+                        fence_async_smem();
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(smem_u32(&b_full[sb]));
+                        mbar_arrive(smem_u32(&w_empty[ws]));
+                    }
+                }
+            }
+        }
+    } else if (warp == 13) {
+        // ---------------- MMA issue (converged warp, elected lane)
+        int i = 0, gu = 0;
+        for (int ch = 0; ch < n_chunks && !*abort_flag; ++ch) {
+            int g0, ng;
+            chunk_of(ch, g0, ng);
+            const int ni = (ng + G - 1) / G;
+            for (int u = 0; u < nbu && !*abort_flag; ++u, ++gu) {
+                const int ab = gu & 1;
+                if (!wait(&t_full[ab], (gu >> 1) & 1)) break;
+                for (int j = 0; j < ni; ++j, ++i) {
+                    const int sb = i % SB, sd = i % SD;
+                    if (!wait(&b_full[sb], (i / SB) & 1) || !wait(&d_free[sd], ((i / SD) & 1) ^ 1)) break;
+                    tc_fence_after();
+                    const uint32_t ta = tmem + (uint32_t)(64 * ab), td = tmem + 128u + (uint32_t)(sd * C::NCOL);
+                    const uint32_t sbase = smem_u32(smem + (size_t)sb * C::BSLOT);
+                    if (elect_one()) {
+#pragma unroll
+                        for (int ks = 0; ks < 8; ++ks) {
+                            if (TYPE == TYPE_Q8_0)
+                                tc_mma_ts(td + (uint32_t)(16 * ks), ta + (uint32_t)(8 * ks),
+                                          umma_desc(sbase + 256 * ks, 128, 2048), C::IDESC, 0);
+                            else
+                                tc_mma_ts(td, ta + (uint32_t)(8 * ks), umma_desc(sbase + 256 * ks, 128, 2048), C::IDESC, ks > 0);
+                        }
+                        tc_commit(smem_u32(&d_full[sd]));
+                        tc_commit(smem_u32(&b_empty[sb]));
+                        if (j == ni - 1) tc_commit(smem_u32(&t_empty[ab]));
+                    }
+                    __syncwarp();
+                }
+            }
+        }
+    } else {
+        // ---------------- activation into TMEM (warps 0-3) and epilogue (warps 0-7)
+        const int q = warp & 3, h = warp >> 2;
+        const int t = 32 * q + lane;  // token lane
+        const bool live = 32 * q < Mb;  // this quadrant holds tokens of the block
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        float acc[4][16];  // chunk row groups c with c % 2 == h, at acc[c / 2]
+        float dx0[C::DX], dx1[C::DX];  // scales of the units in TMEM buffers 0 and 1
+        int i = 0, gu = 0;
+        // activation unit gunit -> TMEM buffer gunit & 1 (warps 0-3), its scales -> dx0 / dx1 (all)
+        auto load_unit = [&](int gunit) -> bool {
+            const int as = gunit % SA, ab = gunit & 1;
+            int ok = 1;
+            if (lane == 0) {
+                ok = wait(&a_full_s[as], (gunit / SA) & 1);
+                if (ok && h == 0) ok = wait(&t_empty[ab], ((gunit >> 1) & 1) ^ 1);
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) return false;
+            const uint8_t *slot = smem + C::OFF_A + (size_t)as * C::ASLOT;
+            const float *dxs = reinterpret_cast<const float *>(slot + C::AQ) + (size_t)t * C::DX;
+#pragma unroll
+            for (int b = 0; b < C::DX; ++b) {
+                const float v = (t < Mb) ? dxs[b] : 0.0f;
+                if (ab) dx1[b] = v;
+                else dx0[b] = v;
+            }
+            if (h == 0) {
+                tc_fence_after();
+                const uint8_t *row = slot + (size_t)t * C::AROW;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t v[32];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const uint4 w4 = (t < Mb) ? lds128(row + 128 * half + 16 * k) : make_uint4(0u, 0u, 0u, 0u);
+                        v[4 * k] = w4.x, v[4 * k + 1] = w4.y, v[4 * k + 2] = w4.z, v[4 * k + 3] = w4.w;
+                    }
+                    tmem_st32(tmem + lane_base + (uint32_t)(64 * ab + 32 * half), v);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+            }
+            __syncwarp();
+            if (lane == 0) {
+                if (h == 0) mbar_arrive(smem_u32(&t_full[ab]));
+                mbar_arrive(smem_u32(&a_empty_s[as]));
+            }
+            return true;
+        };
+        for (int ch = 0; ch < n_chunks && !*abort_flag; ++ch) {
+            int g0, ng;
+            chunk_of(ch, g0, ng);
+            const int ni = (ng + G - 1) / G;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+                for (int r = 0; r < 16; ++r) acc[k][r] = 0.0f;
+            if (!load_unit(gu)) break;
+            for (int u = 0; u < nbu; ++u, ++gu) {
+                if (u + 1 < nbu && !load_unit(gu + 1)) break;
+                const int ab = gu & 1;
+                // items of the unit, unrolled so that every accumulator index is a constant
+#pragma unroll
+                for (int j = 0; j < RGM / G; ++j) {
+                    if (j >= ni) break;
+                    const int it = i + j, sd = it % SD;
+                    int ok = 1;
+                    if (lane == 0) ok = wait(&d_full[sd], (it / SD) & 1);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) break;
+                    tc_fence_after();
+                    if (live) {
+#pragma unroll
+                        for (int gi = 0; gi < G; ++gi) {
+                            const int c = j * G + gi;  // row group within the chunk
+                            if (c >= ng || (c & 1) != h) continue;
+                            const uint8_t *hdr = smem + C::OFF_H + (size_t)(it % SH) * C::HDR + (size_t)gi * 256;
+                            const uint32_t td = tmem + lane_base + 128u + (uint32_t)(sd * C::NCOL + gi * NOP * 16);
+                            if (TYPE == TYPE_Q8_0) {
+                                // eight block terms per (row, token), added in block order below
+                                float t8[8][16];
+#pragma unroll
+                                for (int b = 0; b < 8; ++b) {
+                                    uint32_t D[16];
+                                    tmem_ld16(td + (uint32_t)(16 * b), D);
+                                    tmem_wait_ld();
+                                    const float dxb = ab ? dx1[b] : dx0[b];
+#pragma unroll
+                                    for (int r = 0; r < 16; ++r) {
+                                        const uint32_t dw = *reinterpret_cast<const uint32_t *>(hdr + 16 * r + 4 * (b >> 1));
+                                        const float wd = half_bits_to_float(dw >> (16 * (b & 1)));
+                                        t8[b][r] = __fmul_rn(__fmul_rn(wd, dxb), __int2float_rn((int)D[r]));
+                                    }
+                                }
+#pragma unroll
+                                for (int r = 0; r < 16; ++r)
+#pragma unroll
+                                    for (int b = 0; b < 8; ++b) acc[c >> 1][r] = __fadd_rn(acc[c >> 1][r], t8[b][r]);
+                            } else {
+                                float tm[16];
+                                uint32_t D[NOP][16];
+#pragma unroll
+                                for (int o = 0; o < NOP; ++o) tmem_ld16(td + (uint32_t)(16 * o), D[o]);
+                                tmem_wait_ld();
+                                const float dx = ab ? dx1[0] : dx0[0];
+#pragma unroll
+                                for (int r = 0; r < 16; ++r) {
+                                    if (TYPE == TYPE_Q6_K) {
+                                        const float d = *reinterpret_cast<const float *>(hdr + 8 * r);
+                                        const int sumi = (int)D[0][r] + 8 * (int)D[1][r] + 16 * (int)D[2][r] + 128 * (int)D[3][r];
+                                        tm[r] = __fmul_rn(__fmul_rn(d, dx), __int2float_rn(sumi));
+                                    } else {
+                                        const float2 dd = *reinterpret_cast<const float2 *>(hdr + 8 * r);
+                                        const int sumi = 8 * (int)D[0][r] + (int)D[1][r];
+                                        const int summ = (int)D[2][r];
+                                        tm[r] = __fmul_rn(dx, __fsub_rn(__fmul_rn(dd.x, __int2float_rn(sumi)),
+                                                                        __fmul_rn(dd.y, __int2float_rn(summ))));
+                                    }
+                                }
+#pragma unroll
+                                for (int r = 0; r < 16; ++r) acc[c >> 1][r] = __fadd_rn(acc[c >> 1][r], tm[r]);
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(smem_u32(&d_free[sd]));
+                        mbar_arrive(smem_u32(&h_free[it % SH]));
+                    }
+                }
+                i += ni;
+                if (*abort_flag) break;
+            }
+            if (*abort_flag) break;
+            // results of the chunk: token t, rows of row groups g0 + c (c % 2 == h)
+            if (t < Mb) {
+                const int tok = 128 * tb + t;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int c = 2 * k + h;
+                    if (c >= ng) break;
+                    const int rg = g0 + c;
+                    const Tc2Task &tk = p.task[tc2_task_of(p, rg)];
+#pragma unroll
+                    for (int r = 0; r < 16; ++r) {
+                        const int lr = (tk.rg_first + rg - tk.rg_start) * 16 + r - tk.row_begin;
+                        if (lr < 0 || lr >= tk.rows) continue;
+                        const float v = acc[k][r];
+                        if (tk.dst_f32) tk.dst_f32[(size_t)tok * tk.f32_stride + lr] = v;
+                        if (tk.dst) {
+                            float o = v;
+                            if (tk.res) o = __fadd_rn(o, __half2float(tk.res[(size_t)tok * tk.res_stride + lr]));
+                            tk.dst[(size_t)tok * tk.dst_stride + lr] = __float2half_rn(o);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    // drain: after an early stop, copies in flight must land before the CTA exits
+    if (warp == 12 && lane == 0 && *abort_flag) {
+        int items = 0;
+        for (int ch = 0; ch < n_chunks; ++ch) {
+            int g0, ng;
+            chunk_of(ch, g0, ng);
+            items += ((ng + G - 1) / G) * nbu;
+        }
+        const int units = n_chunks * nbu;
+        for (int k = max(0, items - SW); k < items; ++k)
+            mbar_wait_bounded(smem_u32(&w_full[k % SW]), (k / SW) & 1, p.timeout_ns, nullptr);
+        for (int k = max(0, units - SA); k < units; ++k)
+            mbar_wait_bounded(smem_u32(&a_full_s[k % SA]), (k / SA) & 1, p.timeout_ns, nullptr);
+    }
+}
+
+// x fp16 [M][K] (quantized as quantize_row_fp16_to_q8_k / _q8_0) or pre-quantized blocks ->
+// [token block][unit][128 tokens][272 B] quants + [token block][unit][128][DX] scales.  One
+// warp per (token, unit); lane L holds values 8L .. 8L+7.
+template <int TYPE>
+__global__ void pack_act2_kernel(const __half *x, long long x_stride, const void *act, int M, int K, uint8_t *out,
+                                 float *dx) {
+    constexpr int DX = Tc2Cfg<TYPE>::DX;
+    constexpr unsigned AROW = Tc2Cfg<TYPE>::AROW;
+    const int nbu = K / 256;
+    const int lane = threadIdx.x & 31;
+    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+    for (long long wi = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wi < (long long)M * nbu;
+         wi += warps) {
+        const int m = (int)(wi / nbu), u = (int)(wi % nbu);
+        uint32_t lo, hi;
+        float d;
+        if (x) {
+            const __half *xu = x + (size_t)m * x_stride + (size_t)u * 256 + 8 * lane;
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = __half2float(xu[k]);
+            float amax = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[k]));
+            constexpr int span = (TYPE == TYPE_Q8_0) ? 4 : 32;
+#pragma unroll
+            for (int o = 1; o < span; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            int qv[8];
+            if (amax == 0.0f) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) qv[k] = 0;
+            } else {
+                const float inv = __fdiv_rn(127.0f, amax);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) qv[k] = max(-127, min(127, __float2int_rn(__fmul_rn(v[k], inv))));
+            }
+            lo = (uint32_t)(qv[0] & 0xFF) | ((uint32_t)(qv[1] & 0xFF) << 8) | ((uint32_t)(qv[2] & 0xFF) << 16) |
+                 ((uint32_t)(qv[3] & 0xFF) << 24);
+            hi = (uint32_t)(qv[4] & 0xFF) | ((uint32_t)(qv[5] & 0xFF) << 8) | ((uint32_t)(qv[6] & 0xFF) << 16) |
+                 ((uint32_t)(qv[7] & 0xFF) << 24);
+            d = (amax == 0.0f) ? 0.0f : __fdiv_rn(amax, 127.0f);
+        } else if (TYPE == TYPE_Q8_0) {
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(reinterpret_cast<const BlockQ80 *>(act) +
+                                                                   ((size_t)m * nbu + u) * 8 + (lane >> 2));
+            lo = w[1 + 2 * (lane & 3)];
+            hi = w[2 + 2 * (lane & 3)];
+            d = __uint_as_float(w[0]);
+        } else {
+            const uint32_t *w =
+                reinterpret_cast<const uint32_t *>(reinterpret_cast<const BlockQ8K *>(act) + (size_t)m * nbu + u);
+            lo = w[1 + 2 * lane];
+            hi = w[2 + 2 * lane];
+            d = __uint_as_float(w[0]);
+        }
+        const int tb = m >> 7, t = m & 127;
+        const size_t blk = (size_t)tb * nbu + u;
+        *reinterpret_cast<uint2 *>(out + blk * (128 * AROW) + (size_t)t * AROW + 8 * lane) = make_uint2(lo, hi);
+        if (TYPE == TYPE_Q8_0) {
+            if ((lane & 3) == 0) dx[(blk * 128 + t) * DX + (lane >> 2)] = d;
+        } else {
+            if (lane == 0) dx[blk * 128 + t] = d;
+        }
+    }
+}
+
+template <int TYPE>
+cudaError_t launch_tc2_t(const TcLaunch &L, cudaStream_t stream) {
+    using C = Tc2Cfg<TYPE>;
+    const int nbu = L.K / 256;
+    const int n_tb = (L.M + 127) / 128;
+    const size_t qbytes = (size_t)n_tb * nbu * C::AQ;
+    const size_t need = qbytes + (size_t)n_tb * nbu * 128 * C::DX * 4;
+    if (L.scratch_bytes < need) return cudaErrorInvalidValue;
+    uint8_t *act = reinterpret_cast<uint8_t *>(L.scratch);
+    float *dx = reinterpret_cast<float *>(act + qbytes);
+    {
+        const long long items = (long long)L.M * nbu;
+        const int blocks = (int)std::min<long long>((items + 7) / 8, 148 * 16);
+        pack_act2_kernel<TYPE><<<blocks, 256, 0, stream>>>(reinterpret_cast<const __half *>(L.x), L.x_stride, L.act,
+                                                            L.M, L.K, act, dx);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    static std::mutex mu;
+    static std::unordered_map<int, bool> configured;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!configured[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(gemm_tc2_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+            if (e != cudaSuccess) return e;
+            configured[dev] = true;
+        }
+    }
+    Tc2Params p{};
+    int total_rg = 0;
+    for (int i = 0; i < L.n_tasks; ++i) {
+        const GemvTaskHost &h = L.tasks[i];
+        if (h.rows <= 0) continue;
+        Tc2Task &t = p.task[p.n_tasks++];
+        t.w = h.w;
+        t.rg_first = h.row_begin / 16;
+        t.rg_start = total_rg;
+        t.n_rg = (h.row_begin + h.rows - 1) / 16 - t.rg_first + 1;
+        t.row_begin = h.row_begin;
+        t.rows = h.rows;
+        t.dst = reinterpret_cast<__half *>(h.dst);
+        t.dst_stride = h.dst_stride;
+        t.res = reinterpret_cast<const __half *>(h.res);
+        t.res_stride = h.res_stride;
+        t.dst_f32 = h.dst_f32;
+        t.f32_stride = h.f32_stride;
+        total_rg += t.n_rg;
+    }
+    if (total_rg == 0) return cudaSuccess;
+    p.total_rg = total_rg;
+    p.nbu = nbu;
+    p.M = L.M;
+    p.act = act;
+    p.dx = dx;
+    p.status = L.status;
+    p.timeout_ns = L.timeout_ns;
+    const int sms = L.num_sms > 0 ? L.num_sms : 148;
+    const int gx = std::min(total_rg, std::max((sms + n_tb - 1) / n_tb, (total_rg + C::RGMAX_C - 1) / C::RGMAX_C));
+    gemm_tc2_kernel<TYPE><<<dim3(gx, n_tb), kTc2Threads, C::SMEM, stream>>>(p);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 size_t tc_scratch_bytes(int type, int M, int K) {
     const int nbu = K / 256;
     auto need = [&](int bn, int dxn) { return (size_t)((M + bn - 1) / bn) * nbu * ((size_t)bn * 256 + (size_t)bn * dxn * 4); };
     return type == TYPE_Q8_0 ? need(32, 8) : need(64, 1);
+}
+
+size_t tc2_scratch_bytes(int type, int M, int K) {
+    const size_t blocks = (size_t)((M + 127) / 128) * (K / 256);
+    return blocks * (128 * 272 + 128 * (type == TYPE_Q8_0 ? 8 : 1) * 4);
+}
+
+cudaError_t launch_gemm_tc2(const TcLaunch &L, cudaStream_t stream) {
+    if (L.M < 1 || L.K % 256) return cudaErrorInvalidValue;
+    switch (L.type) {
+        case TYPE_Q4_K: return launch_tc2_t<TYPE_Q4_K>(L, stream);
+        case TYPE_Q5_K: return launch_tc2_t<TYPE_Q5_K>(L, stream);
+        case TYPE_Q6_K: return launch_tc2_t<TYPE_Q6_K>(L, stream);
+        case TYPE_Q8_0: return launch_tc2_t<TYPE_Q8_0>(L, stream);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 cudaError_t launch_gemm_tc(const TcLaunch &L, cudaStream_t stream) {

@@ -68,6 +68,7 @@ struct TcLaunch {
     size_t scratch_bytes;
     int *status;
     unsigned long long timeout_ns;
+    int num_sms = 0;
 };
 
 // kq_gemv.cu
@@ -76,6 +77,9 @@ cudaError_t launch_gemv(const GemvLaunch &L, cudaStream_t stream);
 // kq_gemm_tc.cu
 size_t tc_scratch_bytes(int type, int M, int K);
 cudaError_t launch_gemm_tc(const TcLaunch &L, cudaStream_t stream);
+// token-major variant (activation in tensor memory, row groups spread over all SMs)
+size_t tc2_scratch_bytes(int type, int M, int K);
+cudaError_t launch_gemm_tc2(const TcLaunch &L, cudaStream_t stream);
 
 cudaError_t launch_gather_rows(int type, int K, const uint8_t *src, const uint32_t *ids, int n, uint8_t *dst,
                                cudaStream_t stream);

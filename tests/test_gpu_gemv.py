@@ -49,7 +49,7 @@ FULL_RANGE = {kq.TYPE_Q6_K: dict(q6_scales=(-128, 128)), kq.TYPE_Q8_0: dict(q8_q
 
 @pytest.mark.parametrize("gtype", sorted(FULL_RANGE), ids=lambda t: synth.TYPE_NAMES[t])
 @pytest.mark.parametrize("M", [1, 2, 4, 8, 9, 40])
-@pytest.mark.parametrize("path", [0, 1, 2])
+@pytest.mark.parametrize("path", [0, 1, 2, 3])
 def test_full_range_values_bitexact(kqctx, oracle, gtype, M, path):
     """Q6_K scales over all of int8 (real Q6_K blocks always hold -128 or 127: the quantizer maps
     each block's largest scale there) and Q8_0 quants including -128, on every M > 8 path"""

@@ -17,10 +17,11 @@ from conftest import bits, to_dev
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True)
-def force_tensor_cores(kqctx):
-    """pin the tensor-core path (the default chooses by a cost model)"""
-    kqctx.set_option("gemm_path", 1)
+@pytest.fixture(autouse=True, params=[1, 3], ids=["rowmajor", "tokenmajor"])
+def force_tensor_cores(kqctx, request):
+    """pin a tensor-core kernel (the default chooses by a cost model): 1 = weight rows as the
+    MMA's A operand, 3 = activation tokens as A in tensor memory"""
+    kqctx.set_option("gemm_path", request.param)
     yield
     kqctx.set_option("gemm_path", 0)
 
