@@ -111,6 +111,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr));
 }
 
+// one lane of a converged warp (the MMA is issued by a single thread; converged issue keeps its
+// operands in uniform registers)
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile("{ .reg .pred P; elect.sync _|P, 0xffffffff; selp.u32 %0, 1, 0, P; }" : "=r"(pred));
+    return pred != 0;
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -383,20 +391,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 named_bar_sync(1, kTcCompute);
                 tc_fence_after();
                 if (*reinterpret_cast<volatile int *>(&s_abort)) break;
-                if (tid == 0) {
+                if (warp == 0) {
+                    // converged warp, one elected lane: the MMA operands stay in uniform registers;
+                    // the NA accumulator chains are interleaved so the tensor core overlaps them
                     const uint32_t sa = smem_u32(A), sbm = smem_u32(ring + (size_t)st * C::STAGE);
                     const uint32_t td = tmem + (uint32_t)((b & 1) * 256);
-                    if (TYPE == TYPE_Q8_0) {
-                        for (int jj = 0; jj < 8; ++jj)
-                            tc_mma(td + (uint32_t)(jj * BN), umma_desc(sa + 256 * jj, 128, 2048),
-                                   umma_desc(sbm + 256 * jj, 128, 2048), idesc, 0);
-                    } else {
-                        for (int a = 0; a < NA; ++a)
+                    if (elect_one()) {
+                        if (TYPE == TYPE_Q8_0) {
+#pragma unroll
+                            for (int jj = 0; jj < 8; ++jj)
+                                tc_mma(td + (uint32_t)(jj * BN), umma_desc(sa + 256 * jj, 128, 2048),
+                                       umma_desc(sbm + 256 * jj, 128, 2048), idesc, 0);
+                        } else {
+#pragma unroll
                             for (int ks = 0; ks < 8; ++ks)
-                                tc_mma(td + (uint32_t)(a * BN), umma_desc(sa + a * 32768 + 256 * ks, 128, 2048),
-                                       umma_desc(sbm + 256 * ks, 128, 2048), idesc, ks > 0);
+#pragma unroll
+                                for (int a = 0; a < NA; ++a)
+                                    tc_mma(td + (uint32_t)(a * BN), umma_desc(sa + a * 32768 + 256 * ks, 128, 2048),
+                                           umma_desc(sbm + 256 * ks, 128, 2048), idesc, ks > 0);
+                        }
+                        tc_commit(smem_u32(&bar_mma[b & 1]));
                     }
-                    tc_commit(smem_u32(&bar_mma[b & 1]));
+                    __syncwarp();
                 }
             }
             if (b >= 1) {
@@ -671,13 +687,6 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint
         "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
-// one lane of a converged warp (the MMA is issued by a single thread; converged issue keeps its
-// operands in uniform registers)
-__device__ __forceinline__ bool elect_one() {
-    uint32_t pred;
-    asm volatile("{ .reg .pred P; elect.sync _|P, 0xffffffff; selp.u32 %0, 1, 0, P; }" : "=r"(pred));
-    return pred != 0;
-}
 
 template <int TYPE>
 __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_constant__ Tc2Params p) {
