@@ -155,7 +155,7 @@ __device__ __forceinline__ bool mbar_wait_bounded_sleep(uint32_t bar, uint32_t p
     const uint64_t t0 = global_timer_ns();
     while (true) {
         for (int i = 0; i < 8; ++i)
-            if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
+            if (mbar_try_wait_sleep(bar, parity, 200u)) return true;
         if (global_timer_ns() - t0 > timeout_ns) {
             if (status) atomicExch(status, DEV_ERR_TIMEOUT);
             return false;

@@ -43,7 +43,6 @@ template <int TYPE>
 struct TcCfg {
     static constexpr int BN = (TYPE == TYPE_Q8_0) ? 32 : 64;                   // tokens per CTA
     static constexpr int NA = (TYPE == TYPE_Q8_0) ? 1 : (TYPE == TYPE_Q6_K) ? 4 : 3;  // A operands
-    static constexpr int NACC = (TYPE == TYPE_Q8_0) ? 8 : NA;                  // accumulators per buffer
     static constexpr int S = (TYPE == TYPE_Q6_K) ? 2 : (TYPE == TYPE_Q8_0) ? 4 : 3;   // ring stages
     static constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;                      // scales per token and unit
     static constexpr unsigned B_BYTES = BN * 256;
@@ -602,11 +601,13 @@ cudaError_t launch_tc_t(const TcLaunch &L, cudaStream_t stream) {
 //
 // Items i = (unit u, group of G row groups) in unit-major order flow through four roles:
 //   warp 12    producer: activation unit u (quants + scales) and the group's weight tiles (cp.async.bulk)
-//   warps 8-11 build the B operand of item i (one row group each; Q8_0 items round-robin)
+//   warps 8-11 write activation unit u into TMEM (lane quadrant w % 4 each) and build the B
+//              operand of item i (one row group each; Q8_0 items round-robin)
 //   warp 13    issues the item's MMAs (converged warp, one elected lane) and commits
-//   warps 0-7  write activation units into TMEM (0-3, one lane quadrant each) and run the
-//              epilogue: warp w reads lane quadrant w % 4 for the row groups c of the chunk with
+//   warps 0-7  epilogue: warp w reads lane quadrant w % 4 for the row groups c of the chunk with
 //              c % 2 == w / 4.
+// Token t sits in TMEM lane 32 (t % 4) + t / 4, so a small token count still spreads over all
+// four lane quadrants and all eight epilogue warps.
 // One MMA accumulator chain per item: N = 192 (Q4_K/Q5_K 4 x 48, Q6_K 3 x 64) keeps the tensor
 // core near its peak rate; Q8_0 items are one row group with eight independent 32-block chains.
 // TMEM: columns [0, 128) two activation buffers, [128, 512) SD item accumulators.
@@ -620,19 +621,22 @@ struct Tc2Cfg {
     static constexpr int SD = 384 / NCOL;                                             // accumulator slots (2, Q8_0 3)
     static constexpr int SB = SD;                                                     // B operand slots
     static constexpr int SH = 4;                                                      // header slots
+    static constexpr int SX = 4;                                                      // activation-scale slots
     static constexpr int RGMAX_C = (TYPE == TYPE_Q6_K) ? 6 : 8;                      // row groups per chunk
     static constexpr unsigned BSLOT = (unsigned)(G * NOP) * 4096u;                    // 16 rows x 256 B per operand
     static constexpr unsigned HDR = (unsigned)G * 256u;                               // per-row scales of an item
     static constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;
-    static constexpr int SW = 4, SA = 2;
+    static constexpr int SW = 4, SAMAX = 8;  // activation slots: as many as fit the region, up to 8
     static constexpr unsigned TB = (unsigned)tile_bytes(TYPE);
     static constexpr unsigned WSLOT = (unsigned)G * TB;
     static constexpr unsigned AROW = 272u;  // padded token row: conflict-free 16-byte reads
     static constexpr unsigned AQ = 128u * AROW;
-    static constexpr unsigned ASLOT = AQ + 128u * DX * 4u;
+    static constexpr unsigned AREGION = 2u * (AQ + 128u * DX * 4u);  // two slots of 128 tokens
     static constexpr unsigned OFF_H = SB * BSLOT;
     static constexpr unsigned OFF_A = OFF_H + SH * HDR;
-    static constexpr unsigned OFF_W = OFF_A + SA * ASLOT;
+    static constexpr unsigned OFF_X = OFF_A + AREGION;
+    static constexpr unsigned XSLOT = 128u * DX * 4u;
+    static constexpr unsigned OFF_W = OFF_X + SX * XSLOT;
     static constexpr unsigned SMEM = OFF_W + SW * WSLOT + 1024;
     // b_fmt: Q5_K operands reach 217 (u8), all others fit s8; a_fmt s8 (activation quants)
     static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | ((TYPE == TYPE_Q5_K) ? 0u : (1u << 10)) |
@@ -691,18 +695,24 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint
 template <int TYPE>
 __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_constant__ Tc2Params p) {
     using C = Tc2Cfg<TYPE>;
-    constexpr int SB = C::SB, SD = C::SD, SH = C::SH, SW = C::SW, SA = C::SA, G = C::G, NOP = C::NOP, RGM = C::RGMAX_C;
+    constexpr int SB = C::SB, SD = C::SD, SH = C::SH, SX = C::SX, SW = C::SW, SAM = C::SAMAX, G = C::G, NOP = C::NOP,
+                  RGM = C::RGMAX_C;
     constexpr bool COOP = G > 1;  // prep warps share an item (one row group each)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    __shared__ uint64_t w_full[SW], w_empty[SW], a_full_s[SA], a_empty_s[SA], t_full[2], t_empty[2];
-    __shared__ uint64_t b_full[SB], b_empty[SB], d_full[SD], d_free[SD], h_free[SH];
+    __shared__ uint64_t w_full[SW], w_empty[SW], a_full_s[SAM], a_empty_s[SAM], t_full[2], t_empty[2];
+    __shared__ uint64_t b_full[SB], b_empty[SB], d_full[SD], d_free[SD], h_free[SH], x_free[SX];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tb = blockIdx.y, nbu = p.nbu;
     const int Mb = min(128, p.M - 128 * tb);  // tokens of this block
+    // activation slot: Mb16 token rows of quants, then their scales; as many slots as fit
+    const int Mb16 = (Mb + 15) & ~15;
+    const unsigned a_dx_off = (unsigned)Mb16 * C::AROW;
+    const unsigned a_slot = (a_dx_off + (unsigned)Mb16 * C::DX * 4u + 127u) & ~127u;
+    const int SA = min(SAM, (int)(C::AREGION / a_slot));
     const int rg_lo = (int)((long long)p.total_rg * blockIdx.x / gridDim.x);
     const int rg_hi = (int)((long long)p.total_rg * (blockIdx.x + 1) / gridDim.x);
     const int n_chunks = (rg_hi - rg_lo + RGM - 1) / RGM;
@@ -712,9 +722,9 @@ __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_c
             mbar_init(smem_u32(&w_full[s]), 1);
             mbar_init(smem_u32(&w_empty[s]), COOP ? 4 : 1);
         }
-        for (int s = 0; s < SA; ++s) {
+        for (int s = 0; s < SAM; ++s) {
             mbar_init(smem_u32(&a_full_s[s]), 1);
-            mbar_init(smem_u32(&a_empty_s[s]), 8);
+            mbar_init(smem_u32(&a_empty_s[s]), 4);
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(smem_u32(&t_full[s]), 4);
@@ -729,6 +739,7 @@ __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_c
             mbar_init(smem_u32(&d_free[s]), 8);
         }
         for (int s = 0; s < SH; ++s) mbar_init(smem_u32(&h_free[s]), 8);
+        for (int s = 0; s < SX; ++s) mbar_init(smem_u32(&x_free[s]), 8);
         s_abort = 0;
         mbar_init_fence();
     }
@@ -766,11 +777,11 @@ __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_c
                 const int as = gunit % SA;
                 if (!wait(&a_empty_s[as], ((gunit / SA) & 1) ^ 1)) return false;
                 const uint32_t qb = (uint32_t)Mb * C::AROW, db = ((uint32_t)Mb * C::DX * 4u + 15u) & ~15u;
-                uint8_t *slot = smem + C::OFF_A + (size_t)as * C::ASLOT;
+                uint8_t *slot = smem + C::OFF_A + (size_t)as * a_slot;
                 mbar_arrive_expect_tx(smem_u32(&a_full_s[as]), qb + db);
                 const size_t blk = (size_t)tb * nbu + u;
                 bulk_g2s(smem_u32(slot), p.act + blk * C::AQ, qb, smem_u32(&a_full_s[as]), policy);
-                bulk_g2s(smem_u32(slot + C::AQ), p.dx + blk * 128 * C::DX, db, smem_u32(&a_full_s[as]), policy);
+                bulk_g2s(smem_u32(slot + a_dx_off), p.dx + blk * 128 * C::DX, db, smem_u32(&a_full_s[as]), policy);
                 return true;
             };
             int i = 0, gu = 0;
@@ -802,12 +813,49 @@ __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_c
         // lanes 0-15 take the first half of rows 0-15, lanes 16-31 the second half: the 16-byte
         // stores of 8 consecutive lanes then land in 8 different bank groups
         const int pw = warp - 8, rr = lane & 15, hs = lane >> 4;
-        int i = 0;
+        const int tq = 4 * lane + pw;  // token of this thread's TMEM lane (quadrant pw = warp % 4)
+        int i = 0, gu = 0;
         for (int ch = 0; ch < n_chunks && !*abort_flag; ++ch) {
             int g0, ng;
             chunk_of(ch, g0, ng);
             const int ni = (ng + G - 1) / G;
-            for (int u = 0; u < nbu && !*abort_flag; ++u) {
+            for (int u = 0; u < nbu && !*abort_flag; ++u, ++gu) {
+                {
+                    // activation unit gu -> TMEM buffer gu & 1
+                    const int as = gu % SA, ab = gu & 1;
+                    int ok = 1;
+                    if (lane == 0)
+                        ok = wait(&a_full_s[as], (gu / SA) & 1) && wait(&t_empty[ab], ((gu >> 1) & 1) ^ 1) &&
+                             wait(&x_free[gu % SX], ((gu / SX) & 1) ^ 1);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint8_t *row = smem + C::OFF_A + (size_t)as * a_slot + (size_t)tq * C::AROW;
+                    {
+                        // the token's scales, kept for the epilogue after the activation slot is reused
+                        const float *dxs = reinterpret_cast<const float *>(smem + C::OFF_A + (size_t)as * a_slot + a_dx_off);
+                        float *dxd = reinterpret_cast<float *>(smem + C::OFF_X + (size_t)(gu % SX) * C::XSLOT);
+#pragma unroll
+                        for (int b = 0; b < C::DX; ++b) dxd[tq * C::DX + b] = (tq < Mb) ? dxs[tq * C::DX + b] : 0.0f;
+                    }
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        uint32_t v[32];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const uint4 w4 = (tq < Mb) ? lds128(row + 128 * half + 16 * k) : make_uint4(0u, 0u, 0u, 0u);
+                            v[4 * k] = w4.x, v[4 * k + 1] = w4.y, v[4 * k + 2] = w4.z, v[4 * k + 3] = w4.w;
+                        }
+                        tmem_st32(tmem + ((uint32_t)(32 * pw) << 16) + (uint32_t)(64 * ab + 32 * half), v);
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(smem_u32(&t_full[ab]));
+                        mbar_arrive(smem_u32(&a_empty_s[as]));
+                    }
+                }
                 for (int j = 0; j < ni; ++j, ++i) {
                     if (!COOP && (i & 3) != pw) continue;
                     const int ws = i % SW, sb = i % SB, sh = i % SH;
@@ -872,55 +920,14 @@ __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_c
             }
         }
     } else {
-        // ---------------- activation into TMEM (warps 0-3) and epilogue (warps 0-7)
+        // ---------------- epilogue (warps 0-7)
         const int q = warp & 3, h = warp >> 2;
-        const int t = 32 * q + lane;  // token lane
-        const bool live = 32 * q < Mb;  // this quadrant holds tokens of the block
+        const int t = 4 * lane + q;      // token of this thread's TMEM lane
+        const bool live = q < Mb;        // this quadrant holds tokens of the block
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         float acc[4][16];  // chunk row groups c with c % 2 == h, at acc[c / 2]
-        float dx0[C::DX], dx1[C::DX];  // scales of the units in TMEM buffers 0 and 1
+        float dxr[C::DX];  // the token's scales of the current unit
         int i = 0, gu = 0;
-        // activation unit gunit -> TMEM buffer gunit & 1 (warps 0-3), its scales -> dx0 / dx1 (all)
-        auto load_unit = [&](int gunit) -> bool {
-            const int as = gunit % SA, ab = gunit & 1;
-            int ok = 1;
-            if (lane == 0) {
-                ok = wait(&a_full_s[as], (gunit / SA) & 1);
-                if (ok && h == 0) ok = wait(&t_empty[ab], ((gunit >> 1) & 1) ^ 1);
-            }
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) return false;
-            const uint8_t *slot = smem + C::OFF_A + (size_t)as * C::ASLOT;
-            const float *dxs = reinterpret_cast<const float *>(slot + C::AQ) + (size_t)t * C::DX;
-#pragma unroll
-            for (int b = 0; b < C::DX; ++b) {
-                const float v = (t < Mb) ? dxs[b] : 0.0f;
-                if (ab) dx1[b] = v;
-                else dx0[b] = v;
-            }
-            if (h == 0) {
-                tc_fence_after();
-                const uint8_t *row = slot + (size_t)t * C::AROW;
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    uint32_t v[32];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const uint4 w4 = (t < Mb) ? lds128(row + 128 * half + 16 * k) : make_uint4(0u, 0u, 0u, 0u);
-                        v[4 * k] = w4.x, v[4 * k + 1] = w4.y, v[4 * k + 2] = w4.z, v[4 * k + 3] = w4.w;
-                    }
-                    tmem_st32(tmem + lane_base + (uint32_t)(64 * ab + 32 * half), v);
-                }
-                tmem_wait_st();
-                tc_fence_before();
-            }
-            __syncwarp();
-            if (lane == 0) {
-                if (h == 0) mbar_arrive(smem_u32(&t_full[ab]));
-                mbar_arrive(smem_u32(&a_empty_s[as]));
-            }
-            return true;
-        };
         for (int ch = 0; ch < n_chunks && !*abort_flag; ++ch) {
             int g0, ng;
             chunk_of(ch, g0, ng);
@@ -929,10 +936,7 @@ __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_c
             for (int k = 0; k < 4; ++k)
 #pragma unroll
                 for (int r = 0; r < 16; ++r) acc[k][r] = 0.0f;
-            if (!load_unit(gu)) break;
             for (int u = 0; u < nbu; ++u, ++gu) {
-                if (u + 1 < nbu && !load_unit(gu + 1)) break;
-                const int ab = gu & 1;
                 // items of the unit, unrolled so that every accumulator index is a constant
 #pragma unroll
                 for (int j = 0; j < RGM / G; ++j) {
@@ -943,6 +947,12 @@ __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_c
                     ok = __shfl_sync(0xffffffffu, ok, 0);
                     if (!ok) break;
                     tc_fence_after();
+                    if (j == 0) {
+                        // written by the prep warps before this unit's MMAs were issued
+                        const float *dxs = reinterpret_cast<const float *>(smem + C::OFF_X + (size_t)(gu % SX) * C::XSLOT);
+#pragma unroll
+                        for (int b = 0; b < C::DX; ++b) dxr[b] = dxs[t * C::DX + b];
+                    }
                     if (live) {
 #pragma unroll
                         for (int gi = 0; gi < G; ++gi) {
@@ -951,32 +961,28 @@ __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_c
                             const uint8_t *hdr = smem + C::OFF_H + (size_t)(it % SH) * C::HDR + (size_t)gi * 256;
                             const uint32_t td = tmem + lane_base + 128u + (uint32_t)(sd * C::NCOL + gi * NOP * 16);
                             if (TYPE == TYPE_Q8_0) {
-                                // eight block terms per (row, token), added in block order below
-                                float t8[8][16];
+                                // the eight 32-block terms of each (row, token), added in block order
 #pragma unroll
                                 for (int b = 0; b < 8; ++b) {
                                     uint32_t D[16];
                                     tmem_ld16(td + (uint32_t)(16 * b), D);
                                     tmem_wait_ld();
-                                    const float dxb = ab ? dx1[b] : dx0[b];
+                                    const float dxb = dxr[b];
 #pragma unroll
                                     for (int r = 0; r < 16; ++r) {
                                         const uint32_t dw = *reinterpret_cast<const uint32_t *>(hdr + 16 * r + 4 * (b >> 1));
                                         const float wd = half_bits_to_float(dw >> (16 * (b & 1)));
-                                        t8[b][r] = __fmul_rn(__fmul_rn(wd, dxb), __int2float_rn((int)D[r]));
+                                        acc[c >> 1][r] = __fadd_rn(acc[c >> 1][r],
+                                                                   __fmul_rn(__fmul_rn(wd, dxb), __int2float_rn((int)D[r])));
                                     }
                                 }
-#pragma unroll
-                                for (int r = 0; r < 16; ++r)
-#pragma unroll
-                                    for (int b = 0; b < 8; ++b) acc[c >> 1][r] = __fadd_rn(acc[c >> 1][r], t8[b][r]);
                             } else {
                                 float tm[16];
                                 uint32_t D[NOP][16];
 #pragma unroll
                                 for (int o = 0; o < NOP; ++o) tmem_ld16(td + (uint32_t)(16 * o), D[o]);
                                 tmem_wait_ld();
-                                const float dx = ab ? dx1[0] : dx0[0];
+                                const float dx = dxr[0];
 #pragma unroll
                                 for (int r = 0; r < 16; ++r) {
                                     if (TYPE == TYPE_Q6_K) {
@@ -1004,6 +1010,8 @@ __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_c
                     }
                 }
                 i += ni;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&x_free[gu % SX]));
                 if (*abort_flag) break;
             }
             if (*abort_flag) break;
