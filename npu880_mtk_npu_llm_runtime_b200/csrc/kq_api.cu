@@ -156,24 +156,24 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
         if (!x && !act) return fail(c, KQ_ERR_NOT_READY, "no activation for type %d", type);
         // M > 8: one of two tensor-core kernels or GEMV tiles of 8 tokens, by a cost model fitted
         // to B200 timings of the FFN and attention shapes (M = 9..512):
-        //  * weight-row-major tensor-core kernel (kq_gemm_tc.cu, 128 rows x 64 tokens per CTA,
-        //    all of K serially): ~2.8 us per 256-value unit (Q6_K ~4.2 us) per wave of CTAs;
+        //  * weight-row-major tensor-core kernel (kq_gemm_tc.cu, 128 or 64 rows x 16..64 tokens per
+        //    CTA, all of K serially): ~2-4 us per 256-value unit per wave of CTAs (tc_estimate_us);
         //  * token-major kernel (row groups spread over all SMs): ~3.5 us per item (a unit of
         //    up to 4 row groups, Q6_K 3) per wave;
         //  * GEMV tiles: the weights streamed once per 8 tokens at ~1 TB/s plus ~5 us a launch.
         int tc_kernel = 0;  // 0 GEMV tiles, 1 row-major, 3 token-major
         if (M > 8 && !ex.dbg_sumi && !ex.argmax && !ex.out_ids) {
-            long long rows = 0, rgs = 0;
+            long long rgs = 0;
             double wbytes = 0.0;
             for (int j : idx) {
-                rows += tasks[j].rows;
                 rgs += (tasks[j].row_begin + tasks[j].rows - 1) / 16 - tasks[j].row_begin / 16 + 1;
                 wbytes += (double)tasks[j].rows * (double)tasks[j].w->row_bytes;
             }
             const int nbu = K / 256, sms = c->num_sms;
-            const int bn = (type == KQ_TYPE_Q8_0) ? 32 : 64;
-            const long long ctas1 = ((M + bn - 1) / bn) * ((rows + 127) / 128);
-            const double t1 = (double)((ctas1 + sms - 1) / sms) * nbu * (type == KQ_TYPE_Q6_K ? 4.2e-6 : 2.8e-6);
+            int task_rgs[KQ_MAX_TASKS];
+            for (size_t j = 0; j < idx.size(); ++j)
+                task_rgs[j] = (tasks[idx[j]].row_begin + tasks[idx[j]].rows - 1) / 16 - tasks[idx[j]].row_begin / 16 + 1;
+            const double t1 = kq::tc_estimate_us(type, M, K, task_rgs, (int)idx.size(), sms) * 1e-6;
             const int n_tb = (M + 127) / 128, g = (type == KQ_TYPE_Q6_K) ? 3 : (type == KQ_TYPE_Q8_0) ? 1 : 4;
             const int rgmax = (type == KQ_TYPE_Q6_K) ? 6 : 8;
             const long long gx = std::min<long long>(rgs, std::max<long long>((sms + n_tb - 1) / n_tb, (rgs + rgmax - 1) / rgmax));

@@ -35,22 +35,26 @@ namespace kq {
 
 namespace {
 
-constexpr int kTcRows = 128;
 constexpr int kTcCompute = 256;  // 8 warps: two per TMEM lane quadrant, each half a row / half the tokens
 constexpr int kTcThreads = kTcCompute + 32;
 
-template <int TYPE>
+// ROWS weight rows (128, or 64 when 128-row CTAs would leave SMs idle) x BN tokens per CTA
+template <int TYPE, int BN_, int ROWS_>
 struct TcCfg {
-    static constexpr int BN = (TYPE == TYPE_Q8_0) ? 32 : 64;                   // tokens per CTA
+    static constexpr int BN = BN_, ROWS = ROWS_;
+    static constexpr int RG = ROWS / 16;                                             // row groups per CTA
     static constexpr int NA = (TYPE == TYPE_Q8_0) ? 1 : (TYPE == TYPE_Q6_K) ? 4 : 3;  // A operands
-    static constexpr int S = (TYPE == TYPE_Q6_K) ? 2 : (TYPE == TYPE_Q8_0) ? 4 : 3;   // ring stages
     static constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;                      // scales per token and unit
+    static constexpr unsigned OPS = (unsigned)ROWS * 256u;                      // bytes of one A operand
     static constexpr unsigned B_BYTES = BN * 256;
-    static constexpr unsigned W_BYTES = 8u * (unsigned)tile_bytes(TYPE);
+    static constexpr unsigned W_BYTES = (unsigned)RG * (unsigned)tile_bytes(TYPE);
     static constexpr unsigned DX_BYTES = BN * DX * 4;
     static constexpr unsigned STAGE = B_BYTES + W_BYTES + DX_BYTES;            // multiple of 16
-    static constexpr unsigned A_BYTES = NA * 32768u;
+    static constexpr unsigned A_BYTES = NA * OPS;
+    static constexpr int S_FIT = (int)((200u * 1024u - A_BYTES) / STAGE);
+    static constexpr int S = S_FIT < 2 ? 2 : (S_FIT > 6 ? 6 : S_FIT);          // ring stages
     static constexpr unsigned SMEM = A_BYTES + S * STAGE + 1024;
+    static_assert((TYPE == TYPE_Q8_0 ? 8 : NA) * BN <= 256, "accumulator buffer exceeds 256 TMEM columns");
 };
 
 struct TcParams {
@@ -235,24 +239,39 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, int hs, ui
 
 // ------------------------------------------------------------------ the kernel
 
-template <int TYPE>
+// TMEM load of N consecutive 32-bit columns of this thread's lane (N = 8, 16 or 32)
+template <int N>
+__device__ __forceinline__ void tmem_ldn(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 32) {
+        tmem_ld32(taddr, r);
+    } else if constexpr (N == 16) {
+        tmem_ld16(taddr, r);
+    } else {
+        static_assert(N == 8, "tmem_ldn: N must be 8, 16 or 32");
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                     : "r"(taddr));
+    }
+}
+
+template <int TYPE, int BN_, int ROWS_>
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ TcParams p) {
-    using C = TcCfg<TYPE>;
-    constexpr int BN = C::BN, NA = C::NA, S = C::S;
+    using C = TcCfg<TYPE, BN_, ROWS_>;
+    constexpr int BN = C::BN, NA = C::NA, S = C::S, RG = C::RG, ROWS = C::ROWS;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     __shared__ uint64_t bar_full[S], bar_empty[S], bar_mma[2];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
 
-    uint8_t *A = smem;                      // NA operands of 32 KB
+    uint8_t *A = smem;                      // NA operands of ROWS x 256 bytes
     uint8_t *ring = smem + C::A_BYTES;      // S stages: B | weights | dx
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tok_tile = blockIdx.x, row_tile = blockIdx.y;
     const int nbu = p.nbu;
-    const int rg0 = p.rg_first + 8 * row_tile;                         // first row group of the CTA
+    const int rg0 = p.rg_first + RG * row_tile;                        // first row group of the CTA
     const int rg_end = (p.row_begin + p.rows - 1) / 16 + 1;            // past the task's last row group
-    const int n_rg = min(8, rg_end - rg0);
+    const int n_rg = min(RG, rg_end - rg0);
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -296,12 +315,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         }
         __syncwarp();
     } else {
-        // ---------------- rows: A operands, MMA issue (thread 0), epilogue.  Warp w covers TMEM
-        // lanes / rows 32 (w % 4) .. +31 and half w / 4 of each row's values (A operands) and of
-        // the tokens (epilogue).
+        // ---------------- rows: A operands, MMA issue (warp 0), epilogue.  Warp w covers TMEM lane
+        // quadrant w % 4 and half w / 4 of each row's values (A operands) and of the tokens
+        // (epilogue).  128-row CTAs: row 32 (w % 4) + lane; 64-row CTAs (M = 64 MMA, rows 16 q ..
+        // 16 q + 15 in lanes 0-15 of quadrant q): row 16 (w % 4) + lane for lanes 0-15.
         constexpr int BH = BN / 2;
         const int quad = warp & 3, hs = warp >> 2;
-        const int r = 32 * quad + lane;  // weight row within the CTA = TMEM lane
+        const int r = (ROWS == 128) ? 32 * quad + lane : 16 * quad + (lane & 15);  // weight row within the CTA
+        const bool row_lane = (ROWS == 128) || lane < 16;
         const int g = r >> 4, rr = r & 15;
         float acc[BH];
 #pragma unroll
@@ -309,7 +330,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         float dpp[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // per buffer: d, dmin (Q8_0: block scales, packed)
         uint32_t dqq[2][2] = {{0u, 0u}, {0u, 0u}};
         const uint32_t idesc = (2u << 4) | ((TYPE == TYPE_Q6_K || TYPE == TYPE_Q8_0) ? (1u << 7) : 0u) | (1u << 10) |
-                               ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+                               ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(ROWS >> 4) << 24);
         const uint32_t lane_base = ((uint32_t)(32 * quad) << 16) + (uint32_t)(hs * BH);
 
         // epilogue of super-block e (its accumulators in buffer e & 1, scales in stage e % S)
@@ -322,24 +343,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 const uint32_t dw4[4] = {__float_as_uint(dpp[buf][0]), __float_as_uint(dpp[buf][1]), dqq[buf][0], dqq[buf][1]};
 #pragma unroll
                 for (int jj = 0; jj < 8; ++jj) {
-                    uint32_t D[16];
-                    tmem_ld16(tb + (uint32_t)(jj * BN), D);
+                    uint32_t D[BH];
+                    tmem_ldn<BH>(tb + (uint32_t)(jj * BN), D);
                     tmem_wait_ld();
                     const float dw = half_bits_to_float(dw4[jj >> 1] >> (16 * (jj & 1)));
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
+                    for (int i = 0; i < BH; ++i) {
                         const float t = __fmul_rn(__fmul_rn(dw, dxs[i * 8 + jj]), __int2float_rn((int)D[i]));
                         acc[i] = __fadd_rn(acc[i], t);
                     }
                 }
             } else {
-                uint32_t D[NA][32];
+                uint32_t D[NA][BH];
 #pragma unroll
-                for (int a = 0; a < NA; ++a) tmem_ld32(tb + (uint32_t)(a * BN), D[a]);
+                for (int a = 0; a < NA; ++a) tmem_ldn<BH>(tb + (uint32_t)(a * BN), D[a]);
                 tmem_wait_ld();
                 const float d = dpp[buf][0], dmin = dpp[buf][1];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
+                for (int i = 0; i < BH; ++i) {
                     const float dx = dxs[i];
                     float t;
                     if (TYPE == TYPE_Q6_K) {
@@ -369,11 +390,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                     if (!ok) s_abort = 1;
                 }
                 ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (ok) {
+                if (ok && row_lane) {
                     // A operands of super-block b (the MMAs of b - 1 have finished reading A)
                     const uint8_t *tile = ring + (size_t)st * C::STAGE + C::B_BYTES + (size_t)min(g, n_rg - 1) * tile_bytes(TYPE);
                     float d0, d1;
-                    prep_row<TYPE>(tile, rr, hs, A, r, d0, d1);
+                    prep_row<TYPE, C::OPS>(tile, rr, hs, A, r, d0, d1);
                     if (TYPE == TYPE_Q8_0) {
                         const uint4 dv = lds128(tile + 272 * rr);
                         dpp[b & 1][0] = __uint_as_float(dv.x);
@@ -406,7 +427,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                             for (int ks = 0; ks < 8; ++ks)
 #pragma unroll
                                 for (int a = 0; a < NA; ++a)
-                                    tc_mma(td + (uint32_t)(a * BN), umma_desc(sa + a * 32768 + 256 * ks, 128, 2048),
+                                    tc_mma(td + (uint32_t)(a * BN), umma_desc(sa + a * C::OPS + 256 * ks, 128, 2048),
                                            umma_desc(sbm + 256 * ks, 128, 2048), idesc, ks > 0);
                         }
                         tc_commit(smem_u32(&bar_mma[b & 1]));
@@ -433,7 +454,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         // results: row r, tokens tok_tile * BN + hs * BH + m
         const int row = rg0 * 16 + r;     // weight row
         const int lr = row - p.row_begin;  // task-local row
-        if (!s_abort && r < n_rg * 16 && lr >= 0 && lr < p.rows) {
+        if (!s_abort && row_lane && r < n_rg * 16 && lr >= 0 && lr < p.rows) {
 #pragma unroll
             for (int m = 0; m < BH; ++m) {
                 const int tok = tok_tile * BN + hs * BH + m;
@@ -465,10 +486,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 // plus the scales [token tile][unit][token][DX].  Tokens past M are zero.  One warp per (token,
 // unit); lane L holds values 8L .. 8L+7.
 
-template <int TYPE>
+template <int TYPE, int BN>
 __global__ void pack_act_kernel(const __half *x, long long x_stride, const void *act, int M, int K, int n_tok_tiles,
                                 uint8_t *out, float *dx) {
-    constexpr int BN = TcCfg<TYPE>::BN, DX = TcCfg<TYPE>::DX;
+    constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;
     const int nbu = K / 256;
     const int lane = threadIdx.x & 31;
     const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
@@ -529,35 +550,44 @@ __global__ void pack_act_kernel(const __half *x, long long x_stride, const void 
     }
 }
 
-template <int TYPE>
-cudaError_t launch_tc_t(const TcLaunch &L, cudaStream_t stream) {
-    using C = TcCfg<TYPE>;
-    const int nbu = L.K / 256;
-    const int n_tok_tiles = (L.M + C::BN - 1) / C::BN;
-    const size_t need = (size_t)n_tok_tiles * nbu * (C::B_BYTES + C::DX_BYTES);
-    if (L.scratch_bytes < need) return cudaErrorInvalidValue;
-    uint8_t *act = reinterpret_cast<uint8_t *>(L.scratch);
-    float *dx = reinterpret_cast<float *>(act + (size_t)n_tok_tiles * nbu * C::B_BYTES);
-    {
-        const long long items = (long long)n_tok_tiles * C::BN * nbu;
-        const int blocks = (int)std::min<long long>((items + 7) / 8, 148 * 16);
-        pack_act_kernel<TYPE><<<blocks, 256, 0, stream>>>(reinterpret_cast<const __half *>(L.x), L.x_stride, L.act,
-                                                           L.M, L.K, n_tok_tiles, act, dx);
-        cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
-    }
+template <int TYPE, int BN, int ROWS>
+cudaError_t configure_tc() {
     static std::mutex mu;
     static std::unordered_map<int, bool> configured;
     int dev = 0;
     cudaGetDevice(&dev);
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        if (!configured[dev]) {
-            cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-            if (e != cudaSuccess) return e;
-            configured[dev] = true;
-        }
+    std::lock_guard<std::mutex> lk(mu);
+    if (!configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<TYPE, BN, ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             TcCfg<TYPE, BN, ROWS>::SMEM);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
     }
+    return cudaSuccess;
+}
+
+bool tc_rows64(long long n_tok_tiles, long long n_rg, int sms) {
+    return n_tok_tiles * ((n_rg + 7) / 8) < sms && n_tok_tiles * ((n_rg + 3) / 4) <= sms;
+}
+
+template <int TYPE, int BN>
+cudaError_t launch_tc_bn(const TcLaunch &L, cudaStream_t stream) {
+    constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;
+    const int nbu = L.K / 256;
+    const int n_tok_tiles = (L.M + BN - 1) / BN;
+    const size_t need = (size_t)n_tok_tiles * nbu * ((size_t)BN * 256 + (size_t)BN * DX * 4);
+    if (L.scratch_bytes < need) return cudaErrorInvalidValue;
+    uint8_t *act = reinterpret_cast<uint8_t *>(L.scratch);
+    float *dx = reinterpret_cast<float *>(act + (size_t)n_tok_tiles * nbu * BN * 256);
+    {
+        const long long items = (long long)n_tok_tiles * BN * nbu;
+        const int blocks = (int)std::min<long long>((items + 7) / 8, 148 * 16);
+        pack_act_kernel<TYPE, BN><<<blocks, 256, 0, stream>>>(reinterpret_cast<const __half *>(L.x), L.x_stride, L.act,
+                                                               L.M, L.K, n_tok_tiles, act, dx);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    const int sms = L.num_sms > 0 ? L.num_sms : 148;
     for (int i = 0; i < L.n_tasks; ++i) {
         const GemvTaskHost &h = L.tasks[i];
         if (h.rows <= 0) continue;
@@ -581,12 +611,38 @@ cudaError_t launch_tc_t(const TcLaunch &L, cudaStream_t stream) {
         p.status = L.status;
         p.timeout_ns = L.timeout_ns;
         const int n_rg = (h.row_begin + h.rows - 1) / 16 - p.rg_first + 1;
-        dim3 grid(n_tok_tiles, (n_rg + 7) / 8);
-        gemm_tc_kernel<TYPE><<<grid, kTcThreads, C::SMEM, stream>>>(p);
-        cudaError_t e = cudaGetLastError();
+        // 64-row CTAs when 128-row ones would leave SMs idle and the 64-row grid still fits in one
+        // wave (one CTA per SM)
+        const bool rows64 = tc_rows64(n_tok_tiles, n_rg, sms);
+        cudaError_t e;
+        if (rows64) {
+            if ((e = configure_tc<TYPE, BN, 64>())) return e;
+            gemm_tc_kernel<TYPE, BN, 64><<<dim3(n_tok_tiles, (n_rg + 3) / 4), kTcThreads, TcCfg<TYPE, BN, 64>::SMEM, stream>>>(p);
+        } else {
+            if ((e = configure_tc<TYPE, BN, 128>())) return e;
+            gemm_tc_kernel<TYPE, BN, 128><<<dim3(n_tok_tiles, (n_rg + 7) / 8), kTcThreads, TcCfg<TYPE, BN, 128>::SMEM, stream>>>(p);
+        }
+        e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+// tokens per CTA of the row-major kernel: the smallest tile that holds M (at most 64; Q8_0 32)
+int tc_bn(int type, int M) {
+    const int cap = (type == TYPE_Q8_0) ? 32 : 64;
+    return M <= 16 ? 16 : (M <= 32 || cap == 32) ? 32 : 64;
+}
+
+template <int TYPE>
+cudaError_t launch_tc_t(const TcLaunch &L, cudaStream_t stream) {
+    switch (tc_bn(TYPE, L.M)) {
+        case 16: return launch_tc_bn<TYPE, 16>(L, stream);
+        case 32: return launch_tc_bn<TYPE, 32>(L, stream);
+        default:
+            if constexpr (TYPE != TYPE_Q8_0) return launch_tc_bn<TYPE, 64>(L, stream);
+            return cudaErrorInvalidValue;
+    }
 }
 
 
@@ -1192,9 +1248,22 @@ cudaError_t launch_tc2_t(const TcLaunch &L, cudaStream_t stream) {
 }  // namespace
 
 size_t tc_scratch_bytes(int type, int M, int K) {
-    const int nbu = K / 256;
-    auto need = [&](int bn, int dxn) { return (size_t)((M + bn - 1) / bn) * nbu * ((size_t)bn * 256 + (size_t)bn * dxn * 4); };
-    return type == TYPE_Q8_0 ? need(32, 8) : need(64, 1);
+    const int nbu = K / 256, bn = tc_bn(type, M), dxn = (type == TYPE_Q8_0) ? 8 : 1;
+    return (size_t)((M + bn - 1) / bn) * nbu * ((size_t)bn * 256 + (size_t)bn * dxn * 4);
+}
+
+double tc_estimate_us(int type, int M, int K, const int *task_rgs, int n_tasks, int sms) {
+    const int bn = tc_bn(type, M), nbu = K / 256;
+    const long long tiles = (M + bn - 1) / bn;
+    double t = 0.0;
+    for (int i = 0; i < n_tasks; ++i) {
+        const bool r64 = tc_rows64(tiles, task_rgs[i], sms);
+        const long long ctas = tiles * ((task_rgs[i] + (r64 ? 3 : 7)) / (r64 ? 4 : 8));
+        const bool small = r64 || bn < 64;
+        const double unit = (type == TYPE_Q6_K) ? (small ? 2.5 : 4.2) : (small ? 2.1 : 2.8);
+        t += (double)((ctas + sms - 1) / sms) * nbu * unit;
+    }
+    return t;
 }
 
 size_t tc2_scratch_bytes(int type, int M, int K) {

@@ -76,6 +76,8 @@ cudaError_t launch_gemv(const GemvLaunch &L, cudaStream_t stream);
 // rows ids[0..n) of a tiled tensor -> a new tiled tensor of n rows (weight_bytes(type, n, K))
 // kq_gemm_tc.cu
 size_t tc_scratch_bytes(int type, int M, int K);
+// rough time of the row-major kernel for tasks of task_rgs[i] row groups (cost model, microseconds)
+double tc_estimate_us(int type, int M, int K, const int *task_rgs, int n_tasks, int sms);
 cudaError_t launch_gemm_tc(const TcLaunch &L, cudaStream_t stream);
 // token-major variant (activation in tensor memory, row groups spread over all SMs)
 size_t tc2_scratch_bytes(int type, int M, int K);
