@@ -30,8 +30,8 @@ struct kq_ctx {
     bool own_stream = false;
     int num_sms = 0;
     int gemm_path = 0;           // M > 8: 0 auto, 1 tensor cores, 2 GEMV in tiles of 8 tokens
-    int *d_status = nullptr;     // device-side error word
-    int *h_status = nullptr;     // pinned host copy of it, read after the blocking calls' one sync
+    int *h_status = nullptr;     // error word: pinned host memory mapped into the device
+    int *d_status = nullptr;     // its device address (kernels write errors there)
     bool pdl = true;
     bool inject_timeout = false;  // test hook: GEMV consumers wait on a barrier nothing completes
     unsigned long long timeout_ns = 1000000000ull;
@@ -92,23 +92,17 @@ int ensure(kq_ctx *c, DevBuf &b, size_t bytes) {
     return KQ_OK;
 }
 
-// Read and clear the device status word after the stream drained (blocking calls copy it into
-// pinned host memory on their stream first, so one synchronize covers the work and the status).
-int status_result(kq_ctx *c) {
-    const int st = *c->h_status;
+// Read and clear the device status word after the stream drained.  The word lives in mapped
+// pinned host memory, so one synchronize covers the work and the status: no copy.
+int check_device_status(kq_ctx *c) {
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, e, "cudaStreamSynchronize");
+    volatile int *hs = c->h_status;
+    const int st = *hs;
     if (st == kq::DEV_OK) return KQ_OK;
-    *c->h_status = kq::DEV_OK;
-    cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream);
-    cudaStreamSynchronize(c->stream);
+    *hs = kq::DEV_OK;
     if (st == kq::DEV_ERR_TIMEOUT) return fail(c, KQ_ERR_TIMEOUT, "a device-side wait timed out");
     return fail(c, KQ_ERR_CUDA, "device error code %d", st);
-}
-
-int check_device_status(kq_ctx *c) {
-    cudaError_t e = cudaMemcpyAsync(c->h_status, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
-    if (e != cudaSuccess) return cuda_fail(c, e, "status readback");
-    return status_result(c);
 }
 
 int sync_and_check(kq_ctx *c) { return check_device_status(c); }
@@ -309,6 +303,18 @@ int current_act(kq_ctx *c, uint32_t type, const void **act) {
     return KQ_OK;
 }
 
+// Device address of a host buffer that is pinned and mapped (cudaHostAlloc / cudaMallocHost /
+// cudaHostRegister memory under unified addressing), else nullptr.  Results written there by a
+// kernel are visible to the host after the stream synchronizes, so no copy is needed.
+void *mapped_device_ptr(const void *host) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, host) != cudaSuccess) {
+        cudaGetLastError();  // pageable memory can report an error on some drivers: not sticky
+        return nullptr;
+    }
+    return (a.type == cudaMemoryTypeHost && a.devicePointer) ? a.devicePointer : nullptr;
+}
+
 // Strided row copy; one linear copy when the rows are contiguous on both sides (cheaper to issue).
 cudaError_t copy_rows(void *dst, size_t dpitch, const void *src, size_t spitch, size_t width, size_t height,
                       cudaMemcpyKind kind, cudaStream_t s) {
@@ -368,15 +374,14 @@ extern "C" int kq_init(int device, kq_ctx **out) {
         return KQ_ERR_NO_DEVICE;  // built for sm_100a only
     }
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMalloc(&c->d_status, sizeof(int)) != cudaSuccess ||
-        cudaMemset(c->d_status, 0, sizeof(int)) != cudaSuccess ||
-        cudaMallocHost(&c->h_status, sizeof(int)) != cudaSuccess) {
+        cudaHostAlloc(&c->h_status, sizeof(int), cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(&c->d_status, c->h_status, 0) != cudaSuccess) {
         if (c->stream) cudaStreamDestroy(c->stream);
-        cudaFree(c->d_status);
         if (c->h_status) cudaFreeHost(c->h_status);
         delete c;
         return KQ_ERR_CUDA;
     }
+    *c->h_status = kq::DEV_OK;
     c->own_stream = true;
     *out = c;
     return KQ_OK;
@@ -389,7 +394,6 @@ extern "C" int kq_destroy(kq_ctx *c) {
     for (DevBuf *b : {&c->x, &c->res, &c->out16, &c->out32, &c->q8k_pending, &c->q8k_cur, &c->q80_cur, &c->tmp,
                       &c->misc, &c->keys, &c->tcpack})
         if (b->p) cudaFree(b->p);
-    cudaFree(c->d_status);
     cudaFreeHost(c->h_status);
     if (c->own_stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -626,16 +630,28 @@ extern "C" int kq_sdot_gemm_multi_dispatch(kq_ctx *c, const uint16_t *x, int M, 
     if (int r = ensure(c, c->out32, o32 + 16)) return r;
     if (int r = ensure(c, c->res, ores + 16)) return r;
     kq_task dt[KQ_MAX_TASKS];
+    bool direct16[KQ_MAX_TASKS] = {}, direct32[KQ_MAX_TASKS] = {};
     for (int i = 0; i < n; ++i) {
         dt[i] = tasks[i];
         const size_t rows = (size_t)tasks[i].rows;
+        // outputs in pinned host memory are written by the kernel in place; others are staged
         if (tasks[i].dst) {
-            dt[i].dst = reinterpret_cast<uint16_t *>((uint8_t *)c->out16.p + off16[i]);
-            dt[i].dst_stride = rows;
+            if (void *dp = mapped_device_ptr(tasks[i].dst)) {
+                dt[i].dst = static_cast<uint16_t *>(dp);
+                direct16[i] = true;
+            } else {
+                dt[i].dst = reinterpret_cast<uint16_t *>((uint8_t *)c->out16.p + off16[i]);
+                dt[i].dst_stride = rows;
+            }
         }
         if (tasks[i].dst_f32) {
-            dt[i].dst_f32 = reinterpret_cast<float *>((uint8_t *)c->out32.p + off32[i]);
-            dt[i].dst_f32_stride = rows;
+            if (void *dp = mapped_device_ptr(tasks[i].dst_f32)) {
+                dt[i].dst_f32 = static_cast<float *>(dp);
+                direct32[i] = true;
+            } else {
+                dt[i].dst_f32 = reinterpret_cast<float *>((uint8_t *)c->out32.p + off32[i]);
+                dt[i].dst_f32_stride = rows;
+            }
         }
         if (tasks[i].residual) {
             uint16_t *rd = reinterpret_cast<uint16_t *>((uint8_t *)c->res.p + offr[i]);
@@ -671,10 +687,10 @@ extern "C" int kq_sdot_gemm_multi_dispatch(kq_ctx *c, const uint16_t *x, int M, 
     if (r) return r;
     for (int i = 0; i < n; ++i) {
         const size_t rows = (size_t)tasks[i].rows;
-        if (tasks[i].dst)
+        if (tasks[i].dst && !direct16[i])
             KQ_CUDA(c, copy_rows(tasks[i].dst, tasks[i].dst_stride * 2, dt[i].dst, rows * 2, rows * 2, M,
                                          cudaMemcpyDeviceToHost, c->stream));
-        if (tasks[i].dst_f32)
+        if (tasks[i].dst_f32 && !direct32[i])
             KQ_CUDA(c, copy_rows(tasks[i].dst_f32, tasks[i].dst_f32_stride * 4, dt[i].dst_f32, rows * 4,
                                          rows * 4, M, cudaMemcpyDeviceToHost, c->stream));
     }

@@ -130,6 +130,14 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
     return ok != 0;
 }
 
+// Record a device-side error in the context's status word (pinned host memory mapped into the
+// device: the host reads it after the stream synchronizes, without a copy).  Every writer stores
+// the same kind of code, so a plain store suffices.
+__device__ __forceinline__ void report_error(int *status, int code) {
+    *reinterpret_cast<volatile int *>(status) = code;
+    __threadfence_system();
+}
+
 // Bounded wait on an mbarrier phase.  Gives up after timeout_ns of wall time, records
 // DEV_ERR_TIMEOUT in *status and returns false; never traps.  Polls without a suspend hint
 // (a suspended thread wakes up later than a polling one, which costs latency on the critical
@@ -141,7 +149,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
         for (int i = 0; i < 64; ++i)
             if (mbar_try_wait(bar, parity)) return true;
         if (global_timer_ns() - t0 > timeout_ns) {
-            if (status) atomicExch(status, DEV_ERR_TIMEOUT);
+            if (status) report_error(status, DEV_ERR_TIMEOUT);
             return false;
         }
     }
@@ -157,7 +165,7 @@ __device__ __forceinline__ bool mbar_wait_bounded_sleep(uint32_t bar, uint32_t p
         for (int i = 0; i < 8; ++i)
             if (mbar_try_wait_sleep(bar, parity, 200u)) return true;
         if (global_timer_ns() - t0 > timeout_ns) {
-            if (status) atomicExch(status, DEV_ERR_TIMEOUT);
+            if (status) report_error(status, DEV_ERR_TIMEOUT);
             return false;
         }
     }
@@ -268,7 +276,7 @@ __device__ __forceinline__ bool wait_ge_bounded(const int *p, int v, uint64_t ti
         for (int i = 0; i < 64; ++i)
             if (*vp >= v) return true;
         if (global_timer_ns() - t0 > timeout_ns) {
-            if (status) atomicExch(status, DEV_ERR_TIMEOUT);
+            if (status) report_error(status, DEV_ERR_TIMEOUT);
             return false;
         }
     }

@@ -133,6 +133,28 @@ def test_fp16_input_path_equals_prequantized(kqctx, oracle):
         assert np.array_equal(bits(out.cpu().numpy()), bits(ref))
 
 
+def test_dispatch_golden_pinned_outputs(kqctx):
+    """the same dispatch with outputs in pinned host memory (written by the kernel in place) and a
+    strided fp16 destination; the input stays pageable"""
+    import torch
+    g = load_golden("dispatch_q4k_q6k")
+    K = int(g["K"])
+    W0 = kqctx.upload(g["w0"], kq.TYPE_Q4_K, g["w0"].shape[0], K)
+    W1 = kqctx.upload(g["w1"], kq.TYPE_Q6_K, g["w1"].shape[0], K)
+    M = g["x"].shape[0]
+    t0 = torch.full((M, 48), -1.0, dtype=torch.float16).pin_memory()   # stride 48 > 40 rows
+    t1 = torch.zeros((M, 24), dtype=torch.float16).pin_memory()
+    d0, d1 = t0.numpy(), t1.numpy()
+    try:
+        kqctx.sdot_gemm_multi_dispatch(g["x"], [dict(w=W0, dst=d0, residual=g["res0"], rows=40), dict(w=W1, dst=d1)])
+        assert np.array_equal(bits(d0[:, :40]), bits(g["dst0"]))
+        assert np.all(d0[:, 40:] == -1.0)  # the stride padding is untouched
+        assert np.array_equal(bits(d1), bits(g["dst1"]))
+    finally:
+        W0.free()
+        W1.free()
+
+
 def test_dispatch_golden(kqctx):
     """kq_sdot_gemm_multi_dispatch (host pointers) == the reference dispatch's fp16 outputs"""
     g = load_golden("dispatch_q4k_q6k")
