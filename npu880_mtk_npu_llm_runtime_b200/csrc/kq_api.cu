@@ -38,7 +38,7 @@ struct kq_ctx {
     std::string err;
 
     // scratch (grown on demand, freed at destroy)
-    DevBuf x, res, out16, out32, q8k_pending, q8k_cur, q80_cur, tmp, misc, keys, tcpack;
+    DevBuf x, res, out16, out32, q8k_pending, q8k_cur, q80_cur, tmp, misc, keys, tcpack, tcterms;
 
     // the engine's g_sdot_input state: pending pre-quantized Q8_K input (ENG:4184) and the
     // current input rows for row-level calls (kept as fp16 on the device, quantized lazily)
@@ -171,8 +171,8 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
             const int n_tb = (M + 127) / 128, g = (type == KQ_TYPE_Q6_K) ? 3 : (type == KQ_TYPE_Q8_0) ? 1 : 4;
             const int rgmax = (type == KQ_TYPE_Q6_K) ? 6 : 8;
             const long long gx = std::min<long long>(rgs, std::max<long long>((sms + n_tb - 1) / n_tb, (rgs + rgmax - 1) / rgmax));
-            const long long rg_cta = (rgs + gx - 1) / gx;
-            const double t3 = (double)((gx * n_tb + sms - 1) / sms) * nbu * ((rg_cta + g - 1) / g) * 3.5e-6;
+            const double items = std::max(1.0, (double)rgs / (double)gx / g);  // items per unit of an average CTA
+            const double t3 = (double)((gx * n_tb + sms - 1) / sms) * nbu * items * 3.5e-6;
             const double tg = (double)((M + 7) / 8) * (wbytes / 1.0e12 + 5.0e-6);
             if (c->gemm_path == 1 || c->gemm_path == 3) tc_kernel = c->gemm_path;
             else if (c->gemm_path == 0) tc_kernel = (tg <= std::min(t1, t3)) ? 0 : (t1 <= t3 ? 1 : 3);
@@ -208,6 +208,18 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
             T.status = c->d_status;
             T.timeout_ns = c->timeout_ns;
             T.num_sms = c->num_sms;
+            if (!tc2) {
+                int trows[KQ_MAX_TASKS], trgs[KQ_MAX_TASKS];
+                for (int j = 0; j < T.n_tasks; ++j) {
+                    trows[j] = T.tasks[j].rows;
+                    trgs[j] = (T.tasks[j].row_begin + T.tasks[j].rows - 1) / 16 - T.tasks[j].row_begin / 16 + 1;
+                }
+                T.terms_bytes = kq::tc_split_terms_bytes(type, M, K, trows, trgs, T.n_tasks, c->num_sms);
+                if (T.terms_bytes) {
+                    if (int r = ensure(c, c->tcterms, T.terms_bytes)) return r;
+                    T.terms = c->tcterms.p;
+                }
+            }
             if (cudaError_t e = tc2 ? kq::launch_gemm_tc2(T, c->stream) : kq::launch_gemm_tc(T, c->stream))
                 return cuda_fail(c, e, "tensor-core gemm launch");
             continue;
@@ -392,7 +404,7 @@ extern "C" int kq_destroy(kq_ctx *c) {
     cudaSetDevice(c->device);
     cudaStreamSynchronize(c->stream);
     for (DevBuf *b : {&c->x, &c->res, &c->out16, &c->out32, &c->q8k_pending, &c->q8k_cur, &c->q80_cur, &c->tmp,
-                      &c->misc, &c->keys, &c->tcpack})
+                      &c->misc, &c->keys, &c->tcpack, &c->tcterms})
         if (b->p) cudaFree(b->p);
     cudaFreeHost(c->h_status);
     if (c->own_stream) cudaStreamDestroy(c->stream);

@@ -36,6 +36,7 @@ namespace kq {
 namespace {
 
 constexpr int kTcCompute = 256;  // 8 warps: two per TMEM lane quadrant, each half a row / half the tokens
+constexpr int kTcSplitBN = 32;   // largest token tile that may split K
 constexpr int kTcThreads = kTcCompute + 32;
 
 // ROWS weight rows (128, or 64 when 128-row CTAs would leave SMs idle) x BN tokens per CTA
@@ -73,6 +74,9 @@ struct TcParams {
     long long f32_stride;
     int *status;
     unsigned long long timeout_ns;
+    // split K over gridDim.z chunks: each CTA writes the fp32 block terms of its units to
+    // terms[u][token][task row] and tc_fold_kernel adds them in unit order (nullptr: one chunk)
+    float *terms;
 };
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -272,6 +276,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     const int rg0 = p.rg_first + RG * row_tile;                        // first row group of the CTA
     const int rg_end = (p.row_begin + p.rows - 1) / 16 + 1;            // past the task's last row group
     const int n_rg = min(RG, rg_end - rg0);
+    // units [u0, u0 + nb) of this K chunk (all of K without split)
+    const int u0 = (int)((long long)p.nbu * blockIdx.z / gridDim.z);
+    const int nb = (int)((long long)p.nbu * (blockIdx.z + 1) / gridDim.z) - u0;
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -296,7 +303,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         // ---------------- producer
         if (lane == 0) {
             const uint64_t policy = l2_evict_first_policy();
-            for (int b = 0; b < nbu; ++b) {
+            for (int b = 0; b < nb; ++b) {
                 const int st = b % S;
                 if (b >= S && !mbar_wait_bounded(smem_u32(&bar_empty[st]), ((b / S) - 1) & 1, p.timeout_ns, p.status)) {
                     s_abort = 1;
@@ -305,11 +312,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 const uint32_t full = smem_u32(&bar_full[st]);
                 uint8_t *sb = ring + (size_t)st * C::STAGE;
                 mbar_arrive_expect_tx(full, C::B_BYTES + (uint32_t)n_rg * (uint32_t)tile_bytes(TYPE) + C::DX_BYTES);
-                const size_t tix = (size_t)tok_tile * nbu + b;
+                const size_t tix = (size_t)tok_tile * nbu + u0 + b;
                 bulk_g2s(smem_u32(sb), p.act + tix * C::B_BYTES, C::B_BYTES, full, policy);
                 for (int g = 0; g < n_rg; ++g)
                     bulk_g2s(smem_u32(sb + C::B_BYTES + g * tile_bytes(TYPE)),
-                             p.w + ((size_t)(rg0 + g) * nbu + b) * tile_bytes(TYPE), tile_bytes(TYPE), full, policy);
+                             p.w + ((size_t)(rg0 + g) * nbu + u0 + b) * tile_bytes(TYPE), tile_bytes(TYPE), full, policy);
                 bulk_g2s(smem_u32(sb + C::B_BYTES + C::W_BYTES), p.dx + tix * (BN * C::DX), C::DX_BYTES, full, policy);
             }
         }
@@ -333,6 +340,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                                ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(ROWS >> 4) << 24);
         const uint32_t lane_base = ((uint32_t)(32 * quad) << 16) + (uint32_t)(hs * BH);
 
+        const int lr_out = rg0 * 16 + r - p.row_begin;  // task-local row of this thread
+        const bool row_out = row_lane && r < n_rg * 16 && lr_out >= 0 && lr_out < p.rows;
+        // block term number q (of the whole row) of token slot i: added in order (one chunk) or
+        // stored for the fold
+        auto put = [&](int q, int i, float t) {
+            if constexpr (kTcSplitBN >= BN) {  // split K is planned only for small token tiles
+                if (p.terms) {
+                    const int tok = tok_tile * BN + hs * BH + i;
+                    if (row_out && tok < p.M) p.terms[((size_t)q * p.M + tok) * p.rows + lr_out] = t;
+                    return;
+                }
+            }
+            acc[i] = __fadd_rn(acc[i], t);
+        };
         // epilogue of super-block e (its accumulators in buffer e & 1, scales in stage e % S)
         auto epilogue = [&](int e) {
             const int buf = e & 1;
@@ -350,28 +371,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 #pragma unroll
                     for (int i = 0; i < BH; ++i) {
                         const float t = __fmul_rn(__fmul_rn(dw, dxs[i * 8 + jj]), __int2float_rn((int)D[i]));
-                        acc[i] = __fadd_rn(acc[i], t);
+                        put((u0 + e) * 8 + jj, i, t);
                     }
                 }
             } else {
-                uint32_t D[NA][BH];
-#pragma unroll
-                for (int a = 0; a < NA; ++a) tmem_ldn<BH>(tb + (uint32_t)(a * BN), D[a]);
-                tmem_wait_ld();
+                // split-capable tiles read the accumulators in chunks of at most 16 token columns
+                // (keeps them in registers next to the split bookkeeping)
+                constexpr int CW = (BN > kTcSplitBN || BH < 16) ? BH : 16;
                 const float d = dpp[buf][0], dmin = dpp[buf][1];
 #pragma unroll
-                for (int i = 0; i < BH; ++i) {
-                    const float dx = dxs[i];
-                    float t;
-                    if (TYPE == TYPE_Q6_K) {
-                        const int sumi = (int)D[0][i] + 8 * (int)D[1][i] + 16 * (int)D[2][i] + 128 * (int)D[3][i];
-                        t = __fmul_rn(__fmul_rn(d, dx), __int2float_rn(sumi));
-                    } else {
-                        const int sumi = 8 * (int)D[0][i] + (int)D[1][i];
-                        const int summ = (int)D[2][i];
-                        t = __fmul_rn(dx, __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dmin, __int2float_rn(summ))));
+                for (int c0 = 0; c0 < BH; c0 += CW) {
+                    uint32_t D[NA][CW];
+#pragma unroll
+                    for (int a = 0; a < NA; ++a) tmem_ldn<CW>(tb + (uint32_t)(a * BN + c0), D[a]);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < CW; ++i) {
+                        const float dx = dxs[c0 + i];
+                        float t;
+                        if (TYPE == TYPE_Q6_K) {
+                            const int sumi = (int)D[0][i] + 8 * (int)D[1][i] + 16 * (int)D[2][i] + 128 * (int)D[3][i];
+                            t = __fmul_rn(__fmul_rn(d, dx), __int2float_rn(sumi));
+                        } else {
+                            const int sumi = 8 * (int)D[0][i] + (int)D[1][i];
+                            const int summ = (int)D[2][i];
+                            t = __fmul_rn(dx, __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dmin, __int2float_rn(summ))));
+                        }
+                        put(u0 + e, c0 + i, t);
                     }
-                    acc[i] = __fadd_rn(acc[i], t);
                 }
             }
             tc_fence_before();
@@ -379,8 +406,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 
         // Waits record a failure in s_abort; every warp reads it after the next barrier, so all
         // eight leave the loop together.
-        for (int b = 0; b <= nbu; ++b) {
-            if (b < nbu) {
+        for (int b = 0; b <= nb; ++b) {
+            if (b < nb) {
                 const int st = b % S;
                 int ok = 1;
                 if (lane == 0) {
@@ -452,9 +479,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             }
         }
         // results: row r, tokens tok_tile * BN + hs * BH + m
-        const int row = rg0 * 16 + r;     // weight row
-        const int lr = row - p.row_begin;  // task-local row
-        if (!s_abort && row_lane && r < n_rg * 16 && lr >= 0 && lr < p.rows) {
+        const int lr = lr_out;
+        if (!s_abort && !(kTcSplitBN >= BN && p.terms) && row_out) {
 #pragma unroll
             for (int m = 0; m < BH; ++m) {
                 const int tok = tok_tile * BN + hs * BH + m;
@@ -474,8 +500,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
     // drain: copies in flight must land before the CTA exits (only after an early stop)
     if (tid == kTcCompute) {
-        for (int b = max(0, nbu - S); b < nbu; ++b)
+        for (int b = max(0, nb - S); b < nb; ++b)
             mbar_wait_bounded(smem_u32(&bar_full[b % S]), (b / S) & 1, p.timeout_ns, p.status);
+    }
+}
+
+// Sum of the block terms of one split-K product in unit order (the reference's acc += term
+// sequence), then the outputs as the single-chunk epilogue writes them.  One thread per (token,
+// task row); terms[u][token][row] with nterm terms per row (Q8_0: eight per unit).
+__global__ void tc_fold_kernel(const float *terms, int nterm, int M, int rows, __half *dst, long long dst_stride,
+                               const __half *res, long long res_stride, float *dst_f32, long long f32_stride) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)M * rows) return;
+    const int tok = (int)(idx / rows), lr = (int)(idx % rows);
+    float acc = 0.0f;
+    for (int u = 0; u < nterm; ++u) acc = __fadd_rn(acc, terms[((size_t)u * M + tok) * rows + lr]);
+    if (dst_f32) dst_f32[(size_t)tok * f32_stride + lr] = acc;
+    if (dst) {
+        float v = acc;
+        if (res) v = __fadd_rn(v, __half2float(res[(size_t)tok * res_stride + lr]));
+        dst[(size_t)tok * dst_stride + lr] = __float2half_rn(v);
     }
 }
 
@@ -570,6 +614,21 @@ bool tc_rows64(long long n_tok_tiles, long long n_rg, int sms) {
     return n_tok_tiles * ((n_rg + 7) / 8) < sms && n_tok_tiles * ((n_rg + 3) / 4) <= sms;
 }
 
+// K chunks of the row-major kernel: split K (terms folded by tc_fold_kernel) when the grid would
+// use at most half of the SMs and every chunk keeps at least 4 units
+int tc_ksplit(int type, int bn, long long n_tok_tiles, long long n_rg, int nbu, int sms) {
+    const long long ctas = tc_rows64(n_tok_tiles, n_rg, sms) ? n_tok_tiles * ((n_rg + 3) / 4) : n_tok_tiles * ((n_rg + 7) / 8);
+    // Q8_0 keeps eight terms per unit: its term buffer would outgrow the weights
+    if (type == TYPE_Q8_0 || bn > kTcSplitBN || nbu < 8 || 2 * ctas > sms) return 1;
+    return (int)std::max<long long>(1, std::min<long long>(nbu / 4, sms / ctas));
+}
+
+// fp32 block terms of one split-K task: (terms per row) x M x rows
+size_t tc_terms_bytes(int type, int M, int K, int rows) {
+    const size_t nterm = (size_t)(K / 256) * (type == TYPE_Q8_0 ? 8 : 1);
+    return nterm * (size_t)M * (size_t)rows * 4;
+}
+
 template <int TYPE, int BN>
 cudaError_t launch_tc_bn(const TcLaunch &L, cudaStream_t stream) {
     constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;
@@ -588,6 +647,7 @@ cudaError_t launch_tc_bn(const TcLaunch &L, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
     }
     const int sms = L.num_sms > 0 ? L.num_sms : 148;
+    size_t terms_used = 0;
     for (int i = 0; i < L.n_tasks; ++i) {
         const GemvTaskHost &h = L.tasks[i];
         if (h.rows <= 0) continue;
@@ -612,18 +672,32 @@ cudaError_t launch_tc_bn(const TcLaunch &L, cudaStream_t stream) {
         p.timeout_ns = L.timeout_ns;
         const int n_rg = (h.row_begin + h.rows - 1) / 16 - p.rg_first + 1;
         // 64-row CTAs when 128-row ones would leave SMs idle and the 64-row grid still fits in one
-        // wave (one CTA per SM)
+        // wave (one CTA per SM); K split when even that leaves most SMs idle
         const bool rows64 = tc_rows64(n_tok_tiles, n_rg, sms);
+        const int ks = tc_ksplit(TYPE, BN, n_tok_tiles, n_rg, nbu, sms);
+        if (ks > 1) {
+            if (!L.terms || L.terms_bytes < terms_used + tc_terms_bytes(TYPE, L.M, L.K, h.rows)) return cudaErrorInvalidValue;
+            p.terms = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(L.terms) + terms_used);
+            terms_used += tc_terms_bytes(TYPE, L.M, L.K, h.rows);
+        }
         cudaError_t e;
         if (rows64) {
             if ((e = configure_tc<TYPE, BN, 64>())) return e;
-            gemm_tc_kernel<TYPE, BN, 64><<<dim3(n_tok_tiles, (n_rg + 3) / 4), kTcThreads, TcCfg<TYPE, BN, 64>::SMEM, stream>>>(p);
+            gemm_tc_kernel<TYPE, BN, 64><<<dim3(n_tok_tiles, (n_rg + 3) / 4, ks), kTcThreads, TcCfg<TYPE, BN, 64>::SMEM, stream>>>(p);
         } else {
             if ((e = configure_tc<TYPE, BN, 128>())) return e;
-            gemm_tc_kernel<TYPE, BN, 128><<<dim3(n_tok_tiles, (n_rg + 7) / 8), kTcThreads, TcCfg<TYPE, BN, 128>::SMEM, stream>>>(p);
+            gemm_tc_kernel<TYPE, BN, 128><<<dim3(n_tok_tiles, (n_rg + 7) / 8, ks), kTcThreads, TcCfg<TYPE, BN, 128>::SMEM, stream>>>(p);
         }
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
+        if (ks > 1) {
+            const long long n = (long long)L.M * h.rows;
+            tc_fold_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(p.terms, (TYPE == TYPE_Q8_0) ? 8 * nbu : nbu, L.M, h.rows,
+                                                                       p.dst, p.dst_stride, p.res, p.res_stride, p.dst_f32,
+                                                                       p.f32_stride);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+        }
     }
     return cudaSuccess;
 }
@@ -1252,16 +1326,28 @@ size_t tc_scratch_bytes(int type, int M, int K) {
     return (size_t)((M + bn - 1) / bn) * nbu * ((size_t)bn * 256 + (size_t)bn * dxn * 4);
 }
 
+size_t tc_split_terms_bytes(int type, int M, int K, const int *task_rows, const int *task_rgs, int n_tasks, int sms) {
+    const int bn = tc_bn(type, M);
+    const long long tiles = (M + bn - 1) / bn;
+    size_t total = 0;
+    for (int i = 0; i < n_tasks; ++i)
+        if (tc_ksplit(type, bn, tiles, task_rgs[i], K / 256, sms) > 1) total += tc_terms_bytes(type, M, K, task_rows[i]);
+    return total;
+}
+
 double tc_estimate_us(int type, int M, int K, const int *task_rgs, int n_tasks, int sms) {
     const int bn = tc_bn(type, M), nbu = K / 256;
     const long long tiles = (M + bn - 1) / bn;
     double t = 0.0;
     for (int i = 0; i < n_tasks; ++i) {
         const bool r64 = tc_rows64(tiles, task_rgs[i], sms);
-        const long long ctas = tiles * ((task_rgs[i] + (r64 ? 3 : 7)) / (r64 ? 4 : 8));
+        const int ks = tc_ksplit(type, bn, tiles, task_rgs[i], nbu, sms);
+        const long long ctas = tiles * ((task_rgs[i] + (r64 ? 3 : 7)) / (r64 ? 4 : 8)) * ks;
         const bool small = r64 || bn < 64;
-        const double unit = (type == TYPE_Q6_K) ? (small ? 2.5 : 4.2) : (small ? 2.1 : 2.8);
-        t += (double)((ctas + sms - 1) / sms) * nbu * unit;
+        // per 256-value unit per wave (B200 timings): Q8_0's eight 32-block accumulators per unit
+        // make it the slowest
+        const double unit = (type == TYPE_Q8_0) ? 6.0 : (type == TYPE_Q6_K) ? (small ? 2.5 : 4.2) : (small ? 2.1 : 2.8);
+        t += (double)((ctas + sms - 1) / sms) * ((nbu + ks - 1) / ks) * unit + (ks > 1 ? 3.0 : 0.0);
     }
     return t;
 }

@@ -69,6 +69,8 @@ struct TcLaunch {
     int *status;
     unsigned long long timeout_ns;
     int num_sms = 0;
+    void *terms = nullptr;       // split-K block terms (tc_split_terms_bytes)
+    size_t terms_bytes = 0;
 };
 
 // kq_gemv.cu
@@ -76,6 +78,8 @@ cudaError_t launch_gemv(const GemvLaunch &L, cudaStream_t stream);
 // rows ids[0..n) of a tiled tensor -> a new tiled tensor of n rows (weight_bytes(type, n, K))
 // kq_gemm_tc.cu
 size_t tc_scratch_bytes(int type, int M, int K);
+// bytes of the split-K term buffer the row-major kernel needs for these tasks (0: no split)
+size_t tc_split_terms_bytes(int type, int M, int K, const int *task_rows, const int *task_rgs, int n_tasks, int sms);
 // rough time of the row-major kernel for tasks of task_rgs[i] row groups (cost model, microseconds)
 double tc_estimate_us(int type, int M, int K, const int *task_rgs, int n_tasks, int sms);
 cudaError_t launch_gemm_tc(const TcLaunch &L, cudaStream_t stream);

@@ -88,6 +88,35 @@ def test_tc_fp16_input_tasks_residual(kqctx, oracle, gtype):
             W.free()
 
 
+@pytest.mark.parametrize("gtype", TYPES, ids=lambda t: synth.TYPE_NAMES[t])
+@pytest.mark.parametrize("M", [12, 32])
+def test_tc_split_k(kqctx, oracle, gtype, M):
+    """few rows and a long K: the row-major kernel splits K over CTAs, stores the block terms and
+    a fold kernel adds them in unit order (fp32, fp16 + residual, an unaligned row range)"""
+    import torch
+    rows_w, rb, n, K = 320, 5, 290, 4096
+    w = synth.gen_weights(gtype, rows_w, K, seed=1700 + gtype + M)
+    x = synth.gen_activations(M, K, seed=1701 + M)
+    act = oracle.act_for(gtype, x)
+    res = torch.from_numpy(synth.gen_activations(M, n, seed=1702).view(np.uint16).copy()).to("cuda")
+    W = kqctx.upload(w, gtype, rows_w, K)
+    try:
+        o32 = torch.full((M, n), float("nan"), dtype=torch.float32, device="cuda")
+        o16 = torch.zeros((M, n), dtype=torch.float16, device="cuda")
+        a = to_dev(act)
+        q8k, q80 = (None, a) if gtype == kq.TYPE_Q8_0 else (a, None)
+        kqctx.gemm_multi_q8_async(q8k, q80, M, K, [dict(w=W, row_begin=rb, rows=n, dst_f32=o32, dst=o16, residual=res)])
+        kqctx.synchronize()
+        got = o32.cpu().numpy()
+        got16 = o16.cpu().numpy()
+    finally:
+        W.free()
+    ref = oracle.gemm(gtype, w[rb:rb + n], K, act)
+    assert np.array_equal(bits(got), bits(ref)), f"max |diff| {np.abs(got - ref).max()}"
+    r16 = (ref + res.cpu().numpy().view(np.float16).astype(np.float32)).astype(np.float16)
+    assert np.array_equal(got16.view(np.uint16), r16.view(np.uint16))
+
+
 def test_tc_ffn_down_shape(kqctx, oracle):
     """the tree-verify FFN down projection shape (Q6_K, K = 9728) at M = 16"""
     import torch
