@@ -83,7 +83,11 @@ const char *kq_last_error(const kq_ctx *ctx);
  * "gemm_path" -- products of more than 8 activation rows: 0 chooses by a cost model, 1 always
  * the weight-row-major tensor-core kernel (tcgen05; weight rows as the MMA's A operand), 2 always
  * the GEMV kernel in tiles of 8 rows, 3 always the token-major tensor-core kernel (activation
- * tokens as A in tensor memory, row groups spread over all SMs) (default 0). */
+ * tokens as A in tensor memory, row groups spread over all SMs) (default 0);
+ * "gemv_split" -- GEMV launches (up to 8 activation rows) whose row groups would spread unevenly
+ * over the SMs give every CTA an equal range of 16-row x 256-value tiles instead; a row group
+ * shared by neighbouring CTAs is summed in block order by the last of them (1, default); 0 keeps
+ * whole row groups per CTA. */
 int kq_set_option(kq_ctx *ctx, const char *name, long long value);
 
 /* compute_ggml_bytes / ggml_row_bytes (ENG:364-374, ENG:3940): bytes of one GGUF row of k

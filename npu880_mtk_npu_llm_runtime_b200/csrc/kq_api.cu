@@ -39,6 +39,11 @@ struct kq_ctx {
 
     // scratch (grown on demand, freed at destroy)
     DevBuf x, res, out16, out32, q8k_pending, q8k_cur, q80_cur, tmp, misc, keys, tcpack, tcterms;
+    // balanced GEMV launches: shared-row-group term slots and arrival counts (zero between
+    // launches; re-cleared after a launch that stopped early)
+    DevBuf gsplit, gcount;
+    bool gemv_split = true;
+    bool split_dirty = false;
 
     // the engine's g_sdot_input state: pending pre-quantized Q8_K input (ENG:4184) and the
     // current input rows for row-level calls (kept as fp16 on the device, quantized lazily)
@@ -101,6 +106,7 @@ int check_device_status(kq_ctx *c) {
     const int st = *hs;
     if (st == kq::DEV_OK) return KQ_OK;
     *hs = kq::DEV_OK;
+    c->split_dirty = true;  // a kernel that stopped early may have left arrival counts behind
     if (st == kq::DEV_ERR_TIMEOUT) return fail(c, KQ_ERR_TIMEOUT, "a device-side wait timed out");
     return fail(c, KQ_ERR_CUDA, "device error code %d", st);
 }
@@ -124,6 +130,26 @@ int validate_mk(kq_ctx *c, int M, int K) {
     if (M < 1 || M > KQ_MAX_M) return fail(c, KQ_ERR_SHAPE, "M = %d outside [1, %d]", M, KQ_MAX_M);
     if (K < 256 || K > KQ_MAX_K || (K % 256) != 0)
         return fail(c, KQ_ERR_SHAPE, "K = %d must be a positive multiple of 256 up to %d", K, KQ_MAX_K);
+    return KQ_OK;
+}
+
+// Scratch of a balanced GEMV launch (CTAs own equal tile ranges; see GemvParams::split).  The
+// launch keeps whole row groups per CTA when the option is off or the term slots would exceed
+// 64 MB (very long Q8_0 rows).
+int gemv_split_scratch(kq_ctx *c, int type, int K, int mt, kq::GemvLaunch &L) {
+    if (!c->gemv_split) return KQ_OK;
+    const size_t bytes = kq::gemv_split_bytes(type, K, mt, c->num_sms);
+    if (bytes > ((size_t)64 << 20)) return KQ_OK;
+    if (int r = ensure(c, c->gsplit, bytes)) return r;
+    if (!c->gcount.p || c->split_dirty) {
+        const size_t cb = sizeof(int) * (size_t)kq::gemv_split_slots(c->num_sms);
+        if (int r = ensure(c, c->gcount, cb)) return r;
+        KQ_CUDA(c, cudaMemsetAsync(c->gcount.p, 0, cb, c->stream));
+        c->split_dirty = false;
+    }
+    L.split_terms = static_cast<float *>(c->gsplit.p);
+    L.split_terms_bytes = c->gsplit.cap;
+    L.split_count = static_cast<int *>(c->gcount.p);
     return KQ_OK;
 }
 
@@ -267,6 +293,7 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
             L.argmax = ex.argmax ? ex.argmax + m0 : nullptr;
             L.argmax_f16 = ex.argmax_f16;
             L.inject_wait = c->inject_timeout ? 1 : 0;
+            if (int r = gemv_split_scratch(c, type, K, mt, L)) return r;
             cudaError_t e = kq::launch_gemv(L, c->stream);
             if (e == cudaErrorInvalidConfiguration && mt > 1) {
                 // activation too large for shared memory at this tile: halve the tile
@@ -404,7 +431,7 @@ extern "C" int kq_destroy(kq_ctx *c) {
     cudaSetDevice(c->device);
     cudaStreamSynchronize(c->stream);
     for (DevBuf *b : {&c->x, &c->res, &c->out16, &c->out32, &c->q8k_pending, &c->q8k_cur, &c->q80_cur, &c->tmp,
-                      &c->misc, &c->keys, &c->tcpack, &c->tcterms})
+                      &c->misc, &c->keys, &c->tcpack, &c->tcterms, &c->gsplit, &c->gcount})
         if (b->p) cudaFree(b->p);
     cudaFreeHost(c->h_status);
     if (c->own_stream) cudaStreamDestroy(c->stream);
@@ -454,6 +481,10 @@ extern "C" int kq_set_option(kq_ctx *c, const char *name, long long value) {
     if (!strcmp(name, "gemm_path")) {
         if (value < 0 || value > 3) return fail(c, KQ_ERR_INVALID_ARGUMENT, "gemm_path must be 0..3");
         c->gemm_path = (int)value;
+        return KQ_OK;
+    }
+    if (!strcmp(name, "gemv_split")) {
+        c->gemv_split = value != 0;
         return KQ_OK;
     }
     if (!strcmp(name, "timeout_us")) {

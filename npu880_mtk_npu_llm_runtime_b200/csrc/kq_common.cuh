@@ -198,6 +198,20 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// 4-byte asynchronous copy global -> shared (no register round trip, any number in flight);
+// both addresses 4-byte aligned.  The issuing thread waits with cp_async_wait_all.
+__device__ __forceinline__ void cp_async4(uint32_t sdst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sdst), "l"(src) : "memory");
+}
+// 16-byte asynchronous copy global -> shared through L2 only (data other CTAs wrote); both
+// addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16_cg(uint32_t sdst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sdst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
     return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFFu)));
 }

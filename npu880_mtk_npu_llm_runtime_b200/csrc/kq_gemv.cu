@@ -90,6 +90,14 @@ struct GemvParams {
     int argmax_f16;              // compare the fp16-rounded results (the dispatch's stored logits)
     int inject_wait;             // failure test: consumers first wait on a barrier nothing arrives at
     unsigned off_x, off_dx, off_xs, off_terms, off_stages, off_bars;
+    // Tile-range ownership (the kernels' SPLIT variant): CTA c owns tiles [T c / G, T (c + 1) / G)
+    // of the launch's T = total_rg * nbu tiles, so a row group can be shared by consecutive CTAs.
+    // Each CTA stores its block terms of a shared row group in slot s = (CTA holding the row
+    // group's first tile) of gterms ([G][J][16 MT] floats) and counts its arrival in gcount[s];
+    // the last CTA to arrive adds all J terms in block order and resets gcount[s] to 0.
+    long long total_tiles;
+    float *gterms;
+    int *gcount;
 };
 
 // Total order on floats as unsigned keys: larger float -> larger key.
@@ -158,10 +166,75 @@ __device__ __forceinline__ void quantize_lane(const uint4 raw, uint32_t &lo, uin
     d = (amax == 0.0f) ? 0.0f : __fdiv_rn(amax, 127.0f);
 }
 
-// Stage the M tokens' activation (consumer warps).  Loads of up to 4 units per warp are issued
-// before any is used, so the staging costs about one global-memory latency.
+// Pre-quantized input (BlockQ8K / BlockQ8_0_Fast): every 4-byte word goes straight to its place
+// in shared memory with cp.async -- all copies of the CTA in flight at once, no register round
+// trip -- so the staging costs one global-memory latency whatever M and K.  Q6_K's
+// -32 * (sub-block sums) are then formed from the staged quants.
+template <int TYPE, int MT>
+__device__ __noinline__ void stage_activation_q(const GemvParams &p, uint8_t *smem, int warp, int lane, int W) {
+    constexpr int XP = xpitch<MT>();
+    uint8_t *xq = smem + p.off_x;
+    int *aux = reinterpret_cast<int *>(smem + p.off_xs);
+    const uint32_t xq_s = smem_u32(xq), dx_s = smem_u32(smem + p.off_dx), aux_s = smem_u32(aux);
+    const int nbu = p.nbu, n_units = p.M * nbu;
+    for (int i = warp; i < n_units; i += W) {
+        const int m = i / nbu, u = i - m * nbu;
+        const size_t xbase = use_dp<MT>() ? (size_t)(m * nbu + u) * 320 : (size_t)m * (p.K + 16) + 256 * u;
+        if (TYPE == TYPE_Q8_0) {
+            // lane: quants 8(L%4)..+7 of block L/4 and that block's scale
+            const uint8_t *blk = reinterpret_cast<const uint8_t *>(reinterpret_cast<const BlockQ80 *>(p.act) +
+                                                                   ((size_t)m * nbu + u) * 8 + (lane >> 2));
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int v = 8 * lane + 4 * h;
+                const size_t xo = use_dp<MT>() ? xbase + 80 * (v >> 6) + (v & 63) : xbase + v;
+                cp_async4(xq_s + (uint32_t)xo, blk + 4 + 8 * (lane & 3) + 4 * h);
+            }
+            if ((lane & 3) == 0) cp_async4(dx_s + 4u * (uint32_t)((u * 8 + (lane >> 2)) * XP + m), blk);
+        } else {
+            // BlockQ8K (ENG:868-872): float d at 0, qs[256] at 4, bsum32[8] at 260
+            const uint8_t *blk =
+                reinterpret_cast<const uint8_t *>(reinterpret_cast<const BlockQ8K *>(p.act) + (size_t)m * nbu + u);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int v = 4 * lane + 128 * h;
+                size_t xo;
+                if (!use_dp<MT>()) xo = xbase + v;
+                else if (TYPE == TYPE_Q6_K) xo = xbase + 160 * (v >> 7) + (v & 127);
+                else xo = xbase + 80 * (v >> 6) + (v & 63);
+                cp_async4(xq_s + (uint32_t)xo, blk + 4 + v);
+            }
+            if (lane == 0) cp_async4(dx_s + 4u * (uint32_t)(u * XP + m), blk);
+            if ((TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K) && lane < 8)
+                cp_async4(aux_s + 4u * (uint32_t)((m * nbu + u) * 8 + lane), blk + 260 + 4 * lane);
+        }
+    }
+    cp_async_wait_all();
+    if (TYPE == TYPE_Q6_K) {
+        named_bar_sync(1, W * 32);  // every consumer's copies have landed
+        for (int i = warp * 32 + lane; i < n_units * 16; i += W * 32) {
+            const int s = i & 15, mu = i >> 4, m = mu / nbu, u = mu - m * nbu, v = 16 * s;
+            const size_t xo = use_dp<MT>() ? (size_t)(m * nbu + u) * 320 + 160 * (v >> 7) + (v & 127)
+                                           : (size_t)m * (p.K + 16) + 256 * u + v;
+            const uint4 q = *reinterpret_cast<const uint4 *>(xq + xo);
+            const int s16 = sum_s8x4(q.x) + sum_s8x4(q.y) + sum_s8x4(q.z) + sum_s8x4(q.w);
+            const int h = s >> 3, g = (s >> 1) & 3, l = s & 1;
+            if (use_dp<MT>()) aux[((u * 4 + 2 * h + l) * MT + m) * 4 + g] = -32 * s16;
+            else aux[(u * 16 + s) * XP + m] = -32 * s16;
+        }
+    }
+}
+
+// Stage the M tokens' activation (consumer warps): fp16 input quantized in-kernel, or (up to 2
+// tokens) a pre-quantized input copied through registers.  Loads of up to 4 units per warp are
+// issued before any is used, so the staging costs about one global-memory latency.  Pre-quantized
+// inputs of more tokens (hundreds of units per CTA) go through stage_activation_q.
 template <int TYPE, int MT>
 __device__ __forceinline__ void stage_activation(const GemvParams &p, uint8_t *smem, int warp, int lane, int W) {
+    if (MT > 2 && !p.x) {
+        stage_activation_q<TYPE, MT>(p, smem, warp, lane, W);
+        return;
+    }
     constexpr int XP = xpitch<MT>();
     uint8_t *xq = smem + p.off_x;
     float *dx = reinterpret_cast<float *>(smem + p.off_dx);
@@ -177,7 +250,7 @@ __device__ __forceinline__ void stage_activation(const GemvParams &p, uint8_t *s
             bs[b] = 0;
             if (i < n_units) {
                 const int m = i / nbu, u = i - (i / nbu) * nbu;
-                if (p.x) {
+                if (MT > 2 || p.x) {
                     const __half *xu = p.x + (size_t)m * p.x_stride + (size_t)u * 256 + 8 * lane;
                     if ((reinterpret_cast<uintptr_t>(xu) & 15) == 0) {
                         raw[b] = *reinterpret_cast<const uint4 *>(xu);
@@ -208,7 +281,7 @@ __device__ __forceinline__ void stage_activation(const GemvParams &p, uint8_t *s
             const int m = i / nbu, u = i - (i / nbu) * nbu;
             uint32_t lo, hi;
             float d;
-            if (p.x) {
+            if (MT > 2 || p.x) {
                 quantize_lane<TYPE>(raw[b], lo, hi, d);
             } else {
                 lo = raw[b].x;
@@ -234,7 +307,7 @@ __device__ __forceinline__ void stage_activation(const GemvParams &p, uint8_t *s
                     else aux[(u * 16 + s) * XP + m] = -32 * s16;
                 }
             } else if (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K) {
-                if (p.x) {
+                if (MT > 2 || p.x) {
                     int s = sum_s8x4(lo) + sum_s8x4(hi);
                     s += __shfl_xor_sync(0xffffffffu, s, 1);
                     s += __shfl_xor_sync(0xffffffffu, s, 2);
@@ -718,6 +791,41 @@ __device__ __forceinline__ void fold_one(const GemvParams &p, const float *tb, i
     epilogue(p, tk, r, tok, acc, s_best);
 }
 
+// Row group rg is shared with other CTAs (split launch): store this CTA's block terms (units
+// [ua, ub), smem term block tb of J x 16 MT floats) in the row group's global slot -- indexed by
+// the CTA that holds its first tile, which holds no other shared row group's first tile -- and
+// count the arrival.  The CTA that arrives last copies the other CTAs' terms into tb (16-byte
+// copies through L2, all in flight), adds all J terms of every (row, token) in block order,
+// writes the results and clears the count for the next launch.  No CTA waits for another.
+// One warp.
+template <int MT>
+__device__ __forceinline__ void fold_shared(const GemvParams &p, float *tb, int J, int JU, int ua, int ub, int rg,
+                                            int lane, unsigned long long *s_best) {
+    constexpr int E = 16 * MT;  // floats per term (16 rows x MT tokens): a multiple of 4
+    const long long first = (long long)rg * p.nbu, G = gridDim.x, T = p.total_tiles;
+    const int c_first = (int)(((first + 1) * G - 1) / T);     // CTA owning tile `first`
+    const int c_last = (int)(((first + p.nbu) * G - 1) / T);  // CTA owning the row group's last tile
+    float4 *g4 = reinterpret_cast<float4 *>(p.gterms + (size_t)c_first * J * E);
+    const float4 *t4 = reinterpret_cast<const float4 *>(tb);
+    const int k0 = ua * JU * E / 4, k1 = ub * JU * E / 4, kn = J * E / 4;
+    for (int k = k0 + lane; k < k1; k += 32) __stcg(g4 + k, t4[k]);
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&p.gcount[c_first], 1) == c_last - c_first;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    const uint32_t tbs = smem_u32(tb);
+    for (int k = lane; k < kn; k += 32)
+        if (k < k0 || k >= k1) cp_async16_cg(tbs + 16u * (uint32_t)k, g4 + k);
+    cp_async_wait_all();
+    __syncwarp();
+    for (int e = lane; e < E; e += 32) fold_one<MT>(p, tb, J, e, rg, s_best);
+    __syncwarp();
+    if (lane == 0) p.gcount[c_first] = 0;
+}
+
 // ------------------------------------------------------------------ the kernel
 //
 // CTA c owns row groups [rg_lo, rg_hi) = tiles [t0, t1) of the launch's tile sequence
@@ -731,7 +839,7 @@ __device__ __forceinline__ void fold_one(const GemvParams &p, const float *tb, i
 //         slot's previous use is folded and the warp completing the row group folds it
 //         (monotonic shared-memory counters).
 
-template <int TYPE, int MT, bool SMALL>
+template <int TYPE, int MT, bool SMALL, bool SPLIT>
 __global__ void __launch_bounds__(threads_of<MT>(), 2) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ unsigned long long s_best[8];
@@ -748,10 +856,25 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) gemv_kernel(const __grid_
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tstride = 16 * MT;  // floats per term row
 
-    const int rg_lo = (int)((long long)p.total_rg * blockIdx.x / gridDim.x);
-    const int rg_hi = (int)((long long)p.total_rg * (blockIdx.x + 1) / gridDim.x);
-    const int t0 = rg_lo * nbu;
-    const int n_tiles = (rg_hi - rg_lo) * nbu;
+    // this CTA's tiles [t0, t0 + n_tiles) of the launch's row-group-major tile sequence: whole
+    // row groups, or (SPLIT) an equal share of tiles whose first / last row group may be shared
+    int rg_lo, rg_hi, t0, n_tiles, u_first = 0, u_end = nbu;
+    if (SPLIT) {
+        const long long tl = p.total_tiles * blockIdx.x / gridDim.x;
+        const long long th = p.total_tiles * (blockIdx.x + 1) / gridDim.x;
+        t0 = (int)tl;
+        n_tiles = (int)(th - tl);
+        rg_lo = (int)(tl / nbu);
+        rg_hi = (int)((th + nbu - 1) / nbu);
+        u_first = t0 - rg_lo * nbu;                         // owned units of row group rg_lo: [u_first, nbu)
+        u_end = (int)(th - (long long)(rg_hi - 1) * nbu);  // owned units of row group rg_hi - 1: [0, u_end)
+    } else {
+        rg_lo = (int)((long long)p.total_rg * blockIdx.x / gridDim.x);
+        rg_hi = (int)((long long)p.total_rg * (blockIdx.x + 1) / gridDim.x);
+        t0 = rg_lo * nbu;
+        n_tiles = (rg_hi - rg_lo) * nbu;
+    }
+    const int n_lr = rg_hi - rg_lo;
     const int n_stages_cta = (n_tiles + T - 1) / T;
 
     if (tid < 8) s_best[tid] = 0ull;
@@ -844,7 +967,7 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) gemv_kernel(const __grid_
                 ph ^= 1;
             }
         }
-        int u = i, lr = 0;
+        int u = u_first + i, lr = 0;
         while (u >= nbu) {
             u -= nbu;
             ++lr;
@@ -879,17 +1002,23 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) gemv_kernel(const __grid_
                 if (!all_in && lane == 0) mbar_arrive(smem_u32(&bars[S + slot]));  // T arrivals free the slot
             } else {
                 int last = 0;
+                // the row group is complete when its owned tiles are: slot 0's count misses the
+                // first row group's unowned units, the last row group misses its own
+                const int ua = (SPLIT && lr == 0) ? u_first : 0, ub = (SPLIT && lr == n_lr - 1) ? u_end : nbu;
+                const int missing = SPLIT ? ((ts == 0) ? u_first : 0) + nbu - ub : 0;
                 if (lane == 0) {
                     mbar_arrive(smem_u32(&bars[S + slot]));
                     __threadfence_block();
-                    last = (atomicAdd(&s_done[ts], 1) == (use + 1) * nbu - 1);
+                    last = (atomicAdd(&s_done[ts], 1) == (use + 1) * nbu - missing - 1);
                 }
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
                     // fold the row group: block terms in order, then the epilogue
                     __threadfence_block();
-                    const float *tb = terms + ts * J * tstride;
-                    for (int e = lane; e < 16 * MT; e += 32) fold_one<MT>(p, tb, J, e, rg, s_best);
+                    float *tb = terms + ts * J * tstride;
+                    if (SPLIT && (ua > 0 || ub < nbu)) fold_shared<MT>(p, tb, J, JU, ua, ub, rg, lane, s_best);
+                    else
+                        for (int e = lane; e < 16 * MT; e += 32) fold_one<MT>(p, tb, J, e, rg, s_best);
                     __syncwarp();
                     if (lane == 0) {
                         __threadfence_block();
@@ -919,11 +1048,18 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) gemv_kernel(const __grid_
         if (SMALL) {
             // ---------------- fold all row groups of the share
             named_bar_sync(1, W * 32);
-            const int n_lr = rg_hi - rg_lo, E = 16 * MT;
+            const int E = 16 * MT;
+            const bool part0 = SPLIT && u_first > 0, part1 = SPLIT && u_end < nbu;  // first / last row group shared
             for (int idx = tid; idx < n_lr * E; idx += W * 32) {
                 const int l = idx / E, e = idx - l * E;
+                if ((l == 0 && part0) || (l == n_lr - 1 && part1)) continue;
                 fold_one<MT>(p, terms + (size_t)l * J * tstride, J, e, rg_lo + l, s_best);
             }
+            if (part0 && warp == 0)
+                fold_shared<MT>(p, terms, J, JU, u_first, n_lr == 1 ? u_end : nbu, rg_lo, lane, s_best);
+            if (part1 && (n_lr > 1 || !part0) && warp == (W > 1 ? 1 : 0))
+                fold_shared<MT>(p, terms + (size_t)(n_lr - 1) * J * tstride, J, JU, 0, u_end, rg_hi - 1, lane,
+                                s_best);
         }
     }
     __syncthreads();
@@ -939,6 +1075,16 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) gemv_kernel(const __grid_
 }
 
 // ------------------------------------------------------------------ host launcher
+
+// A split launch has at most 2 CTAs per SM, each the first-tile owner of at most one shared row
+// group: one slot of J block terms x 16 MT (row, token) pairs per possible CTA.
+int gemv_split_slots(int num_sms) { return 2 * num_sms; }
+
+size_t gemv_split_bytes(int type, int K, int M, int num_sms) {
+    const int MT = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
+    const size_t J = (size_t)(K / 256) * (type == TYPE_Q8_0 ? 8 : 1);
+    return (size_t)gemv_split_slots(num_sms) * J * 16 * MT * sizeof(float);
+}
 
 namespace {
 
@@ -959,9 +1105,10 @@ unsigned align_up(unsigned v, unsigned a) { return (v + a - 1) / a * a; }
 //    slots cover the row groups that can be in flight (ring tiles / nbu + 2).
 //  * Q8_0 keeps one term per 32-block (the reference's exact order) when that fits, else one
 //    per tile.
-Plan make_plan(int type, int K, int MT, int total_rg, int num_sms, int n_warps) {
+Plan make_plan(int type, int K, int MT, int total_rg, int num_sms, int n_warps, bool split) {
     Plan pl{};
     const int nbu = K / 256;
+    const long long total_tiles = (long long)total_rg * nbu;
     const unsigned TB = (unsigned)tile_bytes(type);
     const int XP = MT < 2 ? 2 : MT;
     const bool dp = MT <= 2;
@@ -973,16 +1120,24 @@ Plan make_plan(int type, int K, int MT, int total_rg, int num_sms, int n_warps) 
     const unsigned fixed = x_bytes + dx_bytes + xs_bytes;
     const int T = std::max(1, (int)((16384 + TB - 1) / TB));
     const unsigned stage = align_up(T * TB, 128);
+    // Q8_0: the reference's per-block term order (exact) takes precedence over the smaller budget
+    for (int exact = (type == TYPE_Q8_0) ? 1 : 0; exact >= 0; --exact) {
+    const int J = (type == TYPE_Q8_0 && exact) ? 8 * nbu : nbu;
     for (unsigned budget : {110u * 1024u, 220u * 1024u}) {
         for (int ctas : {2, 1}) {
             if (ctas == 2 && budget > 110u * 1024u) continue;
-            const int grid = std::max(1, std::min(total_rg, ctas * num_sms));
-            const int rg_cta = (total_rg + grid - 1) / grid;
-            if (ctas == 2 && rg_cta * nbu < 8 * n_warps) continue;  // small shares: one CTA, room for the next kernel's
-            const int stages_cta = (rg_cta * nbu + T - 1) / T;
+            // split: tile ranges (a CTA spans at most ceil((tiles - 1) / nbu) + 1 row groups);
+            // else whole row groups
+            const int grid = std::max(1, (int)std::min<long long>(split ? total_tiles : total_rg, ctas * num_sms));
+            const int tiles_cta = split ? (int)((total_tiles + grid - 1) / grid) : (total_rg + grid - 1) / grid * nbu;
+            const int rg_cta = split ? std::min(total_rg, (tiles_cta + nbu - 2) / nbu + 1) : tiles_cta / nbu;
+            // one CTA per SM with room for the next kernel's when a share is small (M <= 2: the
+            // next kernel's weight prefetch hides behind this one's arithmetic); many-token
+            // launches are long enough that two of their own CTAs per SM pay more
+            if (ctas == 2 && MT <= 2 && tiles_cta < 8 * n_warps) continue;
+            const int stages_cta = (tiles_cta + T - 1) / T;
             for (int small = dp ? 1 : 0; small >= 0; --small) {
-                for (int exact = (type == TYPE_Q8_0) ? 1 : 0; exact >= 0; --exact) {
-                    const int J = (type == TYPE_Q8_0 && exact) ? 8 * nbu : nbu;
+                {
                     for (int S = std::min(stages_cta, 32); S >= 1; --S) {
                         const int TS = small ? rg_cta
                                              : std::min(std::min(rg_cta, kMaxTermSlots), (S * T + nbu - 1) / nbu + 2);
@@ -1010,6 +1165,7 @@ Plan make_plan(int type, int K, int MT, int total_rg, int num_sms, int n_warps) 
                 }
             }
         }
+    }
     }
     return pl;  // smem 0: does not fit
 }
@@ -1058,8 +1214,27 @@ cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
         total_rg += d.n_rg;
     }
     if (total_rg == 0) return cudaSuccess;
-    const Plan pl = make_plan(TYPE, L.K, MT, total_rg, L.num_sms, warps_of<MT>());
+    Plan pl = make_plan(TYPE, L.K, MT, total_rg, L.num_sms, warps_of<MT>(), false);
+    // Balanced tile ranges only where whole row groups at one CTA per SM leave the SMs badly
+    // unequal (e.g. 160 row groups over 148 SMs, or fewer row groups than SMs): each shared row
+    // group costs its last CTA a few L2 round trips before it can finish, and where a second CTA
+    // fits beside the first the SMs that hold two row groups run them side by side anyway.
+    bool split = L.split_terms != nullptr && L.split_count != nullptr && pl.grid <= L.num_sms;
+    if (split) {
+        const Plan ps = make_plan(TYPE, L.K, MT, total_rg, L.num_sms, warps_of<MT>(), true);
+        const long long nbu = L.K / 256, tt = (long long)total_rg * nbu;
+        auto sm_load = [&](const Plan &q, bool sp) {  // tiles of the busiest SM
+            const long long per = sp ? (tt + q.grid - 1) / q.grid : (long long)((total_rg + q.grid - 1) / q.grid) * nbu;
+            return per * ((q.grid + L.num_sms - 1) / L.num_sms);
+        };
+        split = ps.smem != 0 && (pl.smem == 0 || sm_load(pl, false) * 10 >= sm_load(ps, true) * 14);
+        if (split) pl = ps;
+    }
     if (pl.smem == 0) return cudaErrorInvalidConfiguration;
+    if (split && gemv_split_bytes(TYPE, L.K, L.M, L.num_sms) > L.split_terms_bytes) return cudaErrorInvalidValue;
+    p.total_tiles = (long long)total_rg * (L.K / 256);
+    p.gterms = split ? L.split_terms : nullptr;
+    p.gcount = split ? L.split_count : nullptr;
     p.n_tasks = L.n_tasks;
     p.total_rg = total_rg;
     p.K = L.K;
@@ -1087,7 +1262,8 @@ cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
     p.off_stages = pl.off_stages;
     p.off_bars = pl.off_bars;
 
-    auto kern = pl.small ? gemv_kernel<TYPE, MT, true> : gemv_kernel<TYPE, MT, false>;
+    auto kern = pl.small ? (split ? gemv_kernel<TYPE, MT, true, true> : gemv_kernel<TYPE, MT, true, false>)
+                         : (split ? gemv_kernel<TYPE, MT, false, true> : gemv_kernel<TYPE, MT, false, false>);
     if (cudaError_t e = configure_smem(kern)) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(pl.grid);

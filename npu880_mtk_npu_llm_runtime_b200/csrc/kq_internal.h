@@ -51,6 +51,12 @@ struct GemvLaunch {
     unsigned long long *argmax = nullptr;  // [M] packed keys (device), or nullptr
     int argmax_f16 = 0;
     int inject_wait = 0;  // failure-path test hook (see kq_set_option "inject_timeout")
+    // Balanced split (optional): CTAs own equal tile ranges, row groups may be shared.  Needs
+    // split_terms (gemv_split_bytes) and split_count (gemv_split_slots ints, all zero; every
+    // launch leaves them zero unless it stopped early on a timeout).  nullptr: whole row groups.
+    float *split_terms = nullptr;
+    size_t split_terms_bytes = 0;
+    int *split_count = nullptr;
 };
 
 // Many-token product on the tensor cores (kq_gemm_tc.cu): tasks of one type, the input as fp16
@@ -75,6 +81,9 @@ struct TcLaunch {
 
 // kq_gemv.cu
 cudaError_t launch_gemv(const GemvLaunch &L, cudaStream_t stream);
+// scratch of a split GEMV launch of M (<= 8) tokens: term bytes and counter slots
+size_t gemv_split_bytes(int type, int K, int M, int num_sms);
+int gemv_split_slots(int num_sms);
 // rows ids[0..n) of a tiled tensor -> a new tiled tensor of n rows (weight_bytes(type, n, K))
 // kq_gemm_tc.cu
 size_t tc_scratch_bytes(int type, int M, int K);
