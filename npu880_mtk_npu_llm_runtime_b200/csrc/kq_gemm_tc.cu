@@ -610,17 +610,57 @@ cudaError_t configure_tc() {
     return cudaSuccess;
 }
 
-bool tc_rows64(long long n_tok_tiles, long long n_rg, int sms) {
-    return n_tok_tiles * ((n_rg + 7) / 8) < sms && n_tok_tiles * ((n_rg + 3) / 4) <= sms;
+// Geometry of one task of the row-major kernel: 64- or 128-row CTAs, and K chunks (split K: block
+// terms stored, folded by tc_fold_kernel) when the grid would use at most half of the SMs and
+// every chunk keeps at least 4 units.  Each candidate is costed per 256-value unit per wave of
+// CTAs (B200 timings; Q8_0's eight 32-block accumulators per unit make it the slowest) and the
+// cheapest is taken.
+struct TcTaskPlan {
+    bool r64;
+    int ks;
+    double us;
+};
+
+TcTaskPlan tc_task_plan(int type, int bn, long long n_tok_tiles, long long n_rg, int nbu, int sms) {
+    TcTaskPlan best{false, 1, 1e300};
+    for (int r64 = 0; r64 < 2; ++r64) {
+        const long long ctas = n_tok_tiles * ((n_rg + (r64 ? 3 : 7)) / (r64 ? 4 : 8));
+        int ks = 1;
+        // Q8_0 keeps eight terms per unit: its term buffer would outgrow the weights
+        if (type != TYPE_Q8_0 && bn <= kTcSplitBN && nbu >= 8 && 2 * ctas <= sms)
+            ks = (int)std::max<long long>(1, std::min<long long>(nbu / 4, sms / ctas));
+        const bool small = r64 || bn < 64;
+        const double unit = (type == TYPE_Q8_0) ? 6.0 : (type == TYPE_Q6_K) ? (small ? 2.5 : 4.2) : (small ? 2.1 : 2.8);
+        const double us = (double)((ctas * ks + sms - 1) / sms) * ((nbu + ks - 1) / ks) * unit + (ks > 1 ? 3.0 : 0.0);
+        if (us < best.us) best = TcTaskPlan{r64 != 0, ks, us};
+    }
+    return best;
 }
 
-// K chunks of the row-major kernel: split K (terms folded by tc_fold_kernel) when the grid would
-// use at most half of the SMs and every chunk keeps at least 4 units
-int tc_ksplit(int type, int bn, long long n_tok_tiles, long long n_rg, int nbu, int sms) {
-    const long long ctas = tc_rows64(n_tok_tiles, n_rg, sms) ? n_tok_tiles * ((n_rg + 3) / 4) : n_tok_tiles * ((n_rg + 7) / 8);
-    // Q8_0 keeps eight terms per unit: its term buffer would outgrow the weights
-    if (type == TYPE_Q8_0 || bn > kTcSplitBN || nbu < 8 || 2 * ctas > sms) return 1;
-    return (int)std::max<long long>(1, std::min<long long>(nbu / 4, sms / ctas));
+// tokens per CTA of the row-major kernel: the smallest tile that holds M (at most 64; Q8_0 32)
+int tc_bn(int type, int M) {
+    const int cap = (type == TYPE_Q8_0) ? 32 : 64;
+    return M <= 16 ? 16 : (M <= 32 || cap == 32) ? 32 : 64;
+}
+
+// Token tile of a launch: the natural one, or 32 where two 32-token tiles with K split beat one
+// 64-token tile without (few long rows, e.g. the 2,560 x 9,728 down projection).  The packed
+// activation of 32-token tiles never exceeds that of 64-token ones.
+int tc_pick_bn(int type, int M, int nbu, const int *task_rgs, int n_tasks, int sms) {
+    const int natural = tc_bn(type, M);
+    int best = natural;
+    double best_us = 1e300;
+    for (int bn : {natural, 32}) {
+        if (bn > natural) continue;
+        const long long tiles = (M + bn - 1) / bn;
+        double us = 0.0;
+        for (int i = 0; i < n_tasks; ++i) us += tc_task_plan(type, bn, tiles, task_rgs[i], nbu, sms).us;
+        if (us < best_us) {
+            best_us = us;
+            best = bn;
+        }
+    }
+    return best;
 }
 
 // fp32 block terms of one split-K task: (terms per row) x M x rows
@@ -671,10 +711,9 @@ cudaError_t launch_tc_bn(const TcLaunch &L, cudaStream_t stream) {
         p.status = L.status;
         p.timeout_ns = L.timeout_ns;
         const int n_rg = (h.row_begin + h.rows - 1) / 16 - p.rg_first + 1;
-        // 64-row CTAs when 128-row ones would leave SMs idle and the 64-row grid still fits in one
-        // wave (one CTA per SM); K split when even that leaves most SMs idle
-        const bool rows64 = tc_rows64(n_tok_tiles, n_rg, sms);
-        const int ks = tc_ksplit(TYPE, BN, n_tok_tiles, n_rg, nbu, sms);
+        const TcTaskPlan tp = tc_task_plan(TYPE, BN, n_tok_tiles, n_rg, nbu, sms);
+        const bool rows64 = tp.r64;
+        const int ks = tp.ks;
         if (ks > 1) {
             if (!L.terms || L.terms_bytes < terms_used + tc_terms_bytes(TYPE, L.M, L.K, h.rows)) return cudaErrorInvalidValue;
             p.terms = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(L.terms) + terms_used);
@@ -702,15 +741,12 @@ cudaError_t launch_tc_bn(const TcLaunch &L, cudaStream_t stream) {
     return cudaSuccess;
 }
 
-// tokens per CTA of the row-major kernel: the smallest tile that holds M (at most 64; Q8_0 32)
-int tc_bn(int type, int M) {
-    const int cap = (type == TYPE_Q8_0) ? 32 : 64;
-    return M <= 16 ? 16 : (M <= 32 || cap == 32) ? 32 : 64;
-}
-
 template <int TYPE>
 cudaError_t launch_tc_t(const TcLaunch &L, cudaStream_t stream) {
-    switch (tc_bn(TYPE, L.M)) {
+    int task_rgs[4];
+    for (int i = 0; i < L.n_tasks; ++i)
+        task_rgs[i] = L.tasks[i].rows > 0 ? (L.tasks[i].row_begin + L.tasks[i].rows - 1) / 16 - L.tasks[i].row_begin / 16 + 1 : 0;
+    switch (tc_pick_bn(TYPE, L.M, L.K / 256, task_rgs, L.n_tasks, L.num_sms > 0 ? L.num_sms : 148)) {
         case 16: return launch_tc_bn<TYPE, 16>(L, stream);
         case 32: return launch_tc_bn<TYPE, 32>(L, stream);
         default:
@@ -1327,28 +1363,19 @@ size_t tc_scratch_bytes(int type, int M, int K) {
 }
 
 size_t tc_split_terms_bytes(int type, int M, int K, const int *task_rows, const int *task_rgs, int n_tasks, int sms) {
-    const int bn = tc_bn(type, M);
+    const int nbu = K / 256, bn = tc_pick_bn(type, M, nbu, task_rgs, n_tasks, sms);
     const long long tiles = (M + bn - 1) / bn;
     size_t total = 0;
     for (int i = 0; i < n_tasks; ++i)
-        if (tc_ksplit(type, bn, tiles, task_rgs[i], K / 256, sms) > 1) total += tc_terms_bytes(type, M, K, task_rows[i]);
+        if (tc_task_plan(type, bn, tiles, task_rgs[i], nbu, sms).ks > 1) total += tc_terms_bytes(type, M, K, task_rows[i]);
     return total;
 }
 
 double tc_estimate_us(int type, int M, int K, const int *task_rgs, int n_tasks, int sms) {
-    const int bn = tc_bn(type, M), nbu = K / 256;
+    const int nbu = K / 256, bn = tc_pick_bn(type, M, nbu, task_rgs, n_tasks, sms);
     const long long tiles = (M + bn - 1) / bn;
     double t = 0.0;
-    for (int i = 0; i < n_tasks; ++i) {
-        const bool r64 = tc_rows64(tiles, task_rgs[i], sms);
-        const int ks = tc_ksplit(type, bn, tiles, task_rgs[i], nbu, sms);
-        const long long ctas = tiles * ((task_rgs[i] + (r64 ? 3 : 7)) / (r64 ? 4 : 8)) * ks;
-        const bool small = r64 || bn < 64;
-        // per 256-value unit per wave (B200 timings): Q8_0's eight 32-block accumulators per unit
-        // make it the slowest
-        const double unit = (type == TYPE_Q8_0) ? 6.0 : (type == TYPE_Q6_K) ? (small ? 2.5 : 4.2) : (small ? 2.1 : 2.8);
-        t += (double)((ctas + sms - 1) / sms) * ((nbu + ks - 1) / ks) * unit + (ks > 1 ? 3.0 : 0.0);
-    }
+    for (int i = 0; i < n_tasks; ++i) t += tc_task_plan(type, bn, tiles, task_rgs[i], nbu, sms).us;
     return t;
 }
 

@@ -89,10 +89,11 @@ def test_tc_fp16_input_tasks_residual(kqctx, oracle, gtype):
 
 
 @pytest.mark.parametrize("gtype", TYPES, ids=lambda t: synth.TYPE_NAMES[t])
-@pytest.mark.parametrize("M", [12, 32])
+@pytest.mark.parametrize("M", [12, 32, 48, 64])
 def test_tc_split_k(kqctx, oracle, gtype, M):
     """few rows and a long K: the row-major kernel splits K over CTAs, stores the block terms and
-    a fold kernel adds them in unit order (fp32, fp16 + residual, an unaligned row range)"""
+    a fold kernel adds them in unit order (fp32, fp16 + residual, an unaligned row range).  At
+    M = 48 / 64 it runs two 32-token tiles with K split instead of one 64-token tile."""
     import torch
     rows_w, rb, n, K = 320, 5, 290, 4096
     w = synth.gen_weights(gtype, rows_w, K, seed=1700 + gtype + M)
@@ -117,10 +118,12 @@ def test_tc_split_k(kqctx, oracle, gtype, M):
     assert np.array_equal(got16.view(np.uint16), r16.view(np.uint16))
 
 
-def test_tc_ffn_down_shape(kqctx, oracle):
-    """the tree-verify FFN down projection shape (Q6_K, K = 9728) at M = 16"""
+@pytest.mark.parametrize("M,rows", [(16, 256), (64, 2560)])
+def test_tc_ffn_down_shape(kqctx, oracle, M, rows):
+    """the tree-verify FFN down projection shape (Q6_K, K = 9728) at M = 16 (256 rows) and at
+    M = 64 (all 2,560 rows: 32-token tiles with K split)"""
     import torch
-    gtype, M, rows, K = kq.TYPE_Q6_K, 16, 256, 9728
+    gtype, K = kq.TYPE_Q6_K, 9728
     w = synth.gen_weights(gtype, rows, K, seed=1500)
     x = synth.gen_activations(M, K, seed=1501)
     act = oracle.act_for(gtype, x)
