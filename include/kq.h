@@ -54,7 +54,9 @@ typedef enum kq_status {
     KQ_ERR_OUT_OF_MEMORY = -5,
     KQ_ERR_NO_DEVICE = -6,
     KQ_ERR_TIMEOUT = -7,            /* a bounded device-side wait gave up (the kernel returned early) */
-    KQ_ERR_NOT_READY = -8           /* no pre-quantized activation is pending in the context */
+    KQ_ERR_NOT_READY = -8,          /* no pre-quantized activation is pending in the context */
+    KQ_ERR_FORMAT = -9,             /* not a GGUF v2/v3 image, or a record / tensor past its end */
+    KQ_ERR_NOT_FOUND = -10          /* no such file, tensor name or tensor index */
 } kq_status;
 
 typedef struct kq_ctx kq_ctx;
@@ -235,6 +237,43 @@ int kq_eval_indexed_rows_argmax(kq_ctx *ctx, const kq_weight *w, const uint32_t 
  * bit-exact to dequant_block_<type> (ENG:598-853).  dst fp16 [rows][cols]. */
 int kq_dequant_rows(kq_ctx *ctx, const kq_weight *w, int row_begin, int rows, uint16_t *dst);
 int kq_dequant_rows_async(kq_ctx *ctx, const kq_weight *w, int row_begin, int rows, uint16_t *dst_dev);
+
+/* ---------------------------------------------------------------- GGUF files */
+
+/* The tensor directory of a GGUF v2/v3 file, as parse_gguf_file (ENG:376-413) builds it over the
+ * engine's mmap: magic "GGUF", the key/value pairs (only general.alignment is kept; default 32),
+ * the tensor records, and the data section at the next multiple of the alignment.  Every record
+ * and every tensor's byte range is checked against the file size (KQ_ERR_FORMAT otherwise). */
+typedef struct kq_gguf kq_gguf;
+typedef struct kq_gguf_tensor {
+    const char *name;      /* NUL-terminated, owned by the kq_gguf (GgufTensorInfo.name, ENG:168) */
+    uint32_t type;         /* GGML type id */
+    uint32_t n_dims;       /* 1..4 */
+    uint64_t dims[4];      /* dims[0] = values per row, dims[1] = rows; unused dimensions are 1 */
+    uint64_t n_elems;
+    uint64_t offset;       /* absolute byte offset of the data in the file (abs_offset, ENG:410-412) */
+    uint64_t bytes;        /* compute_ggml_bytes(type, n_elems) (ENG:364-374); 0 for other types */
+    const void *data;      /* the tensor's bytes in the mapped file / caller's image */
+} kq_gguf_tensor;
+
+/* Map a GGUF file read-only and parse its directory (the engine's model open, ENG:376). */
+int kq_gguf_open(const char *path, kq_gguf **out);
+/* Same over a GGUF image already in host memory (borrowed until kq_gguf_close). */
+int kq_gguf_open_memory(const void *bytes, size_t size, kq_gguf **out);
+int kq_gguf_close(kq_gguf *g);
+int kq_gguf_info(const kq_gguf *g, uint32_t *version, uint64_t *alignment, uint64_t *data_offset);
+/* Number of tensor records (GgufContext.n_tensors, ENG:185), or a negative status. */
+int kq_gguf_tensor_count(const kq_gguf *g);
+int kq_gguf_get_tensor(const kq_gguf *g, int index, kq_gguf_tensor *out);
+/* find_tensor (ENG:415-420): the index of the record named `name`, or KQ_ERR_NOT_FOUND. */
+int kq_gguf_find_tensor(const kq_gguf *g, const char *name);
+/* Upload tensor `index` -- a Q4_K / Q5_K / Q6_K / Q8_0 matrix of dims[1] rows x dims[0] values --
+ * with kq_weight_upload (the weight pointer init_sdot_task takes from the mmap, ENG:4163-4181). */
+int kq_gguf_upload(kq_ctx *ctx, const kq_gguf *g, int index, kq_weight **out);
+/* Device weight cache of a whole model: out[i] receives every quantized matrix of the file
+ * (dims[0] a multiple of 256), NULL for the other records (norms, embeddings in f32/f16 ...);
+ * out has kq_gguf_tensor_count entries.  On failure nothing stays uploaded. */
+int kq_gguf_upload_all(kq_ctx *ctx, const kq_gguf *g, kq_weight **out, int *n_uploaded);
 
 #ifdef __cplusplus
 }

@@ -28,7 +28,7 @@ MAX_TASKS = 4
 STATUS = {
     0: "KQ_OK", -1: "KQ_ERR_INVALID_ARGUMENT", -2: "KQ_ERR_UNSUPPORTED_TYPE", -3: "KQ_ERR_SHAPE",
     -4: "KQ_ERR_CUDA", -5: "KQ_ERR_OUT_OF_MEMORY", -6: "KQ_ERR_NO_DEVICE", -7: "KQ_ERR_TIMEOUT",
-    -8: "KQ_ERR_NOT_READY",
+    -8: "KQ_ERR_NOT_READY", -9: "KQ_ERR_FORMAT", -10: "KQ_ERR_NOT_FOUND",
 }
 
 # BlockQ8K (ENG:868-872) / BlockQ8_0_Fast (ENG:874-877) as numpy records
@@ -47,7 +47,15 @@ EXPORTS = (
     "kq_run_ffn", "kq_run_ffn_async",
     "kq_lm_head_argmax", "kq_lm_head_argmax_async", "kq_lm_head_argmax_noalloc", "kq_eval_indexed_rows_argmax",
     "kq_dequant_rows", "kq_dequant_rows_async",
+    "kq_gguf_open", "kq_gguf_open_memory", "kq_gguf_close", "kq_gguf_info", "kq_gguf_tensor_count",
+    "kq_gguf_get_tensor", "kq_gguf_find_tensor", "kq_gguf_upload", "kq_gguf_upload_all",
 )
+
+
+class GgufTensor(C.Structure):
+    """kq_gguf_tensor: one record of a GGUF file's tensor directory (GgufTensorInfo, ENG:167-176)."""
+    _fields_ = [("name", C.c_char_p), ("type", C.c_uint32), ("n_dims", C.c_uint32), ("dims", C.c_uint64 * 4),
+                ("n_elems", C.c_uint64), ("offset", C.c_uint64), ("bytes", C.c_uint64), ("data", C.c_void_p)]
 
 
 class KQError(RuntimeError):
@@ -115,6 +123,15 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "kq_eval_indexed_rows_argmax": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
         "kq_dequant_rows": (_i, [_vp, _vp, _i, _i, _vp]),
         "kq_dequant_rows_async": (_i, [_vp, _vp, _i, _i, _vp]),
+        "kq_gguf_open": (_i, [C.c_char_p, C.POINTER(_vp)]),
+        "kq_gguf_open_memory": (_i, [_vp, _sz, C.POINTER(_vp)]),
+        "kq_gguf_close": (_i, [_vp]),
+        "kq_gguf_info": (_i, [_vp, C.POINTER(_u32), C.POINTER(_u64), C.POINTER(_u64)]),
+        "kq_gguf_tensor_count": (_i, [_vp]),
+        "kq_gguf_get_tensor": (_i, [_vp, _i, C.POINTER(GgufTensor)]),
+        "kq_gguf_find_tensor": (_i, [_vp, C.c_char_p]),
+        "kq_gguf_upload": (_i, [_vp, _vp, _i, C.POINTER(_vp)]),
+        "kq_gguf_upload_all": (_i, [_vp, _vp, C.POINTER(_vp), C.POINTER(_i)]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -371,3 +388,72 @@ def q8k_bytes(M: int, K: int) -> int:
 
 def q8_0_bytes(M: int, K: int) -> int:
     return M * (K // 32) * 36
+
+
+class Gguf:
+    """A GGUF v2/v3 file's tensor directory (kq_gguf): from a path (mapped read-only) or from bytes
+    in memory (kept alive by this object).  Mirrors parse_gguf_file / find_tensor (ENG:376-420)."""
+
+    def __init__(self, path: str | None = None, data: bytes | np.ndarray | None = None):
+        self.L = load_library()
+        h = _vp()
+        self._buf = None
+        if path is not None:
+            st = self.L.kq_gguf_open(path.encode(), C.byref(h))
+        else:
+            self._buf = np.frombuffer(data, dtype=np.uint8) if isinstance(data, (bytes, bytearray)) else np.ascontiguousarray(data)
+            st = self.L.kq_gguf_open_memory(_hp(self._buf), self._buf.nbytes, C.byref(h))
+        if st != 0:
+            raise KQError(st, f"kq_gguf_open: {STATUS.get(st, st)}")
+        self.handle = h.value
+
+    def close(self):
+        if self.handle:
+            self.L.kq_gguf_close(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def info(self):
+        v, a, d = C.c_uint32(), C.c_uint64(), C.c_uint64()
+        self.L.kq_gguf_info(self.handle, C.byref(v), C.byref(a), C.byref(d))
+        return {"version": v.value, "alignment": a.value, "data_offset": d.value}
+
+    def __len__(self) -> int:
+        return self.L.kq_gguf_tensor_count(self.handle)
+
+    def tensor(self, index: int) -> dict:
+        t = GgufTensor()
+        st = self.L.kq_gguf_get_tensor(self.handle, index, C.byref(t))
+        if st != 0:
+            raise KQError(st, f"tensor {index}")
+        return {"name": t.name.decode(), "type": t.type, "n_dims": t.n_dims, "dims": list(t.dims),
+                "n_elems": t.n_elems, "offset": t.offset, "bytes": t.bytes, "data": t.data}
+
+    def find(self, name: str) -> int:
+        return self.L.kq_gguf_find_tensor(self.handle, name.encode())
+
+    def upload(self, ctx: "Context", index: int) -> Weight:
+        h = _vp()
+        ctx.check(self.L.kq_gguf_upload(ctx.handle, self.handle, index, C.byref(h)))
+        t = self.tensor(index)
+        return Weight(ctx, h.value, t["type"], t["dims"][1], t["dims"][0])
+
+    def upload_all(self, ctx: "Context") -> list:
+        """one Weight per quantized matrix of the file, None for the other records"""
+        n = len(self)
+        arr = (_vp * max(1, n))()
+        cnt = _i()
+        ctx.check(self.L.kq_gguf_upload_all(ctx.handle, self.handle, arr, C.byref(cnt)))
+        out = []
+        for i in range(n):
+            if arr[i]:
+                t = self.tensor(i)
+                out.append(Weight(ctx, arr[i], t["type"], t["dims"][1], t["dims"][0]))
+            else:
+                out.append(None)
+        return out

@@ -386,6 +386,8 @@ extern "C" const char *kq_status_string(int s) {
         case KQ_ERR_NO_DEVICE: return "no CUDA device";
         case KQ_ERR_TIMEOUT: return "device-side wait timed out";
         case KQ_ERR_NOT_READY: return "no pending quantized input";
+        case KQ_ERR_FORMAT: return "not a GGUF v2/v3 image or truncated";
+        case KQ_ERR_NOT_FOUND: return "not found";
         default: return "unknown status";
     }
 }

@@ -105,3 +105,49 @@ def gen_gamma(k: int, seed: int) -> np.ndarray:
     """RMSNorm weights around 1.0 as fp16."""
     rng = np.random.default_rng(seed)
     return (1.0 + 0.1 * rng.standard_normal(size=k)).astype(np.float16)
+
+
+# ---------------------------------------------------------------- GGUF files
+
+GGUF_U32, GGUF_F32, GGUF_STRING, GGUF_ARRAY, GGUF_U64 = 4, 6, 8, 9, 10
+
+
+def write_gguf(tensors, kv=None, version: int = 3, alignment: int | None = None) -> bytes:
+    """A GGUF v2/v3 image (the file format the engine mmaps, parsed by ENG:376-413): header, the
+    key/value pairs `kv` ([(key, value_type, value)]; value_type GGUF_U32 / GGUF_U64 / GGUF_F32 /
+    GGUF_STRING, or (GGUF_ARRAY, element type) with a list), the tensor records of `tensors`
+    ([(name, ggml_type, dims, data_bytes)], dims[0] = values per row) and the data section, each
+    tensor at a multiple of the alignment (general.alignment when given, else 32)."""
+    import struct
+
+    def s(x: str) -> bytes:
+        b = x.encode()
+        return struct.pack("<Q", len(b)) + b
+
+    def scalar(t, v) -> bytes:
+        return {GGUF_U32: lambda: struct.pack("<I", v), GGUF_U64: lambda: struct.pack("<Q", v),
+                GGUF_F32: lambda: struct.pack("<f", v), GGUF_STRING: lambda: s(v)}[t]()
+
+    kv = list(kv or [])
+    if alignment is not None:
+        kv.append(("general.alignment", GGUF_U32, alignment))
+    align = alignment or 32
+    out = bytearray(b"GGUF" + struct.pack("<IQQ", version, len(tensors), len(kv)))
+    for key, t, v in kv:
+        out += s(key)
+        if isinstance(t, tuple):
+            out += struct.pack("<IIQ", GGUF_ARRAY, t[1], len(v)) + b"".join(scalar(t[1], e) for e in v)
+        else:
+            out += struct.pack("<I", t) + scalar(t, v)
+    offsets, off = [], 0
+    for _, _, _, data in tensors:
+        offsets.append(off)
+        off = (off + len(data) + align - 1) // align * align
+    for (name, gtype, dims, _), o in zip(tensors, offsets):
+        out += s(name) + struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", d) for d in dims)
+        out += struct.pack("<IQ", gtype, o)
+    out += bytes((-len(out)) % align)
+    base = len(out)
+    for (_, _, _, data), o in zip(tensors, offsets):
+        out += bytes(base + o - len(out)) + bytes(data)
+    return bytes(out)

@@ -289,6 +289,33 @@ class Reference:
         self.init_pool()
         self.L.kqref_turbo(1 if on else 0)
 
+    class GgufTensor(C.Structure):
+        _fields_ = [("name", C.c_char * 128), ("n_dims", C.c_uint32), ("dims", C.c_uint64 * 4), ("type", C.c_uint32),
+                    ("rel_offset", C.c_uint64), ("abs_offset", C.c_uint64), ("n_elems", C.c_uint64),
+                    ("byte_size", C.c_uint64)]
+
+    def gguf_parse(self, image: bytes):
+        """parse_gguf_file (ENG:376-413) on a GGUF image: None if the reference rejects it, else
+        (alignment, data_offset, [records as dicts])"""
+        L = self.L
+        L.kqref_gguf_parse.restype = C.c_int
+        L.kqref_gguf_parse.argtypes = [C.c_char_p, C.c_size_t, C.POINTER(C.c_uint32), C.POINTER(C.c_uint64),
+                                       C.POINTER(C.c_uint64), _vp, C.c_int]
+        recs = (self.GgufTensor * 512)()
+        n, al, do = C.c_uint32(), C.c_uint64(), C.c_uint64()
+        ok = L.kqref_gguf_parse(image, len(image), C.byref(n), C.byref(al), C.byref(do), C.cast(recs, C.c_void_p), 512)
+        if ok != 1:
+            return None
+        out = [{"name": r.name.decode(), "n_dims": r.n_dims, "dims": list(r.dims), "type": r.type,
+                "offset": r.abs_offset, "n_elems": r.n_elems, "bytes": r.byte_size} for r in recs[:n.value]]
+        return al.value, do.value, out
+
+    def gguf_find(self, image: bytes, name: str) -> int:
+        """find_tensor (ENG:415-420): record index, -1 when absent, -2 when the image is rejected"""
+        self.L.kqref_gguf_find.restype = C.c_int
+        self.L.kqref_gguf_find.argtypes = [C.c_char_p, C.c_size_t, C.c_char_p]
+        return self.L.kqref_gguf_find(image, len(image), name.encode())
+
 
 def reference_available() -> bool:
     return os.path.exists(REF_SO)

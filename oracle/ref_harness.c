@@ -133,3 +133,62 @@ KQREF_API void kqref_dispatch(const uint16_t *x, int M, int K, const kqref_task 
     g_sdot_input_q8k_prequantized = prequantized ? 1 : 0;
     sdot_gemm_multi_dispatch((const __fp16 *)x, M, K, tasks, n_tasks);
 }
+
+/* One tensor record of the reference's GGUF parser (GgufTensorInfo, ENG:167-176). */
+typedef struct {
+    char name[128];
+    uint32_t n_dims;
+    uint64_t dims[4];
+    uint32_t type;
+    uint64_t rel_offset, abs_offset, n_elems, byte_size;
+} kqref_gguf_tensor;
+
+/* parse_gguf_file (ENG:376-413) over a GGUF image in memory, as the engine runs it on its mmap.
+ * Returns the parser's result (1 ok, 0 rejected); on success fills up to cap tensor records and
+ * the header fields.  The context is large (MAX_TENSORS records), so it lives on the heap. */
+KQREF_API int kqref_gguf_parse(const void *bytes, size_t size, uint32_t *n_tensors, uint64_t *alignment,
+                               uint64_t *data_offset, kqref_gguf_tensor *out, int cap) {
+    GgufContext *ctx = (GgufContext *)calloc(1, sizeof(GgufContext));
+    if (!ctx) return -1;
+    ctx->base = (const uint8_t *)bytes;
+    ctx->file_size = size;
+    ctx->pos = 0;
+    const int ok = parse_gguf_file(ctx);
+    if (ok) {
+        *n_tensors = ctx->n_tensors;
+        *alignment = ctx->alignment;
+        *data_offset = ctx->data_offset;
+        for (uint32_t i = 0; i < ctx->n_tensors && (int)i < cap; ++i) {
+            const GgufTensorInfo *t = &ctx->tensors[i];
+            memcpy(out[i].name, t->name, sizeof(out[i].name));
+            out[i].n_dims = t->n_dims;
+            for (int d = 0; d < 4; ++d) out[i].dims[d] = t->dims[d];
+            out[i].type = t->type;
+            out[i].rel_offset = t->rel_offset;
+            out[i].abs_offset = t->abs_offset;
+            out[i].n_elems = t->n_elems;
+            out[i].byte_size = t->byte_size;
+        }
+    }
+    free(ctx->vocab_ptrs);
+    free(ctx->vocab_lens);
+    free(ctx);
+    return ok;
+}
+
+/* find_tensor (ENG:415-420): index of the named tensor, or -1. */
+KQREF_API int kqref_gguf_find(const void *bytes, size_t size, const char *name) {
+    GgufContext *ctx = (GgufContext *)calloc(1, sizeof(GgufContext));
+    if (!ctx) return -2;
+    ctx->base = (const uint8_t *)bytes;
+    ctx->file_size = size;
+    int idx = -2;
+    if (parse_gguf_file(ctx)) {
+        const GgufTensorInfo *t = find_tensor(ctx, name);
+        idx = t ? (int)(t - ctx->tensors) : -1;
+    }
+    free(ctx->vocab_ptrs);
+    free(ctx->vocab_lens);
+    free(ctx);
+    return idx;
+}
