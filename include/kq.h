@@ -237,6 +237,14 @@ int kq_eval_indexed_rows_argmax(kq_ctx *ctx, const kq_weight *w, const uint32_t 
  * bit-exact to dequant_block_<type> (ENG:598-853).  dst fp16 [rows][cols]. */
 int kq_dequant_rows(kq_ctx *ctx, const kq_weight *w, int row_begin, int rows, uint16_t *dst);
 int kq_dequant_rows_async(kq_ctx *ctx, const kq_weight *w, int row_begin, int rows, uint16_t *dst_dev);
+/* Embedding lookup: the decode step's dequant_contiguous_fast of row token_id of
+ * token_embd.weight (ENG:8667-8670; the same tensor is the tied LM head), for n tokens at once:
+ * dst fp16 [n][cols], row i = row ids[i], bit-exact to dequant_block_<type>.  HOST ids / dst,
+ * blocking; an id >= rows is KQ_ERR_SHAPE before anything runs. */
+int kq_embed_rows(kq_ctx *ctx, const kq_weight *w, const uint32_t *ids, int n, uint16_t *dst);
+/* Same with DEVICE ids / dst, asynchronous: an id >= rows gives a row of zeros (nothing is read
+ * out of bounds) and the next kq_synchronize reports KQ_ERR_SHAPE. */
+int kq_embed_rows_async(kq_ctx *ctx, const kq_weight *w, const uint32_t *ids_dev, int n, uint16_t *dst_dev);
 
 /* ---------------------------------------------------------------- GGUF files */
 

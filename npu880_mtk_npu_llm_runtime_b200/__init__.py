@@ -46,7 +46,7 @@ EXPORTS = (
     "kq_rmsnorm_fp16_rows", "kq_swiglu_fp16_rows", "kq_rmsnorm_q8k_async", "kq_swiglu_q8k_async",
     "kq_run_ffn", "kq_run_ffn_async",
     "kq_lm_head_argmax", "kq_lm_head_argmax_async", "kq_lm_head_argmax_noalloc", "kq_eval_indexed_rows_argmax",
-    "kq_dequant_rows", "kq_dequant_rows_async",
+    "kq_dequant_rows", "kq_dequant_rows_async", "kq_embed_rows", "kq_embed_rows_async",
     "kq_gguf_open", "kq_gguf_open_memory", "kq_gguf_close", "kq_gguf_info", "kq_gguf_tensor_count",
     "kq_gguf_get_tensor", "kq_gguf_find_tensor", "kq_gguf_upload", "kq_gguf_upload_all",
 )
@@ -123,6 +123,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "kq_eval_indexed_rows_argmax": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
         "kq_dequant_rows": (_i, [_vp, _vp, _i, _i, _vp]),
         "kq_dequant_rows_async": (_i, [_vp, _vp, _i, _i, _vp]),
+        "kq_embed_rows": (_i, [_vp, _vp, _vp, _i, _vp]),
+        "kq_embed_rows_async": (_i, [_vp, _vp, _vp, _i, _vp]),
         "kq_gguf_open": (_i, [C.c_char_p, C.POINTER(_vp)]),
         "kq_gguf_open_memory": (_i, [_vp, _sz, C.POINTER(_vp)]),
         "kq_gguf_close": (_i, [_vp]),
@@ -326,6 +328,16 @@ class Context:
         out = np.zeros((rows, w.cols), dtype=np.float16)
         self.check(self.L.kq_dequant_rows(self.handle, w.handle, row_begin, rows, _hp(out)))
         return out
+
+    def embed_rows(self, w: Weight, ids) -> np.ndarray:
+        """fp16 rows ids[i] of w (the embedding lookup of ENG:8667-8670)"""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        out = np.zeros((len(ids), w.cols), dtype=np.float16)
+        self.check(self.L.kq_embed_rows(self.handle, w.handle, _hp(ids), len(ids), _hp(out)))
+        return out
+
+    def embed_rows_async(self, w: Weight, ids_dev, n: int, out_dev):
+        self.check(self.L.kq_embed_rows_async(self.handle, w.handle, _dp(ids_dev), n, _dp(out_dev)))
 
     # ---- device-pointer (async) entry points
     @staticmethod

@@ -271,12 +271,24 @@ __device__ __forceinline__ uint8_t gguf_byte(int type, int nbu, const uint8_t *t
 
 // One thread per output value of rows [row_begin, row_begin + rows); same rounding sequence as
 // the reference's scalar dequant loops.
-__global__ void dequant_kernel(int type, const uint8_t *tiled, int row_begin, int rows, int K, __half *out) {
+// ids != nullptr: output row j is weight row ids[j] (an embedding lookup); an id past the
+// weight's w_rows rows gives zeros and records DEV_ERR_INDEX (never read out of bounds).
+__global__ void dequant_kernel(int type, const uint8_t *tiled, int row_begin, int rows, int K, __half *out,
+                               const uint32_t *ids, int w_rows, int *status) {
     const int nbu = K / 256;
     const size_t total = (size_t)rows * K;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const int r = row_begin + (int)(i / K);
+        int r = row_begin + (int)(i / K);
         const int e = (int)(i % K);
+        if (ids) {
+            const uint32_t id = ids[i / K];
+            if (id >= (uint32_t)w_rows) {
+                out[i] = __float2half_rn(0.0f);
+                if (e == 0 && status) report_error(status, DEV_ERR_INDEX);
+                continue;
+            }
+            r = (int)id;
+        }
         float y;
         if (type == TYPE_Q8_0) {
             const size_t b = (size_t)(e / 32) * 34;
@@ -322,11 +334,12 @@ __global__ void dequant_kernel(int type, const uint8_t *tiled, int row_begin, in
 }
 
 cudaError_t launch_dequant(int type, const uint8_t *tiled, int row_begin, int rows, int K, void *out,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, const uint32_t *ids, int w_rows, int *status) {
     const size_t total = (size_t)rows * K;
     if (total == 0) return cudaSuccess;
     const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 32);
-    dequant_kernel<<<blocks, 256, 0, stream>>>(type, tiled, row_begin, rows, K, reinterpret_cast<__half *>(out));
+    dequant_kernel<<<blocks, 256, 0, stream>>>(type, tiled, row_begin, rows, K, reinterpret_cast<__half *>(out), ids,
+                                               w_rows, status);
     return cudaGetLastError();
 }
 

@@ -108,6 +108,7 @@ int check_device_status(kq_ctx *c) {
     *hs = kq::DEV_OK;
     c->split_dirty = true;  // a kernel that stopped early may have left arrival counts behind
     if (st == kq::DEV_ERR_TIMEOUT) return fail(c, KQ_ERR_TIMEOUT, "a device-side wait timed out");
+    if (st == kq::DEV_ERR_INDEX) return fail(c, KQ_ERR_SHAPE, "a row id is past the end of the weight");
     return fail(c, KQ_ERR_CUDA, "device error code %d", st);
 }
 
@@ -954,6 +955,30 @@ extern "C" int kq_dequant_rows(kq_ctx *c, const kq_weight *w, int row_begin, int
     if (int r = ensure(c, c->tmp, b + 16)) return r;
     if (int r = kq_dequant_rows_async(c, w, row_begin, rows, reinterpret_cast<uint16_t *>(c->tmp.p))) return r;
     KQ_CUDA(c, cudaMemcpyAsync(dst, c->tmp.p, b, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+extern "C" int kq_embed_rows_async(kq_ctx *c, const kq_weight *w, const uint32_t *ids, int n, uint16_t *dst) {
+    if (!c || !w || !ids || !dst) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (n < 0) return fail(c, KQ_ERR_SHAPE, "n = %d", n);
+    KQ_CUDA(c, kq::launch_dequant((int)w->type, w->d, 0, n, w->cols, dst, c->stream, ids, w->rows, c->d_status));
+    return KQ_OK;
+}
+
+extern "C" int kq_embed_rows(kq_ctx *c, const kq_weight *w, const uint32_t *ids, int n, uint16_t *dst) {
+    if (!c || !w || !ids || !dst) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (n < 0) return fail(c, KQ_ERR_SHAPE, "n = %d", n);
+    for (int i = 0; i < n; ++i)
+        if (ids[i] >= (uint32_t)w->rows) return fail(c, KQ_ERR_SHAPE, "id %u past the weight's %d rows", ids[i], w->rows);
+    if (n == 0) return KQ_OK;
+    cudaSetDevice(c->device);
+    const size_t ob = (size_t)n * w->cols * 2, ib = ((size_t)n * 4 + 255) & ~(size_t)255;
+    if (int r = ensure(c, c->tmp, ib + ob + 16)) return r;
+    uint32_t *dids = reinterpret_cast<uint32_t *>(c->tmp.p);
+    uint16_t *dout = reinterpret_cast<uint16_t *>(reinterpret_cast<uint8_t *>(c->tmp.p) + ib);
+    KQ_CUDA(c, cudaMemcpyAsync(dids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream));
+    if (int r = kq_embed_rows_async(c, w, dids, n, dout)) return r;
+    KQ_CUDA(c, cudaMemcpyAsync(dst, dout, ob, cudaMemcpyDeviceToHost, c->stream));
     return sync_and_check(c);
 }
 

@@ -27,6 +27,7 @@ constexpr int TYPE_Q6_K = 14;
 // device-side error codes written to the context's status word
 constexpr int DEV_OK = 0;
 constexpr int DEV_ERR_TIMEOUT = 1;
+constexpr int DEV_ERR_INDEX = 2;  // a row id past the end of a weight (the access was skipped)
 
 // BlockQ8K of the reference (ENG:868-872): 292 bytes
 struct BlockQ8K {

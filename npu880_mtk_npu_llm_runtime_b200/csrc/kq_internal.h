@@ -108,6 +108,9 @@ cudaError_t launch_rmsnorm_q8k(const void *x, const void *gamma, void *out, void
 cudaError_t launch_swiglu_q8k(void *gate, const void *up, void *q8k, int M, int N, cudaStream_t stream, bool pdl);
 cudaError_t launch_argmax_finalize(const unsigned long long *keys, int M, const uint32_t *ids, uint32_t *toks,
                                    float *vals, cudaStream_t stream);
-cudaError_t launch_dequant(int type, const uint8_t *tiled, int row_begin, int rows, int K, void *out, cudaStream_t stream);
+// rows [row_begin, row_begin + rows) to fp16, or (ids != nullptr) rows ids[0..rows) of a weight of
+// w_rows rows, out-of-range ids giving zeros and DEV_ERR_INDEX in *status
+cudaError_t launch_dequant(int type, const uint8_t *tiled, int row_begin, int rows, int K, void *out, cudaStream_t stream,
+                           const uint32_t *ids = nullptr, int w_rows = 0, int *status = nullptr);
 
 }  // namespace kq

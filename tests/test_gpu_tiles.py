@@ -100,3 +100,35 @@ def test_dequant_tiled(kqctx, oracle, gtype):
         W.free()
     ref = oracle.dequant(gtype, w[7:37], K)
     assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
+
+
+@pytest.mark.parametrize("gtype", TYPES, ids=lambda t: synth.TYPE_NAMES[t])
+def test_embed_rows(kqctx, oracle, gtype):
+    """embedding lookup: rows by token id (repeats, the last row, unsorted), host and device
+    entry points, bit-exact to the reference's dequant of those rows; an id past the end is an
+    error before anything runs (host) or a zero row and KQ_ERR_SHAPE at the next synchronize
+    (device)"""
+    import torch
+    rows, K = 45, 768
+    w = synth.gen_weights(gtype, rows, K, seed=950 + gtype)
+    W = kqctx.upload(w, gtype, rows, K)
+    ids = np.array([44, 3, 3, 17, 0, 31], np.uint32)
+    try:
+        got = kqctx.embed_rows(W, ids)
+        ref = oracle.dequant(gtype, w[ids], K)
+        assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
+        with pytest.raises(kq.KQError) as e:
+            kqctx.embed_rows(W, np.array([2, 45], np.uint32))
+        assert e.value.status == -3
+        dids = torch.from_numpy(np.array([5, 45, 7], np.uint32).view(np.int32)).cuda()
+        out = torch.full((3, K), 1.0, dtype=torch.float16, device="cuda")
+        kqctx.embed_rows_async(W, dids, 3, out)
+        with pytest.raises(kq.KQError) as e:
+            kqctx.synchronize()
+        assert e.value.status == -3
+        o = out.cpu().numpy()
+        assert np.array_equal(o[0].view(np.uint16), oracle.dequant(gtype, w[5:6], K)[0].view(np.uint16))
+        assert not o[1].any()
+        assert np.array_equal(o[2].view(np.uint16), oracle.dequant(gtype, w[7:8], K)[0].view(np.uint16))
+    finally:
+        W.free()
