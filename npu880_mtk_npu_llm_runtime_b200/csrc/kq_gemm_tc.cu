@@ -37,6 +37,7 @@ namespace {
 
 constexpr int kTcCompute = 256;  // 8 warps: two per TMEM lane quadrant, each half a row / half the tokens
 constexpr int kTcSplitBN = 32;   // largest token tile that may split K
+constexpr int kTcQ80SplitUnits = 16;  // Q8_0 rows of at least this many 256-value units may split K
 constexpr int kTcThreads = kTcCompute + 32;
 
 // ROWS weight rows (128, or 64 when 128-row CTAs would leave SMs idle) x BN tokens per CTA
@@ -362,6 +363,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             const uint32_t tb = tmem + lane_base + (uint32_t)(buf * 256);
             if (TYPE == TYPE_Q8_0) {
                 const uint32_t dw4[4] = {__float_as_uint(dpp[buf][0]), __float_as_uint(dpp[buf][1]), dqq[buf][0], dqq[buf][1]};
+                // split K (long rows only): the unit's eight 32-block terms are summed in block
+                // order into one term per unit, so the stored terms stay one per unit as for the
+                // K-quants -- the same products, fp32 grouped per unit (within 1e-5 of the
+                // reference's sequential order); unsplit: each block term in order, exact
+                bool unit_terms = false;
+                if constexpr (kTcSplitBN >= BN) unit_terms = p.terms != nullptr;
+                float ut[BH];
+#pragma unroll
+                for (int i = 0; i < BH; ++i) ut[i] = 0.0f;
 #pragma unroll
                 for (int jj = 0; jj < 8; ++jj) {
                     uint32_t D[BH];
@@ -371,8 +381,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 #pragma unroll
                     for (int i = 0; i < BH; ++i) {
                         const float t = __fmul_rn(__fmul_rn(dw, dxs[i * 8 + jj]), __int2float_rn((int)D[i]));
-                        put((u0 + e) * 8 + jj, i, t);
+                        if (unit_terms) ut[i] = __fadd_rn(ut[i], t);
+                        else put((u0 + e) * 8 + jj, i, t);
                     }
+                }
+                if (unit_terms) {
+#pragma unroll
+                    for (int i = 0; i < BH; ++i) put(u0 + e, i, ut[i]);
                 }
             } else {
                 // split-capable tiles read the accumulators in chunks of at most 16 token columns
@@ -507,7 +522,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 
 // Sum of the block terms of one split-K product in unit order (the reference's acc += term
 // sequence), then the outputs as the single-chunk epilogue writes them.  One thread per (token,
-// task row); terms[u][token][row] with nterm terms per row (Q8_0: eight per unit).
+// task row); terms[u][token][row] with nterm terms per row (one per 256-value unit).
 __global__ void tc_fold_kernel(const float *terms, int nterm, int M, int rows, __half *dst, long long dst_stride,
                                const __half *res, long long res_stride, float *dst_f32, long long f32_stride) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -626,8 +641,8 @@ TcTaskPlan tc_task_plan(int type, int bn, long long n_tok_tiles, long long n_rg,
     for (int r64 = 0; r64 < 2; ++r64) {
         const long long ctas = n_tok_tiles * ((n_rg + (r64 ? 3 : 7)) / (r64 ? 4 : 8));
         int ks = 1;
-        // Q8_0 keeps eight terms per unit: its term buffer would outgrow the weights
-        if (type != TYPE_Q8_0 && bn <= kTcSplitBN && nbu >= 8 && 2 * ctas <= sms)
+        // Q8_0 splits only long rows (its split terms are per-unit sums, see the epilogue)
+        if ((type != TYPE_Q8_0 || nbu >= kTcQ80SplitUnits) && bn <= kTcSplitBN && nbu >= 8 && 2 * ctas <= sms)
             ks = (int)std::max<long long>(1, std::min<long long>(nbu / 4, sms / ctas));
         const bool small = r64 || bn < 64;
         const double unit = (type == TYPE_Q8_0) ? 6.0 : (type == TYPE_Q6_K) ? (small ? 2.5 : 4.2) : (small ? 2.1 : 2.8);
@@ -665,7 +680,8 @@ int tc_pick_bn(int type, int M, int nbu, const int *task_rgs, int n_tasks, int s
 
 // fp32 block terms of one split-K task: (terms per row) x M x rows
 size_t tc_terms_bytes(int type, int M, int K, int rows) {
-    const size_t nterm = (size_t)(K / 256) * (type == TYPE_Q8_0 ? 8 : 1);
+    (void)type;  // one term per 256-value unit for every type (Q8_0: the unit's eight block terms summed)
+    const size_t nterm = (size_t)(K / 256);
     return nterm * (size_t)M * (size_t)rows * 4;
 }
 
@@ -731,7 +747,7 @@ cudaError_t launch_tc_bn(const TcLaunch &L, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         if (ks > 1) {
             const long long n = (long long)L.M * h.rows;
-            tc_fold_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(p.terms, (TYPE == TYPE_Q8_0) ? 8 * nbu : nbu, L.M, h.rows,
+            tc_fold_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(p.terms, nbu, L.M, h.rows,
                                                                        p.dst, p.dst_stride, p.res, p.res_stride, p.dst_f32,
                                                                        p.f32_stride);
             e = cudaGetLastError();

@@ -13,6 +13,7 @@ import pytest
 import npu880_mtk_npu_llm_runtime_b200 as kq
 from npu880_mtk_npu_llm_runtime_b200 import synth
 from conftest import bits, to_dev
+from test_gpu_split import check_q80_tolerance
 
 pytestmark = pytest.mark.gpu
 
@@ -93,7 +94,8 @@ def test_tc_fp16_input_tasks_residual(kqctx, oracle, gtype):
 def test_tc_split_k(kqctx, oracle, gtype, M):
     """few rows and a long K: the row-major kernel splits K over CTAs, stores the block terms and
     a fold kernel adds them in unit order (fp32, fp16 + residual, an unaligned row range).  At
-    M = 48 / 64 it runs two 32-token tiles with K split instead of one 64-token tile."""
+    M = 48 / 64 it runs two 32-token tiles with K split instead of one 64-token tile.  Q8_0's split
+    terms are per-unit sums of its eight 32-block terms (check_q80_tolerance); the others bit-exact."""
     import torch
     rows_w, rb, n, K = 320, 5, 290, 4096
     w = synth.gen_weights(gtype, rows_w, K, seed=1700 + gtype + M)
@@ -113,29 +115,39 @@ def test_tc_split_k(kqctx, oracle, gtype, M):
     finally:
         W.free()
     ref = oracle.gemm(gtype, w[rb:rb + n], K, act)
-    assert np.array_equal(bits(got), bits(ref)), f"max |diff| {np.abs(got - ref).max()}"
     r16 = (ref + res.cpu().numpy().view(np.float16).astype(np.float32)).astype(np.float16)
+    if gtype == kq.TYPE_Q8_0:
+        check_q80_tolerance(got, ref, got16, r16)
+        return
+    assert np.array_equal(bits(got), bits(ref)), f"max |diff| {np.abs(got - ref).max()}"
     assert np.array_equal(got16.view(np.uint16), r16.view(np.uint16))
 
 
-@pytest.mark.parametrize("M,rows", [(16, 256), (64, 2560)])
-def test_tc_ffn_down_shape(kqctx, oracle, M, rows):
-    """the tree-verify FFN down projection shape (Q6_K, K = 9728) at M = 16 (256 rows) and at
-    M = 64 (all 2,560 rows: 32-token tiles with K split)"""
+@pytest.mark.parametrize("gtype,M,rows", [(kq.TYPE_Q6_K, 16, 256), (kq.TYPE_Q6_K, 64, 2560), (kq.TYPE_Q8_0, 64, 2560)],
+                         ids=["q6_k-16", "q6_k-64", "q8_0-64"])
+def test_tc_ffn_down_shape(kqctx, oracle, gtype, M, rows):
+    """the FFN down projection shape (K = 9728): Q6_K (tree verify) at M = 16 (256 rows) and at
+    M = 64 (all 2,560 rows: 32-token tiles with K split), and Q8_0 (the batched-decode stack's
+    down projection) at M = 64 with per-unit split terms (check_q80_tolerance)"""
     import torch
-    gtype, K = kq.TYPE_Q6_K, 9728
+    K = 9728
     w = synth.gen_weights(gtype, rows, K, seed=1500)
     x = synth.gen_activations(M, K, seed=1501)
     act = oracle.act_for(gtype, x)
     W = kqctx.upload(w, gtype, rows, K)
     try:
         out = torch.full((M, rows), float("nan"), dtype=torch.float32, device="cuda")
-        kqctx.gemm_multi_q8_async(to_dev(act), None, M, K, [dict(w=W, dst_f32=out)])
+        a = to_dev(act)
+        kqctx.gemm_multi_q8_async(None if gtype == kq.TYPE_Q8_0 else a, a if gtype == kq.TYPE_Q8_0 else None, M, K,
+                                  [dict(w=W, dst_f32=out)])
         kqctx.synchronize()
         got = out.cpu().numpy()
     finally:
         W.free()
     ref = oracle.gemm(gtype, w, K, act)
+    if gtype == kq.TYPE_Q8_0:
+        check_q80_tolerance(got, ref)
+        return
     assert np.array_equal(bits(got), bits(ref)), f"max |diff| {np.abs(got - ref).max()}"
 
 
