@@ -345,6 +345,34 @@ cudaError_t launch_dequant(int type, const uint8_t *tiled, int row_begin, int ro
 
 // ------------------------------------------------------------------ argmax keys -> (row, value)
 
+// Argmax keys of stored fp16 logits (the LM head's scan of the fp16 logits, ENG:9699-9707, for
+// products that wrote their logits first): keys[m] = max over rows r of argmax_key(logit, r), so
+// the largest logit wins and, among equal ones, the first row -- the strict '>' scan.  keys must
+// start at 0.  Grid: x over rows, y = token.
+__global__ void logits_argmax_kernel(const __half *logits, long long stride, int rows, unsigned long long *keys) {
+    const int m = blockIdx.y;
+    const __half *lg = logits + (size_t)m * stride;
+    unsigned long long best = 0ull;
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+        const unsigned long long k = argmax_key(__half2float(lg[r]), (uint32_t)r);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+        best = k > best ? k : best;
+    }
+    if ((threadIdx.x & 31) == 0 && best) atomicMax(&keys[m], best);
+}
+
+cudaError_t launch_logits_argmax(const void *logits, long long stride, int rows, int M, unsigned long long *keys,
+                                 cudaStream_t stream) {
+    if (M <= 0 || rows <= 0) return cudaSuccess;
+    const int bx = std::min((rows + 255) / 256, 64);
+    logits_argmax_kernel<<<dim3(bx, M), 256, 0, stream>>>(reinterpret_cast<const __half *>(logits), stride, rows, keys);
+    return cudaGetLastError();
+}
+
 // keys[m] = (ordered value << 32) | (0xFFFFFFFF - index); index maps through ids when given.
 __global__ void argmax_finalize_kernel(const unsigned long long *keys, int M, const uint32_t *ids, uint32_t *toks,
                                        float *vals) {

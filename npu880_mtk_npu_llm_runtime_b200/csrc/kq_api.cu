@@ -39,6 +39,7 @@ struct kq_ctx {
 
     // scratch (grown on demand, freed at destroy)
     DevBuf x, res, out16, out32, q8k_pending, q8k_cur, q80_cur, tmp, misc, keys, tcpack, tcterms;
+    DevBuf lmlogits;  // fp16 logits of a many-token LM head when the caller keeps none
     // balanced GEMV launches: shared-row-group term slots and arrival counts (zero between
     // launches; re-cleared after a launch that stopped early)
     DevBuf gsplit, gcount;
@@ -434,7 +435,7 @@ extern "C" int kq_destroy(kq_ctx *c) {
     cudaSetDevice(c->device);
     cudaStreamSynchronize(c->stream);
     for (DevBuf *b : {&c->x, &c->res, &c->out16, &c->out32, &c->q8k_pending, &c->q8k_cur, &c->q80_cur, &c->tmp,
-                      &c->misc, &c->keys, &c->tcpack, &c->tcterms, &c->gsplit, &c->gcount})
+                      &c->misc, &c->keys, &c->tcpack, &c->tcterms, &c->gsplit, &c->gcount, &c->lmlogits})
         if (b->p) cudaFree(b->p);
     cudaFreeHost(c->h_status);
     if (c->own_stream) cudaStreamDestroy(c->stream);
@@ -998,6 +999,19 @@ extern "C" int kq_lm_head_argmax_async(kq_ctx *c, const kq_weight *w, const uint
     t.dst_stride = (size_t)w->rows;
     t.dst_f32 = logits_f32;
     t.dst_f32_stride = (size_t)w->rows;
+    if (M > 8) {
+        // many tokens: the logits come from the tensor-core path (or GEMV tiles, by the cost
+        // model) into the caller's fp16 buffer or a scratch one, then one scan of the fp16 logits
+        if (!t.dst) {
+            if (int r = ensure(c, c->lmlogits, (size_t)M * w->rows * 2)) return r;
+            t.dst = reinterpret_cast<uint16_t *>(c->lmlogits.p);
+        }
+        if (int r = run_gemv(c, &t, 1, M, w->cols, reinterpret_cast<const __half *>(x), w->cols, nullptr, nullptr))
+            return r;
+        KQ_CUDA(c, kq::launch_logits_argmax(t.dst, (long long)w->rows, w->rows, M, keys, c->stream));
+        KQ_CUDA(c, kq::launch_argmax_finalize(keys, M, nullptr, toks, vals, c->stream));
+        return KQ_OK;
+    }
     GemvExtra ex;
     ex.argmax = keys;
     ex.argmax_f16 = 1;  // the reference scans the fp16 logits the dispatch stored (ENG:9699-9707)

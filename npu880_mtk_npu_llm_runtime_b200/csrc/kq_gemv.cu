@@ -100,12 +100,6 @@ struct GemvParams {
     int *gcount;
 };
 
-// Total order on floats as unsigned keys: larger float -> larger key.
-__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
-    const uint32_t b = __float_as_uint(v);
-    const uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-    return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - index);
-}
 
 // token-slot pitch of the dx / -32*xsum tables (mma reads of tokens 2t, 2t+1 stay inside)
 template <int MT>

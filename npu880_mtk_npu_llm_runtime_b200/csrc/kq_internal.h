@@ -106,6 +106,9 @@ cudaError_t launch_repack(int type, const uint8_t *gguf, uint8_t *dev, int rows,
 cudaError_t launch_rmsnorm_q8k(const void *x, const void *gamma, void *out, void *q8k, int M, int K, cudaStream_t stream,
                                bool pdl);
 cudaError_t launch_swiglu_q8k(void *gate, const void *up, void *q8k, int M, int N, cudaStream_t stream, bool pdl);
+// keys[m] = argmax key over the fp16 logits [M][stride] rows 0..rows-1 (keys zeroed before)
+cudaError_t launch_logits_argmax(const void *logits, long long stride, int rows, int M, unsigned long long *keys,
+                                 cudaStream_t stream);
 cudaError_t launch_argmax_finalize(const unsigned long long *keys, int M, const uint32_t *ids, uint32_t *toks,
                                    float *vals, cudaStream_t stream);
 // rows [row_begin, row_begin + rows) to fp16, or (ids != nullptr) rows ids[0..rows) of a weight of

@@ -129,6 +129,28 @@ def test_lm_head_ties_pick_first_row(kqctx, oracle):
     assert np.array_equal(toks, rb) and np.array_equal(bits(vals), bits(rv))
 
 
+@pytest.mark.parametrize("M", [12, 40])
+@pytest.mark.parametrize("want_logits", [True, False], ids=["logits", "no-logits"])
+def test_lm_head_many_tokens(kqctx, oracle, M, want_logits):
+    """more than 8 tokens: fp16 logits from the matrix-product path, then one scan of them --
+    the same tokens, values and first-row-on-ties rule as the fused GEMV argmax; a duplicated
+    winning row checks the tie rule"""
+    K, V = 512, 5000
+    w = synth.gen_weights(kq.TYPE_Q6_K, V, K, 41)
+    x = synth.gen_activations(M, K, 42)
+    act = oracle.quantize_q8k(x)
+    best, _, _ = oracle.rows_argmax(kq.TYPE_Q6_K, w, K, act, f16_compare=True)
+    w2 = w.copy()
+    w2[V - 1] = w[best[0]]   # an equal logit later in the vocabulary: the first row must win
+    W = kqctx.upload(w2, kq.TYPE_Q6_K, V, K)
+    toks, vals, logits = kqctx.lm_head_argmax(W, x, want_logits=want_logits)
+    W.free()
+    rb, rv, ref = oracle.rows_argmax(kq.TYPE_Q6_K, w2, K, act, f16_compare=True, want_logits=True)
+    assert np.array_equal(toks, rb) and np.array_equal(bits(vals), bits(rv))
+    if want_logits:
+        assert np.array_equal(bits(logits), bits(ref.astype(np.float16)))
+
+
 def test_lm_head_config1_shape(kqctx, oracle):
     """BASELINE config 1 at full size: Q6_K LM head, N=151936, K=2560 (logits bit-exact)"""
     import torch
