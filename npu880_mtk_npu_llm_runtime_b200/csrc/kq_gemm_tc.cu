@@ -528,8 +528,24 @@ __global__ void tc_fold_kernel(const float *terms, int nterm, int M, int rows, _
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)M * rows) return;
     const int tok = (int)(idx / rows), lr = (int)(idx % rows);
+    const float *t0 = terms + (size_t)tok * rows + lr;
+    const size_t ts = (size_t)M * rows;  // stride between units
+    // loads 16 at a time (independent), adds one by one in unit order
     float acc = 0.0f;
-    for (int u = 0; u < nterm; ++u) acc = __fadd_rn(acc, terms[((size_t)u * M + tok) * rows + lr]);
+    int u = 0;
+    for (; u + 16 <= nterm; u += 16) {
+        float t[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) t[k] = t0[(size_t)(u + k) * ts];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc = __fadd_rn(acc, t[k]);
+    }
+    float t[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) t[k] = (u + k < nterm) ? t0[(size_t)(u + k) * ts] : 0.0f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+        if (u + k < nterm) acc = __fadd_rn(acc, t[k]);
     if (dst_f32) dst_f32[(size_t)tok * f32_stride + lr] = acc;
     if (dst) {
         float v = acc;
