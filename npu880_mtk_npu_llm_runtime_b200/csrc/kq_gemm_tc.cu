@@ -11,9 +11,9 @@
 // epilogue:
 //   Q4_K / Q5_K   sc = 8 sh + sl:  A0 = q * sh, A1 = q * sl (u8), A2 = the row's min m_j over
 //                 its sub-block (u8);  sumi = 8 D0 + D1, summ = D2 (= sum_j m_j * bsum_j)
-//   Q6_K          q - 32 = 8 qa + qb (qa in -4..3, qb in 0..7), sc = 16 sh + sl (sh in -8..7,
-//                 sl in 0..15; any int8 scale): A0 = sl qb, A1 = sl qa, A2 = sh qb, A3 = sh qa
-//                 (s8); sumi = D0 + 8 D1 + 16 D2 + 128 D3  (= sum_s sc_s * sum_l (q_l - 32) x_l)
+//   Q6_K          P = sc * (q - 32) in -3968..4096 for any int8 scale: P = 64 Ph + Pl with
+//                 Pl = P & 63 (0..63) and Ph = P >> 6 (-62..64): A0 = Ph, A1 = Pl (s8);
+//                 sumi = 64 D0 + D1  (= sum_s sc_s * sum_l (q_l - 32) x_l)
 //   Q8_0          A = the quants (s8); one MMA per 32-value block into its own accumulator
 // D_i are int32 per (row, token) in TMEM.
 //
@@ -45,7 +45,7 @@ template <int TYPE, int BN_, int ROWS_>
 struct TcCfg {
     static constexpr int BN = BN_, ROWS = ROWS_;
     static constexpr int RG = ROWS / 16;                                             // row groups per CTA
-    static constexpr int NA = (TYPE == TYPE_Q8_0) ? 1 : (TYPE == TYPE_Q6_K) ? 4 : 3;  // A operands
+    static constexpr int NA = (TYPE == TYPE_Q8_0) ? 1 : (TYPE == TYPE_Q6_K) ? 2 : 3;  // A operands
     static constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;                      // scales per token and unit
     static constexpr unsigned OPS = (unsigned)ROWS * 256u;                      // bytes of one A operand
     static constexpr unsigned B_BYTES = BN * 256;
@@ -133,19 +133,18 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // per-byte a - b as int8, for bytes a in [0, 127] and b in [0, 128] (no borrow crosses a byte)
-__device__ __forceinline__ uint32_t sub_bytes(uint32_t a, uint32_t b) { return ((a | 0x80808080u) - b) ^ 0x80808080u; }
-// Q6_K operand bytes of one word of four 6-bit quants q: (q - 32) * sc split as in the header,
-// for any int8 scale sc.  All products stay within int8 (|A| <= 105).
-__device__ __forceinline__ void q6_pieces(uint32_t q, int sc, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
-    const uint32_t qb = q & 0x07070707u, qa4 = (q >> 3) & 0x07070707u;  // qa4 = qa + 4
-    const uint32_t sl = (uint32_t)(sc & 15);
-    const int sh = sc >> 4;
-    const uint32_t ash = (uint32_t)(sh < 0 ? -sh : sh);
-    a0 = qb * sl;
-    a1 = sub_bytes(qa4 * sl, 0x01010101u * (4u * sl));
-    const uint32_t pb = qb * ash, pa = qa4 * ash, r4 = 0x01010101u * (4u * ash);
-    a2 = sh < 0 ? sub_bytes(0u, pb) : pb;                        // sh * qb
-    a3 = sh < 0 ? sub_bytes(r4, pa) : sub_bytes(pa, r4);         // sh * qa = |sh| (4 - qa4) or |sh| (qa4 - 4)
+// Q6_K operand bytes of one word of four 6-bit quants q (0..63) for any int8 scale sc:
+// P = sc * (q - 32) = 64 Ph + Pl, Pl = P & 63, Ph = P >> 6, as int8 bytes in ph / pl.  Two quants
+// at a time in 16-bit lanes: one multiply-add gives V = sc * q + 4096 - 32 sc = P + 4096, whose
+// exact value per lane is in 128..8192 (so the 32-bit result, taken modulo 2^32, holds both lanes
+// unchanged); then Ph = (V >> 6) - 64 and Pl = V & 63.  Checked on the CPU for every (q, sc).
+__device__ __forceinline__ void q6_pieces2(uint32_t q, int sc, uint32_t &ph, uint32_t &pl) {
+    const uint32_t k2 = (uint32_t)(4096 - 32 * sc) * 0x00010001u;
+    const uint32_t w02 = __byte_perm(q, 0u, 0x4240), w13 = __byte_perm(q, 0u, 0x4341);  // q0|q2<<16, q1|q3<<16
+    const uint32_t v02 = w02 * (uint32_t)sc + k2, v13 = w13 * (uint32_t)sc + k2;
+    const uint32_t h02 = ((v02 >> 6) + 0x00C000C0u) & 0x00FF00FFu, h13 = ((v13 >> 6) + 0x00C000C0u) & 0x00FF00FFu;
+    ph = __byte_perm(h02, h13, 0x6240);
+    pl = __byte_perm(v02 & 0x003F003Fu, v13 & 0x003F003Fu, 0x6240);
 }
 
 // ---- A operands of one super-block: half hs (values 128 hs .. 128 hs + 127) of row r, from the
@@ -221,13 +220,11 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, int hs, ui
                         else q[i] = ((bv[i] >> 4) & 0x0F0F0F0Fu) | ((hv[i] >> 2) & 0x30303030u);
                     }
                     const uint32_t o = canon256(r, s);  // sub-block s = 16-byte chunk s
-                    uint32_t p0[4], p1[4], p2[4], p3[4];
+                    uint32_t p0[4], p1[4];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) q6_pieces(q[i], sc, p0[i], p1[i], p2[i], p3[i]);
+                    for (int i = 0; i < 4; ++i) q6_pieces2(q[i], sc, p0[i], p1[i]);
                     *reinterpret_cast<uint4 *>(A + o) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
                     *reinterpret_cast<uint4 *>(A + OPS + o) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
-                    *reinterpret_cast<uint4 *>(A + 2 * OPS + o) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
-                    *reinterpret_cast<uint4 *>(A + 3 * OPS + o) = make_uint4(p3[0], p3[1], p3[2], p3[3]);
                 }
             }
         }
@@ -405,7 +402,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                         const float dx = dxs[c0 + i];
                         float t;
                         if (TYPE == TYPE_Q6_K) {
-                            const int sumi = (int)D[0][i] + 8 * (int)D[1][i] + 16 * (int)D[2][i] + 128 * (int)D[3][i];
+                            const int sumi = 64 * (int)D[0][i] + (int)D[1][i];
                             t = __fmul_rn(__fmul_rn(d, dx), __int2float_rn(sumi));
                         } else {
                             const int sumi = 8 * (int)D[0][i] + (int)D[1][i];
@@ -806,13 +803,13 @@ cudaError_t launch_tc_t(const TcLaunch &L, cudaStream_t stream) {
 //              c % 2 == w / 4.
 // Token t sits in TMEM lane 32 (t % 4) + t / 4, so a small token count still spreads over all
 // four lane quadrants and all eight epilogue warps.
-// One MMA accumulator chain per item: N = 192 (Q4_K/Q5_K 4 x 48, Q6_K 3 x 64) keeps the tensor
+// One MMA accumulator chain per item: N = 192 (Q4_K/Q5_K 4 x 48; Q6_K 3 x 32 = 96) keeps the tensor
 // core near its peak rate; Q8_0 items are one row group with eight independent 32-block chains.
 // TMEM: columns [0, 128) two activation buffers, [128, 512) SD item accumulators.
 
 template <int TYPE>
 struct Tc2Cfg {
-    static constexpr int NOP = (TYPE == TYPE_Q6_K) ? 4 : (TYPE == TYPE_Q8_0) ? 1 : 3;
+    static constexpr int NOP = (TYPE == TYPE_Q6_K) ? 2 : (TYPE == TYPE_Q8_0) ? 1 : 3;
     static constexpr int G = (TYPE == TYPE_Q6_K) ? 3 : (TYPE == TYPE_Q8_0) ? 1 : 4;  // row groups per item
     static constexpr int NMMA = (TYPE == TYPE_Q8_0) ? 16 : G * NOP * 16;              // N of one MMA
     static constexpr int NCOL = (TYPE == TYPE_Q8_0) ? 128 : NMMA;                     // D columns per item
@@ -1185,7 +1182,7 @@ __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_c
                                 for (int r = 0; r < 16; ++r) {
                                     if (TYPE == TYPE_Q6_K) {
                                         const float d = *reinterpret_cast<const float *>(hdr + 8 * r);
-                                        const int sumi = (int)D[0][r] + 8 * (int)D[1][r] + 16 * (int)D[2][r] + 128 * (int)D[3][r];
+                                        const int sumi = 64 * (int)D[0][r] + (int)D[1][r];
                                         tm[r] = __fmul_rn(__fmul_rn(d, dx), __int2float_rn(sumi));
                                     } else {
                                         const float2 dd = *reinterpret_cast<const float2 *>(hdr + 8 * r);
