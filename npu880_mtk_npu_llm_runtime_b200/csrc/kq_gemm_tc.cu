@@ -9,8 +9,10 @@
 // scales, does not map onto one int8 MMA (sc * q needs 10-12 bits).  It is split into pieces
 // that fit a byte, each one MMA over the whole 256-value super-block, recombined exactly in the
 // epilogue:
-//   Q4_K / Q5_K   sc = 8 sh + sl:  A0 = q * sh, A1 = q * sl (u8), A2 = the row's min m_j over
-//                 its sub-block (u8);  sumi = 8 D0 + D1, summ = D2 (= sum_j m_j * bsum_j)
+//   Q4_K / Q5_K   sc = 8 sh + sl:  A0 = q * sh, A1 = q * sl (u8);  sumi = 8 D0 + D1.  The mins
+//                 term summ = sum_j m_j * bsum_j comes from two K = 32 MMAs: the row's m_0..m_7
+//                 against the token's bsum32 split as bsum = 64 bh + bl (bl 0..63, bh -64..63):
+//                 D2 = sum_j m_j bl_j, D3 = sum_j m_j bh_j, summ = D2 + 64 D3
 //   Q6_K          P = sc * (q - 32) in -3968..4096 for any int8 scale: P = 64 Ph + Pl with
 //                 Pl = P & 63 (0..63) and Ph = P >> 6 (-62..64): A0 = Ph, A1 = Pl (s8);
 //                 sumi = 64 D0 + D1  (= sum_s sc_s * sum_l (q_l - 32) x_l)
@@ -45,18 +47,22 @@ template <int TYPE, int BN_, int ROWS_>
 struct TcCfg {
     static constexpr int BN = BN_, ROWS = ROWS_;
     static constexpr int RG = ROWS / 16;                                             // row groups per CTA
-    static constexpr int NA = (TYPE == TYPE_Q8_0) ? 1 : (TYPE == TYPE_Q6_K) ? 2 : 3;  // A operands
+    static constexpr int NA = (TYPE == TYPE_Q8_0) ? 1 : 2;                      // A operands over K = 256
+    static constexpr bool MINS = (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K);      // + two K = 32 mins MMAs
+    static constexpr int NACC = MINS ? 4 : NA;                                  // accumulators per unit
     static constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;                      // scales per token and unit
     static constexpr unsigned OPS = (unsigned)ROWS * 256u;                      // bytes of one A operand
     static constexpr unsigned B_BYTES = BN * 256;
     static constexpr unsigned W_BYTES = (unsigned)RG * (unsigned)tile_bytes(TYPE);
     static constexpr unsigned DX_BYTES = BN * DX * 4;
-    static constexpr unsigned STAGE = B_BYTES + W_BYTES + DX_BYTES;            // multiple of 16
-    static constexpr unsigned A_BYTES = NA * OPS;
+    static constexpr unsigned B2_BYTES = MINS ? BN * 32u : 0u;                   // bsum bytes (bl | bh | 0)
+    static constexpr unsigned STAGE = B_BYTES + W_BYTES + DX_BYTES + B2_BYTES;  // multiple of 16
+    static constexpr unsigned A2_BYTES = MINS ? 2u * ROWS * 32u : 0u;           // m_j operands (A2a, A2b)
+    static constexpr unsigned A_BYTES = NA * OPS + A2_BYTES;
     static constexpr int S_FIT = (int)((200u * 1024u - A_BYTES) / STAGE);
     static constexpr int S = S_FIT < 2 ? 2 : (S_FIT > 6 ? 6 : S_FIT);          // ring stages
     static constexpr unsigned SMEM = A_BYTES + S * STAGE + 1024;
-    static_assert((TYPE == TYPE_Q8_0 ? 8 : NA) * BN <= 256, "accumulator buffer exceeds 256 TMEM columns");
+    static_assert((TYPE == TYPE_Q8_0 ? 8 : NACC) * BN <= 256, "accumulator buffer exceeds 256 TMEM columns");
 };
 
 struct TcParams {
@@ -67,6 +73,7 @@ struct TcParams {
     int n_tok_tiles;           // tiles of BN tokens in the packed activation
     const uint8_t *act;        // packed activation: [token tile][unit][BN * 256] K-major
     const float *dx;           // [token tile][unit][BN * DX] scales
+    const uint8_t *bs2;        // Q4_K / Q5_K: [token tile][unit][BN * 32] bsum bytes, K-major (8-row groups 256 B apart)
     __half *dst;
     long long dst_stride;
     const __half *res;
@@ -150,7 +157,10 @@ __device__ __forceinline__ void q6_pieces2(uint32_t q, int sc, uint32_t &ph, uin
 // ---- A operands of one super-block: half hs (values 128 hs .. 128 hs + 127) of row r, from the
 // row's tile bytes.  Also returns what the epilogue needs of the row: d (and dmin).
 
-template <int TYPE, unsigned OPS = 32768u>
+// MINS_K32 (row-major kernel): instead of a third operand of each row's min replicated over its
+// sub-block, half hs writes row r of A2a (hs 0: m_0..m_7 at K 0..7) or A2b (hs 1: at K 8..15), the
+// rest zero, K-major with 8-row groups 256 bytes apart, after the two K = 256 operands.
+template <int TYPE, unsigned OPS = 32768u, bool MINS_K32 = false>
 __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, int hs, uint8_t *A, int r, float &d0, float &d1) {
     if (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K) {
         constexpr int RB = (TYPE == TYPE_Q4_K) ? 144 : 176, QS = (TYPE == TYPE_Q4_K) ? 16 : 48;
@@ -166,6 +176,11 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, int hs, ui
             qh[0] = a.x, qh[1] = a.y, qh[2] = a.z, qh[3] = a.w, qh[4] = b.x, qh[5] = b.y, qh[6] = b.z, qh[7] = b.w;
         }
         const uint32_t scw = hs ? sc[1] : sc[0], mnw = hs ? mn[1] : mn[0];
+        if (MINS_K32) {
+            uint8_t *a2 = A + 2 * OPS + (size_t)hs * (OPS / 8) + (r >> 3) * 256 + (r & 7) * 16;
+            *reinterpret_cast<uint4 *>(a2) = hs ? make_uint4(0u, 0u, mn[0], mn[1]) : make_uint4(mn[0], mn[1], 0u, 0u);
+            *reinterpret_cast<uint4 *>(a2 + 128) = make_uint4(0u, 0u, 0u, 0u);
+        }
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
             const int c = 2 * hs + cc;
@@ -188,7 +203,7 @@ __device__ __forceinline__ void prep_row(const uint8_t *tile, int rr, int hs, ui
                     const uint32_t *qq = q + 4 * h16;
                     *reinterpret_cast<uint4 *>(A + o) = make_uint4(qq[0] * sh, qq[1] * sh, qq[2] * sh, qq[3] * sh);
                     *reinterpret_cast<uint4 *>(A + OPS + o) = make_uint4(qq[0] * sl, qq[1] * sl, qq[2] * sl, qq[3] * sl);
-                    *reinterpret_cast<uint4 *>(A + 2 * OPS + o) = make_uint4(mrep, mrep, mrep, mrep);
+                    if (!MINS_K32) *reinterpret_cast<uint4 *>(A + 2 * OPS + o) = make_uint4(mrep, mrep, mrep, mrep);
                 }
             }
         }
@@ -309,13 +324,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 }
                 const uint32_t full = smem_u32(&bar_full[st]);
                 uint8_t *sb = ring + (size_t)st * C::STAGE;
-                mbar_arrive_expect_tx(full, C::B_BYTES + (uint32_t)n_rg * (uint32_t)tile_bytes(TYPE) + C::DX_BYTES);
+                mbar_arrive_expect_tx(full, C::B_BYTES + (uint32_t)n_rg * (uint32_t)tile_bytes(TYPE) + C::DX_BYTES + C::B2_BYTES);
                 const size_t tix = (size_t)tok_tile * nbu + u0 + b;
                 bulk_g2s(smem_u32(sb), p.act + tix * C::B_BYTES, C::B_BYTES, full, policy);
                 for (int g = 0; g < n_rg; ++g)
                     bulk_g2s(smem_u32(sb + C::B_BYTES + g * tile_bytes(TYPE)),
                              p.w + ((size_t)(rg0 + g) * nbu + u0 + b) * tile_bytes(TYPE), tile_bytes(TYPE), full, policy);
                 bulk_g2s(smem_u32(sb + C::B_BYTES + C::W_BYTES), p.dx + tix * (BN * C::DX), C::DX_BYTES, full, policy);
+                if (C::MINS)
+                    bulk_g2s(smem_u32(sb + C::B_BYTES + C::W_BYTES + C::DX_BYTES), p.bs2 + tix * C::B2_BYTES, C::B2_BYTES,
+                             full, policy);
             }
         }
         __syncwarp();
@@ -393,9 +411,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 const float d = dpp[buf][0], dmin = dpp[buf][1];
 #pragma unroll
                 for (int c0 = 0; c0 < BH; c0 += CW) {
-                    uint32_t D[NA][CW];
+                    constexpr int NACC = C::NACC;
+                    uint32_t D[NACC][CW];
 #pragma unroll
-                    for (int a = 0; a < NA; ++a) tmem_ldn<CW>(tb + (uint32_t)(a * BN + c0), D[a]);
+                    for (int a = 0; a < NACC; ++a) tmem_ldn<CW>(tb + (uint32_t)(a * BN + c0), D[a]);
                     tmem_wait_ld();
 #pragma unroll
                     for (int i = 0; i < CW; ++i) {
@@ -406,7 +425,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                             t = __fmul_rn(__fmul_rn(d, dx), __int2float_rn(sumi));
                         } else {
                             const int sumi = 8 * (int)D[0][i] + (int)D[1][i];
-                            const int summ = (int)D[2][i];
+                            const int summ = (int)D[2][i] + 64 * (int)D[NACC - 1][i];
                             t = __fmul_rn(dx, __fsub_rn(__fmul_rn(d, __int2float_rn(sumi)), __fmul_rn(dmin, __int2float_rn(summ))));
                         }
                         put(u0 + e, c0 + i, t);
@@ -433,7 +452,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                     // A operands of super-block b (the MMAs of b - 1 have finished reading A)
                     const uint8_t *tile = ring + (size_t)st * C::STAGE + C::B_BYTES + (size_t)min(g, n_rg - 1) * tile_bytes(TYPE);
                     float d0, d1;
-                    prep_row<TYPE, C::OPS>(tile, rr, hs, A, r, d0, d1);
+                    prep_row<TYPE, C::OPS, C::MINS>(tile, rr, hs, A, r, d0, d1);
                     if (TYPE == TYPE_Q8_0) {
                         const uint4 dv = lds128(tile + 272 * rr);
                         dpp[b & 1][0] = __uint_as_float(dv.x);
@@ -468,6 +487,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                                 for (int a = 0; a < NA; ++a)
                                     tc_mma(td + (uint32_t)(a * BN), umma_desc(sa + a * C::OPS + 256 * ks, 128, 2048),
                                            umma_desc(sbm + 256 * ks, 128, 2048), idesc, ks > 0);
+                            if (C::MINS) {
+                                // mins: m_j (A2a / A2b) against bl | bh of the token's bsum32 (K = 32)
+                                const uint32_t sb2 = sbm + C::B_BYTES + C::W_BYTES + C::DX_BYTES;
+                                const uint32_t sa2 = sa + NA * C::OPS;
+                                tc_mma(td + (uint32_t)(2 * BN), umma_desc(sa2, 128, 256), umma_desc(sb2, 128, 256), idesc, 0);
+                                tc_mma(td + (uint32_t)(3 * BN), umma_desc(sa2 + C::A2_BYTES / 2, 128, 256),
+                                       umma_desc(sb2, 128, 256), idesc, 0);
+                            }
                         }
                         tc_commit(smem_u32(&bar_mma[b & 1]));
                     }
@@ -560,7 +587,7 @@ __global__ void tc_fold_kernel(const float *terms, int nterm, int M, int rows, _
 
 template <int TYPE, int BN>
 __global__ void pack_act_kernel(const __half *x, long long x_stride, const void *act, int M, int K, int n_tok_tiles,
-                                uint8_t *out, float *dx) {
+                                uint8_t *out, float *dx, uint8_t *bs2) {
     constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;
     const int nbu = K / 256;
     const int lane = threadIdx.x & 31;
@@ -618,6 +645,24 @@ __global__ void pack_act_kernel(const __half *x, long long x_stride, const void 
             if ((lane & 3) == 0) dx[tix * (BN * DX) + mm * DX + (lane >> 2)] = d;
         } else {
             if (lane == 0) dx[tix * BN + mm] = d;
+        }
+        if (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K) {
+            // bsum32 of sub-block j = lane / 4 as bl = bsum & 63 (K = j) and bh = bsum >> 6 (K = 8 + j),
+            // K 16..31 zero: one token row of the K = 32 mins operand (8-row groups 256 B apart)
+            auto sum4 = [](uint32_t w) {
+                return (int)(int8_t)(w & 0xFF) + (int)(int8_t)((w >> 8) & 0xFF) + (int)(int8_t)((w >> 16) & 0xFF) +
+                       (int)(int8_t)(w >> 24);
+            };
+            int bsum = sum4(lo) + sum4(hi);
+            bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
+            bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
+            uint8_t *b2 = bs2 + tix * (BN * 32) + (mm >> 3) * 256 + (mm & 7) * 16;
+            if ((lane & 3) == 0) {
+                const int j = lane >> 2;
+                b2[j] = (uint8_t)(bsum & 63);
+                b2[8 + j] = (uint8_t)(int8_t)(bsum >> 6);
+            }
+            if (lane == 0) *reinterpret_cast<uint4 *>(b2 + 128) = make_uint4(0u, 0u, 0u, 0u);
         }
     }
 }
@@ -703,15 +748,17 @@ cudaError_t launch_tc_bn(const TcLaunch &L, cudaStream_t stream) {
     constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;
     const int nbu = L.K / 256;
     const int n_tok_tiles = (L.M + BN - 1) / BN;
-    const size_t need = (size_t)n_tok_tiles * nbu * ((size_t)BN * 256 + (size_t)BN * DX * 4);
+    constexpr size_t B2 = (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K) ? 32 : 0;  // bsum bytes per token
+    const size_t need = (size_t)n_tok_tiles * nbu * ((size_t)BN * 256 + (size_t)BN * DX * 4 + (size_t)BN * B2);
     if (L.scratch_bytes < need) return cudaErrorInvalidValue;
     uint8_t *act = reinterpret_cast<uint8_t *>(L.scratch);
     float *dx = reinterpret_cast<float *>(act + (size_t)n_tok_tiles * nbu * BN * 256);
+    uint8_t *bs2 = reinterpret_cast<uint8_t *>(dx + (size_t)n_tok_tiles * nbu * BN * DX);
     {
         const long long items = (long long)n_tok_tiles * BN * nbu;
         const int blocks = (int)std::min<long long>((items + 7) / 8, 148 * 16);
         pack_act_kernel<TYPE, BN><<<blocks, 256, 0, stream>>>(reinterpret_cast<const __half *>(L.x), L.x_stride, L.act,
-                                                               L.M, L.K, n_tok_tiles, act, dx);
+                                                               L.M, L.K, n_tok_tiles, act, dx, bs2);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
@@ -731,6 +778,7 @@ cudaError_t launch_tc_bn(const TcLaunch &L, cudaStream_t stream) {
         p.n_tok_tiles = n_tok_tiles;
         p.act = act;
         p.dx = dx;
+        p.bs2 = bs2;
         p.dst = reinterpret_cast<__half *>(h.dst);
         p.dst_stride = h.dst_stride;
         p.res = reinterpret_cast<const __half *>(h.res);
@@ -1388,7 +1436,8 @@ cudaError_t launch_tc2_t(const TcLaunch &L, cudaStream_t stream) {
 
 size_t tc_scratch_bytes(int type, int M, int K) {
     const int nbu = K / 256, bn = tc_bn(type, M), dxn = (type == TYPE_Q8_0) ? 8 : 1;
-    return (size_t)((M + bn - 1) / bn) * nbu * ((size_t)bn * 256 + (size_t)bn * dxn * 4);
+    const size_t b2 = (type == TYPE_Q4_K || type == TYPE_Q5_K) ? 32 : 0;
+    return (size_t)((M + bn - 1) / bn) * nbu * ((size_t)bn * 256 + (size_t)bn * dxn * 4 + (size_t)bn * b2);
 }
 
 size_t tc_split_terms_bytes(int type, int M, int K, const int *task_rows, const int *task_rgs, int n_tasks, int sms) {
