@@ -353,9 +353,24 @@ __global__ void logits_argmax_kernel(const __half *logits, long long stride, int
     const int m = blockIdx.y;
     const __half *lg = logits + (size_t)m * stride;
     unsigned long long best = 0ull;
-    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
-        const unsigned long long k = argmax_key(__half2float(lg[r]), (uint32_t)r);
-        best = k > best ? k : best;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x, nt = gridDim.x * blockDim.x;
+    if ((rows & 7) == 0 && (stride & 7) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0) {
+        // 8 logits per 16-byte load
+        for (int r8 = t; r8 < rows / 8; r8 += nt) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(lg + 8 * (size_t)r8);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float f = __half2float(__ushort_as_half((unsigned short)(w[i >> 1] >> (16 * (i & 1)))));
+                const unsigned long long k = argmax_key(f, (uint32_t)(8 * r8 + i));
+                best = k > best ? k : best;
+            }
+        }
+    } else {
+        for (int r = t; r < rows; r += nt) {
+            const unsigned long long k = argmax_key(__half2float(lg[r]), (uint32_t)r);
+            best = k > best ? k : best;
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -368,7 +383,7 @@ __global__ void logits_argmax_kernel(const __half *logits, long long stride, int
 cudaError_t launch_logits_argmax(const void *logits, long long stride, int rows, int M, unsigned long long *keys,
                                  cudaStream_t stream) {
     if (M <= 0 || rows <= 0) return cudaSuccess;
-    const int bx = std::min((rows + 255) / 256, 64);
+    const int bx = std::min((rows / 8 + 255) / 256 + 1, 64);
     logits_argmax_kernel<<<dim3(bx, M), 256, 0, stream>>>(reinterpret_cast<const __half *>(logits), stride, rows, keys);
     return cudaGetLastError();
 }
