@@ -349,22 +349,31 @@ cudaError_t launch_dequant(int type, const uint8_t *tiled, int row_begin, int ro
 // products that wrote their logits first): keys[m] = max over rows r of argmax_key(logit, r), so
 // the largest logit wins and, among equal ones, the first row -- the strict '>' scan.  keys must
 // start at 0.  Grid: x over rows, y = token.
-__global__ void logits_argmax_kernel(const __half *logits, long long stride, int rows, unsigned long long *keys) {
+__global__ void __launch_bounds__(256) logits_argmax_kernel(const __half *logits, long long stride, int rows,
+                                                             unsigned long long *keys) {
     const int m = blockIdx.y;
     const __half *lg = logits + (size_t)m * stride;
     unsigned long long best = 0ull;
     const int t = blockIdx.x * blockDim.x + threadIdx.x, nt = gridDim.x * blockDim.x;
-    if ((rows & 7) == 0 && (stride & 7) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0) {
-        // 8 logits per 16-byte load
-        for (int r8 = t; r8 < rows / 8; r8 += nt) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(lg + 8 * (size_t)r8);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    auto scan8 = [&](const uint4 v, int r8) {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float f = __half2float(__ushort_as_half((unsigned short)(w[i >> 1] >> (16 * (i & 1)))));
-                const unsigned long long k = argmax_key(f, (uint32_t)(8 * r8 + i));
-                best = k > best ? k : best;
-            }
+        for (int i = 0; i < 8; ++i) {
+            const float f = __half2float(__ushort_as_half((unsigned short)(w[i >> 1] >> (16 * (i & 1)))));
+            const unsigned long long k = argmax_key(f, (uint32_t)(8 * r8 + i));
+            best = k > best ? k : best;
+        }
+    };
+    if ((rows & 7) == 0 && (stride & 7) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0) {
+        // 8 logits per 16-byte load, two loads in flight per thread
+        const int n8 = rows / 8;
+        for (int r8 = t; r8 < n8; r8 += 2 * nt) {
+            const uint4 v0 = __ldcs(reinterpret_cast<const uint4 *>(lg + 8 * (size_t)r8));
+            const bool two = r8 + nt < n8;
+            uint4 v1 = make_uint4(0u, 0u, 0u, 0u);
+            if (two) v1 = __ldcs(reinterpret_cast<const uint4 *>(lg + 8 * (size_t)(r8 + nt)));
+            scan8(v0, r8);
+            if (two) scan8(v1, r8 + nt);
         }
     } else {
         for (int r = t; r < rows; r += nt) {
@@ -377,13 +386,21 @@ __global__ void logits_argmax_kernel(const __half *logits, long long stride, int
         const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
         best = k > best ? k : best;
     }
-    if ((threadIdx.x & 31) == 0 && best) atomicMax(&keys[m], best);
+    // one atomic per block: the blocks of a token all update the same key
+    __shared__ unsigned long long s_best[8];
+    if ((threadIdx.x & 31) == 0) s_best[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int w = 1; w < 8; ++w) best = s_best[w] > best ? s_best[w] : best;
+        if (best) atomicMax(&keys[m], best);
+    }
 }
 
 cudaError_t launch_logits_argmax(const void *logits, long long stride, int rows, int M, unsigned long long *keys,
                                  cudaStream_t stream) {
     if (M <= 0 || rows <= 0) return cudaSuccess;
-    const int bx = std::min((rows / 8 + 255) / 256 + 1, 64);
+    const int bx = std::min((rows / 8 + 511) / 512 + 1, 64);
     logits_argmax_kernel<<<dim3(bx, M), 256, 0, stream>>>(reinterpret_cast<const __half *>(logits), stride, rows, keys);
     return cudaGetLastError();
 }
