@@ -843,7 +843,6 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) gemv_kernel(const __grid_
     uint8_t *ring = smem + p.off_stages;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.off_bars);  // full[S], empty[S], dead
     float *terms = reinterpret_cast<float *>(smem + p.off_terms);
-    constexpr int IPT = 1;  // items per tile
     const int S = p.n_stages, T = p.tiles_per_stage, TS = p.term_slots, J = p.terms_per_rg;
     constexpr int W = warps_of<MT>();
     const int nbu = p.nbu;
