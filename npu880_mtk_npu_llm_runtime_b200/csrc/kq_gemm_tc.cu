@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&bar_full[s]), 1);
-            mbar_init(smem_u32(&bar_empty[s]), 1);
+            mbar_init(smem_u32(&bar_empty[s]), kTcCompute / 32);  // one arrival per compute warp
         }
         mbar_init(smem_u32(&bar_mma[0]), 1);
         mbar_init(smem_u32(&bar_mma[1]), 1);
@@ -512,14 +512,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 tc_fence_after();
                 if (ok) epilogue(e);
-                named_bar_sync(1, kTcCompute);  // the stage of e (its dx, weights, B) is no longer read
-                if (*reinterpret_cast<volatile int *>(&s_abort)) break;
-                if (tid == 0) mbar_arrive(smem_u32(&bar_empty[e % S]));
+                // this warp no longer reads the stage of e (its dx, weights, B): the producer refills
+                // it after all eight arrivals.  No block barrier here -- a warp that is done starts
+                // the A operands of b + 1 while others still read accumulators of e; the barrier
+                // after the A operands orders every read of buffer e & 1 before the MMAs that
+                // overwrite it, and checks s_abort.
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&bar_empty[e % S]));
             }
         }
         // results: row r, tokens tok_tile * BN + hs * BH + m
         const int lr = lr_out;
-        if (!s_abort && !(kTcSplitBN >= BN && p.terms) && row_out) {
+        if (!*reinterpret_cast<volatile int *>(&s_abort) && !(kTcSplitBN >= BN && p.terms) && row_out) {
 #pragma unroll
             for (int m = 0; m < BH; ++m) {
                 const int tok = tok_tile * BN + hs * BH + m;
