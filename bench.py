@@ -350,7 +350,10 @@ def run_ours(args, rank, world, local_rank):
             "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "steps": e2e_steps,
                     "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(rows_local * 4),
-                    "api": "kq_sdot_gemm_multi_dispatch (host buffers, blocking)"},
+                    "api": "kq_sdot_gemm_multi_dispatch (host buffers, blocking)",
+                    "scope": ("each rank's blocking call over its vocabulary slice, max over ranks; "
+                              "the logit all-gather is not in e2e" if gather_chunks is not None
+                              else "one blocking call per step")},
             "gpu_launches": steps * launches_per_step,
         }
     for W in Ws:
