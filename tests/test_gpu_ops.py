@@ -100,6 +100,49 @@ def test_ffn_tree_verify_shape(kqctx, oracle, M):
     ffn_check(out, ref, x)
 
 
+@pytest.mark.parametrize("M", [1, 16])
+def test_ffn_block_as_one_graph(M):
+    """kq_run_ffn_async (RMSNorm+Q8_K, gate/up, SwiGLU+Q8_K, down+residual: four launches linked by
+    programmatic dependent launch) captured once into a CUDA graph after an eager call has sized
+    its scratch; two replays give the eager call's bits (GEMV path at 1 token, tensor cores at 16)"""
+    import torch
+    hidden, ffn = 2560, 9728
+    wg = synth.gen_weights(kq.TYPE_Q4_K, ffn, hidden, 211)
+    wu = synth.gen_weights(kq.TYPE_Q4_K, ffn, hidden, 212)
+    wd = synth.gen_weights(kq.TYPE_Q6_K, hidden, ffn, 213)
+    x16 = synth.gen_activations(M, hidden, 214)
+    gamma = (synth.gen_gamma(hidden, 215).astype(np.float32) * 0.1).astype(np.float16)
+    s = torch.cuda.Stream()
+    with kq.Context(0) as ctx:  # its own context: the session context keeps its stream
+        ctx.set_stream(s.cuda_stream)
+        Ws = [ctx.upload(wg, kq.TYPE_Q4_K, ffn, hidden), ctx.upload(wu, kq.TYPE_Q4_K, ffn, hidden),
+              ctx.upload(wd, kq.TYPE_Q6_K, hidden, ffn)]
+        x = to_dev(x16.view(np.uint16))
+        gm = to_dev(gamma.view(np.uint16))
+        eager = torch.zeros((M, hidden), dtype=torch.float16, device="cuda")
+        outg = torch.zeros((M, hidden), dtype=torch.float16, device="cuda")
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.stream(s):
+                ctx.run_ffn_async(*Ws, M, x, gm, eager)
+            ctx.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                ctx.run_ffn_async(*Ws, M, x, gm, outg)
+            want = bits(eager.cpu().numpy())
+            for _ in range(2):
+                with torch.cuda.stream(s):
+                    outg.fill_(float("nan"))
+                    g.replay()
+                ctx.synchronize()
+                assert np.array_equal(bits(outg.cpu().numpy()), want)
+        finally:
+            del g
+            torch.cuda.synchronize()
+            for W in Ws:
+                W.free()
+
+
 def test_lm_head_golden_and_argmax(kqctx, oracle):
     g = load_golden("lm_head_q6k")
     K = int(g["K"])
