@@ -90,3 +90,62 @@ def test_sharded_lm_head_gloo():
     ref_vals = full[np.arange(M), full.argmax(axis=1)].tolist()
     for _, r, v in got:
         assert r == ref_rows and np.allclose(v, ref_vals, rtol=0, atol=0)
+
+
+def _planted_logits(V, K, M):
+    """the whole vocabulary's fp32 logits (oracle) with ties planted across slice boundaries for
+    4 ranks: activation row 0 has its maximum at rows 1 and 2 (ranks 0 and 1), row 1 at rows 3 and
+    4 (ranks 1 and 2)"""
+    from oracle.oracle import Oracle
+    w = synth.gen_weights(synth.TYPE_Q6_K, V, K, seed=63)
+    O = Oracle()
+    full = O.gemm(synth.TYPE_Q6_K, w, K, O.quantize_q8k(synth.gen_activations(M, K, seed=64)))
+    full[0, 1] = full[0, 2] = 1e9
+    full[1, 3] = full[1, 4] = 1e9
+    return full
+
+
+def _rank_main4(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        V, K, M = 5, 256, 3
+        first, n = shard.vocab_slice(rank, world, V)
+        if n == 0:  # an empty slice contributes (-inf, row -1) for every activation row
+            vals = torch.full((M,), float("-inf"))
+            rows = torch.full((M,), -1, dtype=torch.int64)
+        else:
+            logits = _planted_logits(V, K, M)[:, first:first + n]
+            i = logits.argmax(axis=1)
+            vals = torch.from_numpy(logits[np.arange(M), i].astype(np.float32))
+            rows = torch.from_numpy((i + first).astype(np.int64))
+        r, v = shard.gather_argmax_torch(vals, rows)
+        q.put((rank, n, r.tolist(), v.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_lm_head_gloo_4_ranks_empty_slice():
+    """4 ranks over a 5-row vocabulary (slices of 2, 2, 1 and 0 rows): ties across two slice
+    boundaries go to the smaller row and the empty slice never wins"""
+    import torch.multiprocessing as mp
+    world = 4
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main4, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    got = [q.get(timeout=10) for _ in range(world)]
+    assert sorted(n for _, n, _, _ in got) == [0, 1, 2, 2]
+    full = _planted_logits(5, 256, 3)
+    ref_rows = full.argmax(axis=1).tolist()
+    assert ref_rows[:2] == [1, 3]
+    ref_vals = full[np.arange(3), full.argmax(axis=1)].tolist()
+    for _, _, r, v in got:
+        assert r == ref_rows and v == ref_vals
