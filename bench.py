@@ -1,18 +1,23 @@
 """Benchmark of the B200 K-quant matmul path (one JSON line on rank 0).
 
-Default workload: BASELINE config 0 -- Q4_K x Q8_K GEMV, M=1, N=9728 rows, K=2560 (the FFN gate
+Default workload: benchmark config 0 -- Q4_K x Q8_K GEMV, M=1, N=9728 rows, K=2560 (the FFN gate
 shape of a 4B model), synthetic seeded GGUF blocks.  One step = one dispatch: the fp16
 activation is quantized to Q8_K inside the kernel and the 9728 fp32 outputs are written.
 
   value  : weight GB/s over all ranks with inputs resident in HBM (kq_gemm_multi_async, steps
-           captured in a CUDA graph, 24 rotating weight copies = 336 MB > 2x L2 so every step
-           streams its weights from HBM)
+           captured in a CUDA graph, rotating weight copies holding more than 2.6x the 126 MB L2
+           so every step streams its weights from HBM)
   e2e    : the same metric through the reference-facing C ABI with host buffers
-           (kq_sdot_gemm_multi_dispatch: pinned fp16 input copied in, fp32 result copied out,
-           one blocking call per step)
-  roofline, cpu_baseline, clocks, gpu_launches: see DESIGN.md
+           (kq_sdot_gemm_multi_dispatch: pinned fp16 input copied in, fp32 result written by
+           the kernel into pinned host memory, one blocking call per step)
+  roofline: algorithmic bytes per launch (weights + Q8_K activation + fp32 outputs) over the
+           CUDA-event launch time, against the measured HBM copy bandwidth
+  cpu_baseline: the reference's own dispatch on its thread pool (or the C restatement where the
+           reference was not built), timed on this host's cores for a bounded sample
+  clocks : SM clock and throttle reasons sampled by nvidia-smi during the timed region
+  gpu_launches: kernels of this library launched inside the timed region
 
---config lm_head runs BASELINE config 1 (Q6_K LM head, N=151936, K=2560) with vocab rows
+--config lm_head runs config 1 (Q6_K LM head, N=151936, K=2560) with vocab rows
 sharded over the ranks and the logit slices all-gathered with NCCL.
 --impl reference times the reference engine's own CPU path (oracle/_ref, built from its
 sources) on this host on the same workload.
@@ -291,7 +296,7 @@ def run_ours(args, rank, world, local_rank):
     ms_per_step = dt / steps * 1e3
 
     # roofline of the GEMV kernel on this rank: algorithmic bytes per launch / launch duration
-    act_bytes = (K // 256) * 292            # Q8_K activation (SURVEY: 2,920 B at K=2560)
+    act_bytes = (K // 256) * 292            # Q8_K activation: 292 B per 256 values (2,920 B at K=2560)
     out_bytes = rows_local * 4
     algo = wbytes + act_bytes + out_bytes
     avg_launch_s = dt_local / (steps * launches_per_step)
@@ -337,7 +342,7 @@ def run_ours(args, rank, world, local_rank):
             "metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
             "warmup": max(3, args.warmup), "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
             "scaling": "weak" if args.config == "gemv" else "strong", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (seeded GGUF blocks per BASELINE distributions; activations N(0,1) -> fp16)",
+            "data": "synthetic (seeded GGUF blocks per the benchmark configs' distributions; activations N(0,1) -> fp16)",
             "config": {"workload": ("config0: Q4_K x Q8_K GEMV M=1 N=9728 K=2560" if args.config == "gemv"
                                     else "config1: Q6_K LM head M=1 N=151936 K=2560, vocab rows sharded, "
                                          "NCCL all-gather of fp32 logit slices"),
@@ -375,7 +380,7 @@ HIDDEN, FFN_DIM, Q_DIM, KV_DIM, VOCAB = 2560, 9728, 4096, 1024, 151936
 
 
 def stack_layout(kind):
-    """(name, type, rows, K) of one layer: SURVEY/BASELINE config 3 (Q4_K_M) or config 4 (Q5_K/Q8_0)."""
+    """(name, type, rows, K) of one layer: config 3 (Q4_K_M prefill stack) or config 4 (Q5_K/Q8_0 decode stack)."""
     from npu880_mtk_npu_llm_runtime_b200 import synth as sy
     if kind == "prefill":
         a, b = sy.TYPE_Q4_K, sy.TYPE_Q6_K
@@ -503,7 +508,7 @@ def run_stack(args, rank, world, local_rank):
             "metric": METRIC_FFN, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
             "warmup": max(3, args.warmup), "ms_per_step": round(dt / steps * 1e3, 6), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (seeded GGUF blocks per BASELINE distributions; activations N(0,1) -> fp16)",
+            "data": "synthetic (seeded GGUF blocks per the benchmark configs' distributions; activations N(0,1) -> fp16)",
             "config": {"workload": f"config2: tree-verify FFN block M={M}, hidden 2560, intermediate 9728",
                        "m": M, "weight_bytes_per_step": wbytes, "tops": round(ops * steps / dt / 1e12, 3),
                        "l2": f"{n_sets} rotating weight sets ({n_sets * wbytes / 2**20:.0f} MiB > 2x126 MB L2)",
@@ -572,7 +577,7 @@ def run_stack(args, rank, world, local_rank):
             "metric": METRIC_PREFILL, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": steps,
             "warmup": max(3, args.warmup), "ms_per_step": round(dt / steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (seeded GGUF blocks per BASELINE distributions; activations N(0,1) -> Q8_K)",
+            "data": "synthetic (seeded GGUF blocks per the benchmark configs' distributions; activations N(0,1) -> Q8_K)",
             "config": {"workload": f"config3: prefill GEMMs of a {L}-layer Q4_K_M stack (q/k/o/gate/up Q4_K, v/down Q6_K) at M={M}",
                        "m": M, "layers": L, "ops_per_step": ops,
                        "l2": f"inputs larger than L2: {L} layers x {sum(h.nbytes for h in host.values()) / 2**20:.0f} MiB of weights",
@@ -653,7 +658,7 @@ def run_stack(args, rank, world, local_rank):
                 "metric": METRIC_DECODE, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
                 "warmup": max(3, args.warmup), "ms_per_step": round(dt / steps * 1e3, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "int8",
-                "data": "synthetic (seeded GGUF blocks per BASELINE distributions; activations N(0,1))",
+                "data": "synthetic (seeded GGUF blocks per the benchmark configs' distributions; activations N(0,1))",
                 "config": {"workload": f"config4: {SEQ} sequences x 1 token, {L}-layer stack (q/o/gate/up Q5_K, "
                                        f"k/v/down Q8_0) + Q6_K LM head {VOCAB}x{HIDDEN} vocab-sharded",
                            "rows_per_rank": Mr, "layers": L, "weight_bytes_per_step_per_rank": wbytes,
@@ -704,7 +709,7 @@ def run_reference(args, rank, world):
         "value": round(v, 4), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 3),
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
         "scaling": "weak" if args.config == "gemv" else "strong", "vs_baseline": None, "dtype": "int8",
-        "data": "synthetic (seeded GGUF blocks per BASELINE distributions)",
+        "data": "synthetic (seeded GGUF blocks per the benchmark configs' distributions)",
         "config": {"workload": "config0: Q4_K x Q8_K GEMV M=1 N=9728 K=2560" if args.config == "gemv"
                    else "config1: Q6_K LM head M=1 N=151936 K=2560", "m": 1, "n": n_rows, "k": 2560},
         "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample},

@@ -210,7 +210,7 @@ def test_dispatch_strides_row_ranges_and_mtiles(kqctx, oracle):
 
 
 def test_config0_shape_bitexact(kqctx, oracle):
-    """BASELINE config 0 at full size: Q4_K x Q8_K GEMV, M=1, N=9728, K=2560"""
+    """Benchmark config 0 at full size: Q4_K x Q8_K GEMV, M=1, N=9728, K=2560"""
     N, K = 9728, 2560
     w = synth.gen_weights(kq.TYPE_Q4_K, N, K, seed=1234)
     x = synth.gen_activations(1, K, seed=1235)

@@ -82,7 +82,7 @@ def test_ffn_golden(kqctx):
 
 @pytest.mark.parametrize("M", [1, 4, 8, 16])
 def test_ffn_tree_verify_shape(kqctx, oracle, M):
-    """BASELINE config 2 FFN block (hidden 2560, intermediate 9728): gate/up Q4_K, down Q6_K"""
+    """Benchmark config 2 FFN block (hidden 2560, intermediate 9728): gate/up Q4_K, down Q6_K"""
     hidden, ffn = 2560, 9728
     wg = synth.gen_weights(kq.TYPE_Q4_K, ffn, hidden, 201)
     wu = synth.gen_weights(kq.TYPE_Q4_K, ffn, hidden, 202)
@@ -197,7 +197,7 @@ def test_lm_head_many_tokens(kqctx, oracle, M, want_logits, V):
 
 
 def test_lm_head_config1_shape(kqctx, oracle):
-    """BASELINE config 1 at full size: Q6_K LM head, N=151936, K=2560 (logits bit-exact)"""
+    """Benchmark config 1 at full size: Q6_K LM head, N=151936, K=2560 (logits bit-exact)"""
     import torch
     V, K = 151936, 2560
     w = synth.gen_weights(kq.TYPE_Q6_K, V, K, 4321)
