@@ -274,3 +274,34 @@ def test_bounded_wait_times_out_and_context_survives(kqctx, oracle):
     W.free()
     ref = oracle.epilogue_f16(oracle.gemm(kq.TYPE_Q4_K, w, K, oracle.quantize_q8k(x)))
     assert np.array_equal(bits(d), bits(ref))
+
+
+@pytest.mark.parametrize("gtype", TYPES, ids=lambda t: synth.TYPE_NAMES[t])
+@pytest.mark.parametrize("M", [3, 16])
+def test_edge_activations_fp16_input(kqctx, oracle, gtype, M):
+    """fp16 inputs quantized inside the kernels (GEMV at 3 tokens, tensor cores at 16): a row with
+    an all-zero super-block (d = 0) and a row holding +-65504 and fp16 subnormals (clamp at +-127,
+    tiny products) give the oracle's results -- bit for bit, except Q8_0 rows that the tensor-core
+    path sums one 256-value tile at a time (1e-5 of the output scale)"""
+    import torch
+    from test_gpu_split import check_q80_tolerance
+    rows, K = 100, 2560
+    w = synth.gen_weights(gtype, rows, K, seed=300 + gtype)
+    x = synth.gen_activations(M, K, seed=301 + M)
+    x[1, :256] = 0
+    x[2, ::7] = np.float16(65504.0)
+    x[2, 3::11] = np.float16(-65504.0)
+    x[2, 5::13] = np.float16(6e-8)
+    W = kqctx.upload(w, gtype, rows, K)
+    out = torch.full((M, rows), float("nan"), dtype=torch.float32, device="cuda")
+    try:
+        kqctx.gemm_multi_async(to_dev(x.view(np.uint16)), M, K, [dict(w=W, dst_f32=out)])
+        kqctx.synchronize()
+    finally:
+        W.free()
+    got = out.cpu().numpy()
+    ref = oracle.gemm(gtype, w, K, oracle.act_for(gtype, x))
+    if gtype == kq.TYPE_Q8_0 and M > 8:
+        check_q80_tolerance(got, ref)
+    else:
+        assert np.array_equal(bits(got), bits(ref)), f"max |diff| {np.abs(got - ref).max()}"
