@@ -44,6 +44,7 @@ sys.path.insert(0, ROOT)
 METRIC_GEMV = "Q4_K GEMV weight GB/s (% B200 HBM peak)"
 METRIC_LM = "Q6_K LM-head GEMV weight GB/s (vocab-sharded, all-gathered)"
 L2_BYTES = 126 * 1024 * 1024
+DATA_DESC = "synthetic (seeded GGUF blocks per the benchmark configs' distributions; activations N(0,1) -> fp16)"
 STEPS_DEFAULT = 300000
 
 
@@ -137,15 +138,30 @@ def physical_gpu_index(local_rank):
 
 # ---------------------------------------------------------------------------- CPU baselines
 
-def cpu_reference_gemv(n_rows, k, gtype, seconds=10.0, max_steps=None, warmup=1):
+def cpu_reference_gemv(n_rows, k, gtype, seconds=10.0, max_steps=None, warmup=1, single_thread=True):
     """The reference engine's own CPU path (sdot_gemm_multi_dispatch on its 4-thread pinned pool,
-    turbo mode, scalar kernels on x86) over full GEMVs of the workload.
-    Returns (weight GB/s, steps, seconds per step, kind, cores, sample description)."""
+    turbo mode, scalar kernels on x86) over full GEMVs of the workload, and the same dispatch on one
+    thread (its job function run by the calling thread alone).
+    Returns a dict: value (weight GB/s of the pool), steps, seconds_per_step, kind, cores, sample,
+    single_thread ({value, seconds_per_step, steps} or None)."""
     from npu880_mtk_npu_llm_runtime_b200 import synth
     from oracle.oracle import Reference, reference_available, Oracle
     w = synth.gen_weights(gtype, n_rows, k, seed=1234)
     x = synth.gen_activations(1, k, seed=1235)
     wbytes = w.nbytes
+
+    def timed(fn, budget, cap):
+        t0 = time.perf_counter()
+        fn()
+        t1 = time.perf_counter() - t0
+        n = max(2, int(budget / max(t1, 1e-6)))
+        if cap:
+            n = min(n, cap)
+        t0 = time.perf_counter()
+        for _ in range(n):
+            fn()
+        return n, (time.perf_counter() - t0) / n
+
     if reference_available():
         R = Reference()
         R.init_pool()
@@ -153,216 +169,330 @@ def cpu_reference_gemv(n_rows, k, gtype, seconds=10.0, max_steps=None, warmup=1)
         R.turbo(True)
         for _ in range(warmup):
             R.dispatch(x, [(gtype, w, dst, None)])
-        t0 = time.perf_counter()
-        R.dispatch(x, [(gtype, w, dst, None)])
-        t1 = time.perf_counter() - t0
-        steps = max(2, int(seconds / max(t1, 1e-6)))
-        if max_steps:
-            steps = min(steps, max_steps)
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            R.dispatch(x, [(gtype, w, dst, None)])
-        dt = time.perf_counter() - t0
+        steps, sec = timed(lambda: R.dispatch(x, [(gtype, w, dst, None)]), seconds, max_steps)
         R.turbo(False)
-        return (wbytes * steps / dt / 1e9, steps, dt / steps, "reference", R.pool_threads,
-                f"{steps} full GEMVs (N={n_rows}, K={k}) through the reference's sdot_gemm_multi_dispatch "
-                f"on its {R.pool_threads}-thread pool (scalar x86 kernels, turbo mode)")
+        one = None
+        if single_thread:
+            n1, s1 = timed(lambda: R.dispatch_1thread(x, [(gtype, w, dst, None)]), seconds / 3, max_steps)
+            one = {"value": round(wbytes / s1 / 1e9, 4), "unit": "GB/s", "cores": 1, "steps": n1,
+                   "seconds_per_step": s1,
+                   "sample": f"{n1} full GEMVs through the same dispatch with its job function "
+                             f"(exec_sdot_job_work_stealing) run on one thread"}
+        return {"value": wbytes / sec / 1e9, "steps": steps, "seconds_per_step": sec, "kind": "reference",
+                "cores": R.pool_threads,
+                "sample": f"{steps} full GEMVs (N={n_rows}, K={k}) through the reference's sdot_gemm_multi_dispatch "
+                          f"on its {R.pool_threads}-thread pool (scalar x86 kernels, turbo mode)",
+                "single_thread": one}
     O = Oracle()
     act = O.quantize_q8k(x)
-    t0 = time.perf_counter()
-    O.gemm(gtype, w, k, act)
-    t1 = time.perf_counter() - t0
-    steps = max(1, int(seconds / max(t1, 1e-6)))
-    if max_steps:
-        steps = min(steps, max_steps)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        O.gemm(gtype, w, k, act)
-    dt = time.perf_counter() - t0
-    return (wbytes * steps / dt / 1e9, steps, dt / steps, "port", 1,
-            f"{steps} full GEMVs (N={n_rows}, K={k}) through the oracle's scalar C restatement, 1 thread")
+    steps, sec = timed(lambda: O.gemm(gtype, w, k, act), seconds, max_steps)
+    return {"value": wbytes / sec / 1e9, "steps": steps, "seconds_per_step": sec, "kind": "port", "cores": 1,
+            "sample": f"{steps} full GEMVs (N={n_rows}, K={k}) through the oracle's scalar C restatement, 1 thread",
+            "single_thread": None}
 
 
-# ---------------------------------------------------------------------------- our arm
+# ---------------------------------------------------------------------------- timing helpers
+
+GRAPH_MAX = 1000  # launches per captured graph
+
+
+def graph_timed(stream, step, steps, warmup, world, per_step_launches=1):
+    """Time `steps` calls of step(i) on the device, hot: one eager call configures the kernels,
+    then a CUDA graph holds the `warmup` untimed steps, a timing event, the `steps` timed steps and
+    a second event, so the timed steps start right after warm-up steps with the GPU busy (no idle
+    gap, no graph boundary inside the timed region).  Beyond GRAPH_MAX steps the timed steps are
+    replayed from graphs of at most GRAPH_MAX steps.  Returns seconds (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    with torch.cuda.stream(stream):
+        step(0)
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True, external=True)
+    ev1 = torch.cuda.Event(enable_timing=True, external=True)
+    graphs = []
+    try:
+        if steps <= GRAPH_MAX:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(warmup):
+                    step(i)
+                ev0.record()
+                for i in range(steps):
+                    step(warmup + i)
+                ev1.record()
+            graphs.append(g)
+            plan = [g]
+        else:
+            gw = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gw, stream=stream):
+                for i in range(warmup):
+                    step(i)
+                ev0.record()
+            graphs.append(gw)
+            full, rem = divmod(steps, GRAPH_MAX)
+            gt = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gt, stream=stream):
+                for i in range(GRAPH_MAX):
+                    step(warmup + i)
+            graphs.append(gt)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for i in range(rem):
+                    step(warmup + i)
+                ev1.record()
+            graphs.append(gr)
+            plan = [gw] + [gt] * full + [gr]
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for g in plan:
+                g.replay()
+        ev1.synchronize()
+        dt = ev0.elapsed_time(ev1) / 1e3
+    finally:
+        torch.cuda.synchronize()
+        del graphs[:]
+    t = torch.tensor([dt], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def e2e_timed(stream, call, steps, warmup, world):
+    """Blocking host-buffer calls: `warmup` untimed calls right before `steps` timed ones, CUDA
+    events on the context stream around the timed calls.  Returns seconds (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    for i in range(warmup):
+        call(i)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        call(warmup + i)
+    e1.record(stream)
+    e1.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------- our arm: configs 0 and 1
+
+def gemv_config(world, n_copies=None, wbytes=None):
+    """The `config` record both arms print for config 0 (the reference arm without run facts)."""
+    return {"workload": "config0: Q4_K x Q8_K GEMV M=1 N=9728 K=2560", "m": 1, "n": 9728, "k": 2560,
+            "weight_bytes_per_step_per_rank": 14008320,
+            "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2: rotating weight copies of > 2x126 MB L2 per rank",
+            "timing": "CUDA graph: warm-up steps, event, timed steps, event (one replay); CUDA events"}
+
+
+def lm_config(world):
+    return {"workload": "config1: Q6_K LM head M=1 N=151936 K=2560, vocab rows sharded, "
+                        "NCCL all-gather of fp32 logit slices",
+            "m": 1, "n": 151936, "k": 2560, "weight_bytes_per_step_per_rank": None,
+            "parallelism": f"vocab-shard x{world}",
+            "l2": "inputs larger than L2: rotating weight copies of > 2x126 MB L2 per rank",
+            "timing": "CUDA graph of (GEMV + NCCL all-gather) steps: warm-up steps, event, timed steps, event; "
+                      "max over ranks"}
+
+
+def lm_head_sharded(ctx, args, rank, world, dev, stream, steps, warmup, want_argmax=True):
+    """Config 1 on `world` ranks: each rank streams its contiguous slice of the 151,936 Q6_K vocab
+    rows (GEMV, fp32 logits written straight into its chunk of the gather buffer), then one NCCL
+    all-gather of the logit slices (in place); GEMV + all-gather captured in CUDA graphs.  With
+    want_argmax also the argmax-only exchange: each rank's fused GEMV argmax, an all-gather of one
+    (value, row) pair per rank, merged on the device (largest value, first row on ties)."""
+    import torch
+    import torch.distributed as dist
+    import npu880_mtk_npu_llm_runtime_b200 as kq
+    from npu880_mtk_npu_llm_runtime_b200 import shard, synth
+    V, K = 151936, 2560
+    row0, rows = shard.vocab_slice(rank, world, V)
+    chunk = (V + world - 1) // world
+    w_host = synth.gen_weights(kq.TYPE_Q6_K, V, K, seed=4321)[row0:row0 + rows]
+    x_host = synth.gen_activations(1, K, seed=4322)
+    wbytes = w_host.nbytes
+    raw = torch.from_numpy(np.ascontiguousarray(w_host)).to(dev)
+    n_copies = max(2, math.ceil(2.6 * L2_BYTES / max(1, wbytes)))
+    Ws = [ctx.upload_device(raw, kq.TYPE_Q6_K, rows, K) for _ in range(n_copies)]
+    del raw
+    x = torch.from_numpy(x_host.view(np.uint16).copy()).to(dev)
+    gather = torch.zeros((world * chunk,), dtype=torch.float32, device=dev)
+    mine = gather[rank * chunk:(rank + 1) * chunk]
+    tasks = [ctx.make_tasks([dict(w=Ws[i], dst_f32=mine[:rows].view(1, rows), dst_f32_stride=rows)])
+             for i in range(n_copies)]
+
+    def step(i):
+        ctx.gemm_multi_async(x, 1, K, tasks[i % n_copies])
+        if world > 1:
+            dist.all_gather_into_tensor(gather, mine)
+
+    dt = graph_timed(stream, step, steps, warmup, world)
+    total = torch.tensor([float(wbytes)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.SUM)
+    value = float(total.item()) * steps / dt / 1e9
+    rec = {"value": round(value, 1), "unit": "GB/s", "ms_per_step": round(dt / steps * 1e3, 6), "steps": steps,
+           "warmup": warmup, "n_gpus": world, "rows_per_rank": chunk, "weight_bytes_per_rank": wbytes,
+           "gather_bytes_per_rank": chunk * 4}
+    if want_argmax:
+        toks = torch.zeros((1,), dtype=torch.int32, device=dev)
+        vals = torch.zeros((1,), dtype=torch.float32, device=dev)
+        pair = torch.zeros((2,), dtype=torch.float32, device=dev)
+        pairs = torch.zeros((world, 2), dtype=torch.float32, device=dev)
+        best = torch.zeros((2,), dtype=torch.float32, device=dev)
+
+        def step_a(i):
+            ctx.lm_head_argmax_async(Ws[i % n_copies], x, 1, None, None, toks, vals)
+            pair[0:1].copy_(vals)
+            pair[1:2].copy_((toks + row0).float())   # global row (< 2^24: exact in fp32)
+            if world > 1:
+                dist.all_gather_into_tensor(pairs.view(-1), pair)
+            else:
+                pairs[0].copy_(pair)
+            r = torch.argmax(pairs[:, 0]).view(1)        # first rank with the maximum = first row
+            best.copy_(torch.index_select(pairs, 0, r).view(2))
+
+        dta = graph_timed(stream, step_a, steps, warmup, world)
+        rec["argmax_exchange"] = {"value": round(float(total.item()) * steps / dta / 1e9, 1), "unit": "GB/s",
+                                  "ms_per_step": round(dta / steps * 1e3, 6), "exchange_bytes_per_rank": 8}
+    for W in Ws:
+        W.free()
+    return rec
+
 
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
     import npu880_mtk_npu_llm_runtime_b200 as kq
-    from npu880_mtk_npu_llm_runtime_b200 import build as kqbuild, shard, synth
+    from npu880_mtk_npu_llm_runtime_b200 import build as kqbuild, synth
 
     kqbuild.build()
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     ctx = kq.Context(local_rank)
     stream = torch.cuda.Stream(device=dev)
     ctx.set_stream(stream.cuda_stream)
+    warmup = max(3, args.warmup)
+    steps = args.steps
+    peak, peak_kind = measured_peaks()
+    clk = ClockSampler(physical_gpu_index(local_rank))
+    clk.__enter__()  # sampling runs from before the warm-up to after the timed steps
 
-    if args.config == "gemv":
-        gtype, N, K = kq.TYPE_Q4_K, 9728, 2560
-        rows_local, row0 = N, 0
-        metric = METRIC_GEMV
-    else:
-        gtype, N, K = kq.TYPE_Q6_K, 151936, 2560
-        row0, rows_local = shard.vocab_slice(rank, world, N)
-        metric = METRIC_LM
-    w_host = synth.gen_weights(gtype, N, K, seed=1234)[row0:row0 + rows_local]
+    if args.config == "lm_head":
+        rec = lm_head_sharded(ctx, args, rank, world, dev, stream, steps, warmup)
+        clk.__exit__()
+        clocks = clk.summary()
+        result = None
+        if rank == 0:
+            cfg = lm_config(world)
+            cfg["weight_bytes_per_step_per_rank"] = rec["weight_bytes_per_rank"]
+            avg_s = rec["ms_per_step"] / 1e3
+            algo = rec["weight_bytes_per_rank"] + rec["rows_per_rank"] * 4 + 2920
+            result = {
+                "metric": METRIC_LM, "value": rec["value"], "unit": "GB/s", "n_gpus": world, "steps": steps,
+                "warmup": warmup, "ms_per_step": rec["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "int8", "data": DATA_DESC, "config": cfg,
+                "roofline": {"bound": "hbm", "achieved": round(algo / avg_s / 1e9, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(algo / avg_s / 1e9 / peak, 4), "peak_source": peak_kind,
+                             "traffic": ncu_traffic("gemv_q6k_lmhead"),
+                             "note": "step time includes the all-gather at N > 1"},
+                "argmax_exchange": rec.get("argmax_exchange"), "cpu_baseline": None, "clocks": clocks,
+                "e2e": None, "gpu_launches": steps * (1 + (world > 1)),
+            }
+        ctx.close()
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return result
+
+    # ---------------- config 0: Q4_K GEMV, replicated on every rank
+    gtype, N, K = kq.TYPE_Q4_K, 9728, 2560
+    w_host = synth.gen_weights(gtype, N, K, seed=1234)
     x_host = synth.gen_activations(1, K, seed=1235)
-    wbytes = w_host.nbytes                      # GGUF bytes this rank streams per step
+    wbytes = w_host.nbytes
     raw = torch.from_numpy(np.ascontiguousarray(w_host)).to(dev)
     n_copies = max(2, math.ceil(2.6 * L2_BYTES / max(1, wbytes)))
-    Ws = [ctx.upload_device(raw, gtype, rows_local, K) for _ in range(n_copies)]
+    Ws = [ctx.upload_device(raw, gtype, N, K) for _ in range(n_copies)]
     del raw
     x = torch.from_numpy(x_host.view(np.uint16).copy()).to(dev)
-    out = torch.zeros((n_copies, rows_local), dtype=torch.float32, device=dev)
-    full = torch.zeros((N if args.config == "lm_head" else rows_local,), dtype=torch.float32, device=dev)
-    tasks = [ctx.make_tasks([dict(w=Ws[i], dst_f32=out[i:i + 1], dst_f32_stride=rows_local)])
-             for i in range(n_copies)]
+    out = torch.zeros((n_copies, N), dtype=torch.float32, device=dev)
+    tasks = [ctx.make_tasks([dict(w=Ws[i], dst_f32=out[i:i + 1], dst_f32_stride=N)]) for i in range(n_copies)]
 
     def step(i):
         ctx.gemm_multi_async(x, 1, K, tasks[i % n_copies])
 
-    gather_chunks = None
-    if args.config == "lm_head" and world > 1:
-        # every rank owns an equal slice (the last one padded) so all_gather_into_tensor applies
-        chunk = (N + world - 1) // world
-        gather_chunks = torch.zeros((world * chunk,), dtype=torch.float32, device=dev)
-        slice_buf = torch.zeros((chunk,), dtype=torch.float32, device=dev)
-
-    def step_with_gather(i):
-        step(i)
-        if gather_chunks is not None:
-            slice_buf[:rows_local].copy_(out[i % n_copies])
-            dist.all_gather_into_tensor(gather_chunks, slice_buf)
-
-    # warm-up (eager), also configures the kernels before capture
-    with torch.cuda.stream(stream):
-        for i in range(max(3, args.warmup)):
-            step_with_gather(i)
-    ctx.synchronize()
-    torch.cuda.synchronize(dev)
-
-    steps = args.steps
-    G = min(steps, 1000 if args.config == "gemv" else 50)
-    graph = None
-    if gather_chunks is None:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            ctx.set_stream(torch.cuda.current_stream(dev).cuda_stream)
-            for i in range(G):
-                step(i)
-        ctx.set_stream(stream.cuda_stream)
-        reps = max(1, math.ceil(steps / G))
-        steps = reps * G
-        with torch.cuda.stream(stream):
-            graph.replay()
-        torch.cuda.synchronize(dev)
-    launches_per_step = 1
-
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(physical_gpu_index(local_rank)) as clk:
-        ev0.record(stream)
-        with torch.cuda.stream(stream):
-            if graph is not None:
-                for _ in range(reps):
-                    graph.replay()
-            else:
-                for i in range(steps):
-                    step_with_gather(i)
-        ev1.record(stream)
-        ev1.synchronize()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    dt_local = ev0.elapsed_time(ev1) / 1e3
-    t = torch.tensor([dt_local], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dt = float(t.item())
-    clocks = clk.summary()
-
+    dt = graph_timed(stream, step, steps, warmup, world)
+    dt_local = dt  # max over ranks already; the roofline uses the same launch time
     total_wbytes = torch.tensor([float(wbytes)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(total_wbytes, op=dist.ReduceOp.SUM)
     value = float(total_wbytes.item()) * steps / dt / 1e9
     ms_per_step = dt / steps * 1e3
 
-    # roofline of the GEMV kernel on this rank: algorithmic bytes per launch / launch duration
+    # roofline of the GEMV kernel: algorithmic bytes per launch / launch duration
     act_bytes = (K // 256) * 292            # Q8_K activation: 292 B per 256 values (2,920 B at K=2560)
-    out_bytes = rows_local * 4
-    algo = wbytes + act_bytes + out_bytes
-    avg_launch_s = dt_local / (steps * launches_per_step)
-    achieved = algo / avg_launch_s / 1e9
-    peak, peak_kind = measured_peaks()
+    algo = wbytes + act_bytes + N * 4
+    achieved = algo / (dt_local / steps) / 1e9
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-            "traffic": ncu_traffic("gemv_q4k_cfg0" if args.config == "gemv" else "gemv_q6k_lmhead"),
+            "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": ncu_traffic("gemv_q4k_cfg0"),
             "algorithmic_bytes_per_launch": algo}
 
-    # e2e through the reference-facing C ABI with host buffers (rank-local, blocking calls)
+    # e2e through the reference-facing C ABI with host buffers (blocking calls)
     e2e_steps = min(steps, args.e2e_steps)
     xp = torch.from_numpy(x_host.view(np.uint16).copy()).pin_memory()
-    op = torch.zeros((1, rows_local), dtype=torch.float32).pin_memory()
+    op = torch.zeros((1, N), dtype=torch.float32).pin_memory()
     xp_np = xp.numpy().view(np.float16)
     op_np = op.numpy()
     htasks = [ctx.make_host_tasks([dict(w=Ws[i], dst_f32=op_np)]) for i in range(n_copies)]
-    for i in range(3):
-        ctx.sdot_gemm_multi_dispatch(xp_np, htasks[i % n_copies])
-    if world > 1:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(e2e_steps):
-        ctx.sdot_gemm_multi_dispatch(xp_np, htasks[i % n_copies])
-    e1.record(stream)
-    e1.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = float(total_wbytes.item()) * e2e_steps / float(te.item()) / 1e9
+    te = e2e_timed(stream, lambda i: ctx.sdot_gemm_multi_dispatch(xp_np, htasks[i % n_copies]), e2e_steps,
+                   warmup, world)
+    e2e_value = float(total_wbytes.item()) * e2e_steps / te / 1e9
+    for W in Ws:
+        W.free()
+
+    # the sharded LM head (config 1) at this rank count, as a nested record
+    lm = None
+    if not args.no_lm_head:
+        lm = lm_head_sharded(ctx, args, rank, world, dev, stream, min(steps, 2000), warmup)
+    clk.__exit__()
+    clocks = clk.summary()
 
     result = None
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            v, st, sec, kind, cores, sample = cpu_reference_gemv(N if args.config == "gemv" else 24832, K, gtype,
-                                                               seconds=args.cpu_seconds)
-            cpu = {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample,
-                   "seconds_per_step": sec}
+            c = cpu_reference_gemv(N, K, gtype, seconds=args.cpu_seconds)
+            cpu = {"value": round(c["value"], 4), "unit": "GB/s", "cores": c["cores"], "kind": c["kind"],
+                   "sample": c["sample"], "seconds_per_step": c["seconds_per_step"],
+                   "single_thread": c["single_thread"]}
+        cfg = gemv_config(world)
+        cfg["weight_bytes_per_step_per_rank"] = wbytes
+        cfg["l2"] = f"inputs larger than L2: {n_copies} rotating weight copies ({n_copies * wbytes / 2**20:.0f} MiB > 2x126 MB L2)"
+        if lm is not None:
+            cfg["lm_head_sharded"] = dict(lm, workload=lm_config(world)["workload"],
+                                          parallelism=f"vocab-shard x{world}")
         result = {
-            "metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
-            "warmup": max(3, args.warmup), "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
-            "scaling": "weak" if args.config == "gemv" else "strong", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (seeded GGUF blocks per the benchmark configs' distributions; activations N(0,1) -> fp16)",
-            "config": {"workload": ("config0: Q4_K x Q8_K GEMV M=1 N=9728 K=2560" if args.config == "gemv"
-                                    else "config1: Q6_K LM head M=1 N=151936 K=2560, vocab rows sharded, "
-                                         "NCCL all-gather of fp32 logit slices"),
-                       "m": 1, "n": N, "k": K, "weight_bytes_per_step_per_rank": wbytes,
-                       "l2": f"inputs larger than L2: {n_copies} rotating weight copies "
-                             f"({n_copies * wbytes / 2**20:.0f} MiB > 2x126 MB L2)",
-                       "parallelism": (f"replicas x{world}" if args.config == "gemv" else f"vocab-shard x{world}"),
-                       "timing": "CUDA graph of back-to-back dispatches (PDL), CUDA events on the launch stream"
-                                 if graph is not None else "eager launches + NCCL all-gather per step"},
+            "metric": METRIC_GEMV, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": DATA_DESC, "config": cfg,
             "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "steps": e2e_steps,
-                    "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(rows_local * 4),
+                    "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(N * 4),
                     "api": "kq_sdot_gemm_multi_dispatch (host buffers, blocking)",
-                    "scope": ("each rank's blocking call over its vocabulary slice, max over ranks; "
-                              "the logit all-gather is not in e2e" if gather_chunks is not None
-                              else "one blocking call per step")},
-            "gpu_launches": steps * launches_per_step,
+                    "scope": "one blocking call per step; max over ranks"},
+            "gpu_launches": steps,
         }
-    for W in Ws:
-        W.free()
     ctx.close()
     if world > 1:
         dist.barrier()
@@ -700,20 +830,23 @@ def run_reference(args, rank, world):
     from npu880_mtk_npu_llm_runtime_b200 import synth
     gtype = synth.TYPE_Q4_K if args.config == "gemv" else synth.TYPE_Q6_K
     n_rows = 9728 if args.config == "gemv" else 151936
-    # each step is one full GEMV on the reference pool; the step count is capped so the whole
-    # arm ends within a few minutes
-    v, steps, sec, kind, cores, sample = cpu_reference_gemv(n_rows, 2560, gtype, seconds=args.ref_seconds,
-                                                           max_steps=args.steps, warmup=min(args.warmup, 3))
+    warmup = max(3, args.warmup)
+    # each step is one full GEMV on the reference pool; the step count is capped by time so the
+    # whole arm ends within a few minutes
+    c = cpu_reference_gemv(n_rows, 2560, gtype, seconds=args.ref_seconds, max_steps=args.steps, warmup=warmup)
+    cfg = gemv_config(world) if args.config == "gemv" else lm_config(world)
+    if args.config == "lm_head":
+        cfg["weight_bytes_per_step_per_rank"] = n_rows * 2100
+    v = round(c["value"], 4)
     return {
         "impl": "reference", "metric": METRIC_GEMV if args.config == "gemv" else METRIC_LM,
-        "value": round(v, 4), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 3),
-        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
+        "value": v, "unit": "GB/s", "n_gpus": world, "steps": c["steps"], "warmup": warmup,
+        "ms_per_step": round(c["seconds_per_step"] * 1e3, 3), "higher_is_better": True,
         "scaling": "weak" if args.config == "gemv" else "strong", "vs_baseline": None, "dtype": "int8",
-        "data": "synthetic (seeded GGUF blocks per the benchmark configs' distributions)",
-        "config": {"workload": "config0: Q4_K x Q8_K GEMV M=1 N=9728 K=2560" if args.config == "gemv"
-                   else "config1: Q6_K LM head M=1 N=151936 K=2560", "m": 1, "n": n_rows, "k": 2560},
-        "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample},
-        "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "data": DATA_DESC, "config": cfg,
+        "cpu_baseline": {"value": v, "unit": "GB/s", "cores": c["cores"], "kind": c["kind"], "sample": c["sample"],
+                         "single_thread": c["single_thread"]},
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
@@ -730,6 +863,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=30.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-lm-head", action="store_true", help="config 0 without the nested sharded LM-head record")
     args = ap.parse_args()
     rank = env_int("RANK", 0)
     world = env_int("WORLD_SIZE", 1)

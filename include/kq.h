@@ -89,7 +89,17 @@ const char *kq_last_error(const kq_ctx *ctx);
  * "gemv_split" -- GEMV launches (up to 8 activation rows) whose row groups would spread unevenly
  * over the SMs give every CTA an equal range of 16-row x 256-value tiles instead; a row group
  * shared by neighbouring CTAs is summed in block order by the last of them (1, default); 0 keeps
- * whole row groups per CTA. */
+ * whole row groups per CTA;
+ * "swiglu_exp" -- where SwiGLU takes expf(-g) from: 0 (default) a table of the host C library's
+ * expf at the 65,536 fp16 values of g, made once by kq_init -- the function the reference's
+ * scalar SwiGLU calls (ENG:4354), so the results match it bit for bit on the same host; 1 an fp64
+ * exp on the GPU rounded once to fp32 (the correctly rounded value except in rare double-rounding
+ * cases; glibc 2.39's expf is not correctly rounded at 16 fp16 inputs);
+ * "graph_released" -- a context whose calls were captured into a CUDA graph keeps its scratch
+ * buffers where the graph recorded them: a later call that would have to grow one returns
+ * KQ_ERR_INVALID_ARGUMENT instead of freeing it.  Setting 1 declares those graphs destroyed and
+ * lets scratch grow again.  (Calls made during a capture never allocate: make one eager call of
+ * the largest shape before capturing.) */
 int kq_set_option(kq_ctx *ctx, const char *name, long long value);
 
 /* compute_ggml_bytes / ggml_row_bytes (ENG:364-374, ENG:3940): bytes of one GGUF row of k
@@ -208,18 +218,29 @@ int kq_lm_head_argmax_async(kq_ctx *ctx, const kq_weight *w, const uint16_t *x_d
                             float *logits_f32_dev, uint32_t *top_toks_dev, float *top_vals_dev);
 
 /* LM-head argmax that allocates nothing.  No counterpart in the reference: an addition for
- * callers that cannot allocate device memory when they call, such as a decode loop whose memory
- * is fixed after start-up or that runs inside another runtime's allocator.  Same computation and
- * results as kq_lm_head_argmax_async (fused GEMV over all rows of w, fp16 logits to logits_dev
- * when not NULL, argmax of the fp16 logits to toks_dev / vals_dev), with no context: DEVICE
- * pointers, enqueued on `stream` (a cudaStream_t; NULL = the default stream) of the current
- * device.  Its only scratch is a static device array of KQ_NOALLOC_MAX_M argmax slots that every
- * GPU which loads the library keeps until exit; M > KQ_NOALLOC_MAX_M returns KQ_ERR_SHAPE.  The
- * first call on a device looks up that array's device address once (cudaGetSymbolAddress), so
- * make the first call on each device before any stream capture.  All calls share the array and
- * clear it on their stream at the start: calls that overlap on the GPU (different streams) race
- * and must be serialised by the caller.  Device-side wait timeouts are not reported by this
- * call. */
+ * callers that cannot allocate device memory when they call -- a decode loop whose memory is fixed
+ * after start-up, or code running inside another runtime's allocator, where a cudaMalloc would
+ * break that runtime's accounting or stall.  It computes the fused GEMV over all rows of w, fp16
+ * logits to logits_dev when not NULL, and the argmax of the fp16 logits (strict '>', first maximal
+ * row wins) to toks_dev / vals_dev, with no context: DEVICE pointers, enqueued on `stream` (a
+ * cudaStream_t; NULL = the default stream) of the current device, where w must live (another
+ * device's weight: KQ_ERR_INVALID_ARGUMENT).
+ *  - Results: for Q4_K / Q5_K / Q6_K weights the same bits as kq_lm_head_argmax_async (both are
+ *    bit-exact to the reference); for Q8_0 weights the logits agree within the Q8_0 long-row
+ *    tolerance (1e-5 of the output scale plus one fp16 ulp; the two calls may sum Q8_0 block terms
+ *    in different orders), so between nearly equal logits the argmax may differ.
+ *  - Cost: tiles of up to 8 activation rows, one pass over the weights per tile: M rows read the
+ *    weights ceil(M / 8) times (kq_lm_head_argmax_async reads them once for M > 8).
+ *  - Scratch: a static device array of KQ_NOALLOC_MAX_M argmax slots and a status word, which
+ *    every GPU that loads the library keeps until exit; M > KQ_NOALLOC_MAX_M returns KQ_ERR_SHAPE.
+ *    The first call on a device (and the first after that device's context was reset) looks up
+ *    the array's device address (cudaGetSymbolAddress), so make the first call on each device
+ *    before any stream capture.  All calls share the array and clear it on their stream at the
+ *    start: calls that overlap on the GPU (different streams) race and must be serialised by the
+ *    caller.
+ *  - A device-side wait that timed out (a kernel that stopped early) cannot be returned as a
+ *    status by an asynchronous call: every row then gets the sentinel token 0xFFFFFFFF and value
+ *    NaN instead. */
 #define KQ_NOALLOC_MAX_M 64
 int kq_lm_head_argmax_noalloc(const kq_weight *w, const uint16_t *x_dev, int M, uint16_t *logits_dev,
                               uint32_t *top_toks_dev, float *top_vals_dev, void *stream);

@@ -2,15 +2,18 @@
 //
 // All of these are bandwidth-trivial next to the weight stream; they are written so that the
 // integer/byte outputs are bit-exact to the reference engine (src/v182_r22_breakthrough_engine.c):
-//   quantize_row_fp16_to_q8_k  ENG:925-990    -> quantize_kernel<Q8_K>
-//   quantize_row_fp16_to_q8_0  ENG:1016-1064  -> quantize_kernel<Q8_0>
-//   rmsnorm_fp16_rows_fast     ENG:4264-4314  -> rmsnorm_q8k_kernel (fp32 sum in tree order)
-//   swiglu_fp16_rows_fast      ENG:4326-4383  -> swiglu_q8k_kernel (CUDA expf)
-//   dequant_block_<type>       ENG:598-853    -> dequant_kernel
+//   quantize_row_fp16_to_q8_k  ENG:925-990    -> kq_quantize<Q8_K>
+//   quantize_row_fp16_to_q8_0  ENG:1016-1064  -> kq_quantize<Q8_0>
+//   rmsnorm_fp16_rows_fast     ENG:4264-4314  -> kq_rmsnorm_q8k (the sequential fp32 sum)
+//   swiglu_fp16_rows_fast      ENG:4326-4383  -> kq_swiglu_q8k (the C library's expf)
+//   dequant_block_<type>       ENG:598-853    -> kq_dequant
 #include "kq_common.cuh"
 #include "kq_internal.h"
 
 #include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
 
 namespace kq {
 
@@ -86,7 +89,7 @@ __device__ __forceinline__ void load8_f16(const __half *p, float v[8]) {
 
 // One warp per 256-value unit of one row.
 template <int TARGET>
-__global__ void __launch_bounds__(256) quantize_kernel(const __half *x, long long x_stride, int M, int K, void *out) {
+__global__ void __launch_bounds__(256) kq_quantize(const __half *x, long long x_stride, int M, int K, void *out) {
     const int nbu = K / 256;
     const int unit = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -107,55 +110,134 @@ cudaError_t launch_quantize(int target_type, const void *x, long long x_stride, 
     if (units == 0) return cudaSuccess;
     const dim3 grid((units + 7) / 8), block(256);
     if (target_type == TYPE_Q8_0)
-        quantize_kernel<TYPE_Q8_0><<<grid, block, 0, stream>>>(reinterpret_cast<const __half *>(x), x_stride, M, K, out);
+        kq_quantize<TYPE_Q8_0><<<grid, block, 0, stream>>>(reinterpret_cast<const __half *>(x), x_stride, M, K, out);
     else
-        quantize_kernel<TYPE_Q4_K><<<grid, block, 0, stream>>>(reinterpret_cast<const __half *>(x), x_stride, M, K, out);
+        kq_quantize<TYPE_Q4_K><<<grid, block, 0, stream>>>(reinterpret_cast<const __half *>(x), x_stride, M, K, out);
     return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ RMSNorm (+ Q8_K)
+//
+// x_out = fp16((x * inv_rms) * gamma), inv_rms = 1 / sqrt(sum_sq * (1/K) + 1e-6), every operation
+// rounded as in the reference's scalar branch (ENG:4291-4299), where sum_sq is the fp32 sum of
+// the squares added one after another in index order.  That order is kept exactly; the chain
+// of K dependent adds is shortened by splitting the row into RMS_SEG segments:
+//  * thread 0 adds segment 0 from 0;
+//  * for every later segment j, RMS_CAND threads add the segment starting from the RMS_CAND
+//    consecutive fp32 values around an estimate of the running sum at its start (the fp64 sum
+//    of the squares before it, rounded to fp32), all at the same time as thread 0;
+//  * then thread 0 walks the segments: the true running sum at the start of segment j is one of
+//    the candidates (it lies within a few fp32 steps of the estimate) and that candidate's end
+//    is the true running sum at the end; when it is not, thread 0 adds the segment itself.
+// Every result is the sequential fp32 sum; the squares of fp16 values are exact in fp32.
+// The fp32 running sum drifts from the exact sum by up to ~50 fp32 steps over 2,560 N(0,1) terms
+// (CPU simulation of 5,600 segment starts: all within +-63 at K = 2560; a few percent of the
+// segment starts fall outside at K = 9728, which only costs time).
+constexpr int RMS_THREADS = 1024;
+constexpr int RMS_SEG = 8;
+constexpr int RMS_CAND = 127;  // start values bits(estimate) - 63 .. bits(estimate) + 63
+static_assert(1 + (RMS_SEG - 1) * RMS_CAND <= RMS_THREADS, "one thread per candidate");
 
-// One CTA per row.  x_out = fp16((x * inv_rms) * gamma), inv_rms = 1 / sqrt(sum(x^2) / K + 1e-6)
-// with each operation rounded as in ENG:4291-4299; the fp32 sum of squares is a tree sum
-// (the reference's scalar loop adds sequentially, its NEON loop in eight lanes), so outputs
-// can differ from either in the last fp16 bit.
-__global__ void __launch_bounds__(256) rmsnorm_q8k_kernel(const __half *x, const __half *gamma, __half *out,
-                                                          BlockQ8K *q8k, int K) {
-    const int m = blockIdx.x;
+// Sequential fp32 sum of squares of xs[a, b) (fp16 in shared memory, a and b multiples of 8)
+// starting from s.
+__device__ __forceinline__ float sumsq_chain(const __half *xs, int a, int b, float s) {
+#pragma unroll 4
+    for (int i = a; i < b; i += 8) {
+        const uint4 raw = *reinterpret_cast<const uint4 *>(xs + i);
+        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = __half22float2(h2[k]);
+            s = __fadd_rn(s, __fmul_rn(f.x, f.x));
+            s = __fadd_rn(s, __fmul_rn(f.y, f.y));
+        }
+    }
+    return s;
+}
+
+// One CTA per row; the row is staged in dynamic shared memory (K fp16).
+__global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, const __half *gamma, __half *out,
+                                                                  BlockQ8K *q8k, int K) {
+    extern __shared__ __align__(16) uint8_t rms_smem[];
+    __half *xs = reinterpret_cast<__half *>(rms_smem);
+    __shared__ double s_part[RMS_SEG][RMS_THREADS / 32];
+    __shared__ float s_end[RMS_SEG][RMS_CAND];
+    __shared__ uint32_t s_lo[RMS_SEG];
+    __shared__ float s_first, s_inv;
+    const int m = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const __half *xr = x + (size_t)m * K;
     __half *yr = out + (size_t)m * K;
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < K; i += 256) {
-        const float v = __half2float(xr[i]);
-        ss = __fadd_rn(ss, __fmul_rn(v, v));
+    // the next kernel may start now: its weight stream does not depend on this one
+    asm volatile("griddepcontrol.launch_dependents;");
+    if ((reinterpret_cast<uintptr_t>(xr) & 15) == 0) {
+        for (int i = 8 * tid; i < K; i += 8 * RMS_THREADS)
+            *reinterpret_cast<uint4 *>(xs + i) = *reinterpret_cast<const uint4 *>(xr + i);
+    } else {
+        for (int i = tid; i < K; i += RMS_THREADS) xs[i] = xr[i];
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-    __shared__ float red[8];
-    __shared__ float s_inv;
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float t = 0.0f;
-        for (int i = 0; i < 8; ++i) t = __fadd_rn(t, red[i]);
+    // segment j = [j L, min(K, (j + 1) L)), L a multiple of 8
+    const int L = ((K + RMS_SEG - 1) / RMS_SEG + 7) & ~7;
+    // fp64 sums of the squares of each segment (exact enough to centre the candidate windows)
+    for (int j = 0; j < RMS_SEG - 1; ++j) {
+        double d = 0.0;
+        const int a = j * L, b = min(K, a + L);
+        for (int i = a + tid; i < b; i += RMS_THREADS) {
+            const double v = (double)__half2float(xs[i]);
+            d += v * v;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == 0) s_part[j][warp] = d;
+    }
+    __syncthreads();
+    if (tid < RMS_SEG) {
+        if (tid == 0) {
+            s_lo[0] = 0;
+        } else {
+            double pre = 0.0;
+            for (int j = 0; j < tid; ++j)
+                for (int w = 0; w < RMS_THREADS / 32; ++w) pre += s_part[j][w];
+            const uint32_t c = __float_as_uint(__double2float_rn(pre));
+            s_lo[tid] = c > (uint32_t)(RMS_CAND / 2) ? c - (uint32_t)(RMS_CAND / 2) : 0u;
+        }
+    }
+    __syncthreads();
+    // the chains: thread 0 = segment 0 from 0; thread 1 + (j - 1) RMS_CAND + k = segment j from
+    // candidate k
+    if (tid == 0) {
+        s_first = sumsq_chain(xs, 0, min(K, L), 0.0f);
+    } else if (tid < 1 + (RMS_SEG - 1) * RMS_CAND) {
+        const int j = 1 + (tid - 1) / RMS_CAND, k = (tid - 1) % RMS_CAND;
+        const int a = j * L, b = min(K, a + L);
+        if (a < b) s_end[j][k] = sumsq_chain(xs, a, b, __uint_as_float(s_lo[j] + (uint32_t)k));
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float s = s_first;
+        for (int j = 1; j < RMS_SEG; ++j) {
+            const int a = j * L, b = min(K, a + L);
+            if (a >= b) break;
+            const uint32_t sb = __float_as_uint(s);
+            if (sb >= s_lo[j] && sb - s_lo[j] < (uint32_t)RMS_CAND) s = s_end[j][sb - s_lo[j]];
+            else s = sumsq_chain(xs, a, b, s);  // outside the window: add the segment here
+        }
         const float inv_k = __fdiv_rn(1.0f, (float)K);
-        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(t, inv_k), 1.0e-6f)));
+        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, inv_k), 1.0e-6f)));
     }
     __syncthreads();
     const float inv_rms = s_inv;
-    asm volatile("griddepcontrol.launch_dependents;");
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nbu = K / 256;
-    for (int b = warp; b < nbu; b += 8) {
+    for (int b = warp; b < nbu; b += RMS_THREADS / 32) {
         const int base = b * 256 + 8 * lane;
         float v[8];
         uint32_t packed[4];
 #pragma unroll
         for (int i = 0; i < 8; i += 2) {
-            const float y0 = __fmul_rn(__fmul_rn(__half2float(xr[base + i]), inv_rms), __half2float(gamma[base + i]));
+            const float y0 = __fmul_rn(__fmul_rn(__half2float(xs[base + i]), inv_rms), __half2float(gamma[base + i]));
             const float y1 =
-                __fmul_rn(__fmul_rn(__half2float(xr[base + i + 1]), inv_rms), __half2float(gamma[base + i + 1]));
+                __fmul_rn(__fmul_rn(__half2float(xs[base + i + 1]), inv_rms), __half2float(gamma[base + i + 1]));
             const __half h0 = __float2half_rn(y0), h1 = __float2half_rn(y1);
             v[i] = __half2float(h0);
             v[i + 1] = __half2float(h1);
@@ -174,25 +256,46 @@ __global__ void __launch_bounds__(256) rmsnorm_q8k_kernel(const __half *x, const
 cudaError_t launch_rmsnorm_q8k(const void *x, const void *gamma, void *out, void *q8k, int M, int K,
                                cudaStream_t stream, bool pdl) {
     if (M == 0) return cudaSuccess;
+    // the staged row takes up to 128 KB (K <= 65536): raise the kernel's dynamic shared memory
+    // limit once per device
+    static std::mutex mu;
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64) {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!configured[dev]) {
+            cudaError_t e =
+                cudaFuncSetAttribute(kq_rmsnorm_q8k, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
+            if (e != cudaSuccess) return e;
+            configured[dev] = true;
+        }
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(M);
-    cfg.blockDim = dim3(256);
+    cfg.blockDim = dim3(RMS_THREADS);
+    cfg.dynamicSmemBytes = (size_t)K * 2;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, rmsnorm_q8k_kernel, reinterpret_cast<const __half *>(x),
+    return cudaLaunchKernelEx(&cfg, kq_rmsnorm_q8k, reinterpret_cast<const __half *>(x),
                               reinterpret_cast<const __half *>(gamma), reinterpret_cast<__half *>(out),
                               reinterpret_cast<BlockQ8K *>(q8k), K);
 }
 
 // ------------------------------------------------------------------ SwiGLU (+ Q8_K)
 
-// One warp per 256-value unit: gate = fp16((g / (1 + exp(-g))) * u), ENG:4350-4356, then Q8_K
-// of the rounded values (ENG:4357).
-__global__ void __launch_bounds__(256) swiglu_q8k_kernel(__half *gate, const __half *up, BlockQ8K *q8k, int M, int N) {
+// One warp per 256-value unit: gate = fp16((g / (1 + expf(-g))) * u), ENG:4350-4356, then Q8_K
+// of the rounded values (ENG:4357).  expf is the C library's, which is not correctly rounded (its
+// last bit depends on the library), so its values come from exp_tab: expf(-g) for each of the
+// 65,536 fp16 patterns of g, tabulated with the host's expf when the context was created.  With
+// exp_tab == nullptr the kernel computes exp in fp64 and rounds once to fp32 (the correctly
+// rounded value except in rare double-rounding cases), for callers that want no host table.
+__global__ void __launch_bounds__(256) kq_swiglu_q8k(__half *gate, const __half *up, BlockQ8K *q8k, int M, int N,
+                                                         const float *exp_tab) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     const int nbu = N / 256;
@@ -201,18 +304,30 @@ __global__ void __launch_bounds__(256) swiglu_q8k_kernel(__half *gate, const __h
     if (unit >= M * nbu) return;
     const int m = unit / nbu, b = unit % nbu;
     const size_t off = (size_t)m * N + (size_t)b * 256 + 8 * lane;
-    float g[8], u[8], v[8];
-    load8_f16(gate + off, g);
+    uint16_t gb[8];
+    float u[8], v[8];
+    if ((reinterpret_cast<uintptr_t>(gate + off) & 15) == 0) {
+        const uint4 raw = *reinterpret_cast<const uint4 *>(gate + off);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) gb[i] = (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) gb[i] = __half_as_ushort(gate[off + i]);
+    }
     load8_f16(up + off, u);
     uint32_t packed[4];
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
-        const float y0 = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, expf(-g[i]))), u[i]);
-        const float y1 = __fmul_rn(__fdiv_rn(g[i + 1], __fadd_rn(1.0f, expf(-g[i + 1]))), u[i + 1]);
-        const __half h0 = __float2half_rn(y0), h1 = __float2half_rn(y1);
-        v[i] = __half2float(h0);
-        v[i + 1] = __half2float(h1);
-        packed[i / 2] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+        __half hv[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const float g = __half2float(__ushort_as_half(gb[i + k]));
+            const float e = exp_tab ? __ldg(exp_tab + gb[i + k]) : (float)exp(-(double)g);
+            hv[k] = __float2half_rn(__fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u[i + k]));
+            v[i + k] = __half2float(hv[k]);
+        }
+        packed[i / 2] = (uint32_t)__half_as_ushort(hv[0]) | ((uint32_t)__half_as_ushort(hv[1]) << 16);
     }
     if ((reinterpret_cast<uintptr_t>(gate + off) & 15) == 0) {
         *reinterpret_cast<uint4 *>(gate + off) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
@@ -223,7 +338,8 @@ __global__ void __launch_bounds__(256) swiglu_q8k_kernel(__half *gate, const __h
     if (q8k) warp_store_q8k(v, q8k + (size_t)m * nbu + b, lane);
 }
 
-cudaError_t launch_swiglu_q8k(void *gate, const void *up, void *q8k, int M, int N, cudaStream_t stream, bool pdl) {
+cudaError_t launch_swiglu_q8k(void *gate, const void *up, void *q8k, int M, int N, cudaStream_t stream, bool pdl,
+                              const float *exp_tab) {
     const int units = M * (N / 256);
     if (units == 0) return cudaSuccess;
     cudaLaunchConfig_t cfg{};
@@ -235,15 +351,44 @@ cudaError_t launch_swiglu_q8k(void *gate, const void *up, void *q8k, int M, int 
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, swiglu_q8k_kernel, reinterpret_cast<__half *>(gate),
-                              reinterpret_cast<const __half *>(up), reinterpret_cast<BlockQ8K *>(q8k), M, N);
+    return cudaLaunchKernelEx(&cfg, kq_swiglu_q8k, reinterpret_cast<__half *>(gate),
+                              reinterpret_cast<const __half *>(up), reinterpret_cast<BlockQ8K *>(q8k), M, N, exp_tab);
+}
+
+// expf(-g) for every fp16 bit pattern g (the table kq_swiglu_q8k reads), with this host's C
+// library -- the expf the reference's scalar SwiGLU calls (ENG:4354).
+void fill_swiglu_exp_table(float *tab) {
+    for (uint32_t h = 0; h < 65536u; ++h) {
+        // binary16 -> binary32, exact
+        const uint32_t sign = (h & 0x8000u) << 16, e = (h >> 10) & 0x1Fu, f = h & 0x3FFu;
+        uint32_t bits;
+        if (e == 0x1F) {
+            bits = sign | 0x7F800000u | (f << 13);
+        } else if (e != 0) {
+            bits = sign | ((e + 112u) << 23) | (f << 13);
+        } else if (f == 0) {
+            bits = sign;
+        } else {  // subnormal: normalise
+            int sh = 0;
+            uint32_t mnt = f;
+            while (!(mnt & 0x400u)) {
+                mnt <<= 1;
+                ++sh;
+            }
+            bits = sign | ((uint32_t)(113 - sh) << 23) | ((mnt & 0x3FFu) << 13);
+        }
+        float g;
+        std::memcpy(&g, &bits, 4);
+        volatile float ng = -g;  // computed at run time by the library, never folded
+        tab[h] = expf(ng);
+    }
 }
 
 // ------------------------------------------------------------------ weight repack
 
 // GGUF rows -> row-group tiles (kq_common.cuh).  One thread per GGUF byte (the padding rows of
 // the last group were zeroed before); runs once per tensor at upload.
-__global__ void repack_kernel(int type, int nbu, const uint8_t *gguf, uint8_t *dev, int rows, size_t gguf_rb) {
+__global__ void kq_repack(int type, int nbu, const uint8_t *gguf, uint8_t *dev, int rows, size_t gguf_rb) {
     const size_t total = (size_t)rows * gguf_rb;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int r = (int)(i / gguf_rb);
@@ -258,7 +403,7 @@ cudaError_t launch_repack(int type, const uint8_t *gguf, uint8_t *dev, int rows,
     const size_t total = (size_t)rows * rb;
     const int threads = 256;
     const int blocks = (int)std::min<size_t>((total + threads - 1) / threads, 148 * 64);
-    repack_kernel<<<blocks, threads, 0, stream>>>(type, K / 256, gguf, dev, rows, rb);
+    kq_repack<<<blocks, threads, 0, stream>>>(type, K / 256, gguf, dev, rows, rb);
     return cudaGetLastError();
 }
 
@@ -273,7 +418,7 @@ __device__ __forceinline__ uint8_t gguf_byte(int type, int nbu, const uint8_t *t
 // the reference's scalar dequant loops.
 // ids != nullptr: output row j is weight row ids[j] (an embedding lookup); an id past the
 // weight's w_rows rows gives zeros and records DEV_ERR_INDEX (never read out of bounds).
-__global__ void dequant_kernel(int type, const uint8_t *tiled, int row_begin, int rows, int K, __half *out,
+__global__ void kq_dequant(int type, const uint8_t *tiled, int row_begin, int rows, int K, __half *out,
                                const uint32_t *ids, int w_rows, int *status) {
     const int nbu = K / 256;
     const size_t total = (size_t)rows * K;
@@ -338,7 +483,7 @@ cudaError_t launch_dequant(int type, const uint8_t *tiled, int row_begin, int ro
     const size_t total = (size_t)rows * K;
     if (total == 0) return cudaSuccess;
     const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 32);
-    dequant_kernel<<<blocks, 256, 0, stream>>>(type, tiled, row_begin, rows, K, reinterpret_cast<__half *>(out), ids,
+    kq_dequant<<<blocks, 256, 0, stream>>>(type, tiled, row_begin, rows, K, reinterpret_cast<__half *>(out), ids,
                                                w_rows, status);
     return cudaGetLastError();
 }
@@ -349,7 +494,7 @@ cudaError_t launch_dequant(int type, const uint8_t *tiled, int row_begin, int ro
 // products that wrote their logits first): keys[m] = max over rows r of argmax_key(logit, r), so
 // the largest logit wins and, among equal ones, the first row -- the strict '>' scan.  keys must
 // start at 0.  Grid: x over rows, y = token.
-__global__ void __launch_bounds__(256) logits_argmax_kernel(const __half *logits, long long stride, int rows,
+__global__ void __launch_bounds__(256) kq_logits_argmax(const __half *logits, long long stride, int rows,
                                                              unsigned long long *keys) {
     const int m = blockIdx.y;
     const __half *lg = logits + (size_t)m * stride;
@@ -401,15 +546,22 @@ cudaError_t launch_logits_argmax(const void *logits, long long stride, int rows,
                                  cudaStream_t stream) {
     if (M <= 0 || rows <= 0) return cudaSuccess;
     const int bx = std::min((rows / 8 + 511) / 512 + 1, 64);
-    logits_argmax_kernel<<<dim3(bx, M), 256, 0, stream>>>(reinterpret_cast<const __half *>(logits), stride, rows, keys);
+    kq_logits_argmax<<<dim3(bx, M), 256, 0, stream>>>(reinterpret_cast<const __half *>(logits), stride, rows, keys);
     return cudaGetLastError();
 }
 
-// keys[m] = (ordered value << 32) | (0xFFFFFFFF - index); index maps through ids when given.
-__global__ void argmax_finalize_kernel(const unsigned long long *keys, int M, const uint32_t *ids, uint32_t *toks,
-                                       float *vals) {
+// keys[m] = (ordered value << 32) | (0xFFFFFFFF - index); index maps through ids when given.  When
+// `status` is given and holds an error (a product kernel stopped early on a wait timeout), every
+// row gets the "no result" sentinel instead: token 0xFFFFFFFF, value NaN.
+__global__ void kq_argmax_finalize(const unsigned long long *keys, int M, const uint32_t *ids, uint32_t *toks,
+                                   float *vals, const int *status) {
     const int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m >= M) return;
+    if (status && *reinterpret_cast<const volatile int *>(status) != DEV_OK) {
+        if (toks) toks[m] = 0xFFFFFFFFu;
+        if (vals) vals[m] = __int_as_float(0x7FC00000);
+        return;
+    }
     const unsigned long long k = keys[m];
     if (k == 0ull) {  // no row reported (empty list or a kernel that stopped early)
         if (toks) toks[m] = 0xFFFFFFFFu;
@@ -424,8 +576,8 @@ __global__ void argmax_finalize_kernel(const unsigned long long *keys, int M, co
 }
 
 cudaError_t launch_argmax_finalize(const unsigned long long *keys, int M, const uint32_t *ids, uint32_t *toks,
-                                   float *vals, cudaStream_t stream) {
-    argmax_finalize_kernel<<<(M + 127) / 128, 128, 0, stream>>>(keys, M, ids, toks, vals);
+                                   float *vals, cudaStream_t stream, const int *status) {
+    kq_argmax_finalize<<<(M + 127) / 128, 128, 0, stream>>>(keys, M, ids, toks, vals, status);
     return cudaGetLastError();
 }
 

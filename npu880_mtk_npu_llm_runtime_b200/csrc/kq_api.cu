@@ -33,6 +33,8 @@ struct kq_ctx {
     int *h_status = nullptr;     // error word: pinned host memory mapped into the device
     int *d_status = nullptr;     // its device address (kernels write errors there)
     bool pdl = true;
+    float *exp_tab = nullptr;    // SwiGLU: expf(-g) for every fp16 g, from this host's C library
+    bool swiglu_gpu_exp = false; // option "swiglu_exp" = 1: exp in fp64 on the GPU instead
     bool inject_timeout = false;  // test hook: GEMV consumers wait on a barrier nothing completes
     unsigned long long timeout_ns = 1000000000ull;
     std::string err;
@@ -45,6 +47,7 @@ struct kq_ctx {
     DevBuf gsplit, gcount;
     bool gemv_split = true;
     bool split_dirty = false;
+    bool graph_holds_scratch = false;  // a call of this context was captured into a CUDA graph
 
     // the engine's g_sdot_input state: pending pre-quantized Q8_K input (ENG:4184) and the
     // current input rows for row-level calls (kept as fp16 on the device, quantized lazily)
@@ -82,19 +85,38 @@ int cuda_fail(kq_ctx *c, cudaError_t e, const char *what) {
 bool is_kquant(uint32_t t) { return t == KQ_TYPE_Q4_K || t == KQ_TYPE_Q5_K || t == KQ_TYPE_Q6_K; }
 bool supported(uint32_t t) { return is_kquant(t) || t == KQ_TYPE_Q8_0; }
 
+// Scratch of at least `bytes`.  A buffer that must grow is freed and allocated again, which a
+// CUDA graph captured from this context's calls would not see: work captured into a graph keeps
+// the scratch addresses it was recorded with.  So once a call of this context was captured
+// (graph_holds_scratch), growing an existing buffer is refused with an error instead, until the
+// caller declares the graphs gone (option "graph_released"); a buffer not yet allocated may
+// still be allocated outside a capture.  During a capture nothing may be allocated.
 int ensure(kq_ctx *c, DevBuf &b, size_t bytes) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(c->stream, &cap) != cudaSuccess) cap = cudaStreamCaptureStatusNone;
+    if (cap != cudaStreamCaptureStatusNone) c->graph_holds_scratch = true;
     if (b.cap >= bytes) return KQ_OK;
+    if (cap != cudaStreamCaptureStatusNone)
+        return fail(c, KQ_ERR_INVALID_ARGUMENT,
+                    "scratch of %zu bytes needed during stream capture: make one eager call of the largest shape "
+                    "before capturing",
+                    bytes);
+    if (b.p && c->graph_holds_scratch)
+        return fail(c, KQ_ERR_INVALID_ARGUMENT,
+                    "scratch must grow to %zu bytes but a captured CUDA graph may still use it: destroy those graphs "
+                    "and set option \"graph_released\" first",
+                    bytes);
     if (b.p) {
         cudaStreamSynchronize(c->stream);
         cudaFree(b.p);
         b.p = nullptr;
         b.cap = 0;
     }
-    size_t cap = std::max<size_t>(bytes, 4096);
-    cap = (cap + 255) & ~(size_t)255;
-    cudaError_t e = cudaMalloc(&b.p, cap);
+    size_t want = std::max<size_t>(bytes, 4096);
+    want = (want + 255) & ~(size_t)255;
+    cudaError_t e = cudaMalloc(&b.p, want);
     if (e != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(scratch)");
-    b.cap = cap;
+    b.cap = want;
     return KQ_OK;
 }
 
@@ -115,8 +137,13 @@ int check_device_status(kq_ctx *c) {
 
 int sync_and_check(kq_ctx *c) { return check_device_status(c); }
 
+const float *swiglu_table(const kq_ctx *c) { return c->swiglu_gpu_exp ? nullptr : c->exp_tab; }
+
 int validate_task(kq_ctx *c, const kq_task &t, int K) {
     if (!t.w) return fail(c, KQ_ERR_INVALID_ARGUMENT, "task weight is NULL");
+    if (t.w->device != c->device)
+        return fail(c, KQ_ERR_INVALID_ARGUMENT, "task weight lives on device %d, the context on device %d", t.w->device,
+                    c->device);
     if (t.w->cols != K) return fail(c, KQ_ERR_SHAPE, "task weight has %d columns, input K = %d", t.w->cols, K);
     if (t.rows < 0 || t.row_begin < 0 || (long long)t.row_begin + t.rows > t.w->rows)
         return fail(c, KQ_ERR_SHAPE, "task rows [%d, %d) outside weight rows %d", t.row_begin, t.row_begin + t.rows,
@@ -125,6 +152,14 @@ int validate_task(kq_ctx *c, const kq_task &t, int K) {
     if (t.residual && t.res_stride < (size_t)t.rows) return fail(c, KQ_ERR_INVALID_ARGUMENT, "res_stride < rows");
     if (t.dst_f32 && t.dst_f32_stride < (size_t)t.rows)
         return fail(c, KQ_ERR_INVALID_ARGUMENT, "dst_f32_stride < rows");
+    return KQ_OK;
+}
+
+// A weight is used only by contexts on the device that holds it.
+int check_weight_device(kq_ctx *c, const kq_weight *w) {
+    if (w->device != c->device)
+        return fail(c, KQ_ERR_INVALID_ARGUMENT, "weight lives on device %d, the context on device %d", w->device,
+                    c->device);
     return KQ_OK;
 }
 
@@ -426,6 +461,18 @@ extern "C" int kq_init(int device, kq_ctx **out) {
     }
     *c->h_status = kq::DEV_OK;
     c->own_stream = true;
+    {
+        std::vector<float> tab(65536);
+        kq::fill_swiglu_exp_table(tab.data());
+        if (cudaMalloc(&c->exp_tab, tab.size() * sizeof(float)) != cudaSuccess ||
+            cudaMemcpy(c->exp_tab, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+            if (c->exp_tab) cudaFree(c->exp_tab);
+            cudaStreamDestroy(c->stream);
+            cudaFreeHost(c->h_status);
+            delete c;
+            return KQ_ERR_CUDA;
+        }
+    }
     *out = c;
     return KQ_OK;
 }
@@ -437,6 +484,7 @@ extern "C" int kq_destroy(kq_ctx *c) {
     for (DevBuf *b : {&c->x, &c->res, &c->out16, &c->out32, &c->q8k_pending, &c->q8k_cur, &c->q80_cur, &c->tmp,
                       &c->misc, &c->keys, &c->tcpack, &c->tcterms, &c->gsplit, &c->gcount, &c->lmlogits})
         if (b->p) cudaFree(b->p);
+    cudaFree(c->exp_tab);
     cudaFreeHost(c->h_status);
     if (c->own_stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -487,6 +535,15 @@ extern "C" int kq_set_option(kq_ctx *c, const char *name, long long value) {
         c->gemm_path = (int)value;
         return KQ_OK;
     }
+    if (!strcmp(name, "graph_released")) {
+        c->graph_holds_scratch = value == 0;
+        return KQ_OK;
+    }
+    if (!strcmp(name, "swiglu_exp")) {
+        if (value < 0 || value > 1) return fail(c, KQ_ERR_INVALID_ARGUMENT, "swiglu_exp must be 0 or 1");
+        c->swiglu_gpu_exp = value == 1;
+        return KQ_OK;
+    }
     if (!strcmp(name, "gemv_split")) {
         c->gemv_split = value != 0;
         return KQ_OK;
@@ -525,6 +582,7 @@ static int weight_create(kq_ctx *c, const void *src, bool src_on_device, uint32_
     cudaSetDevice(c->device);
     const size_t gguf_bytes = (size_t)rows * kq_row_bytes(type, cols);
     kq_weight *w = new kq_weight();
+    w->device = c->device;
     w->type = type;
     w->rows = rows;
     w->cols = cols;
@@ -569,7 +627,11 @@ extern "C" int kq_weight_free(kq_ctx *c, kq_weight *w) {
         cudaSetDevice(c->device);
         cudaStreamSynchronize(c->stream);
     }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != w->device) cudaSetDevice(w->device);
     cudaFree(w->d);
+    if (prev != w->device) cudaSetDevice(prev);
     delete w;
     return KQ_OK;
 }
@@ -747,6 +809,7 @@ extern "C" int kq_sdot_gemm_multi_dispatch(kq_ctx *c, const uint16_t *x, int M, 
 // Row-level entry points over the current input.
 static int row_level(kq_ctx *c, const kq_weight *w, uint32_t row, int m0, int M, float *out) {
     if (!c || !w || !out) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = check_weight_device(c, w)) return r;
     if ((int)row >= w->rows) return fail(c, KQ_ERR_SHAPE, "row %u >= rows %d", row, w->rows);
     if (c->cur_M == 0) return fail(c, KQ_ERR_NOT_READY, "no current input");
     if (w->cols != c->cur_K) return fail(c, KQ_ERR_SHAPE, "weight cols %d != current K %d", w->cols, c->cur_K);
@@ -825,7 +888,7 @@ extern "C" int kq_swiglu_q8k_async(kq_ctx *c, uint16_t *gate, const uint16_t *up
         c->pending_M = M;
         c->pending_K = N;
     }
-    KQ_CUDA(c, kq::launch_swiglu_q8k(gate, up, q8k, M, N, c->stream, c->pdl));
+    KQ_CUDA(c, kq::launch_swiglu_q8k(gate, up, q8k, M, N, c->stream, c->pdl, swiglu_table(c)));
     return KQ_OK;
 }
 
@@ -868,6 +931,8 @@ extern "C" int kq_run_ffn_async(kq_ctx *c, const kq_weight *gate, const kq_weigh
                                 const uint16_t *x_in, const uint16_t *gamma, uint16_t *x_out) {
     if (!c || !gate || !up || !down || !x_in || !gamma || !x_out)
         return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    for (const kq_weight *w : {gate, up, down})
+        if (int r = check_weight_device(c, w)) return r;
     const int hidden = gate->cols, ffn = gate->rows;
     if (up->cols != hidden || up->rows != ffn || down->cols != ffn || down->rows != hidden)
         return fail(c, KQ_ERR_SHAPE, "FFN weights do not chain: gate %dx%d up %dx%d down %dx%d", gate->rows,
@@ -908,7 +973,7 @@ extern "C" int kq_run_ffn_async(kq_ctx *c, const kq_weight *gate, const kq_weigh
     gu[1].dst_stride = ffn;
     if (int r = run_gemv(c, gu, 2, M, hidden, nullptr, 0, q_a, gu_q80 ? q_a0 : nullptr)) return r;
     // SwiGLU (+ Q8_K), ENG:8292
-    KQ_CUDA(c, kq::launch_swiglu_q8k(g, u, q_h, M, ffn, c->stream, c->pdl));
+    KQ_CUDA(c, kq::launch_swiglu_q8k(g, u, q_h, M, ffn, c->stream, c->pdl, swiglu_table(c)));
     if (down->type == KQ_TYPE_Q8_0) KQ_CUDA(c, kq::launch_quantize(KQ_TYPE_Q8_0, g, ffn, M, ffn, q_h0, c->stream));
     // down + residual, ENG:8294-8296
     kq_task dn{};
@@ -944,6 +1009,7 @@ extern "C" int kq_run_ffn(kq_ctx *c, const kq_weight *gate, const kq_weight *up,
 
 extern "C" int kq_dequant_rows_async(kq_ctx *c, const kq_weight *w, int row_begin, int rows, uint16_t *dst) {
     if (!c || !w || !dst) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = check_weight_device(c, w)) return r;
     if (row_begin < 0 || rows < 0 || (long long)row_begin + rows > w->rows) return fail(c, KQ_ERR_SHAPE, "row range");
     KQ_CUDA(c, kq::launch_dequant((int)w->type, w->d, row_begin, rows, w->cols, dst, c->stream));
     return KQ_OK;
@@ -961,6 +1027,7 @@ extern "C" int kq_dequant_rows(kq_ctx *c, const kq_weight *w, int row_begin, int
 
 extern "C" int kq_embed_rows_async(kq_ctx *c, const kq_weight *w, const uint32_t *ids, int n, uint16_t *dst) {
     if (!c || !w || !ids || !dst) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = check_weight_device(c, w)) return r;
     if (n < 0) return fail(c, KQ_ERR_SHAPE, "n = %d", n);
     KQ_CUDA(c, kq::launch_dequant((int)w->type, w->d, 0, n, w->cols, dst, c->stream, ids, w->rows, c->d_status));
     return KQ_OK;
@@ -988,6 +1055,7 @@ extern "C" int kq_embed_rows(kq_ctx *c, const kq_weight *w, const uint32_t *ids,
 extern "C" int kq_lm_head_argmax_async(kq_ctx *c, const kq_weight *w, const uint16_t *x, int M, uint16_t *logits,
                                        float *logits_f32, uint32_t *toks, float *vals) {
     if (!c || !w || !x) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = check_weight_device(c, w)) return r;
     if (int r = validate_mk(c, M, w->cols)) return r;
     if (int r = ensure(c, c->keys, (size_t)M * 8)) return r;
     auto *keys = reinterpret_cast<unsigned long long *>(c->keys.p);
@@ -1046,6 +1114,7 @@ extern "C" int kq_lm_head_argmax(kq_ctx *c, const kq_weight *w, const uint16_t *
 extern "C" int kq_eval_indexed_rows_argmax(kq_ctx *c, const kq_weight *w, const uint32_t *row_ids, int n_rows, int M,
                                            uint16_t *logits_m1, uint32_t *top_toks, float *top_vals) {
     if (!c || !w || !row_ids || !top_toks || !top_vals) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = check_weight_device(c, w)) return r;
     if (n_rows <= 0 || M <= 0) return KQ_OK;  // ENG:9591
     if (logits_m1 && M != 1) return fail(c, KQ_ERR_INVALID_ARGUMENT, "logits_m1 needs M == 1 (ENG:9569)");
     if (c->cur_M == 0) return fail(c, KQ_ERR_NOT_READY, "no current input");

@@ -83,7 +83,7 @@ struct TcParams {
     int *status;
     unsigned long long timeout_ns;
     // split K over gridDim.z chunks: each CTA writes the fp32 block terms of its units to
-    // terms[u][token][task row] and tc_fold_kernel adds them in unit order (nullptr: one chunk)
+    // terms[u][token][task row] and kq_tc_fold adds them in unit order (nullptr: one chunk)
     float *terms;
 };
 
@@ -272,7 +272,7 @@ __device__ __forceinline__ void tmem_ldn(uint32_t taddr, uint32_t (&r)[N]) {
 }
 
 template <int TYPE, int BN_, int ROWS_>
-__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(kTcThreads, 1) kq_gemm_tc(const __grid_constant__ TcParams p) {
     using C = TcCfg<TYPE, BN_, ROWS_>;
     constexpr int BN = C::BN, NA = C::NA, S = C::S, RG = C::RG, ROWS = C::ROWS;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -551,7 +551,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 // Sum of the block terms of one split-K product in unit order (the reference's acc += term
 // sequence), then the outputs as the single-chunk epilogue writes them.  One thread per (token,
 // task row); terms[u][token][row] with nterm terms per row (one per 256-value unit).
-__global__ void tc_fold_kernel(const float *terms, int nterm, int M, int rows, __half *dst, long long dst_stride,
+__global__ void kq_tc_fold(const float *terms, int nterm, int M, int rows, __half *dst, long long dst_stride,
                                const __half *res, long long res_stride, float *dst_f32, long long f32_stride) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)M * rows) return;
@@ -590,7 +590,7 @@ __global__ void tc_fold_kernel(const float *terms, int nterm, int M, int rows, _
 // unit); lane L holds values 8L .. 8L+7.
 
 template <int TYPE, int BN>
-__global__ void pack_act_kernel(const __half *x, long long x_stride, const void *act, int M, int K, int n_tok_tiles,
+__global__ void kq_pack_act(const __half *x, long long x_stride, const void *act, int M, int K, int n_tok_tiles,
                                 uint8_t *out, float *dx, uint8_t *bs2) {
     constexpr int DX = (TYPE == TYPE_Q8_0) ? 8 : 1;
     const int nbu = K / 256;
@@ -679,7 +679,7 @@ cudaError_t configure_tc() {
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lk(mu);
     if (!configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<TYPE, BN, ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(kq_gemm_tc<TYPE, BN, ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              TcCfg<TYPE, BN, ROWS>::SMEM);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
@@ -688,7 +688,7 @@ cudaError_t configure_tc() {
 }
 
 // Geometry of one task of the row-major kernel: 64- or 128-row CTAs, and K chunks (split K: block
-// terms stored, folded by tc_fold_kernel) when the grid would use at most half of the SMs and
+// terms stored, folded by kq_tc_fold) when the grid would use at most half of the SMs and
 // every chunk keeps at least 4 units.  Each candidate is costed per 256-value unit per wave of
 // CTAs (B200 timings; Q8_0's eight 32-block accumulators per unit make it the slowest) and the
 // cheapest is taken.
@@ -761,7 +761,7 @@ cudaError_t launch_tc_bn(const TcLaunch &L, cudaStream_t stream) {
     {
         const long long items = (long long)n_tok_tiles * BN * nbu;
         const int blocks = (int)std::min<long long>((items + 7) / 8, 148 * 16);
-        pack_act_kernel<TYPE, BN><<<blocks, 256, 0, stream>>>(reinterpret_cast<const __half *>(L.x), L.x_stride, L.act,
+        kq_pack_act<TYPE, BN><<<blocks, 256, 0, stream>>>(reinterpret_cast<const __half *>(L.x), L.x_stride, L.act,
                                                                L.M, L.K, n_tok_tiles, act, dx, bs2);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
@@ -803,16 +803,16 @@ cudaError_t launch_tc_bn(const TcLaunch &L, cudaStream_t stream) {
         cudaError_t e;
         if (rows64) {
             if ((e = configure_tc<TYPE, BN, 64>())) return e;
-            gemm_tc_kernel<TYPE, BN, 64><<<dim3(n_tok_tiles, (n_rg + 3) / 4, ks), kTcThreads, TcCfg<TYPE, BN, 64>::SMEM, stream>>>(p);
+            kq_gemm_tc<TYPE, BN, 64><<<dim3(n_tok_tiles, (n_rg + 3) / 4, ks), kTcThreads, TcCfg<TYPE, BN, 64>::SMEM, stream>>>(p);
         } else {
             if ((e = configure_tc<TYPE, BN, 128>())) return e;
-            gemm_tc_kernel<TYPE, BN, 128><<<dim3(n_tok_tiles, (n_rg + 7) / 8, ks), kTcThreads, TcCfg<TYPE, BN, 128>::SMEM, stream>>>(p);
+            kq_gemm_tc<TYPE, BN, 128><<<dim3(n_tok_tiles, (n_rg + 7) / 8, ks), kTcThreads, TcCfg<TYPE, BN, 128>::SMEM, stream>>>(p);
         }
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         if (ks > 1) {
             const long long n = (long long)L.M * h.rows;
-            tc_fold_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(p.terms, nbu, L.M, h.rows,
+            kq_tc_fold<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(p.terms, nbu, L.M, h.rows,
                                                                        p.dst, p.dst_stride, p.res, p.res_stride, p.dst_f32,
                                                                        p.f32_stride);
             e = cudaGetLastError();
@@ -940,7 +940,7 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint
 
 
 template <int TYPE>
-__global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_constant__ Tc2Params p) {
+__global__ void __launch_bounds__(kTc2Threads, 1) kq_gemm_tc2(const __grid_constant__ Tc2Params p) {
     using C = Tc2Cfg<TYPE>;
     constexpr int SB = C::SB, SD = C::SD, SH = C::SH, SX = C::SX, SW = C::SW, SAM = C::SAMAX, G = C::G, NOP = C::NOP,
                   RGM = C::RGMAX_C;
@@ -1311,7 +1311,7 @@ __global__ void __launch_bounds__(kTc2Threads, 1) gemm_tc2_kernel(const __grid_c
 // [token block][unit][128 tokens][272 B] quants + [token block][unit][128][DX] scales.  One
 // warp per (token, unit); lane L holds values 8L .. 8L+7.
 template <int TYPE>
-__global__ void pack_act2_kernel(const __half *x, long long x_stride, const void *act, int M, int K, uint8_t *out,
+__global__ void kq_pack_act2(const __half *x, long long x_stride, const void *act, int M, int K, uint8_t *out,
                                  float *dx) {
     constexpr int DX = Tc2Cfg<TYPE>::DX;
     constexpr unsigned AROW = Tc2Cfg<TYPE>::AROW;
@@ -1385,7 +1385,7 @@ cudaError_t launch_tc2_t(const TcLaunch &L, cudaStream_t stream) {
     {
         const long long items = (long long)L.M * nbu;
         const int blocks = (int)std::min<long long>((items + 7) / 8, 148 * 16);
-        pack_act2_kernel<TYPE><<<blocks, 256, 0, stream>>>(reinterpret_cast<const __half *>(L.x), L.x_stride, L.act,
+        kq_pack_act2<TYPE><<<blocks, 256, 0, stream>>>(reinterpret_cast<const __half *>(L.x), L.x_stride, L.act,
                                                             L.M, L.K, act, dx);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
@@ -1397,7 +1397,7 @@ cudaError_t launch_tc2_t(const TcLaunch &L, cudaStream_t stream) {
     {
         std::lock_guard<std::mutex> lk(mu);
         if (!configured[dev]) {
-            cudaError_t e = cudaFuncSetAttribute(gemm_tc2_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+            cudaError_t e = cudaFuncSetAttribute(kq_gemm_tc2<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
             if (e != cudaSuccess) return e;
             configured[dev] = true;
         }
@@ -1432,7 +1432,7 @@ cudaError_t launch_tc2_t(const TcLaunch &L, cudaStream_t stream) {
     p.timeout_ns = L.timeout_ns;
     const int sms = L.num_sms > 0 ? L.num_sms : 148;
     const int gx = std::min(total_rg, std::max((sms + n_tb - 1) / n_tb, (total_rg + C::RGMAX_C - 1) / C::RGMAX_C));
-    gemm_tc2_kernel<TYPE><<<dim3(gx, n_tb), kTc2Threads, C::SMEM, stream>>>(p);
+    kq_gemm_tc2<TYPE><<<dim3(gx, n_tb), kTc2Threads, C::SMEM, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -834,7 +834,7 @@ __device__ __forceinline__ void fold_shared(const GemvParams &p, float *tb, int 
 //         (monotonic shared-memory counters).
 
 template <int TYPE, int MT, bool SMALL, bool SPLIT>
-__global__ void __launch_bounds__(threads_of<MT>(), 2) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ unsigned long long s_best[8];
     __shared__ int s_abort, s_issued;
@@ -1255,8 +1255,8 @@ cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
     p.off_stages = pl.off_stages;
     p.off_bars = pl.off_bars;
 
-    auto kern = pl.small ? (split ? gemv_kernel<TYPE, MT, true, true> : gemv_kernel<TYPE, MT, true, false>)
-                         : (split ? gemv_kernel<TYPE, MT, false, true> : gemv_kernel<TYPE, MT, false, false>);
+    auto kern = pl.small ? (split ? kq_gemv<TYPE, MT, true, true> : kq_gemv<TYPE, MT, true, false>)
+                         : (split ? kq_gemv<TYPE, MT, false, true> : kq_gemv<TYPE, MT, false, false>);
     if (cudaError_t e = configure_smem(kern)) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(pl.grid);
@@ -1283,7 +1283,7 @@ cudaError_t launch_type(const GemvLaunch &L, cudaStream_t stream) {
 
 // Copy weight rows ids[0..n) into a fresh tiled tensor (row i of dst = row ids[i] of src), so a
 // row-id list runs through the same GEMV kernel.  One thread per GGUF byte of a row.
-__global__ void gather_rows_kernel(int type, int nbu, const uint8_t *src, const uint32_t *ids, int n, uint8_t *dst,
+__global__ void kq_gather_rows(int type, int nbu, const uint8_t *src, const uint32_t *ids, int n, uint8_t *dst,
                                    size_t gguf_row_bytes) {
     const size_t total = (size_t)n * gguf_row_bytes;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -1314,7 +1314,7 @@ cudaError_t launch_gather_rows(int type, int K, const uint8_t *src, const uint32
     if (e != cudaSuccess) return e;
     const size_t total = (size_t)n * rb;
     const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
-    gather_rows_kernel<<<blocks, 256, 0, stream>>>(type, K / 256, src, ids, n, dst, rb);
+    kq_gather_rows<<<blocks, 256, 0, stream>>>(type, K / 256, src, ids, n, dst, rb);
     return cudaGetLastError();
 }
 

@@ -8,6 +8,7 @@
 // A GGUF tensor resident in HBM in this library's row-group tile layout (opaque kq_weight of
 // kq.h; layout in kq_common.cuh).
 struct kq_weight {
+    int device;        // CUDA device holding d
     uint32_t type;
     int rows, cols;
     size_t row_bytes;  // GGUF bytes per row (compute_ggml_bytes)
@@ -105,12 +106,17 @@ cudaError_t launch_quantize(int target_type /*12 = Q8_K, 8 = Q8_0*/, const void 
 cudaError_t launch_repack(int type, const uint8_t *gguf, uint8_t *dev, int rows, int K, cudaStream_t stream);
 cudaError_t launch_rmsnorm_q8k(const void *x, const void *gamma, void *out, void *q8k, int M, int K, cudaStream_t stream,
                                bool pdl);
-cudaError_t launch_swiglu_q8k(void *gate, const void *up, void *q8k, int M, int N, cudaStream_t stream, bool pdl);
+// exp_tab: expf(-g) per fp16 pattern of g (fill_swiglu_exp_table), or nullptr for an fp64 exp on the GPU
+cudaError_t launch_swiglu_q8k(void *gate, const void *up, void *q8k, int M, int N, cudaStream_t stream, bool pdl,
+                              const float *exp_tab);
+// host: tab[65536] = expf(-g) with this host's C library, g = every fp16 bit pattern
+void fill_swiglu_exp_table(float *tab);
 // keys[m] = argmax key over the fp16 logits [M][stride] rows 0..rows-1 (keys zeroed before)
 cudaError_t launch_logits_argmax(const void *logits, long long stride, int rows, int M, unsigned long long *keys,
                                  cudaStream_t stream);
+// status (optional): when it holds an error, every row gets token 0xFFFFFFFF and value NaN
 cudaError_t launch_argmax_finalize(const unsigned long long *keys, int M, const uint32_t *ids, uint32_t *toks,
-                                   float *vals, cudaStream_t stream);
+                                   float *vals, cudaStream_t stream, const int *status = nullptr);
 // rows [row_begin, row_begin + rows) to fp16, or (ids != nullptr) rows ids[0..rows) of a weight of
 // w_rows rows, out-of-range ids giving zeros and DEV_ERR_INDEX in *status
 cudaError_t launch_dequant(int type, const uint8_t *tiled, int row_begin, int rows, int K, void *out, cudaStream_t stream,

@@ -193,6 +193,7 @@ class Reference:
         L.kqref_swiglu.argtypes = [_vp, _vp, C.c_int, C.c_int]
         L.kqref_turbo.argtypes = [C.c_int]
         L.kqref_dispatch.argtypes = [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int]
+        L.kqref_dispatch_1thread.argtypes = [_vp, C.c_int, C.c_int, _vp, C.c_int]
         self.max_batch = L.kqref_max_batch()
         self.max_k = L.kqref_max_k()
         self.pool_threads = L.kqref_pool_threads()
@@ -284,6 +285,21 @@ class Reference:
             arr[i].residual = None if res is None else res.ctypes.data
             arr[i].res_stride = 0 if res is None else res.shape[1]
         self.L.kqref_dispatch(_ptr(x16), M, K, C.cast(arr, C.c_void_p), len(tasks), int(bool(prequantized)))
+
+    def dispatch_1thread(self, x16, tasks):
+        """The same dispatch on the calling thread alone (the reference's job function over all rows)."""
+        x16 = np.ascontiguousarray(x16, dtype=np.float16)
+        M, K = x16.shape
+        arr = (self.Task * len(tasks))()
+        for i, (gtype, w, dst, res) in enumerate(tasks):
+            arr[i].w_base = w.ctypes.data
+            arr[i].type = gtype
+            arr[i].rows = w.shape[0]
+            arr[i].dst = dst.ctypes.data
+            arr[i].dst_stride = dst.shape[1]
+            arr[i].residual = None if res is None else res.ctypes.data
+            arr[i].res_stride = 0 if res is None else res.shape[1]
+        self.L.kqref_dispatch_1thread(_ptr(x16), M, K, C.cast(arr, C.c_void_p), len(tasks))
 
     def turbo(self, on: bool):
         self.init_pool()

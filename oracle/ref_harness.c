@@ -134,6 +134,44 @@ KQREF_API void kqref_dispatch(const uint16_t *x, int M, int K, const kqref_task 
     sdot_gemm_multi_dispatch((const __fp16 *)x, M, K, tasks, n_tasks);
 }
 
+/* The single-thread figure: sdot_gemm_multi_dispatch's work (ENG:4188-4262) -- the input quantized
+ * once, then the reference's own job function exec_sdot_job_work_stealing (ENG:3491-3619) over all
+ * rows -- run by the calling thread alone instead of the pool. */
+KQREF_API void kqref_dispatch_1thread(const uint16_t *x, int M, int K, const kqref_task *t, int n_tasks) {
+    static PoolJob job;
+    int need_q8k = 0, need_q80 = 0, total = 0;
+    if (n_tasks > 4) n_tasks = 4;
+    memset(&job, 0, sizeof(job));
+    for (int i = 0; i < n_tasks; ++i) {
+        SdotMatrixTask *T = &job.sdot_tasks_inline[i];
+        T->w_base = t[i].w_base;
+        T->type = t[i].type;
+        T->row_bytes = ggml_row_bytes(t[i].type, (size_t)K);
+        T->dst = (__fp16 *)t[i].dst;
+        T->dst_stride = t[i].dst_stride;
+        T->residual = (const __fp16 *)t[i].residual;
+        T->res_stride = t[i].res_stride;
+        T->rows = t[i].rows;
+        T->cols = K;
+        T->start_row = total;
+        total += t[i].rows;
+        if (t[i].type == GGML_TYPE_Q8_0) need_q80 = 1;
+        else need_q8k = 1;
+    }
+    g_sdot_input.M = M;
+    g_sdot_input.K = K;
+    g_sdot_input.x_fp16 = (const __fp16 *)x;
+    for (int m = 0; m < M; ++m) {
+        if (need_q8k) quantize_row_fp16_to_q8_k((const __fp16 *)x + (size_t)m * K, g_sdot_input.q8k[m], K);
+        if (need_q80) quantize_row_fp16_to_q8_0((const __fp16 *)x + (size_t)m * K, g_sdot_input.q80[m], K);
+    }
+    job.type = 100;
+    job.n_sdot_tasks = n_tasks;
+    job.sdot_total_rows = total;
+    job.total_chunks = (total + SDOT_ROW_GRAIN - 1) / SDOT_ROW_GRAIN;
+    exec_sdot_job_work_stealing(&job);
+}
+
 /* One tensor record of the reference's GGUF parser (GgufTensorInfo, ENG:167-176). */
 typedef struct {
     char name[128];

@@ -61,3 +61,26 @@ def to_dev(a):
 def bits(a):
     a = np.ascontiguousarray(a)
     return a.view({1: np.uint8, 2: np.uint16, 4: np.uint32, 8: np.uint64}[a.dtype.itemsize])
+
+
+def rmsnorm_cases():
+    """(M, K, x fp16, gamma fp16) RMSNorm cases: the benchmark hidden size at 1-64 rows, short and
+    long rows, small and large magnitudes, a zero row (sum 0), +-65504 and fp16 subnormals"""
+    rng = np.random.default_rng(77)
+    cases = []
+    for M, K, scale in [(1, 2560, 1.0), (8, 2560, 1.0), (64, 2560, 1.0), (5, 256, 30.0), (3, 9728, 1.0),
+                        (2, 2560, 1e-3), (2, 2560, 3000.0)]:
+        x = (rng.standard_normal((M, K)) * scale).astype(np.float16)
+        g = (rng.standard_normal(K) * 0.5 + 1.0).astype(np.float16)
+        cases.append((M, K, x, g))
+    x = np.zeros((3, 2560), np.float16)
+    x[1, ::7] = np.float16(65504.0)
+    x[1, 3::7] = np.float16(-65504.0)
+    x[2] = (rng.standard_normal(2560) * 6e-5).astype(np.float16)
+    cases.append((3, 2560, x, np.ones(2560, np.float16)))
+    return cases
+
+
+def all_fp16_gate(rows: int) -> np.ndarray:
+    """every fp16 bit pattern once, as `rows` rows"""
+    return np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16).reshape(rows, 65536 // rows)

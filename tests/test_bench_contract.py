@@ -40,3 +40,16 @@ def test_reference_arm_other_ranks_print_nothing():
     lines = run_bench("--impl", "reference", "--gpus", "2", "--steps", "2", "--warmup", "1",
                       env_extra={"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"})
     assert lines == []
+
+
+def test_reference_arm_config_keys_match_ours():
+    """both arms print the same config keys and warm-up for the default workload"""
+    sys.path.insert(0, ROOT)
+    import bench
+    lines = run_bench("--impl", "reference", "--steps", "2", "--warmup", "5")
+    d = json.loads(lines[0])
+    assert set(d["config"]) == set(bench.gemv_config(1))
+    assert d["warmup"] == 5
+    st = d["cpu_baseline"]["single_thread"]
+    if d["cpu_baseline"]["kind"] == "reference":
+        assert st["cores"] == 1 and st["value"] > 0

@@ -12,6 +12,7 @@ import pytest
 
 from npu880_mtk_npu_llm_runtime_b200 import synth
 from oracle.oracle import TYPE_Q8_0, reference_available
+from conftest import all_fp16_gate, rmsnorm_cases
 
 TYPES = [synth.TYPE_Q4_K, synth.TYPE_Q5_K, synth.TYPE_Q6_K, synth.TYPE_Q8_0]
 
@@ -69,3 +70,34 @@ def test_oracle_equals_reference(oracle, ref, gtype, K, M):
                          ids=["q6_k_full_scales", "q8_0_full_quants"])
 def test_oracle_equals_reference_full_range(oracle, ref, gtype, opts):
     check(oracle, ref, gtype, 40, 2560, 8, seed=900 + gtype, **opts)
+
+
+def test_rmsnorm_oracle_equals_reference(oracle, ref):
+    """rmsnorm_fp16_rows_fast (ENG:4264-4314): the oracle's sequential fp32 sum of squares and
+    rounding steps give the compiled reference's fp16 rows (and Q8_K where the reference makes
+    one: M <= 32, K <= 9216) on the cases the GPU test uses"""
+    for M, K, x, gamma in rmsnorm_cases():
+        o, oq = oracle.rmsnorm(x, gamma)
+        r, rq = ref.rmsnorm(x, gamma)
+        assert np.array_equal(bits(o), bits(r)), (M, K)
+        if M <= 32 and K <= 9216:
+            fin = np.isfinite(r).all(axis=1)
+            assert oq[fin].tobytes() == rq[fin].tobytes()
+
+
+@pytest.mark.parametrize("up_kind", ["ones", "random"])
+def test_swiglu_oracle_equals_reference_all_fp16(oracle, ref, up_kind):
+    """swiglu_fp16_rows_fast (ENG:4326-4383) over every fp16 gate value (32 rows x 2048, the
+    reference's input buffer holds 32 rows): the oracle's libm expf path gives the compiled
+    reference's fp16 outputs bit for bit (NaN where it is NaN) and its Q8_K of all-finite rows"""
+    gate = all_fp16_gate(32)
+    rng = np.random.default_rng(5)
+    up = (np.ones(gate.shape, np.float16) if up_kind == "ones"
+          else (rng.standard_normal(gate.shape) * 2.0).astype(np.float16))
+    o, oq = oracle.swiglu(gate, up)
+    r, rq = ref.swiglu(gate, up)
+    nan = np.isnan(r)
+    assert np.array_equal(np.isnan(o), nan)
+    assert np.array_equal(bits(o)[~nan], bits(r)[~nan])
+    fin = np.isfinite(r).all(axis=1)
+    assert oq[fin].tobytes() == rq[fin].tobytes()
