@@ -456,7 +456,7 @@ def run_ours(args, rank, world, local_rank):
     op_np = op.numpy()
     htasks = [ctx.make_host_tasks([dict(w=Ws[i], dst_f32=op_np)]) for i in range(n_copies)]
     te = e2e_timed(stream, lambda i: ctx.sdot_gemm_multi_dispatch(xp_np, htasks[i % n_copies]), e2e_steps,
-                   warmup, world)
+                   max(warmup, 100), world)
     e2e_value = float(total_wbytes.item()) * e2e_steps / te / 1e9
     for W in Ws:
         W.free()
@@ -522,44 +522,39 @@ def stack_layout(kind):
 
 
 def time_device(stream, step, steps, warmup, gpu_index, graph=True, world=1):
-    """Run `step(i)` warmup + steps times; the timed steps are captured in a CUDA graph when asked.
-    Returns (seconds for `steps` steps, clock summary)."""
+    """Time `steps` calls of step(i) after `warmup` untimed ones, with the clock sampler running
+    from before the warm-up.  graph: graph_timed (warm-up and timed steps in one CUDA graph).
+    Eager: the ranks meet at a barrier, then the warm-up steps, a timing event and the timed steps
+    are enqueued back to back, so the timed steps start with the GPU busy.  Returns (seconds, max
+    over ranks; clock summary)."""
     import torch
     import torch.distributed as dist
-    with torch.cuda.stream(stream):
-        for i in range(warmup):
-            step(i)
-    torch.cuda.synchronize()
-    g = None
-    if graph:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for i in range(steps):
-                step(i)
-        with torch.cuda.stream(stream):
-            g.replay()
-        torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(gpu_index) as clk:
-        e0.record(stream)
-        with torch.cuda.stream(stream):
-            if g is not None:
-                g.replay()
-            else:
-                for i in range(steps):
+    clk = ClockSampler(gpu_index)
+    clk.__enter__()
+    try:
+        if graph:
+            dt = graph_timed(stream, step, steps, warmup, world)
+        else:
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                for i in range(warmup):
                     step(i)
-        e1.record(stream)
-        e1.synchronize()
-    torch.cuda.synchronize()
-    t = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    del g
-    return float(t.item()), clk.summary()
+                e0.record(stream)
+                for i in range(steps):
+                    step(warmup + i)
+                e1.record(stream)
+            e1.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device="cuda")
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+    finally:
+        clk.__exit__()
+    return dt, clk.summary()
 
 
 def run_stack(args, rank, world, local_rank):
@@ -592,39 +587,68 @@ def run_stack(args, rank, world, local_rank):
 
     if args.config == "ffn":
         # config 2: RMSNorm -> {gate, up} Q4_K -> SwiGLU -> down Q6_K + residual, M draft tokens
+        # (M in the hundreds or thousands: the batched prefill FFN).  One GPU: the library's FFN
+        # entry point.  N GPUs: rows sharded (shard.RowShardedFfn, two NCCL all-gathers per step)
         M = args.m or 8
         per_set = [synth.gen_weights(synth.TYPE_Q4_K, FFN_DIM, HIDDEN, 2001), synth.gen_weights(synth.TYPE_Q4_K, FFN_DIM, HIDDEN, 2002),
                    synth.gen_weights(synth.TYPE_Q6_K, HIDDEN, FFN_DIM, 2003)]
         wbytes = sum(w.nbytes for w in per_set)
-        n_sets = max(2, math.ceil(2.2 * L2_BYTES / wbytes))
-        sets = [(ctx.upload(per_set[0], synth.TYPE_Q4_K, FFN_DIM, HIDDEN), ctx.upload(per_set[1], synth.TYPE_Q4_K, FFN_DIM, HIDDEN),
-                 ctx.upload(per_set[2], synth.TYPE_Q6_K, HIDDEN, FFN_DIM)) for _ in range(n_sets)]
+        plan = shard.FfnShardPlan(HIDDEN, FFN_DIM, world)
+        c0, C = plan.inter(rank)
+        r0, R = plan.hid(rank)
+        local = [per_set[0][c0:c0 + C], per_set[1][c0:c0 + C], per_set[2][r0:r0 + R]]
+        rank_wbytes = sum(w.nbytes for w in local)
+        n_sets = max(2, math.ceil(2.2 * L2_BYTES / rank_wbytes))
+        shapes = [(synth.TYPE_Q4_K, C, HIDDEN), (synth.TYPE_Q4_K, C, HIDDEN), (synth.TYPE_Q6_K, R, FFN_DIM)]
+        sets = [tuple(ctx.upload(w, t, r, k) for w, (t, r, k) in zip(local, shapes)) for _ in range(n_sets)]
         x16 = synth.gen_activations(M, HIDDEN, 2004)
         gamma = (synth.gen_gamma(HIDDEN, 2005) * np.float16(0.1)).astype(np.float16)
-        x = torch.from_numpy(x16.view(np.uint16).copy()).to(dev)
+        x = torch.from_numpy(x16.view(np.uint16).copy()).to(dev).view(torch.float16).view(M, HIDDEN)
         gm = torch.from_numpy(gamma.view(np.uint16).copy()).to(dev)
         out = torch.zeros((M, HIDDEN), dtype=torch.float16, device=dev)
+        if world == 1:
+            def step(i):
+                g_, u_, d_ = sets[i % n_sets]
+                ctx.run_ffn_async(g_, u_, d_, M, x, gm, out)
+            launches = 4
+        else:
+            rk = shard.RowShardedFfn(ctx, plan, rank, M, dev)
+            tks = [rk.tasks(*st_, x) for st_ in sets]
 
-        def step(i):
-            g_, u_, d_ = sets[i % n_sets]
-            ctx.run_ffn_async(g_, u_, d_, M, x, gm, out)
+            def gather(o, i_):
+                dist.all_gather_into_tensor(o, i_)
+
+            def step(i):
+                gu, dn = tks[i % n_sets]
+                rk.forward(x, gm, out, gu, dn, gather)
+            launches = 6
 
         steps = args.steps
-        dt, clocks = time_device(stream, step, steps, max(3, args.warmup), gpu)
+        warmup = max(3, args.warmup)
+        dt, clocks = time_device(stream, step, steps, warmup, gpu, world=world)
         value = wbytes * steps / dt / 1e9
         ops = 2.0 * M * (2 * FFN_DIM * HIDDEN + HIDDEN * FFN_DIM)
-        # e2e: the blocking C-ABI call with host buffers
-        xp = np.ascontiguousarray(x16)
-        for _ in range(2):
-            ctx.run_ffn(sets[0][0], sets[0][1], sets[0][2], xp, gamma)
+        # e2e with host buffers: one GPU, the blocking C-ABI call kq_run_ffn; N GPUs, each rank
+        # copies the pinned input in, runs its sharded step and copies the assembled output out
         e2e_steps = min(steps, 200)
-        t0 = time.perf_counter()
-        for i in range(e2e_steps):
-            g_, u_, d_ = sets[i % n_sets]
-            ctx.run_ffn(g_, u_, d_, xp, gamma)
-        e2e_dt = time.perf_counter() - t0
+        if world == 1:
+            xp = np.ascontiguousarray(x16)
+            e2e_dt = e2e_timed(stream, lambda i: ctx.run_ffn(*sets[i % n_sets], xp, gamma), e2e_steps, 20, world)
+            e2e_api = "kq_run_ffn (host buffers, blocking)"
+        else:
+            xh = torch.from_numpy(x16.view(np.uint16).copy()).pin_memory()
+            oh = torch.zeros((M, HIDDEN), dtype=torch.float16).pin_memory()
+
+            def call(i):
+                with torch.cuda.stream(stream):
+                    x.view(torch.uint16).copy_(xh.view(M, HIDDEN), non_blocking=True)
+                    step(i)
+                    oh.copy_(out, non_blocking=True)
+                stream.synchronize()
+            e2e_dt = e2e_timed(stream, call, e2e_steps, 20, world)
+            e2e_api = "pinned input copied in, row-sharded step (library calls + NCCL), output copied out"
         cpu = None
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and rank == 0 and world == 1 and M <= 64:
             from oracle.oracle import Oracle
             O = Oracle()
             t0 = time.perf_counter()
@@ -634,23 +658,28 @@ def run_stack(args, rank, world, local_rank):
                    "sample": f"1 FFN block at M={M} through the oracle's C restatement of the reference's SDOT "
                              f"FFN sequence (ENG:8283-8298; its dispatch limit K <= 9216 excludes down, K = 9728)",
                    "seconds_per_step": sec}
+        per_rank = rank_wbytes * steps / dt / 1e9
         result = {
             "metric": METRIC_FFN, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
-            "warmup": max(3, args.warmup), "ms_per_step": round(dt / steps * 1e3, 6), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (seeded GGUF blocks per the benchmark configs' distributions; activations N(0,1) -> fp16)",
-            "config": {"workload": f"config2: tree-verify FFN block M={M}, hidden 2560, intermediate 9728",
-                       "m": M, "weight_bytes_per_step": wbytes, "tops": round(ops * steps / dt / 1e12, 3),
-                       "l2": f"{n_sets} rotating weight sets ({n_sets * wbytes / 2**20:.0f} MiB > 2x126 MB L2)",
-                       "parallelism": f"replicas x{world}",
-                       "timing": "CUDA graph of back-to-back kq_run_ffn_async steps, CUDA events"},
-            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak_hbm, "unit": "GB/s",
-                         "frac": round(value / peak_hbm, 4), "peak_source": peak_kind, "traffic": None},
+            "warmup": warmup, "ms_per_step": round(dt / steps * 1e3, 6), "higher_is_better": True,
+            "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "int8",
+            "data": DATA_DESC,
+            "config": {"workload": f"config2: FFN block M={M}, hidden 2560, intermediate 9728"
+                                   + (" (batched prefill FFN)" if M > 64 else " (tree verify)"),
+                       "m": M, "weight_bytes_per_step": wbytes, "weight_bytes_per_step_per_rank": rank_wbytes,
+                       "tops": round(ops * steps / dt / 1e12, 3),
+                       "l2": f"{n_sets} rotating weight sets per rank ({n_sets * rank_wbytes / 2**20:.0f} MiB > 2x126 MB L2)",
+                       "parallelism": "replicas x1" if world == 1 else f"row-shard x{world}",
+                       "timing": "CUDA graph: warm-up steps, event, timed steps, event"
+                                 + ("" if world == 1 else " (NCCL all-gathers captured); max over ranks")},
+            "roofline": {"bound": "hbm", "achieved": round(per_rank, 1), "peak": peak_hbm, "unit": "GB/s",
+                         "frac": round(per_rank / peak_hbm, 4), "peak_source": peak_kind, "traffic": None,
+                         "note": "weight bytes of this rank's share per step time (the whole block at 1 GPU)"},
             "cpu_baseline": cpu, "clocks": clocks,
             "e2e": {"value": round(wbytes * e2e_steps / e2e_dt / 1e9, 2), "unit": "GB/s", "steps": e2e_steps,
-                    "h2d_bytes_per_step": int(x16.nbytes + gamma.nbytes), "d2h_bytes_per_step": int(x16.nbytes),
-                    "api": "kq_run_ffn (host buffers, blocking)"},
-            "gpu_launches": steps * 5,
+                    "h2d_bytes_per_step": int(x16.nbytes + (gamma.nbytes if world == 1 else 0)),
+                    "d2h_bytes_per_step": int(x16.nbytes), "api": e2e_api},
+            "gpu_launches": steps * launches,
         }
         for st_ in sets:
             for w_ in st_:

@@ -26,9 +26,8 @@
 //    fold everything after one barrier (and, when the ring holds the whole share, wait for the
 //    stages once); otherwise the warp that completes a row group folds it (shared-memory
 //    counters).
-//    Under half an SM per CTA, the next kernel's CTA (programmatic dependent launch, enabled
-//    once this CTA has staged its activation) prefetches its weights during this one's
-//    arithmetic.
+//    Under half an SM per CTA, the next kernel's CTA (programmatic dependent launch, enabled at
+//    CTA start) prefetches its weights during this one's wait and arithmetic.
 //  * Every wait is bounded (globaltimer); on timeout the kernel records DEV_ERR_TIMEOUT,
 //    drains its own copies in flight (bounded) and returns.
 #include "kq_common.cuh"
@@ -767,10 +766,10 @@ __device__ __forceinline__ DbgOut make_dbg(const GemvParams &p, const GemvTaskDe
 
 // Sum the block terms of one (row, token) of local row group lr in order and write it.
 template <int MT>
-__device__ __forceinline__ void fold_one(const GemvParams &p, const float *tb, int J, int e, int rg,
-                                         unsigned long long *s_best) {
+__device__ __forceinline__ void fold_one(const GemvParams &p, const GemvTaskDev *tasks, const float *tb, int J, int e,
+                                         int rg, unsigned long long *s_best) {
     const int rr = e / MT, tok = e - rr * MT;
-    const GemvTaskDev &tk = p.task[task_of_rg(p, rg)];
+    const GemvTaskDev &tk = tasks[task_of_rg(p, rg)];
     const int r = (tk.rg_first + rg - tk.rg_start) * 16 + rr - tk.row_begin;
     if (tok >= p.M || r < 0 || r >= tk.rows) return;
     constexpr int ST = 16 * MT;
@@ -793,8 +792,8 @@ __device__ __forceinline__ void fold_one(const GemvParams &p, const float *tb, i
 // writes the results and clears the count for the next launch.  No CTA waits for another.
 // One warp.
 template <int MT>
-__device__ __forceinline__ void fold_shared(const GemvParams &p, float *tb, int J, int JU, int ua, int ub, int rg,
-                                            int lane, unsigned long long *s_best) {
+__device__ __forceinline__ void fold_shared(const GemvParams &p, const GemvTaskDev *tasks, float *tb, int J, int JU,
+                                            int ua, int ub, int rg, int lane, unsigned long long *s_best) {
     constexpr int E = 16 * MT;  // floats per term (16 rows x MT tokens): a multiple of 4
     const long long first = (long long)rg * p.nbu, G = gridDim.x, T = p.total_tiles;
     const int c_first = (int)(((first + 1) * G - 1) / T);     // CTA owning tile `first`
@@ -815,7 +814,7 @@ __device__ __forceinline__ void fold_shared(const GemvParams &p, float *tb, int 
         if (k < k0 || k >= k1) cp_async16_cg(tbs + 16u * (uint32_t)k, g4 + k);
     cp_async_wait_all();
     __syncwarp();
-    for (int e = lane; e < E; e += 32) fold_one<MT>(p, tb, J, e, rg, s_best);
+    for (int e = lane; e < E; e += 32) fold_one<MT>(p, tasks, tb, J, e, rg, s_best);
     __syncwarp();
     if (lane == 0) p.gcount[c_first] = 0;
 }
@@ -839,6 +838,9 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
     __shared__ unsigned long long s_best[8];
     __shared__ int s_abort, s_issued;
     __shared__ int s_done[kMaxTermSlots], s_folded[kMaxTermSlots];
+    // the tasks' fields, read per tile and per output row: from shared memory rather than by a
+    // run-time index into the kernel parameters
+    __shared__ GemvTaskDev s_task[4];
 
     uint8_t *ring = smem + p.off_stages;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.off_bars);  // full[S], empty[S], dead
@@ -870,6 +872,7 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
     const int n_lr = rg_hi - rg_lo;
     const int n_stages_cta = (n_tiles + T - 1) / T;
 
+    if (tid < 4 && tid < p.n_tasks) s_task[tid] = p.task[tid];
     if (tid < 8) s_best[tid] = 0ull;
     if (tid < kMaxTermSlots) {
         s_done[tid] = 0;
@@ -887,9 +890,11 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
     }
     __syncthreads();
 
-    // The next kernel in the stream may launch (programmatic dependent launch) once this CTA
-    // has staged its activation: its weight prefetch then overlaps this kernel's arithmetic
-    // instead of competing with this kernel's activation loads.
+    // The next kernel in the stream may launch (programmatic dependent launch) as soon as every
+    // CTA of this one is resident: it only streams its weights before its own griddepcontrol.wait,
+    // so its weight stream overlaps this kernel's wait, activation staging and arithmetic (a chain
+    // of such launches is then bound by the weight stream, not by the dependent-launch release).
+    pdl_launch_dependents();
     if (warp == W) {
         // ---------------- producer: the weight stream does not depend on earlier kernels
         const uint64_t policy = l2_evict_first_policy();
@@ -914,9 +919,17 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
         const int first = min(S, n_stages_cta);  // stages that need no free slot
         if (lane == 0)
             for (int s = 0; s < first; ++s) issue(s);
+        if (SMALL && n_stages_cta <= S && lane == 0) {
+            // the ring holds the whole share: wait for it here, while the consumers stage the
+            // activation, so they find every tile in place after the barrier below
+            for (int s = 0; s < n_stages_cta; ++s)
+                if (!mbar_wait_bounded(smem_u32(&bars[s]), 0, p.timeout_ns, p.status)) {
+                    s_abort = 1;
+                    break;
+                }
+        }
         __syncwarp();
-        __syncthreads();  // activation staged
-        pdl_launch_dependents();
+        __syncthreads();  // activation staged (and, all in, the weights landed)
         if (lane == 0) {
             for (int s = first; s < n_stages_cta; ++s) {
                 if (!mbar_wait_bounded(smem_u32(&bars[S + s % S]), ((s / S) - 1) & 1, p.timeout_ns, p.status)) {
@@ -935,22 +948,66 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
             if (!mbar_wait_bounded(smem_u32(&bars[2 * S]), 0, p.timeout_ns, p.status)) s_abort = 1;
         }
         __syncthreads();  // activation staged
-        pdl_launch_dependents();
 
-        // tile walk: tile i advances by W; stage/slot/phase, unit and row group incremental.  In a
-        // SMALL launch whose ring holds the whole share every stage was issued before the
-        // barrier above: wait for all of them once instead of per tile.
+        // tile walk: tile i advances by W; stage/slot/phase, unit and row group incremental.
         constexpr int TSTEP = W;
         const bool all_in = SMALL && n_stages_cta <= S;
+        const int JU = (TYPE == TYPE_Q8_0 && p.q80_exact) ? 8 : 1;  // terms per unit
+        bool any_dbg = false;
+        for (int k = 0; k < p.n_tasks; ++k) any_dbg |= s_task[k].dbg_sumi != nullptr;
+        // all in: the producer saw every stage land before the barrier above, so the loop has no
+        // waits; without a split each row group is folded by the warp that completes it (the
+        // row-group counters s_done), overlapping the folds with the other warps' tiles
+        const bool early_fold = all_in && !SPLIT && n_lr <= kMaxTermSlots;
         if (all_in) {
-            int ok = 1;
-            if (lane == 0)
-                for (int s2 = 0; s2 < n_stages_cta && ok; ++s2)
-                    ok = mbar_wait_bounded(smem_u32(&bars[s2]), 0, p.timeout_ns, p.status);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok && lane == 0) s_abort = 1;
+            int tt = warp, sg = 0;
+            while (tt >= T) {
+                tt -= T;
+                ++sg;
+            }
+            int u = u_first + warp, lr = 0;
+            while (u >= nbu) {
+                u -= nbu;
+                ++lr;
+            }
+            const bool go = !*reinterpret_cast<volatile int *>(&s_abort);
+            for (int i = warp; go && i < n_tiles; i += TSTEP) {
+                const uint8_t *tile = ring + sg * p.stage_bytes + tt * p.tile_bytes;
+                DbgOut db;
+                db.si = nullptr;
+                if (any_dbg) {
+                    const GemvTaskDev &tk = s_task[task_of_rg(p, rg_lo + lr)];
+                    if (tk.dbg_sumi) db = make_dbg(p, tk, rg_lo + lr, u, TYPE == TYPE_Q8_0);
+                }
+                float *tdst = terms + (lr * J + u * JU) * tstride;
+                compute_item<TYPE, MT>(p, tile, u, smem, lane, tdst, db);
+                __syncwarp();
+                if (early_fold) {
+                    int last = 0;
+                    if (lane == 0) {
+                        __threadfence_block();
+                        last = atomicAdd(&s_done[lr], 1) == nbu - 1;
+                    }
+                    last = __shfl_sync(0xffffffffu, last, 0);
+                    if (last) {
+                        __threadfence_block();
+                        for (int e = lane; e < 16 * MT; e += 32)
+                            fold_one<MT>(p, s_task, terms + (size_t)lr * J * tstride, J, e, rg_lo + lr, s_best);
+                    }
+                }
+                tt += TSTEP;
+                while (tt >= T) {
+                    tt -= T;
+                    ++sg;
+                }
+                u += TSTEP;
+                while (u >= nbu) {
+                    u -= nbu;
+                    ++lr;
+                }
+            }
         }
-        int i = warp;
+        int i = all_in ? n_tiles : warp;
         int tt = i, sg = 0, slot = 0, ph = 0;
         while (tt >= T) {
             tt -= T;
@@ -966,7 +1023,6 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
             ++lr;
         }
         int ts = lr % TS, use = lr / TS;
-        const int JU = (TYPE == TYPE_Q8_0 && p.q80_exact) ? 8 : 1;  // terms per unit
         for (; i < n_tiles; i += TSTEP) {
             if (*reinterpret_cast<volatile int *>(&s_abort)) break;
             if (!all_in) {
@@ -984,7 +1040,7 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
             }
             const uint8_t *tile = ring + slot * p.stage_bytes + tt * p.tile_bytes;
             const int rg = rg_lo + lr;
-            const GemvTaskDev &tk = p.task[task_of_rg(p, rg)];
+            const GemvTaskDev &tk = s_task[task_of_rg(p, rg)];
             DbgOut db;
             db.si = nullptr;
             if (tk.dbg_sumi) db = make_dbg(p, tk, rg, u, TYPE == TYPE_Q8_0);
@@ -1009,9 +1065,9 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
                     // fold the row group: block terms in order, then the epilogue
                     __threadfence_block();
                     float *tb = terms + ts * J * tstride;
-                    if (SPLIT && (ua > 0 || ub < nbu)) fold_shared<MT>(p, tb, J, JU, ua, ub, rg, lane, s_best);
+                    if (SPLIT && (ua > 0 || ub < nbu)) fold_shared<MT>(p, s_task, tb, J, JU, ua, ub, rg, lane, s_best);
                     else
-                        for (int e = lane; e < 16 * MT; e += 32) fold_one<MT>(p, tb, J, e, rg, s_best);
+                        for (int e = lane; e < 16 * MT; e += 32) fold_one<MT>(p, s_task, tb, J, e, rg, s_best);
                     __syncwarp();
                     if (lane == 0) {
                         __threadfence_block();
@@ -1038,7 +1094,7 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
                 }
             }
         }
-        if (SMALL) {
+        if (SMALL && !early_fold) {
             // ---------------- fold all row groups of the share
             named_bar_sync(1, W * 32);
             const int E = 16 * MT;
@@ -1046,13 +1102,13 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
             for (int idx = tid; idx < n_lr * E; idx += W * 32) {
                 const int l = idx / E, e = idx - l * E;
                 if ((l == 0 && part0) || (l == n_lr - 1 && part1)) continue;
-                fold_one<MT>(p, terms + (size_t)l * J * tstride, J, e, rg_lo + l, s_best);
+                fold_one<MT>(p, s_task, terms + (size_t)l * J * tstride, J, e, rg_lo + l, s_best);
             }
             if (part0 && warp == 0)
-                fold_shared<MT>(p, terms, J, JU, u_first, n_lr == 1 ? u_end : nbu, rg_lo, lane, s_best);
+                fold_shared<MT>(p, s_task, terms, J, JU, u_first, n_lr == 1 ? u_end : nbu, rg_lo, lane, s_best);
             if (part1 && (n_lr > 1 || !part0) && warp == (W > 1 ? 1 : 0))
-                fold_shared<MT>(p, terms + (size_t)(n_lr - 1) * J * tstride, J, JU, 0, u_end, rg_hi - 1, lane,
-                                s_best);
+                fold_shared<MT>(p, s_task, terms + (size_t)(n_lr - 1) * J * tstride, J, JU, 0, u_end, rg_hi - 1,
+                                lane, s_best);
         }
     }
     __syncthreads();
@@ -1060,7 +1116,8 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
     // drain: a slot's most recent copy must land before the CTA exits (matters only after an
     // early stop); consumers never arrive on full barriers, so the last S issued stages are
     // exactly the outstanding candidates
-    if (tid == 0) {
+    // (without an early stop the consumers waited for every issued stage already)
+    if (tid == 0 && s_abort) {
         const int issued = s_issued;
         for (int s = max(0, issued - S); s < issued; ++s)
             mbar_wait_bounded(smem_u32(&bars[s % S]), (s / S) & 1, p.timeout_ns, p.status);

@@ -48,3 +48,152 @@ def gather_argmax_torch(vals, rows, group=None):
     dist.all_gather_into_tensor(out, pair, group=group)
     o = out.cpu().numpy().reshape(world, 2, -1)
     return merge_argmax(o[:, 0, :], o[:, 1, :].astype(np.int64))
+
+
+# ---------------------------------------------------------------------------- FFN row sharding
+
+def balanced_split(n: int, world: int) -> list[tuple[int, int]]:
+    """(first, count) of each rank's contiguous share of n items; the first n % world ranks take
+    one more."""
+    q, r = divmod(n, world)
+    out, first = [], 0
+    for k in range(world):
+        c = q + (1 if k < r else 0)
+        out.append((first, c))
+        first += c
+    return out
+
+
+class FfnShardPlan:
+    """Row sharding of the FFN block x_out = x + W_down . swiglu(W_gate . xn, W_up . xn),
+    xn = rmsnorm(x) (the engine's SDOT FFN sequence, src/v182_r22_breakthrough_engine.c:8283-8298),
+    over `world` ranks, one process per GPU:
+
+      * rank r owns intermediate values [inter_first, inter_first + inter_count) in whole
+        256-value blocks -- those rows of W_gate and W_up, so its SwiGLU inputs are local -- and
+        quantizes its slice of the SwiGLU output to Q8_K itself: Q8_K blocks are independent
+        (one scale per 256 values), so the slices concatenate to the full row's Q8_K;
+      * one all-gather of the Q8_K blocks (292 bytes per 256 values, every rank padded to the
+        largest share) gives every rank the whole intermediate activation;
+      * rank r owns hidden rows [hid_first, hid_first + hid_count) of W_down in whole 16-row
+        groups (the device tile height) and writes that slice of x_out (residual added), and a
+        second all-gather assembles x_out.
+
+    Every output value is computed by exactly the operations of the unsharded block, so the
+    sharded result is bit-identical to it."""
+
+    def __init__(self, hidden: int, ffn: int, world: int):
+        if hidden % 256 or ffn % 256:
+            raise ValueError("hidden and ffn must be multiples of 256")
+        self.hidden, self.ffn, self.world = hidden, ffn, world
+        self.inter_blocks = [(f, c) for f, c in balanced_split(ffn // 256, world)]
+        self.hid_groups = [(f, c) for f, c in balanced_split(hidden // 16, world)]
+        self.inter_max = max(c for _, c in self.inter_blocks)        # blocks per rank, padded
+        self.hid_max = max(c for _, c in self.hid_groups) * 16       # hidden rows per rank, padded
+
+    def inter(self, rank: int) -> tuple[int, int]:
+        """(first value, values) of rank's intermediate slice"""
+        f, c = self.inter_blocks[rank]
+        return f * 256, c * 256
+
+    def hid(self, rank: int) -> tuple[int, int]:
+        """(first row, rows) of rank's hidden slice of W_down / x_out"""
+        f, c = self.hid_groups[rank]
+        return f * 16, c * 16
+
+    def inter_index(self) -> np.ndarray:
+        """positions, in the gathered [world * inter_max] block axis, of blocks 0 .. ffn/256 - 1"""
+        return np.concatenate([r * self.inter_max + np.arange(c) for r, (_, c) in enumerate(self.inter_blocks)])
+
+    def hid_index(self) -> np.ndarray:
+        """positions, in the gathered [world * hid_max] column axis, of hidden columns 0 .. hidden - 1"""
+        return np.concatenate([r * self.hid_max + np.arange(c * 16) for r, (_, c) in enumerate(self.hid_groups)])
+
+
+class RowShardedFfn:
+    """One rank's part of the row-sharded FFN block on its GPU (plan: FfnShardPlan).  The rank holds
+    its rows of W_gate / W_up / W_down (kq Weight objects of plan.inter(rank)[1] / plan.hid(rank)[1]
+    rows) and preallocated buffers, so a step allocates nothing and can be captured in a CUDA graph
+    together with the collectives.  A step (forward):
+
+      1. RMSNorm + Q8_K of the whole input rows (every rank);
+      2. its gate / up rows (one dispatch, two tasks) -> fp16 [M, C];
+      3. SwiGLU + Q8_K of its slice -> send buffer of M * inter_max Q8_K blocks;
+      4. all-gather of the send buffers, then the Q8_K blocks put in row order (one index_select);
+      5. its rows of W_down with the residual -> fp16 send buffer [M, hid_max];
+      6. all-gather, then the output columns put in row order into y.
+
+    all_gather(out, inp) is torch.distributed.all_gather_into_tensor (NCCL) on real ranks; a test
+    may pass a function that emulates it.  Everything -- the library calls, the index gathers and
+    the collectives -- is ordered on the context's CUDA stream."""
+
+    def __init__(self, ctx, plan: FfnShardPlan, rank: int, M: int, device):
+        import torch
+        self.ctx, self.plan, self.rank, self.M = ctx, plan, rank, M
+        hid, ffn, W = plan.hidden, plan.ffn, plan.world
+        self.c0, self.C = plan.inter(rank)
+        self.r0, self.R = plan.hid(rank)
+        u8, f16 = torch.uint8, torch.float16
+        self.xn = torch.empty((M, hid), dtype=f16, device=device)
+        self.q_x = torch.empty((M * (hid // 256) * 292,), dtype=u8, device=device)
+        self.g = torch.empty((M, self.C), dtype=f16, device=device)
+        self.u = torch.empty((M, self.C), dtype=f16, device=device)
+        self.h_send = torch.zeros((M * plan.inter_max * 292,), dtype=u8, device=device)
+        self.h_all = torch.zeros((W * M * plan.inter_max * 292,), dtype=u8, device=device)
+        self.h_full = torch.empty((M * (ffn // 256) * 292,), dtype=u8, device=device)
+        self.o_send = torch.zeros((M, plan.hid_max), dtype=f16, device=device)
+        self.o_all = torch.zeros((W * M * plan.hid_max,), dtype=f16, device=device)
+        # block (m, j) of the intermediate: rank r's send buffer holds its blocks row-major
+        # [M][count_r] from offset 0 (SwiGLU writes its Q8_K rows contiguously)
+        idx = np.empty((M, ffn // 256), np.int64)
+        for r, (first, cnt) in enumerate(plan.inter_blocks):
+            for m in range(M):
+                idx[m, first:first + cnt] = r * M * plan.inter_max + m * cnt + np.arange(cnt)
+        self.h_idx = torch.from_numpy(idx.reshape(-1)).to(device)
+        # column c of output row m: rank r's send buffer is [M][hid_max] with its rows first
+        oidx = np.empty((M, hid), np.int64)
+        for r, (first, cnt) in enumerate(plan.hid_groups):
+            for m in range(M):
+                oidx[m, first * 16:(first + cnt) * 16] = (r * M + m) * plan.hid_max + np.arange(cnt * 16)
+        self.o_idx = torch.from_numpy(oidx.reshape(-1)).to(device)
+
+    def tasks(self, gate, up, down, x):
+        """kq task arrays of one weight set (its row slices) for input/residual x [M, hidden]"""
+        ctx = self.ctx
+        gu = ctx.make_tasks([dict(w=gate, dst=self.g, dst_stride=self.C), dict(w=up, dst=self.u, dst_stride=self.C)])
+        dn = ctx.make_tasks([dict(w=down, dst=self.o_send, dst_stride=self.plan.hid_max,
+                                  residual=x[:, self.r0:], res_stride=self.plan.hidden)])
+        return gu, dn
+
+    def part1(self, x, gamma, gu_tasks):
+        M, hid, ctx = self.M, self.plan.hidden, self.ctx
+        ctx.rmsnorm_q8k_async(x, gamma, self.xn, M, hid, self.q_x)
+        ctx.gemm_multi_q8_async(self.q_x, None, M, hid, gu_tasks)
+        ctx.swiglu_q8k_async(self.g, self.u, M, self.C, self.h_send)
+
+    def _on_ctx_stream(self):
+        import torch
+        return torch.cuda.stream(torch.cuda.ExternalStream(self.ctx.stream, device=self.h_idx.device))
+
+    def assemble_inter(self):
+        import torch
+        with self._on_ctx_stream():
+            torch.index_select(self.h_all.view(-1, 292), 0, self.h_idx, out=self.h_full.view(-1, 292))
+
+    def part2(self, dn_tasks):
+        self.ctx.gemm_multi_q8_async(self.h_full, None, self.M, self.plan.ffn, dn_tasks)
+
+    def assemble_out(self, y):
+        import torch
+        with self._on_ctx_stream():
+            torch.index_select(self.o_all, 0, self.o_idx, out=y.view(-1))
+
+    def forward(self, x, gamma, y, gu_tasks, dn_tasks, all_gather):
+        self.part1(x, gamma, gu_tasks)
+        with self._on_ctx_stream():
+            all_gather(self.h_all, self.h_send)
+        self.assemble_inter()
+        self.part2(dn_tasks)
+        with self._on_ctx_stream():
+            all_gather(self.o_all, self.o_send.view(-1))
+        self.assemble_out(y)

@@ -149,3 +149,82 @@ def test_sharded_lm_head_gloo_4_ranks_empty_slice():
     ref_vals = full[np.arange(3), full.argmax(axis=1)].tolist()
     for _, _, r, v in got:
         assert r == ref_rows and v == ref_vals
+
+
+# ---------------------------------------------------------------------------- FFN row sharding
+
+FFN_HIDDEN, FFN_DIM, FFN_M = 512, 1280, 3  # 5 intermediate blocks: uneven shares at 2 and 4 ranks
+
+
+def _ffn_inputs():
+    wg = synth.gen_weights(synth.TYPE_Q4_K, FFN_DIM, FFN_HIDDEN, seed=71)
+    wu = synth.gen_weights(synth.TYPE_Q4_K, FFN_DIM, FFN_HIDDEN, seed=72)
+    wd = synth.gen_weights(synth.TYPE_Q6_K, FFN_HIDDEN, FFN_DIM, seed=73)
+    x = synth.gen_activations(FFN_M, FFN_HIDDEN, seed=74)
+    gamma = (synth.gen_gamma(FFN_HIDDEN, 75).astype(np.float32) * 0.1).astype(np.float16)
+    return wg, wu, wd, x, gamma
+
+
+def _ffn_rank_main(rank, world, port, q):
+    """One rank of the row-sharded FFN block with the oracle for the products: its gate/up rows,
+    SwiGLU and Q8_K of its intermediate slice, an all-gather of the Q8_K blocks, its rows of down
+    with the residual, an all-gather of the output slices."""
+    import torch
+    import torch.distributed as dist
+    from oracle.oracle import Oracle, Q8K_DTYPE
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        O = Oracle()
+        wg, wu, wd, x, gamma = _ffn_inputs()
+        plan = shard.FfnShardPlan(FFN_HIDDEN, FFN_DIM, world)
+        M = FFN_M
+        _, xq = O.rmsnorm(x, gamma)                                   # every rank: the whole row
+        c0, C = plan.inter(rank)
+        g = O.epilogue_f16(O.gemm(synth.TYPE_Q4_K, wg[c0:c0 + C], FFN_HIDDEN, xq))
+        u = O.epilogue_f16(O.gemm(synth.TYPE_Q4_K, wu[c0:c0 + C], FFN_HIDDEN, xq))
+        _, hq = O.swiglu(g, u)                                         # Q8_K of this slice
+        pad = np.zeros((M, plan.inter_max), Q8K_DTYPE)
+        pad[:, :C // 256] = hq
+        got = torch.zeros((world * M, plan.inter_max * 292), dtype=torch.uint8)
+        dist.all_gather_into_tensor(got, torch.from_numpy(pad.view(np.uint8).reshape(M, -1).copy()))
+        blocks = got.view(world, M, plan.inter_max, 292).permute(1, 0, 2, 3).reshape(M, -1, 292)
+        h_full = np.ascontiguousarray(blocks[:, torch.from_numpy(plan.inter_index())].numpy()).view(Q8K_DTYPE)
+        h_full = h_full.reshape(M, FFN_DIM // 256)
+        r0, R = plan.hid(rank)
+        part = O.epilogue_f16(O.gemm(synth.TYPE_Q6_K, wd[r0:r0 + R], FFN_DIM, h_full),
+                              np.ascontiguousarray(x[:, r0:r0 + R]))
+        opad = np.zeros((M, plan.hid_max), np.float16)
+        opad[:, :R] = part
+        go = torch.zeros((world * M, plan.hid_max * 2), dtype=torch.uint8)  # fp16 bytes
+        dist.all_gather_into_tensor(go, torch.from_numpy(opad.view(np.uint8).copy()))
+        cols = go.view(world, M, plan.hid_max, 2).permute(1, 0, 2, 3).reshape(M, -1, 2)
+        out = np.ascontiguousarray(cols[:, torch.from_numpy(plan.hid_index())].numpy())
+        q.put((rank, C, R, out.tobytes()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_row_sharded_ffn_gloo(world):
+    """The FFN block row-sharded over 2 / 4 CPU ranks (uneven intermediate shares, padded
+    all-gathers) reassembles the single-process oracle result bit for bit on every rank."""
+    import torch.multiprocessing as mp
+    from oracle.oracle import Oracle
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ffn_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+        assert p.exitcode == 0
+    got = [q.get(timeout=10) for _ in range(world)]
+    wg, wu, wd, x, gamma = _ffn_inputs()
+    ref = Oracle().ffn(wg, synth.TYPE_Q4_K, wu, synth.TYPE_Q4_K, wd, synth.TYPE_Q6_K, FFN_HIDDEN, FFN_DIM, x, gamma)
+    plan = shard.FfnShardPlan(FFN_HIDDEN, FFN_DIM, world)
+    assert sorted(c for _, c, _, _ in got) == sorted(plan.inter(r)[1] for r in range(world))
+    assert len({c for _, c, _, _ in got}) == 2  # the shares really are uneven
+    for _, _, _, b in got:
+        assert b == ref.view(np.uint16).tobytes()
