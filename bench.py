@@ -685,154 +685,220 @@ def run_stack(args, rank, world, local_rank):
             for w_ in st_:
                 w_.free()
 
-    elif args.config == "prefill":
-        # config 3: every GEMM of a 36-layer Q4_K_M stack at M tokens (activations pre-quantized)
-        M = args.m or 2048
+    elif args.config in ("prefill", "decode"):
+        # configs 3 and 4: the decoder stack's matrix products chained layer by layer through the
+        # producers.  Per layer: RMSNorm + Q8_K (and Q8_0 for Q8_0 weights) -> q / k / v (one
+        # dispatch) -> o over q's output with the residual (the attention core is outside the
+        # path, so q's output stands in for its result) -> the FFN block (RMSNorm, gate / up,
+        # SwiGLU, down + residual).  Config 3 (prefill, M tokens): at N GPUs the FFN rows are
+        # sharded (shard.RowShardedFfn), the projections replicated.  Config 4 (decode, 64
+        # sequences): the sequences split over the ranks, then the final RMSNorm, an all-gather of
+        # the normalised rows, each rank's vocabulary slice of the LM head for all rows, and the
+        # per-row (value, row) pairs all-gathered and merged on the device.
+        prefill = args.config == "prefill"
+        kind = "prefill" if prefill else "decode"
         L = args.layers
-        layout = stack_layout("prefill")
-        host = {n: synth.gen_weights(t, r, k, 3000 + i) for i, (n, t, r, k) in enumerate(layout)}
-        layers = [{n: ctx.upload(host[n], t, r, k) for (n, t, r, k) in layout} for _ in range(L)]
-        acts = {}
-        for K_ in (HIDDEN, Q_DIM, FFN_DIM):
-            x16 = torch.from_numpy(synth.gen_activations(M, K_, 3100 + K_).view(np.uint16).copy()).to(dev)
-            acts[K_] = qact(x16, M, K_, synth.TYPE_Q4_K)[0]
-        outs = {n: torch.zeros((M, r), dtype=torch.float16, device=dev) for (n, t, r, k) in layout}
-        groups = [(["q", "k", "v"], HIDDEN), (["o"], Q_DIM), (["gate", "up"], HIDDEN), (["down"], FFN_DIM)]
-        task_sets = [[(ctx.make_tasks([dict(w=lay[n], dst=outs[n]) for n in names]), K_) for names, K_ in groups]
-                     for lay in layers]
-
-        def step(i):
-            for ts in task_sets:
-                for tasks, K_ in ts:
-                    ctx.gemm_multi_q8_async(acts[K_], None, M, K_, tasks)
-
-        steps = args.steps
-        dt, clocks = time_device(stream, step, steps, max(3, args.warmup), gpu, graph=False)
-        ops = 2.0 * M * sum(r * k for (_, _, r, k) in layout) * L
-        value = ops * steps / dt / 1e12
-        peak_int8 = 2.0 * measured_bf16()
-        cpu = None
-        if not args.no_cpu_baseline:
-            from oracle.oracle import Reference, reference_available, Oracle
-            rows_s, Ms = 256, 32
-            w_s = host["gate"][:rows_s]
-            act_s = Oracle().quantize_q8k(synth.gen_activations(Ms, HIDDEN, 3200))
-            if reference_available():
-                R = Reference()
-                t0 = time.perf_counter()
-                R.gemm(synth.TYPE_Q4_K, w_s, HIDDEN, act_s)
-                sec = time.perf_counter() - t0
-                kind, smp = "reference", (f"{rows_s} gate rows x {Ms} tokens through the reference's own row "
-                                          f"kernels (sdot_row_q4_k_batch, scalar x86), 1 thread")
-            else:
-                O = Oracle()
-                t0 = time.perf_counter()
-                O.gemm(synth.TYPE_Q4_K, w_s, HIDDEN, act_s)
-                sec = time.perf_counter() - t0
-                kind, smp = "port", f"{rows_s} gate rows x {Ms} tokens through the oracle, 1 thread"
-            cpu = {"value": round(2.0 * rows_s * HIDDEN * Ms / sec / 1e12, 6), "unit": "TOPS", "cores": 1,
-                   "kind": kind, "sample": smp}
-        result = {
-            "metric": METRIC_PREFILL, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": steps,
-            "warmup": max(3, args.warmup), "ms_per_step": round(dt / steps * 1e3, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (seeded GGUF blocks per the benchmark configs' distributions; activations N(0,1) -> Q8_K)",
-            "config": {"workload": f"config3: prefill GEMMs of a {L}-layer Q4_K_M stack (q/k/o/gate/up Q4_K, v/down Q6_K) at M={M}",
-                       "m": M, "layers": L, "ops_per_step": ops,
-                       "l2": f"inputs larger than L2: {L} layers x {sum(h.nbytes for h in host.values()) / 2**20:.0f} MiB of weights",
-                       "parallelism": f"replicas x{world}",
-                       "timing": "eager launches of all layers per step, CUDA events"},
-            "roofline": {"bound": "tensor", "achieved": round(value, 2), "peak": round(peak_int8, 1), "unit": "TOPS",
-                         "frac": round(value / peak_int8, 4),
-                         "peak_source": "2 x measured dense bf16 TF/s (int8 runs at twice the bf16 rate)",
-                         "traffic": None},
-            "cpu_baseline": cpu, "clocks": clocks, "e2e": None,
-            "gpu_launches": steps * L * 7 * 2,
-        }
-        for lay in layers:
-            for w_ in lay.values():
-                w_.free()
-
-    else:
-        # config 4: 64 sequences, one token each per step, split over the ranks; every rank runs the
-        # 36-layer stack for its rows, then the hidden rows are all-gathered, each rank computes its
-        # vocabulary slice of the LM head for all 64 rows, and the per-row argmax keys are all-gathered
         SEQ = 64
-        L = args.layers
-        Mr = SEQ // world
-        layout = stack_layout("decode")
-        host = {n: synth.gen_weights(t, r, k, 4000 + i) for i, (n, t, r, k) in enumerate(layout)}
-        layers = [{n: ctx.upload(host[n], t, r, k) for (n, t, r, k) in layout} for _ in range(L)]
-        v0, vrows = shard.vocab_slice(rank, world, VOCAB)
-        lm = ctx.upload(synth.gen_weights(synth.TYPE_Q6_K, VOCAB, HIDDEN, 4100)[v0:v0 + vrows], synth.TYPE_Q6_K, vrows, HIDDEN)
-        acts = {}
-        for K_ in (HIDDEN, Q_DIM, FFN_DIM):
-            x16 = torch.from_numpy(synth.gen_activations(Mr, K_, 4200 + K_ + rank).view(np.uint16).copy()).to(dev)
-            acts[K_] = (qact(x16, Mr, K_, synth.TYPE_Q5_K)[0], qact(x16, Mr, K_, synth.TYPE_Q8_0)[1])
-        outs = {n: torch.zeros((Mr, r), dtype=torch.float16, device=dev) for (n, t, r, k) in layout}
-        groups = [(["q", "k", "v"], HIDDEN), (["o"], Q_DIM), (["gate", "up"], HIDDEN), (["down"], FFN_DIM)]
-        task_sets = [[(ctx.make_tasks([dict(w=lay[n], dst=outs[n]) for n in names]), K_) for names, K_ in groups]
-                     for lay in layers]
-        hid = torch.from_numpy(synth.gen_activations(Mr, HIDDEN, 4300 + rank).view(np.uint16).copy()).to(dev)
-        hid_all = torch.zeros((SEQ, HIDDEN), dtype=torch.float16, device=dev)
-        toks = torch.zeros((SEQ,), dtype=torch.int32, device=dev)
-        vals = torch.zeros((SEQ,), dtype=torch.float32, device=dev)
-        pair = torch.zeros((SEQ, 2), dtype=torch.float32, device=dev)
-        pair_all = torch.zeros((world, SEQ, 2), dtype=torch.float32, device=dev)
+        M = (args.m or 2048) if prefill else SEQ // world
+        sharded_ffn = prefill and world > 1
+        layout = stack_layout(kind)
+        host = {n: synth.gen_weights(t, r, k, (3000 if prefill else 4000) + i) for i, (n, t, r, k) in enumerate(layout)}
+        types = {n: t for (n, t, r, k) in layout}
+        plan = shard.FfnShardPlan(HIDDEN, FFN_DIM, world)
+        c0, C = plan.inter(rank)
+        r0, R = plan.hid(rank)
+        rank_wbytes = 0
+        layers = []
+        for _ in range(L):
+            lay = {}
+            for (n, t, r, k) in layout:
+                w_ = host[n]
+                if sharded_ffn and n in ("gate", "up"):
+                    w_, r = w_[c0:c0 + C], C
+                elif sharded_ffn and n == "down":
+                    w_, r = w_[r0:r0 + R], R
+                lay[n] = ctx.upload(w_, t, r, k)
+                rank_wbytes += w_.nbytes
+            layers.append(lay)
+        g_attn = torch.from_numpy((synth.gen_gamma(HIDDEN, 3900) * np.float16(0.1)).astype(np.float16).view(np.uint16).copy()).to(dev)
+        g_ffn = torch.from_numpy((synth.gen_gamma(HIDDEN, 3901) * np.float16(0.1)).astype(np.float16).view(np.uint16).copy()).to(dev)
+        f16 = torch.float16
+        h_a = torch.zeros((M, HIDDEN), dtype=f16, device=dev)
+        h_b = torch.zeros_like(h_a)
+        h_mid = torch.zeros_like(h_a)
+        xn = torch.zeros_like(h_a)
+        qx = torch.zeros(kq.q8k_bytes(M, HIDDEN), dtype=torch.uint8, device=dev)
+        need_q80 = any(types[n] == synth.TYPE_Q8_0 for n in ("q", "k", "v"))
+        qx0 = torch.zeros(kq.q8_0_bytes(M, HIDDEN), dtype=torch.uint8, device=dev) if need_q80 else None
+        qo = torch.zeros((M, Q_DIM), dtype=f16, device=dev)
+        ko = torch.zeros((M, KV_DIM), dtype=f16, device=dev)
+        vo = torch.zeros((M, KV_DIM), dtype=f16, device=dev)
+        x_host = synth.gen_activations(M, HIDDEN, (3100 if prefill else 4300) + rank)
+        x_dev = torch.from_numpy(x_host.view(np.uint16).copy()).to(dev).view(f16).view(M, HIDDEN)
+        qkv = [ctx.make_tasks([dict(w=lay["q"], dst=qo), dict(w=lay["k"], dst=ko), dict(w=lay["v"], dst=vo)])
+               for lay in layers]
+        o_tasks = [[ctx.make_tasks([dict(w=lay["o"], dst=dst, residual=src)]) for (src, dst) in ((h_a, h_mid), (h_b, h_mid))]
+                   for lay in layers]
+        rk = None
+        if sharded_ffn:
+            rk = shard.RowShardedFfn(ctx, plan, rank, M, dev)
+            ffn_tasks = [[rk.tasks(lay["gate"], lay["up"], lay["down"], h_mid)] for lay in layers]
 
-        def step(i):
-            for ts in task_sets:
-                for tasks, K_ in ts:
-                    ctx.gemm_multi_q8_async(acts[K_][0], acts[K_][1], Mr, K_, tasks)
-            if world > 1:
-                dist.all_gather_into_tensor(hid_all, hid.view(torch.float16))
-            else:
-                hid_all.copy_(hid.view(torch.float16))
-            ctx.lm_head_argmax_async(lm, hid_all, SEQ, None, None, toks, vals)
-            if world > 1:
-                pair[:, 0] = vals
-                pair[:, 1] = (toks + v0).float()
-                dist.all_gather_into_tensor(pair_all, pair)
+            def gather(o, i_):
+                dist.all_gather_into_tensor(o, i_)
+
+        def run_layers():
+            src, dst = h_a, h_b
+            for li, lay in enumerate(layers):
+                ctx.rmsnorm_q8k_async(src, g_attn, xn, M, HIDDEN, qx)
+                if need_q80:
+                    ctx.quantize_q8_0_async(xn, M, HIDDEN, qx0)
+                ctx.gemm_multi_q8_async(qx, qx0, M, HIDDEN, qkv[li])
+                ctx.gemm_multi_async(qo, M, Q_DIM, o_tasks[li][0 if src is h_a else 1])
+                if rk is not None:
+                    gu, dn = ffn_tasks[li][0]
+                    rk.forward(h_mid, g_ffn, dst, gu, dn, gather)
+                else:
+                    ctx.run_ffn_async(lay["gate"], lay["up"], lay["down"], M, h_mid, g_ffn, dst)
+                src, dst = dst, src
+            return src
+
+        if prefill:
+            def step(i):
+                h_a.copy_(x_dev)
+                run_layers()
+            launches_per_step = L * (5 + (7 if sharded_ffn else 4)) + 1
+        else:
+            v0, vrows = shard.vocab_slice(rank, world, VOCAB)
+            lm_host = synth.gen_weights(synth.TYPE_Q6_K, VOCAB, HIDDEN, 4100)[v0:v0 + vrows]
+            lm = ctx.upload(lm_host, synth.TYPE_Q6_K, vrows, HIDDEN)
+            rank_wbytes += lm_host.nbytes
+            g_out = torch.from_numpy((synth.gen_gamma(HIDDEN, 3902) * np.float16(0.1)).astype(np.float16).view(np.uint16).copy()).to(dev)
+            nrm = torch.zeros((M, HIDDEN), dtype=f16, device=dev)
+            nrm_all = torch.zeros((SEQ, HIDDEN), dtype=f16, device=dev)
+            toks = torch.zeros((SEQ,), dtype=torch.int32, device=dev)
+            vals = torch.zeros((SEQ,), dtype=torch.float32, device=dev)
+            pair = torch.zeros((2, SEQ), dtype=torch.float32, device=dev)
+            pair_all = torch.zeros((world * 2, SEQ), dtype=torch.float32, device=dev)
+            best = torch.zeros((SEQ,), dtype=torch.int64, device=dev)
+            cols = torch.arange(SEQ, device=dev)
+
+            def step(i):
+                h_a.copy_(x_dev)
+                last = run_layers()
+                ctx.rmsnorm_q8k_async(last, g_out, nrm, M, HIDDEN, qx)   # final norm of this rank's rows
+                if world > 1:
+                    dist.all_gather_into_tensor(nrm_all, nrm)
+                else:
+                    nrm_all.copy_(nrm)
+                ctx.lm_head_argmax_async(lm, nrm_all, SEQ, None, None, toks, vals)
+                pair[0].copy_(vals)
+                pair[1].copy_((toks + v0).float())          # global rows (< 2^24: exact in fp32)
+                if world > 1:
+                    dist.all_gather_into_tensor(pair_all, pair)
+                else:
+                    pair_all.copy_(pair)
+                pv = pair_all.view(world, 2, SEQ)
+                r_ = torch.argmax(pv[:, 0, :], dim=0)       # first rank with the maximum = first row
+                best.copy_(pv[:, 1, :][r_, cols].long())
+            launches_per_step = L * (5 + 4 + (1 if need_q80 else 0)) + 4
 
         steps = args.steps
-        dt, clocks = time_device(stream, step, steps, max(3, args.warmup), gpu, graph=False, world=world)
-        value = SEQ * steps / dt
-        wbytes = sum(h.nbytes for h in host.values()) * L + lm.device_bytes
+        warmup = max(3, args.warmup)
+        dt, clocks = time_device(stream, step, steps, warmup, gpu, graph=not prefill, world=world)
+        # e2e with host buffers: the step's input rows copied in from pinned memory, the result
+        # (prefill: the last hidden rows; decode: the 64 next tokens) copied out
+        xh = torch.from_numpy(x_host.view(np.uint16).copy()).pin_memory()
+        if prefill:
+            oh = torch.zeros((M, HIDDEN), dtype=torch.float16).pin_memory()
+            d2h = M * HIDDEN * 2
+        else:
+            oh = torch.zeros((SEQ,), dtype=torch.int64).pin_memory()
+            d2h = SEQ * 8
+
+        def call(i):
+            with torch.cuda.stream(stream):
+                x_dev.view(torch.uint16).copy_(xh.view(M, HIDDEN), non_blocking=True)
+                step(i)
+                oh.copy_(h_a if (prefill and L % 2 == 0) else (h_b if prefill else best), non_blocking=True)
+            stream.synchronize()
+        e2e_steps = max(1, min(steps, 3 if prefill else 20))
+        e2e_dt = e2e_timed(stream, call, e2e_steps, 1, world)
+        ops = 2.0 * (M * world if not prefill else M) * sum(r * k for (_, _, r, k) in layout) * L
         cpu = None
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            from oracle.oracle import Oracle
-            O = Oracle()
-            rows_s, Ms = 128, 8
+            from oracle.oracle import Reference, reference_available, Oracle
+            rows_s, Ms = (256, 32) if prefill else (128, 8)
             t_layer = 0.0
+            kind_s = "port"
             for (n, t, r, k) in layout:
-                a_ = O.act_for(t, synth.gen_activations(Ms, k, 4400))
+                a_ = Oracle().act_for(t, synth.gen_activations(Ms, k, 3200))
                 t0 = time.perf_counter()
-                O.gemm(t, host[n][:rows_s], k, a_)
+                if reference_available() and k <= 9216:
+                    Reference().gemm(t, host[n][:rows_s], k, a_)
+                    kind_s = "reference"
+                else:
+                    Oracle().gemm(t, host[n][:rows_s], k, a_)
                 t_layer += (time.perf_counter() - t0) * r / rows_s
-            cpu = {"value": round(Ms / (t_layer * L), 4), "unit": "tok/s", "cores": 1, "kind": "port",
-                   "sample": f"first {rows_s} rows of each matrix of one layer at {Ms} tokens through the oracle "
-                             f"(1 thread), scaled to full rows and {L} layers; LM head not included"}
+            if prefill:
+                cpu = {"value": round(2.0 * Ms * sum(r * k for (_, _, r, k) in layout) / t_layer / 1e12, 6),
+                       "unit": "TOPS", "cores": 1, "kind": kind_s,
+                       "sample": f"first {rows_s} rows of every matrix of one layer at {Ms} tokens through the "
+                                 f"reference's row kernels (sdot_row_<type>_batch, scalar x86; the down projection, "
+                                 f"K = 9728 > the reference's 9216, through the oracle), 1 thread, scaled to full rows"}
+            else:
+                cpu = {"value": round(Ms / (t_layer * L), 4), "unit": "tok/s", "cores": 1, "kind": kind_s,
+                       "sample": f"first {rows_s} rows of every matrix of one layer at {Ms} tokens through the "
+                                 f"reference's row kernels (the 9728-value down projection through the oracle), "
+                                 f"1 thread, scaled to full rows and {L} layers; LM head not included"}
         if rank == 0:
-            result = {
-                "metric": METRIC_DECODE, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
-                "warmup": max(3, args.warmup), "ms_per_step": round(dt / steps * 1e3, 4), "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "int8",
-                "data": "synthetic (seeded GGUF blocks per the benchmark configs' distributions; activations N(0,1))",
-                "config": {"workload": f"config4: {SEQ} sequences x 1 token, {L}-layer stack (q/o/gate/up Q5_K, "
-                                       f"k/v/down Q8_0) + Q6_K LM head {VOCAB}x{HIDDEN} vocab-sharded",
-                           "rows_per_rank": Mr, "layers": L, "weight_bytes_per_step_per_rank": wbytes,
-                           "parallelism": f"batch-split x{world}, LM head vocab-split + NCCL all-gathers",
-                           "timing": "eager launches per step, CUDA events, max over ranks"},
-                "roofline": {"bound": "hbm", "achieved": round(wbytes * steps / dt / 1e9, 1), "peak": peak_hbm,
-                             "unit": "GB/s", "frac": round(wbytes * steps / dt / 1e9 / peak_hbm, 4),
-                             "peak_source": peak_kind, "traffic": None},
-                "cpu_baseline": cpu, "clocks": clocks, "e2e": None,
-                "gpu_launches": None,
-            }
+            common = {"n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": round(dt / steps * 1e3, 4),
+                      "higher_is_better": True, "vs_baseline": None, "dtype": "int8", "data": DATA_DESC,
+                      "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": steps * launches_per_step}
+            if prefill:
+                value = ops * steps / dt / 1e12
+                peak_int8 = 2.0 * measured_bf16()
+                result = dict(common, **{
+                    "metric": METRIC_PREFILL, "value": round(value, 2), "unit": "TOPS", "scaling": "strong",
+                    "config": {"workload": f"config3: {L}-layer Q4_K_M stack (q/k/o/gate/up Q4_K, v/down Q6_K) at "
+                                           f"M={M}, layers chained through RMSNorm / SwiGLU (attention core outside "
+                                           f"the path: o takes q's output)",
+                               "m": M, "layers": L, "ops_per_step": ops, "weight_bytes_per_rank": rank_wbytes,
+                               "l2": f"inputs larger than L2: {rank_wbytes / 2**20:.0f} MiB of weights per rank",
+                               "parallelism": "replicas x1" if world == 1 else
+                               f"FFN row-shard x{world} (NCCL all-gathers), projections replicated",
+                               "timing": "launches of all layers per step, warm-up steps then timed steps back to "
+                                         "back, CUDA events, max over ranks"},
+                    "roofline": {"bound": "tensor", "achieved": round(value, 2), "peak": round(peak_int8, 1),
+                                 "unit": "TOPS", "frac": round(value / peak_int8, 4),
+                                 "peak_source": "assumed: 2 x measured dense bf16 TF/s (int8 at twice the bf16 rate); "
+                                                "no int8 figure is measured", "traffic": None},
+                    "e2e": {"value": round(ops * e2e_steps / e2e_dt / 1e12, 2), "unit": "TOPS", "steps": e2e_steps,
+                            "h2d_bytes_per_step": M * HIDDEN * 2, "d2h_bytes_per_step": d2h,
+                            "api": "pinned input rows copied in, the stack, the last hidden rows copied out"},
+                })
+            else:
+                value = SEQ * steps / dt
+                result = dict(common, **{
+                    "metric": METRIC_DECODE, "value": round(value, 1), "unit": "tok/s", "scaling": "strong",
+                    "config": {"workload": f"config4: {SEQ} sequences x 1 token, {L}-layer stack (q/o/gate/up Q5_K, "
+                                           f"k/v/down Q8_0) chained through RMSNorm / SwiGLU + final norm + Q6_K LM head "
+                                           f"{VOCAB}x{HIDDEN} vocab-sharded with the argmax merged on the device",
+                               "rows_per_rank": M, "layers": L, "weight_bytes_per_step_per_rank": rank_wbytes,
+                               "parallelism": f"batch-split x{world}, LM head vocab-split + NCCL all-gathers",
+                               "timing": "CUDA graph: warm-up steps, event, timed steps, event; max over ranks"},
+                    "roofline": {"bound": "hbm", "achieved": round(rank_wbytes * steps / dt / 1e9, 1), "peak": peak_hbm,
+                                 "unit": "GB/s", "frac": round(rank_wbytes * steps / dt / 1e9 / peak_hbm, 4),
+                                 "peak_source": peak_kind, "traffic": None},
+                    "e2e": {"value": round(SEQ * e2e_steps / e2e_dt, 1), "unit": "tok/s", "steps": e2e_steps,
+                            "h2d_bytes_per_step": M * HIDDEN * 2, "d2h_bytes_per_step": d2h,
+                            "api": "pinned input rows copied in, the stack + LM head, the 64 next tokens copied out"},
+                })
         for lay in layers:
             for w_ in lay.values():
                 w_.free()
-        lm.free()
+        if not prefill:
+            lm.free()
     ctx.close()
     if world > 1:
         dist.barrier()
