@@ -589,7 +589,7 @@ def run_stack(args, rank, world, local_rank):
         # config 2: RMSNorm -> {gate, up} Q4_K -> SwiGLU -> down Q6_K + residual, M draft tokens
         # (M in the hundreds or thousands: the batched prefill FFN).  One GPU: the library's FFN
         # entry point.  N GPUs: rows sharded (shard.RowShardedFfn, two NCCL all-gathers per step)
-        M = args.m or 8
+        M = args.tokens or 8
         per_set = [synth.gen_weights(synth.TYPE_Q4_K, FFN_DIM, HIDDEN, 2001), synth.gen_weights(synth.TYPE_Q4_K, FFN_DIM, HIDDEN, 2002),
                    synth.gen_weights(synth.TYPE_Q6_K, HIDDEN, FFN_DIM, 2003)]
         wbytes = sum(w.nbytes for w in per_set)
@@ -699,7 +699,7 @@ def run_stack(args, rank, world, local_rank):
         kind = "prefill" if prefill else "decode"
         L = args.layers
         SEQ = 64
-        M = (args.m or 2048) if prefill else SEQ // world
+        M = (args.tokens or 2048) if prefill else SEQ // world
         sharded_ffn = prefill and world > 1
         layout = stack_layout(kind)
         host = {n: synth.gen_weights(t, r, k, (3000 if prefill else 4000) + i) for i, (n, t, r, k) in enumerate(layout)}
@@ -952,7 +952,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=300)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["gemv", "lm_head", "ffn", "prefill", "decode"], default="gemv")
-    ap.add_argument("--m", type=int, default=0, help="tokens (ffn: 8/16/32/64, prefill: 512/2048)")
+    # (not "--m": torchrun's own parser takes it for an abbreviation of its options)
+    ap.add_argument("--tokens", "--m", dest="tokens", type=int, default=0, help="tokens (ffn: 8/16/32/64 or 512/2048, prefill: 512/2048)")
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
