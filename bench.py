@@ -64,15 +64,16 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def ncu_traffic(key):
-    """DRAM bytes per launch of a kernel from the committed ncu summary (profiles/traffic.json)."""
+def ncu_traffic(key, field="dram_bytes_per_launch"):
+    """DRAM bytes of a kernel launch (or of one step) from the committed ncu summaries
+    (profiles/traffic.json; each entry names the capture it comes from)."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(p):
         return None
     with open(p) as f:
         d = json.load(f)
-    v = d.get(key)
-    return None if v is None else float(v["dram_bytes_per_launch"])
+    v = d.get(key, {}).get(field)
+    return None if v is None else float(v)
 
 
 class ClockSampler:
@@ -673,8 +674,10 @@ def run_stack(args, rank, world, local_rank):
                        "timing": "CUDA graph: warm-up steps, event, timed steps, event"
                                  + ("" if world == 1 else " (NCCL all-gathers captured); max over ranks")},
             "roofline": {"bound": "hbm", "achieved": round(per_rank, 1), "peak": peak_hbm, "unit": "GB/s",
-                         "frac": round(per_rank / peak_hbm, 4), "peak_source": peak_kind, "traffic": None,
-                         "note": "weight bytes of this rank's share per step time (the whole block at 1 GPU)"},
+                         "frac": round(per_rank / peak_hbm, 4), "peak_source": peak_kind,
+                         "traffic": ncu_traffic(f"ffn_m{M}", "dram_bytes_per_step") if world == 1 else None,
+                         "note": "weight bytes of this rank's share per step time (the whole block at 1 GPU); "
+                                 "traffic = DRAM bytes of one whole step (all its kernels) from the ncu summary"},
             "cpu_baseline": cpu, "clocks": clocks,
             "e2e": {"value": round(wbytes * e2e_steps / e2e_dt / 1e9, 2), "unit": "GB/s", "steps": e2e_steps,
                     "h2d_bytes_per_step": int(x16.nbytes + (gamma.nbytes if world == 1 else 0)),
