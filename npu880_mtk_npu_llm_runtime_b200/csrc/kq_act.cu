@@ -138,8 +138,8 @@ constexpr int RMS_SEG = 8;
 constexpr int RMS_CAND = 127;  // start values bits(estimate) - 63 .. bits(estimate) + 63
 static_assert(1 + (RMS_SEG - 1) * RMS_CAND <= RMS_THREADS, "one thread per candidate");
 
-// Sequential fp32 sum of squares of xs[a, b) (fp16 in shared memory, a and b multiples of 8)
-// starting from s.
+// Sequential fp32 sum of squares xs[i]^2, i in [a, b) (fp16 in shared memory, a and b multiples
+// of 8), starting from s.
 __device__ __forceinline__ float sumsq_chain(const __half *xs, int a, int b, float s) {
 #pragma unroll 4
     for (int i = a; i < b; i += 8) {
@@ -155,11 +155,31 @@ __device__ __forceinline__ float sumsq_chain(const __half *xs, int a, int b, flo
     return s;
 }
 
-// One CTA per row; the row is staged in dynamic shared memory (K fp16).
+// The same from the squares staged in shared memory as fp32 (exact: an fp16 value has 11
+// significant bits, its square 22), one 16-byte load per four adds.
+__device__ __forceinline__ float sq_chain(const float *sq, int a, int b, float s) {
+#pragma unroll 8
+    for (int i = a; i < b; i += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(sq + i);
+        s = __fadd_rn(s, v.x);
+        s = __fadd_rn(s, v.y);
+        s = __fadd_rn(s, v.z);
+        s = __fadd_rn(s, v.w);
+    }
+    return s;
+}
+
+// Rows up to this length also stage their squares (2 + 4 bytes per value in shared memory).
+constexpr int RMS_SQ_MAX_K = 32768;
+
+// One CTA per row; the row is staged in dynamic shared memory (K fp16, then K fp32 squares when
+// K <= RMS_SQ_MAX_K).
 __global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, const __half *gamma, __half *out,
                                                                   BlockQ8K *q8k, int K) {
     extern __shared__ __align__(16) uint8_t rms_smem[];
     __half *xs = reinterpret_cast<__half *>(rms_smem);
+    float *sq = reinterpret_cast<float *>(rms_smem + (size_t)K * 2);  // 16-byte aligned: K % 256 == 0
+    const bool have_sq = K <= RMS_SQ_MAX_K;
     __shared__ double s_part[RMS_SEG][RMS_THREADS / 32];
     __shared__ float s_end[RMS_SEG][RMS_CAND];
     __shared__ uint32_t s_lo[RMS_SEG];
@@ -171,12 +191,33 @@ __global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, c
     // the next kernel may start now: its weight stream does not depend on this one
     asm volatile("griddepcontrol.launch_dependents;");
     if ((reinterpret_cast<uintptr_t>(xr) & 15) == 0) {
-        for (int i = 8 * tid; i < K; i += 8 * RMS_THREADS)
-            *reinterpret_cast<uint4 *>(xs + i) = *reinterpret_cast<const uint4 *>(xr + i);
+        for (int i = 8 * tid; i < K; i += 8 * RMS_THREADS) {
+            const uint4 raw = *reinterpret_cast<const uint4 *>(xr + i);
+            *reinterpret_cast<uint4 *>(xs + i) = raw;
+            if (have_sq) {
+                const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+                float f[8];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float2 v = __half22float2(h2[k]);
+                    f[2 * k] = __fmul_rn(v.x, v.x);
+                    f[2 * k + 1] = __fmul_rn(v.y, v.y);
+                }
+                *reinterpret_cast<float4 *>(sq + i) = make_float4(f[0], f[1], f[2], f[3]);
+                *reinterpret_cast<float4 *>(sq + i + 4) = make_float4(f[4], f[5], f[6], f[7]);
+            }
+        }
     } else {
-        for (int i = tid; i < K; i += RMS_THREADS) xs[i] = xr[i];
+        for (int i = tid; i < K; i += RMS_THREADS) {
+            xs[i] = xr[i];
+            if (have_sq) {
+                const float v = __half2float(xr[i]);
+                sq[i] = __fmul_rn(v, v);
+            }
+        }
     }
     __syncthreads();
+    auto chain = [&](int a, int b, float s0) { return have_sq ? sq_chain(sq, a, b, s0) : sumsq_chain(xs, a, b, s0); };
     // segment j = [j L, min(K, (j + 1) L)), L a multiple of 8
     const int L = ((K + RMS_SEG - 1) / RMS_SEG + 7) & ~7;
     // fp64 sums of the squares of each segment (exact enough to centre the candidate windows)
@@ -184,8 +225,12 @@ __global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, c
         double d = 0.0;
         const int a = j * L, b = min(K, a + L);
         for (int i = a + tid; i < b; i += RMS_THREADS) {
-            const double v = (double)__half2float(xs[i]);
-            d += v * v;
+            if (have_sq) {
+                d += (double)sq[i];
+            } else {
+                const double v = (double)__half2float(xs[i]);
+                d += v * v;
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
@@ -207,11 +252,11 @@ __global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, c
     // the chains: thread 0 = segment 0 from 0; thread 1 + (j - 1) RMS_CAND + k = segment j from
     // candidate k
     if (tid == 0) {
-        s_first = sumsq_chain(xs, 0, min(K, L), 0.0f);
+        s_first = chain(0, min(K, L), 0.0f);
     } else if (tid < 1 + (RMS_SEG - 1) * RMS_CAND) {
         const int j = 1 + (tid - 1) / RMS_CAND, k = (tid - 1) % RMS_CAND;
         const int a = j * L, b = min(K, a + L);
-        if (a < b) s_end[j][k] = sumsq_chain(xs, a, b, __uint_as_float(s_lo[j] + (uint32_t)k));
+        if (a < b) s_end[j][k] = chain(a, b, __uint_as_float(s_lo[j] + (uint32_t)k));
     }
     __syncthreads();
     if (tid == 0) {
@@ -221,7 +266,7 @@ __global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, c
             if (a >= b) break;
             const uint32_t sb = __float_as_uint(s);
             if (sb >= s_lo[j] && sb - s_lo[j] < (uint32_t)RMS_CAND) s = s_end[j][sb - s_lo[j]];
-            else s = sumsq_chain(xs, a, b, s);  // outside the window: add the segment here
+            else s = chain(a, b, s);  // outside the window: add the segment here
         }
         const float inv_k = __fdiv_rn(1.0f, (float)K);
         s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, inv_k), 1.0e-6f)));
@@ -256,8 +301,8 @@ __global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, c
 cudaError_t launch_rmsnorm_q8k(const void *x, const void *gamma, void *out, void *q8k, int M, int K,
                                cudaStream_t stream, bool pdl) {
     if (M == 0) return cudaSuccess;
-    // the staged row takes up to 128 KB (K <= 65536): raise the kernel's dynamic shared memory
-    // limit once per device
+    // the staged row takes up to 192 KB (K <= 32768: fp16 values and fp32 squares; longer rows
+    // only the values, up to 128 KB): raise the kernel's dynamic shared memory limit once per device
     static std::mutex mu;
     static bool configured[64] = {};
     int dev = 0;
@@ -266,7 +311,7 @@ cudaError_t launch_rmsnorm_q8k(const void *x, const void *gamma, void *out, void
         std::lock_guard<std::mutex> lk(mu);
         if (!configured[dev]) {
             cudaError_t e =
-                cudaFuncSetAttribute(kq_rmsnorm_q8k, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
+                cudaFuncSetAttribute(kq_rmsnorm_q8k, cudaFuncAttributeMaxDynamicSharedMemorySize, 192 * 1024);
             if (e != cudaSuccess) return e;
             configured[dev] = true;
         }
@@ -274,7 +319,7 @@ cudaError_t launch_rmsnorm_q8k(const void *x, const void *gamma, void *out, void
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(M);
     cfg.blockDim = dim3(RMS_THREADS);
-    cfg.dynamicSmemBytes = (size_t)K * 2;
+    cfg.dynamicSmemBytes = (size_t)K * (K <= RMS_SQ_MAX_K ? 6 : 2);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -65,11 +65,12 @@ def bits(a):
 
 def rmsnorm_cases():
     """(M, K, x fp16, gamma fp16) RMSNorm cases: the benchmark hidden size at 1-64 rows, short and
-    long rows, small and large magnitudes, a zero row (sum 0), +-65504 and fp16 subnormals"""
+    long rows (40,960 values: longer than the kernel stages squares for), small and large
+    magnitudes, a zero row (sum 0), +-65504 and fp16 subnormals"""
     rng = np.random.default_rng(77)
     cases = []
     for M, K, scale in [(1, 2560, 1.0), (8, 2560, 1.0), (64, 2560, 1.0), (5, 256, 30.0), (3, 9728, 1.0),
-                        (2, 2560, 1e-3), (2, 2560, 3000.0)]:
+                        (2, 2560, 1e-3), (2, 2560, 3000.0), (1, 40960, 1.0)]:
         x = (rng.standard_normal((M, K)) * scale).astype(np.float16)
         g = (rng.standard_normal(K) * 0.5 + 1.0).astype(np.float16)
         cases.append((M, K, x, g))
