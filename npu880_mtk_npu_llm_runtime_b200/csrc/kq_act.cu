@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, c
     __half *xs = reinterpret_cast<__half *>(rms_smem);
     float *sq = reinterpret_cast<float *>(rms_smem + (size_t)K * 2);  // 16-byte aligned: K % 256 == 0
     const bool have_sq = K <= RMS_SQ_MAX_K;
-    __shared__ double s_part[RMS_SEG][RMS_THREADS / 32];
+    __shared__ double s_seg[RMS_SEG];
     __shared__ float s_end[RMS_SEG][RMS_CAND];
     __shared__ uint32_t s_lo[RMS_SEG];
     __shared__ float s_first, s_inv;
@@ -220,11 +220,13 @@ __global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, c
     auto chain = [&](int a, int b, float s0) { return have_sq ? sq_chain(sq, a, b, s0) : sumsq_chain(xs, a, b, s0); };
     // segment j = [j L, min(K, (j + 1) L)), L a multiple of 8
     const int L = ((K + RMS_SEG - 1) / RMS_SEG + 7) & ~7;
-    // fp64 sums of the squares of each segment (exact enough to centre the candidate windows)
-    for (int j = 0; j < RMS_SEG - 1; ++j) {
+    // fp64 sum of the squares of each segment (exact enough to centre the candidate windows):
+    // warp j sums segment j, all segments at once; then each window start is a prefix of at
+    // most RMS_SEG - 1 of them
+    if (warp < RMS_SEG - 1) {
         double d = 0.0;
-        const int a = j * L, b = min(K, a + L);
-        for (int i = a + tid; i < b; i += RMS_THREADS) {
+        const int a = warp * L, b = min(K, a + L);
+        for (int i = a + lane; i < b; i += 32) {
             if (have_sq) {
                 d += (double)sq[i];
             } else {
@@ -234,7 +236,7 @@ __global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, c
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        if (lane == 0) s_part[j][warp] = d;
+        if (lane == 0) s_seg[warp] = d;
     }
     __syncthreads();
     if (tid < RMS_SEG) {
@@ -242,8 +244,7 @@ __global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, c
             s_lo[0] = 0;
         } else {
             double pre = 0.0;
-            for (int j = 0; j < tid; ++j)
-                for (int w = 0; w < RMS_THREADS / 32; ++w) pre += s_part[j][w];
+            for (int j = 0; j < tid; ++j) pre += s_seg[j];
             const uint32_t c = __float_as_uint(__double2float_rn(pre));
             s_lo[tid] = c > (uint32_t)(RMS_CAND / 2) ? c - (uint32_t)(RMS_CAND / 2) : 0u;
         }
