@@ -90,6 +90,10 @@ const char *kq_last_error(const kq_ctx *ctx);
  * over the SMs give every CTA an equal range of 16-row x 256-value tiles instead; a row group
  * shared by neighbouring CTAs is summed in block order by the last of them (1, default); 0 keeps
  * whole row groups per CTA;
+ * "ffn_fused" -- kq_run_ffn / kq_run_ffn_async for 1-2 rows with Q4_K / Q5_K gate and up and a
+ * Q4_K / Q5_K / Q6_K down projection run the whole block as one persistent kernel, one CTA per SM,
+ * all resident at once, with one grid-wide barrier between gate/up and down (1, default); the
+ * results are bit for bit those of the four launches that 0 selects (and that other shapes use);
  * "swiglu_exp" -- where SwiGLU takes expf(-g) from: 0 (default) a table of the host C library's
  * expf at the 65,536 fp16 values of g, made once by kq_init -- the function the reference's
  * scalar SwiGLU calls (ENG:4354), so the results match it bit for bit on the same host; 1 an fp64

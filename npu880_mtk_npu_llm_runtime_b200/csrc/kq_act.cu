@@ -9,6 +9,7 @@
 //   dequant_block_<type>       ENG:598-853    -> kq_dequant
 #include "kq_common.cuh"
 #include "kq_internal.h"
+#include "kq_rms_seq.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -120,54 +121,10 @@ cudaError_t launch_quantize(int target_type, const void *x, long long x_stride, 
 //
 // x_out = fp16((x * inv_rms) * gamma), inv_rms = 1 / sqrt(sum_sq * (1/K) + 1e-6), every operation
 // rounded as in the reference's scalar branch (ENG:4291-4299), where sum_sq is the fp32 sum of
-// the squares added one after another in index order.  That order is kept exactly; the chain
-// of K dependent adds is shortened by splitting the row into RMS_SEG segments:
-//  * thread 0 adds segment 0 from 0;
-//  * for every later segment j, RMS_CAND threads add the segment starting from the RMS_CAND
-//    consecutive fp32 values around an estimate of the running sum at its start (the fp64 sum
-//    of the squares before it, rounded to fp32), all at the same time as thread 0;
-//  * then thread 0 walks the segments: the true running sum at the start of segment j is one of
-//    the candidates (it lies within a few fp32 steps of the estimate) and that candidate's end
-//    is the true running sum at the end; when it is not, thread 0 adds the segment itself.
-// Every result is the sequential fp32 sum; the squares of fp16 values are exact in fp32.
-// The fp32 running sum drifts from the exact sum by up to ~50 fp32 steps over 2,560 N(0,1) terms
-// (CPU simulation of 5,600 segment starts: all within +-63 at K = 2560; a few percent of the
-// segment starts fall outside at K = 9728, which only costs time).
+// the squares added one after another in index order: rms_seq_sum (kq_rms_seq.cuh) computes
+// exactly that sum with a few dozen short chains instead of one chain of K adds.
 constexpr int RMS_THREADS = 1024;
-constexpr int RMS_SEG = 8;
-constexpr int RMS_CAND = 127;  // start values bits(estimate) - 63 .. bits(estimate) + 63
-static_assert(1 + (RMS_SEG - 1) * RMS_CAND <= RMS_THREADS, "one thread per candidate");
-
-// Sequential fp32 sum of squares xs[i]^2, i in [a, b) (fp16 in shared memory, a and b multiples
-// of 8), starting from s.
-__device__ __forceinline__ float sumsq_chain(const __half *xs, int a, int b, float s) {
-#pragma unroll 4
-    for (int i = a; i < b; i += 8) {
-        const uint4 raw = *reinterpret_cast<const uint4 *>(xs + i);
-        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float2 f = __half22float2(h2[k]);
-            s = __fadd_rn(s, __fmul_rn(f.x, f.x));
-            s = __fadd_rn(s, __fmul_rn(f.y, f.y));
-        }
-    }
-    return s;
-}
-
-// The same from the squares staged in shared memory as fp32 (exact: an fp16 value has 11
-// significant bits, its square 22), one 16-byte load per four adds.
-__device__ __forceinline__ float sq_chain(const float *sq, int a, int b, float s) {
-#pragma unroll 8
-    for (int i = a; i < b; i += 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(sq + i);
-        s = __fadd_rn(s, v.x);
-        s = __fadd_rn(s, v.y);
-        s = __fadd_rn(s, v.z);
-        s = __fadd_rn(s, v.w);
-    }
-    return s;
-}
+static_assert(RMS_THREADS >= RMS_MIN_THREADS, "threads for the chains");
 
 // Rows up to this length also stage their squares (2 + 4 bytes per value in shared memory).
 constexpr int RMS_SQ_MAX_K = 32768;
@@ -180,110 +137,68 @@ __global__ void __launch_bounds__(RMS_THREADS) kq_rmsnorm_q8k(const __half *x, c
     __half *xs = reinterpret_cast<__half *>(rms_smem);
     float *sq = reinterpret_cast<float *>(rms_smem + (size_t)K * 2);  // 16-byte aligned: K % 256 == 0
     const bool have_sq = K <= RMS_SQ_MAX_K;
-    __shared__ double s_seg[RMS_SEG];
-    __shared__ float s_end[RMS_SEG][RMS_CAND];
-    __shared__ uint32_t s_lo[RMS_SEG];
-    __shared__ float s_first, s_inv;
+    __shared__ float s_hsum[RMS_SQ_MAX_K / 128 * 2];  // K / 128 estimates (K <= 65536)
+    __shared__ uint4 s_desc[RMS_MAX_SEG * 4];
+    __shared__ float s_inv;
     const int m = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const __half *xr = x + (size_t)m * K;
     __half *yr = out + (size_t)m * K;
+    const int nbu = K / 256;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     // the next kernel may start now: its weight stream does not depend on this one
     asm volatile("griddepcontrol.launch_dependents;");
-    if ((reinterpret_cast<uintptr_t>(xr) & 15) == 0) {
-        for (int i = 8 * tid; i < K; i += 8 * RMS_THREADS) {
-            const uint4 raw = *reinterpret_cast<const uint4 *>(xr + i);
-            *reinterpret_cast<uint4 *>(xs + i) = raw;
-            if (have_sq) {
-                const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
-                float f[8];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float2 v = __half22float2(h2[k]);
-                    f[2 * k] = __fmul_rn(v.x, v.x);
-                    f[2 * k + 1] = __fmul_rn(v.y, v.y);
-                }
-                *reinterpret_cast<float4 *>(sq + i) = make_float4(f[0], f[1], f[2], f[3]);
-                *reinterpret_cast<float4 *>(sq + i + 4) = make_float4(f[4], f[5], f[6], f[7]);
-            }
-        }
-    } else {
-        for (int i = tid; i < K; i += RMS_THREADS) {
-            xs[i] = xr[i];
-            if (have_sq) {
-                const float v = __half2float(xr[i]);
-                sq[i] = __fmul_rn(v, v);
-            }
-        }
-    }
-    __syncthreads();
-    auto chain = [&](int a, int b, float s0) { return have_sq ? sq_chain(sq, a, b, s0) : sumsq_chain(xs, a, b, s0); };
-    // segment j = [j L, min(K, (j + 1) L)), L a multiple of 8
-    const int L = ((K + RMS_SEG - 1) / RMS_SEG + 7) & ~7;
-    // fp64 sum of the squares of each segment (exact enough to centre the candidate windows):
-    // warp j sums segment j, all segments at once; then each window start is a prefix of at
-    // most RMS_SEG - 1 of them
-    if (warp < RMS_SEG - 1) {
-        double d = 0.0;
-        const int a = warp * L, b = min(K, a + L);
-        for (int i = a + lane; i < b; i += 32) {
-            if (have_sq) {
-                d += (double)sq[i];
-            } else {
-                const double v = (double)__half2float(xs[i]);
-                d += v * v;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        if (lane == 0) s_seg[warp] = d;
-    }
-    __syncthreads();
-    if (tid < RMS_SEG) {
-        if (tid == 0) {
-            s_lo[0] = 0;
+    // this warp's first unit of gamma, consumed after the sum: its load latency hides behind it
+    float gv[8];
+    if (warp < nbu) load8_f16(gamma + warp * 256 + 8 * lane, gv);
+    const bool x_al = (reinterpret_cast<uintptr_t>(xr) & 15) == 0;
+    for (int i = 8 * tid; i < K; i += 8 * RMS_THREADS) {  // a warp covers whole 256-value units
+        uint4 raw;
+        if (x_al) {
+            raw = *reinterpret_cast<const uint4 *>(xr + i);
         } else {
-            double pre = 0.0;
-            for (int j = 0; j < tid; ++j) pre += s_seg[j];
-            const uint32_t c = __float_as_uint(__double2float_rn(pre));
-            s_lo[tid] = c > (uint32_t)(RMS_CAND / 2) ? c - (uint32_t)(RMS_CAND / 2) : 0u;
+            uint32_t hv[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) hv[k] = __half_as_ushort(xr[i + k]);
+            raw = make_uint4(hv[0] | (hv[1] << 16), hv[2] | (hv[3] << 16), hv[4] | (hv[5] << 16), hv[6] | (hv[7] << 16));
         }
+        *reinterpret_cast<uint4 *>(xs + i) = raw;
+        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+        float f[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 v = __half22float2(h2[k]);
+            f[2 * k] = __fmul_rn(v.x, v.x);
+            f[2 * k + 1] = __fmul_rn(v.y, v.y);
+        }
+        if (have_sq) {
+            *reinterpret_cast<float4 *>(sq + i) = make_float4(f[0], f[1], f[2], f[3]);
+            *reinterpret_cast<float4 *>(sq + i + 4) = make_float4(f[4], f[5], f[6], f[7]);
+        }
+        // estimate of the sum of each 128 values (16 lanes), any order
+        float h = ((f[0] + f[1]) + (f[2] + f[3])) + ((f[4] + f[5]) + (f[6] + f[7]));
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) h += __shfl_xor_sync(0xffffffffu, h, o);
+        if ((lane & 15) == 0) s_hsum[i / 128] = h;
     }
     __syncthreads();
-    // the chains: thread 0 = segment 0 from 0; thread 1 + (j - 1) RMS_CAND + k = segment j from
-    // candidate k
+    auto bar = [] { __syncthreads(); };
+    const float ssum = have_sq ? rms_seq_sum(RmsSqF32{sq}, s_hsum, s_desc, K, tid, bar)
+                               : rms_seq_sum(RmsSqF16{xs}, s_hsum, s_desc, K, tid, bar);
     if (tid == 0) {
-        s_first = chain(0, min(K, L), 0.0f);
-    } else if (tid < 1 + (RMS_SEG - 1) * RMS_CAND) {
-        const int j = 1 + (tid - 1) / RMS_CAND, k = (tid - 1) % RMS_CAND;
-        const int a = j * L, b = min(K, a + L);
-        if (a < b) s_end[j][k] = chain(a, b, __uint_as_float(s_lo[j] + (uint32_t)k));
-    }
-    __syncthreads();
-    if (tid == 0) {
-        float s = s_first;
-        for (int j = 1; j < RMS_SEG; ++j) {
-            const int a = j * L, b = min(K, a + L);
-            if (a >= b) break;
-            const uint32_t sb = __float_as_uint(s);
-            if (sb >= s_lo[j] && sb - s_lo[j] < (uint32_t)RMS_CAND) s = s_end[j][sb - s_lo[j]];
-            else s = chain(a, b, s);  // outside the window: add the segment here
-        }
         const float inv_k = __fdiv_rn(1.0f, (float)K);
-        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, inv_k), 1.0e-6f)));
+        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ssum, inv_k), 1.0e-6f)));
     }
     __syncthreads();
     const float inv_rms = s_inv;
-    const int nbu = K / 256;
     for (int b = warp; b < nbu; b += RMS_THREADS / 32) {
         const int base = b * 256 + 8 * lane;
+        if (b != warp) load8_f16(gamma + base, gv);
         float v[8];
         uint32_t packed[4];
 #pragma unroll
         for (int i = 0; i < 8; i += 2) {
-            const float y0 = __fmul_rn(__fmul_rn(__half2float(xs[base + i]), inv_rms), __half2float(gamma[base + i]));
-            const float y1 =
-                __fmul_rn(__fmul_rn(__half2float(xs[base + i + 1]), inv_rms), __half2float(gamma[base + i + 1]));
+            const float y0 = __fmul_rn(__fmul_rn(__half2float(xs[base + i]), inv_rms), gv[i]);
+            const float y1 = __fmul_rn(__fmul_rn(__half2float(xs[base + i + 1]), inv_rms), gv[i + 1]);
             const __half h0 = __float2half_rn(y0), h1 = __float2half_rn(y1);
             v[i] = __half2float(h0);
             v[i + 1] = __half2float(h1);

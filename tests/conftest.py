@@ -79,6 +79,20 @@ def rmsnorm_cases():
     x[1, 3::7] = np.float16(-65504.0)
     x[2] = (rng.standard_normal(2560) * 6e-5).astype(np.float16)
     cases.append((3, 2560, x, np.ones(2560, np.float16)))
+    # rows whose running sum crosses binades in unusual ways: one outlier (several binades in one
+    # add), magnitudes growing along the row, mostly zeros, a step pattern
+    K = 2560
+    i = np.arange(K)
+    x = np.empty((4, K), np.float16)
+    x[0] = (rng.standard_normal(K) * 0.1).astype(np.float16)
+    x[0, K // 3] = np.float16(300.0)
+    x[1] = (rng.standard_normal(K) * (1.0 + i / 100.0)).astype(np.float16)
+    x[2] = np.where(i % 7 == 0, rng.standard_normal(K), 0.0).astype(np.float16)
+    x[3] = np.where(i % 64 == 0, 8.0, 0.01).astype(np.float16)
+    cases.append((4, K, x, (rng.standard_normal(K) * 0.5 + 1.0).astype(np.float16)))
+    for M, K in [(2, 4096), (1, 65536)]:
+        x = rng.standard_normal((M, K)).astype(np.float16)
+        cases.append((M, K, x, (rng.standard_normal(K) * 0.5 + 1.0).astype(np.float16)))
     return cases
 
 
