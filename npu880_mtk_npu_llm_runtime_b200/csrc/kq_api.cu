@@ -44,8 +44,9 @@ struct kq_ctx {
     DevBuf lmlogits;  // fp16 logits of a many-token LM head when the caller keeps none
     // balanced GEMV launches: shared-row-group term slots and arrival counts (zero between
     // launches; re-cleared after a launch that stopped early)
-    DevBuf gsplit, gcount;
+    DevBuf gsplit, gcount;  // gcount: the split launches' arrival counts, then the fused FFN's grid barrier
     bool gemv_split = true;
+    bool ffn_fused = true;  // FFN blocks of 1-2 tokens as one persistent kernel where a plan exists
     bool split_dirty = false;
     bool graph_holds_scratch = false;  // a call of this context was captured into a CUDA graph
 
@@ -173,17 +174,25 @@ int validate_mk(kq_ctx *c, int M, int K) {
 // Scratch of a balanced GEMV launch (CTAs own equal tile ranges; see GemvParams::split).  The
 // launch keeps whole row groups per CTA when the option is off or the term slots would exceed
 // 64 MB (very long Q8_0 rows).
+// The arrival counts of balanced launches (gemv_split_slots ints), then the two words of the fused
+// FFN kernel's grid barrier and its `extra` pair counts, all zero; cleared again after a launch
+// that stopped early.
+int split_counts(kq_ctx *c, size_t extra = 0) {
+    const size_t cb = sizeof(int) * ((size_t)kq::gemv_split_slots(c->num_sms) + 2 + extra);
+    if (!c->gcount.p || c->split_dirty || c->gcount.cap < cb) {
+        if (int r = ensure(c, c->gcount, cb)) return r;
+        KQ_CUDA(c, cudaMemsetAsync(c->gcount.p, 0, cb, c->stream));
+        c->split_dirty = false;
+    }
+    return KQ_OK;
+}
+
 int gemv_split_scratch(kq_ctx *c, int type, int K, int mt, kq::GemvLaunch &L) {
     if (!c->gemv_split) return KQ_OK;
     const size_t bytes = kq::gemv_split_bytes(type, K, mt, c->num_sms);
     if (bytes > ((size_t)64 << 20)) return KQ_OK;
     if (int r = ensure(c, c->gsplit, bytes)) return r;
-    if (!c->gcount.p || c->split_dirty) {
-        const size_t cb = sizeof(int) * (size_t)kq::gemv_split_slots(c->num_sms);
-        if (int r = ensure(c, c->gcount, cb)) return r;
-        KQ_CUDA(c, cudaMemsetAsync(c->gcount.p, 0, cb, c->stream));
-        c->split_dirty = false;
-    }
+    if (int r = split_counts(c)) return r;
     L.split_terms = static_cast<float *>(c->gsplit.p);
     L.split_terms_bytes = c->gsplit.cap;
     L.split_count = static_cast<int *>(c->gcount.p);
@@ -542,6 +551,10 @@ extern "C" int kq_set_option(kq_ctx *c, const char *name, long long value) {
     if (!strcmp(name, "swiglu_exp")) {
         if (value < 0 || value > 1) return fail(c, KQ_ERR_INVALID_ARGUMENT, "swiglu_exp must be 0 or 1");
         c->swiglu_gpu_exp = value == 1;
+        return KQ_OK;
+    }
+    if (!strcmp(name, "ffn_fused")) {
+        c->ffn_fused = value != 0;
         return KQ_OK;
     }
     if (!strcmp(name, "gemv_split")) {
@@ -957,6 +970,38 @@ extern "C" int kq_run_ffn_async(kq_ctx *c, const kq_weight *gate, const kq_weigh
     void *q_a0 = (uint8_t *)q_h + al(qh);
     void *q_h0 = (uint8_t *)q_a0 + al(qa0);
 
+    if (c->ffn_fused && gate->type == up->type &&
+        kq::ffn_fused_supported((int)gate->type, (int)down->type, hidden, ffn, M, c->num_sms)) {
+        // the whole block as one persistent kernel (bit for bit the launches below)
+        const size_t sb = kq::gemv_split_bytes((int)down->type, ffn, M, c->num_sms);
+        if (int r = ensure(c, c->gsplit, sb)) return r;
+        if (int r = split_counts(c, (size_t)ffn / 16)) return r;
+        kq::FfnFusedLaunch F{};
+        F.gate_type = (int)gate->type;
+        F.down_type = (int)down->type;
+        F.hidden = hidden;
+        F.ffn = ffn;
+        F.M = M;
+        F.gate = gate->d;
+        F.up = up->d;
+        F.down = down->d;
+        F.x = x_in;
+        F.gamma = gamma;
+        F.g = g;
+        F.u = u;
+        F.y = x_out;
+        F.exp_tab = swiglu_table(c);
+        F.split_terms = static_cast<float *>(c->gsplit.p);
+        F.split_count = static_cast<int *>(c->gcount.p);
+        F.gbar = reinterpret_cast<unsigned *>(static_cast<int *>(c->gcount.p) + kq::gemv_split_slots(c->num_sms));
+        F.pair = static_cast<int *>(c->gcount.p) + kq::gemv_split_slots(c->num_sms) + 2;
+        F.status = c->d_status;
+        F.timeout_ns = c->timeout_ns;
+        F.pdl = c->pdl;
+        F.num_sms = c->num_sms;
+        KQ_CUDA(c, kq::launch_ffn_fused(F, c->stream));
+        return KQ_OK;
+    }
     // RMSNorm (+ Q8_K), ENG:8285
     KQ_CUDA(c, kq::launch_rmsnorm_q8k(x_in, gamma, xn, q_a, M, hidden, c->stream, c->pdl));
     const bool gu_q80 = gate->type == KQ_TYPE_Q8_0 || up->type == KQ_TYPE_Q8_0;

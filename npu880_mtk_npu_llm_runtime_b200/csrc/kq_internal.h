@@ -82,6 +82,29 @@ struct TcLaunch {
 
 // kq_gemv.cu
 cudaError_t launch_gemv(const GemvLaunch &L, cudaStream_t stream);
+
+// The FFN block for 1-2 tokens as one persistent kernel (kq_ffn_fused.cu): RMSNorm + Q8_K ->
+// gate / up -> SwiGLU + Q8_K -> down + residual, bit for bit the four-launch form.
+struct FfnFusedLaunch {
+    int gate_type, down_type;  // gate and up share a type
+    int hidden, ffn, M;        // M in 1..2
+    const uint8_t *gate, *up, *down;  // tiled weights
+    const void *x, *gamma;     // fp16 [M][hidden], [hidden]
+    void *g, *u;               // fp16 [M][ffn] scratch, 16-byte aligned
+    void *y;                   // fp16 [M][hidden]
+    const float *exp_tab;      // SwiGLU expf table, or nullptr
+    float *split_terms;        // gemv_split_bytes(down_type, ffn, M, num_sms)
+    int *split_count;          // gemv_split_slots(num_sms) ints, zero
+    unsigned *gbar;            // 2 words, zero before the first launch
+    int *pair;                 // ffn / 16 ints, zero before the first launch
+    int *status;
+    unsigned long long timeout_ns;
+    bool pdl;
+    int num_sms;               // the grid: one CTA per SM, all resident
+};
+bool ffn_fused_supported(int gate_type, int down_type, int hidden, int ffn, int M, int num_sms);
+// cudaErrorNotSupported when the shapes or types have no plan
+cudaError_t launch_ffn_fused(const FfnFusedLaunch &L, cudaStream_t stream);
 // scratch of a split GEMV launch of M (<= 8) tokens: term bytes and counter slots
 size_t gemv_split_bytes(int type, int K, int M, int num_sms);
 int gemv_split_slots(int num_sms);
