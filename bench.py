@@ -343,6 +343,27 @@ def lm_head_sharded(ctx, args, rank, world, dev, stream, steps, warmup, want_arg
     rec = {"value": round(value, 1), "unit": "GB/s", "ms_per_step": round(dt / steps * 1e3, 6), "steps": steps,
            "warmup": warmup, "n_gpus": world, "rows_per_rank": chunk, "weight_bytes_per_rank": wbytes,
            "gather_bytes_per_rank": chunk * 4}
+    # the all-gather inside the GEMV: its epilogue stores every logit into every rank's gather
+    # buffer over NVLink, then a bounded wait for all ranks' slices copies the gathered logits out
+    pg = shard.PeerGather(ctx, rank, world, 1, V, row0,
+                          exchange=(lambda h: shard.torch_exchange(h, dev)) if world > 1 else None)
+    p2p_out = torch.zeros((1, pg.row_stride), dtype=torch.float32, device=dev)
+
+    def step_p(i):
+        pg.gather(Ws[i % n_copies], x)
+        pg.wait(p2p_out)
+
+    dtp = graph_timed(stream, step_p, steps, warmup, world)
+    torch.cuda.synchronize()
+    same = bool(torch.equal(p2p_out[0, :V], gather[:V]))
+    rec["p2p_gather"] = {"value": round(float(total.item()) * steps / dtp / 1e9, 1), "unit": "GB/s",
+                         "ms_per_step": round(dtp / steps * 1e3, 6), "equal_to_nccl_gather": same,
+                         "how": "GEMV epilogue stores each logit into every rank's buffer over NVLink as one 64-bit "
+                                "(step, fp32) entry; a bounded wait reads the entries until all carry the step and "
+                                "writes the fp32 logits out"}
+    if world > 1:
+        dist.barrier()
+    pg.close()
     if want_argmax:
         toks = torch.zeros((1,), dtype=torch.int32, device=dev)
         vals = torch.zeros((1,), dtype=torch.float32, device=dev)
@@ -408,7 +429,8 @@ def run_ours(args, rank, world, local_rank):
                              "frac": round(algo / avg_s / 1e9 / peak, 4), "peak_source": peak_kind,
                              "traffic": ncu_traffic("gemv_q6k_lmhead"),
                              "note": "step time includes the all-gather at N > 1"},
-                "argmax_exchange": rec.get("argmax_exchange"), "cpu_baseline": None, "clocks": clocks,
+                "argmax_exchange": rec.get("argmax_exchange"), "p2p_gather": rec.get("p2p_gather"),
+                "cpu_baseline": None, "clocks": clocks,
                 "e2e": None, "gpu_launches": steps * (1 + (world > 1)),
             }
         ctx.close()
@@ -860,7 +882,7 @@ def run_stack(args, rank, world, local_rank):
                       "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": steps * launches_per_step}
             if prefill:
                 value = ops * steps / dt / 1e12
-                peak_int8 = 2.0 * measured_bf16()
+                peak_int8, peak_int8_src = measured_int8_tops(local_rank)
                 result = dict(common, **{
                     "metric": METRIC_PREFILL, "value": round(value, 2), "unit": "TOPS", "scaling": "strong",
                     "config": {"workload": f"config3: {L}-layer Q4_K_M stack (q/k/o/gate/up Q4_K, v/down Q6_K) at "
@@ -874,8 +896,7 @@ def run_stack(args, rank, world, local_rank):
                                          "back, CUDA events, max over ranks"},
                     "roofline": {"bound": "tensor", "achieved": round(value, 2), "peak": round(peak_int8, 1),
                                  "unit": "TOPS", "frac": round(value / peak_int8, 4),
-                                 "peak_source": "assumed: 2 x measured dense bf16 TF/s (int8 at twice the bf16 rate); "
-                                                "no int8 figure is measured", "traffic": None},
+                                 "peak_source": peak_int8_src, "traffic": None},
                     "e2e": {"value": round(ops * e2e_steps / e2e_dt / 1e12, 2), "unit": "TOPS", "steps": e2e_steps,
                             "h2d_bytes_per_step": M * HIDDEN * 2, "d2h_bytes_per_step": d2h,
                             "api": "pinned input rows copied in, the stack, the last hidden rows copied out"},
@@ -907,6 +928,23 @@ def run_stack(args, rank, world, local_rank):
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+def measured_int8_tops(device):
+    """(dense int8 tensor TOPS, how it was obtained): this GPU measured live by kq_measure_int8_tops
+    (every SM issuing back-to-back tcgen05.mma kind::i8 128x256x32), else 2 x the measured bf16
+    figure."""
+    import ctypes as C
+    import npu880_mtk_npu_llm_runtime_b200 as kq
+    t = C.c_double(0.0)
+    try:
+        rc = kq.load_library().kq_measure_int8_tops(device, 1024, C.byref(t))
+    except (OSError, AttributeError):
+        rc = -1
+    if rc == 0 and t.value > 0:
+        return t.value, ("measured here: kq_measure_int8_tops (tcgen05.mma kind::i8 128x256x32 back to back on "
+                         "every SM, s32 in TMEM, best of 3 launches)")
+    return 2.0 * measured_bf16(), "assumed: 2 x measured dense bf16 TF/s (the int8 measurement failed)"
 
 
 def measured_bf16():

@@ -308,6 +308,45 @@ int kq_gguf_upload(kq_ctx *ctx, const kq_gguf *g, int index, kq_weight **out);
  * out has kq_gguf_tensor_count entries.  On failure nothing stays uploaded. */
 int kq_gguf_upload_all(kq_ctx *ctx, const kq_gguf *g, kq_weight **out, int *n_uploaded);
 
+/* ---------------------------------------------------------------- several GPUs: the LM head
+ * with its all-gather in the GEMV (no counterpart in the single-process reference; its LM head is
+ * ENG:9686-9707, the all-gather is what north_star adds for vocabulary rows split over GPUs).
+ *
+ * One process per GPU.  Each rank allocates a gather region with kq_peer_alloc, the ranks exchange
+ * the IPC handles (any channel: torch.distributed, MPI, a file) and open each other's regions with
+ * kq_peer_open.  A region holds control words and two buffers of [M][row_stride] 64-bit entries
+ * (kq_peer_region_bytes).  kq_gemm_peer_gather_async streams this rank's vocabulary slice and its
+ * epilogue stores every logit into the current buffer of EVERY rank's region over NVLink, as one
+ * aligned 64-bit store of (step number, fp32 value) -- plain stores, no TMA, no multicast, no
+ * fence or flag.  kq_peer_gather_wait_async reads the current buffer until every entry carries the
+ * step number (bounded: KQ_ERR_TIMEOUT after the context's timeout) and copies the fp32 values to
+ * `out`.  row_stride is the total number of rows, and the ranks' slices must cover every row each
+ * step.  Steps alternate between the two buffers, so a rank may start step s + 1 while a peer still
+ * reads step s.  Every rank must issue the same sequence of gather and wait calls, each wait after
+ * its gather on the same stream, and nothing of a step may be skipped. */
+#define KQ_MAX_PEERS 8
+#define KQ_IPC_HANDLE_BYTES 64
+typedef struct kq_peer_gather {
+    int world, rank;
+    int M;                         /* activation rows of every step (1..8) */
+    long long row_stride;          /* entries per row: the total number of vocabulary rows */
+    int row_begin;                 /* global row of this rank's first weight row */
+    void *regions[KQ_MAX_PEERS];   /* every rank's region: this rank's own, the others as opened */
+} kq_peer_gather;
+size_t kq_peer_region_bytes(int M, long long row_stride);
+/* cudaMalloc'd, zeroed region of `bytes` on the context's device and its IPC handle
+ * (KQ_IPC_HANDLE_BYTES bytes written to ipc_handle). */
+int kq_peer_alloc(kq_ctx *ctx, size_t bytes, void **region_dev, void *ipc_handle);
+int kq_peer_free(kq_ctx *ctx, void *region_dev);
+/* Map another process's region (its handle) into this context's device. */
+int kq_peer_open(kq_ctx *ctx, const void *ipc_handle, void **region_dev);
+int kq_peer_close(kq_ctx *ctx, void *region_dev);
+/* This rank's slice: all rows of w against the fp16 activation x_dev [M][K] (K = w's cols). */
+int kq_gemm_peer_gather_async(kq_ctx *ctx, const kq_weight *w, const uint16_t *x_dev, const kq_peer_gather *pg);
+/* Wait for every rank's slice of the current step; out_dev (fp32 [M][row_stride]) receives the
+ * gathered logits (NULL: wait only). */
+int kq_peer_gather_wait_async(kq_ctx *ctx, const kq_peer_gather *pg, float *out_dev);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,7 +35,7 @@ STATUS = {
 Q8K_DTYPE = np.dtype([("d", "<f4"), ("qs", "i1", (256,)), ("bsum32", "<i4", (8,))])
 Q8_0_DTYPE = np.dtype([("d", "<f4"), ("qs", "i1", (32,))])
 
-# every symbol declared in include/kq.h
+# every symbol declared in include/*.h
 EXPORTS = (
     "kq_version", "kq_status_string", "kq_init", "kq_destroy", "kq_set_stream", "kq_get_stream",
     "kq_synchronize", "kq_last_error", "kq_set_option", "kq_row_bytes",
@@ -49,7 +49,19 @@ EXPORTS = (
     "kq_dequant_rows", "kq_dequant_rows_async", "kq_embed_rows", "kq_embed_rows_async",
     "kq_gguf_open", "kq_gguf_open_memory", "kq_gguf_close", "kq_gguf_info", "kq_gguf_tensor_count",
     "kq_gguf_get_tensor", "kq_gguf_find_tensor", "kq_gguf_upload", "kq_gguf_upload_all",
+    "kq_peer_region_bytes", "kq_peer_alloc", "kq_peer_free", "kq_peer_open", "kq_peer_close",
+    "kq_gemm_peer_gather_async", "kq_peer_gather_wait_async",
+    "kq_measure_int8_tops",
 )
+
+MAX_PEERS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class PeerGatherStruct(C.Structure):
+    """kq_peer_gather (include/kq.h): the ranks' gather regions of one sharded LM head."""
+    _fields_ = [("world", C.c_int), ("rank", C.c_int), ("M", C.c_int), ("row_stride", C.c_longlong),
+                ("row_begin", C.c_int), ("regions", C.c_void_p * 8)]
 
 
 class GgufTensor(C.Structure):
@@ -134,6 +146,14 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "kq_gguf_find_tensor": (_i, [_vp, C.c_char_p]),
         "kq_gguf_upload": (_i, [_vp, _vp, _i, C.POINTER(_vp)]),
         "kq_gguf_upload_all": (_i, [_vp, _vp, C.POINTER(_vp), C.POINTER(_i)]),
+        "kq_peer_region_bytes": (_sz, [_i, C.c_longlong]),
+        "kq_peer_alloc": (_i, [_vp, _sz, C.POINTER(_vp), _vp]),
+        "kq_peer_free": (_i, [_vp, _vp]),
+        "kq_peer_open": (_i, [_vp, _vp, C.POINTER(_vp)]),
+        "kq_peer_close": (_i, [_vp, _vp]),
+        "kq_gemm_peer_gather_async": (_i, [_vp, _vp, _vp, C.POINTER(PeerGatherStruct)]),
+        "kq_peer_gather_wait_async": (_i, [_vp, C.POINTER(PeerGatherStruct), _vp]),
+        "kq_measure_int8_tops": (_i, [_i, _i, C.POINTER(C.c_double)]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -384,6 +404,35 @@ class Context:
     def run_ffn_async(self, gate: Weight, up: Weight, down: Weight, M: int, x_dev, gamma_dev, out_dev):
         self.check(self.L.kq_run_ffn_async(self.handle, gate.handle, up.handle, down.handle, M, _dp(x_dev),
                                            _dp(gamma_dev), _dp(out_dev)))
+
+    # ---- several GPUs: the gather in the LM head GEMV (kq_peer_*, kq_gemm_peer_gather_async)
+    def peer_region_bytes(self, M: int, row_stride: int) -> int:
+        return int(self.L.kq_peer_region_bytes(M, row_stride))
+
+    def peer_alloc(self, nbytes: int):
+        """(device pointer, IPC handle bytes) of a zeroed gather region on this context's device"""
+        ptr = _vp()
+        h = (C.c_ubyte * IPC_HANDLE_BYTES)()
+        self.check(self.L.kq_peer_alloc(self.handle, nbytes, C.byref(ptr), h))
+        return int(ptr.value), bytes(h)
+
+    def peer_free(self, ptr: int):
+        self.check(self.L.kq_peer_free(self.handle, ptr))
+
+    def peer_open(self, handle: bytes) -> int:
+        ptr = _vp()
+        buf = (C.c_ubyte * IPC_HANDLE_BYTES).from_buffer_copy(handle)
+        self.check(self.L.kq_peer_open(self.handle, buf, C.byref(ptr)))
+        return int(ptr.value)
+
+    def peer_close(self, ptr: int):
+        self.check(self.L.kq_peer_close(self.handle, ptr))
+
+    def gemm_peer_gather_async(self, w: Weight, x_dev, pg: PeerGatherStruct):
+        self.check(self.L.kq_gemm_peer_gather_async(self.handle, w.handle, _dp(x_dev), C.byref(pg)))
+
+    def peer_gather_wait_async(self, pg: PeerGatherStruct, out_dev=None):
+        self.check(self.L.kq_peer_gather_wait_async(self.handle, C.byref(pg), _dp(out_dev)))
 
     def lm_head_argmax_async(self, w: Weight, x_dev, M: int, logits_dev=None, logits_f32_dev=None, toks_dev=None,
                              vals_dev=None):

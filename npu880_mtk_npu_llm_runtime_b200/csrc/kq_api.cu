@@ -207,6 +207,7 @@ struct GemvExtra {
     int argmax_f16 = 0;
     const uint32_t *out_ids = nullptr;     // tasks[0]: output column of local row r (device)
     bool no_pdl = false;                   // the weights were written by the previous kernel
+    const kq::PeerOut *peer = nullptr;     // task 0's fp32 outputs also into every rank's gather buffer
 };
 
 int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half *x, long long x_stride,
@@ -339,6 +340,7 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
             L.argmax = ex.argmax ? ex.argmax + m0 : nullptr;
             L.argmax_f16 = ex.argmax_f16;
             L.inject_wait = c->inject_timeout ? 1 : 0;
+            if (ex.peer) L.peer = *ex.peer;
             if (int r = gemv_split_scratch(c, type, K, mt, L)) return r;
             cudaError_t e = kq::launch_gemv(L, c->stream);
             if (e == cudaErrorInvalidConfiguration && mt > 1) {
@@ -1214,5 +1216,117 @@ extern "C" int kq_eval_indexed_rows_argmax(kq_ctx *c, const kq_weight *w, const 
             top_toks[m] = bt[m];
         }
     }
+    return KQ_OK;
+}
+
+// =================================================================== several GPUs: the gather
+
+namespace {
+
+int check_peer_gather(kq_ctx *c, const kq_peer_gather *pg) {
+    if (!pg) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL kq_peer_gather");
+    if (pg->world < 1 || pg->world > KQ_MAX_PEERS || pg->rank < 0 || pg->rank >= pg->world)
+        return fail(c, KQ_ERR_INVALID_ARGUMENT, "rank %d of world %d (1..%d ranks)", pg->rank, pg->world, KQ_MAX_PEERS);
+    if (pg->M < 1 || pg->M > 8) return fail(c, KQ_ERR_SHAPE, "gather M = %d outside [1, 8]", pg->M);
+    if (pg->row_stride < 1 || pg->row_begin < 0)
+        return fail(c, KQ_ERR_SHAPE, "row_stride %lld, row_begin %d", pg->row_stride, pg->row_begin);
+    for (int q = 0; q < pg->world; ++q)
+        if (!pg->regions[q]) return fail(c, KQ_ERR_INVALID_ARGUMENT, "region of rank %d is NULL", q);
+    return KQ_OK;
+}
+
+}  // namespace
+
+extern "C" size_t kq_peer_region_bytes(int M, long long row_stride) {
+    if (M < 1 || row_stride < 1) return 0;
+    return kq::PEER_CTRL_BYTES + 2 * (size_t)M * (size_t)row_stride * sizeof(unsigned long long);
+}
+
+extern "C" int kq_peer_alloc(kq_ctx *c, size_t bytes, void **region_dev, void *ipc_handle) {
+    if (!c || !region_dev || !ipc_handle) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (bytes < kq::PEER_CTRL_BYTES) return fail(c, KQ_ERR_INVALID_ARGUMENT, "region of %zu bytes", bytes);
+    static_assert(sizeof(cudaIpcMemHandle_t) == KQ_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaSetDevice(c->device);
+    void *p = nullptr;
+    KQ_CUDA(c, cudaMalloc(&p, bytes));
+    cudaError_t e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(c, e, "peer region");
+    }
+    memcpy(ipc_handle, &h, sizeof h);
+    *region_dev = p;
+    return KQ_OK;
+}
+
+extern "C" int kq_peer_free(kq_ctx *c, void *region_dev) {
+    if (!c || !region_dev) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    cudaSetDevice(c->device);
+    KQ_CUDA(c, cudaFree(region_dev));
+    return KQ_OK;
+}
+
+extern "C" int kq_peer_open(kq_ctx *c, const void *ipc_handle, void **region_dev) {
+    if (!c || !ipc_handle || !region_dev) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    cudaSetDevice(c->device);
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof h);
+    KQ_CUDA(c, cudaIpcOpenMemHandle(region_dev, h, cudaIpcMemLazyEnablePeerAccess));
+    return KQ_OK;
+}
+
+extern "C" int kq_peer_close(kq_ctx *c, void *region_dev) {
+    if (!c || !region_dev) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    cudaSetDevice(c->device);
+    KQ_CUDA(c, cudaIpcCloseMemHandle(region_dev));
+    return KQ_OK;
+}
+
+extern "C" int kq_gemm_peer_gather_async(kq_ctx *c, const kq_weight *w, const uint16_t *x_dev,
+                                         const kq_peer_gather *pg) {
+    if (!c || !w || !x_dev) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = check_peer_gather(c, pg)) return r;
+    if (int r = check_weight_device(c, w)) return r;
+    if ((long long)pg->row_begin + w->rows > pg->row_stride)
+        return fail(c, KQ_ERR_SHAPE, "rows [%d, %d) past row_stride %lld", pg->row_begin, pg->row_begin + w->rows,
+                    pg->row_stride);
+    cudaSetDevice(c->device);
+    kq::PeerOut po;
+    po.n = pg->world;
+    po.rank = pg->rank;
+    for (int q = 0; q < pg->world; ++q)
+        po.buf[q] = reinterpret_cast<unsigned long long *>(static_cast<uint8_t *>(pg->regions[q]) + kq::PEER_CTRL_BYTES);
+    uint8_t *own = static_cast<uint8_t *>(pg->regions[pg->rank]);
+    po.step = reinterpret_cast<const unsigned long long *>(own + 64);
+    po.row_stride = pg->row_stride;
+    po.buf_stride = (long long)pg->M * pg->row_stride;
+    po.row0 = pg->row_begin;
+    kq_task t{};
+    t.w = w;
+    t.row_begin = 0;
+    t.rows = w->rows;
+    GemvExtra ex;
+    ex.peer = &po;
+    return run_gemv(c, &t, 1, pg->M, w->cols, reinterpret_cast<const __half *>(x_dev), w->cols, nullptr, nullptr, ex);
+}
+
+extern "C" int kq_peer_gather_wait_async(kq_ctx *c, const kq_peer_gather *pg, float *out_dev) {
+    if (!c) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (int r = check_peer_gather(c, pg)) return r;
+    cudaSetDevice(c->device);
+    uint8_t *own = static_cast<uint8_t *>(pg->regions[pg->rank]);
+    kq::PeerWait W{};
+    W.step = reinterpret_cast<unsigned long long *>(own + 64);
+    W.arrivals = reinterpret_cast<unsigned *>(own + 76);
+    W.buf = reinterpret_cast<const unsigned long long *>(own + kq::PEER_CTRL_BYTES);
+    W.buf_stride = (long long)pg->M * pg->row_stride;
+    W.n_entries = (long long)pg->M * pg->row_stride;
+    W.out = out_dev;
+    W.status = c->d_status;
+    W.timeout_ns = c->timeout_ns;
+    W.pdl = c->pdl;
+    KQ_CUDA(c, kq::launch_peer_wait(W, c->stream));
     return KQ_OK;
 }

@@ -294,6 +294,31 @@ __device__ __forceinline__ int sbyte(uint32_t w, int k) {
     return r;
 }
 
+// fp32 outputs of a GEMV also stored into every rank's gather buffer (several GPUs, one process
+// each, buffers mapped over NVLink).  A kq_peer_gather region is 256 bytes of control words --
+// this rank's completed steps (u64 at 64), the wait kernel's CTA arrivals (u32 at 76) -- then two
+// buffers of [M][row_stride] 64-bit entries, used by alternate steps.  Each entry is one aligned
+// 64-bit store of (step tag << 32 | fp32 bits): a reader that sees the tag of the step it waits
+// for has the value, with no fence or flag between writer and reader.
+constexpr int PEER_MAX = 8;
+constexpr size_t PEER_CTRL_BYTES = 256;
+struct PeerOut {
+    int n = 0, rank = 0;
+    unsigned long long *buf[PEER_MAX];         // every rank's entries (region + 256)
+    const unsigned long long *step = nullptr;  // this rank's completed steps
+    long long row_stride = 0, buf_stride = 0;  // entries per row / per buffer
+    int row0 = 0;                              // global row of local row 0
+};
+
+// The step the current launch produces: one more than the steps this rank completed (written by
+// an earlier kernel, constant during this one: read through the read-only cache).
+__device__ __forceinline__ unsigned long long peer_step(const PeerOut &po) { return __ldg(po.step) + 1ull; }
+
+__device__ __forceinline__ void peer_store(unsigned long long *p, float v, uint32_t tag) {
+    const unsigned long long e = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(e) : "memory");
+}
+
 // Bounded wait until *p >= v (a shared-memory counter other warps advance).
 __device__ __forceinline__ bool wait_ge_bounded(const int *p, int v, uint64_t timeout_ns, int *status) {
     const volatile int *vp = p;

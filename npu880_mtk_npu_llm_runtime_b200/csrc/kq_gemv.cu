@@ -525,6 +525,7 @@ cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
     p.argmax = L.argmax;
     p.argmax_f16 = L.argmax_f16;
     p.inject_wait = L.inject_wait;
+    p.peer = L.peer;
     p.off_x = pl.off_x;
     p.off_dx = pl.off_dx;
     p.off_xs = pl.off_xs;
@@ -593,6 +594,83 @@ cudaError_t launch_gather_rows(int type, int K, const uint8_t *src, const uint32
     const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
     kq_gather_rows<<<blocks, 256, 0, stream>>>(type, K / 256, src, ids, n, dst, rb);
     return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ the ranks' gather
+
+// Every thread reads its share of the M x row_stride entries of buffer s % 2 (s = completed steps
+// + 1) until each carries tag s -- bounded: the first thread to give up records DEV_ERR_TIMEOUT and
+// every thread stops waiting -- and writes the values to `out`.  The last CTA to finish counts the
+// step as completed.  It may be launched while this rank's GEMV still runs (programmatic dependent
+// launch), but reads nothing before the GEMV grid has completed (griddepcontrol.wait), so it never
+// spins on a kernel of its own GPU; it lets the next kernel launch at once.
+__global__ void __launch_bounds__(256) kq_peer_gather_wait(const __grid_constant__ PeerWait W) {
+    __shared__ unsigned long long s_step;
+    __shared__ int s_fail;
+    const int tid = threadIdx.x;
+    // the next GEMV (launched with programmatic dependent launch) may stream its weights while
+    // this kernel waits; it reads the step counter and the buffers only after this grid completes
+    asm volatile("griddepcontrol.launch_dependents;");
+    // this rank's GEMV must be complete before anything is read: a dependent-launch wait (the
+    // hardware orders it), not a spin on a kernel of this GPU
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (tid == 0) {
+        s_step = *reinterpret_cast<const volatile unsigned long long *>(W.step) + 1ull;
+        s_fail = 0;
+    }
+    __syncthreads();
+    const unsigned long long s = s_step;
+    const uint32_t tag = (uint32_t)s;
+    const unsigned long long *src = W.buf + (size_t)(s & 1ull) * W.buf_stride;
+    const uint64_t t0 = global_timer_ns();
+    // four consecutive entries per thread, loaded together; an entry without the tag yet is polled
+    const long long stride = (long long)gridDim.x * blockDim.x * 4;
+    for (long long i0 = ((long long)blockIdx.x * blockDim.x + tid) * 4; i0 < W.n_entries; i0 += stride) {
+        unsigned long long e[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (i0 + k < W.n_entries)
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(e[k]) : "l"(src + i0 + k) : "memory");
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (i0 + k >= W.n_entries) break;
+            int polls = 0;
+            while ((uint32_t)(e[k] >> 32) != tag) {
+                if ((++polls & 63) == 0) {
+                    if (*reinterpret_cast<volatile int *>(&s_fail)) break;
+                    if (global_timer_ns() - t0 > W.timeout_ns) {
+                        report_error(W.status, DEV_ERR_TIMEOUT);
+                        s_fail = 1;
+                        break;
+                    }
+                }
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(e[k]) : "l"(src + i0 + k) : "memory");
+            }
+            if (W.out) W.out[i0 + k] = __uint_as_float((uint32_t)e[k]);
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(W.arrivals, 1u) == gridDim.x - 1) {
+            *reinterpret_cast<volatile unsigned *>(W.arrivals) = 0u;
+            __threadfence();
+            *reinterpret_cast<volatile unsigned long long *>(W.step) = s;
+        }
+    }
+}
+
+cudaError_t launch_peer_wait(const PeerWait &W, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)std::min<long long>(1024, std::max<long long>(1, (W.n_entries + 1023) / 1024)));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = W.pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kq_peer_gather_wait, W);
 }
 
 }  // namespace kq

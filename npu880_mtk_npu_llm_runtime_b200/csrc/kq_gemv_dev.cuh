@@ -66,6 +66,7 @@ struct GemvParams {
     long long total_tiles;
     float *gterms;
     int *gcount;
+    PeerOut peer;  // task 0's fp32 outputs also into every rank's gather buffer (peer.n > 0)
 };
 
 
@@ -692,6 +693,14 @@ __device__ __forceinline__ void epilogue(const GemvParams &p, const GemvTaskDev 
                                          unsigned long long *s_best) {
     const size_t col = tk.out_ids ? (size_t)tk.out_ids[r] : (size_t)r;
     if (tk.dst_f32) tk.dst_f32[(size_t)tok * tk.f32_stride + col] = acc;
+    if (p.peer.n) {
+        const unsigned long long st = peer_step(p.peer);
+        const size_t o = (size_t)(st & 1ull) * p.peer.buf_stride + (size_t)tok * p.peer.row_stride +
+                         (size_t)(p.peer.row0 + r);
+#pragma unroll
+        for (int q = 0; q < PEER_MAX; ++q)
+            if (q < p.peer.n) peer_store(p.peer.buf[q] + o, acc, (uint32_t)st);
+    }
     if (tk.dst) {
         float v = acc;
         if (tk.res) v = __fadd_rn(v, __half2float(tk.res[(size_t)tok * tk.res_stride + col]));

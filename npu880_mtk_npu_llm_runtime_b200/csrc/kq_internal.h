@@ -5,6 +5,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "kq_common.cuh"  // PeerOut
+
 // A GGUF tensor resident in HBM in this library's row-group tile layout (opaque kq_weight of
 // kq.h; layout in kq_common.cuh).
 struct kq_weight {
@@ -58,7 +60,24 @@ struct GemvLaunch {
     float *split_terms = nullptr;
     size_t split_terms_bytes = 0;
     int *split_count = nullptr;
+    PeerOut peer;  // n > 0: task 0's fp32 outputs also into every rank's gather buffer
 };
+
+// Wait (bounded) until every entry of the gather buffer of the step after this rank's completed
+// steps carries that step's tag, write the values to `out` (may be nullptr) and count the step as
+// completed.
+struct PeerWait {
+    unsigned long long *step;        // this rank's completed steps
+    unsigned *arrivals;              // the wait kernel's CTA arrivals
+    const unsigned long long *buf;   // this rank's entries
+    long long buf_stride;            // entries per buffer
+    long long n_entries;             // entries to read (M x row_stride)
+    float *out;
+    int *status;
+    unsigned long long timeout_ns;
+    bool pdl;  // may launch while the preceding kernel runs (it waits for it with griddepcontrol.wait)
+};
+cudaError_t launch_peer_wait(const PeerWait &W, cudaStream_t stream);
 
 // Many-token product on the tensor cores (kq_gemm_tc.cu): tasks of one type, the input as fp16
 // x or pre-quantized act (as in GemvLaunch), packed into `scratch` (tc_scratch_bytes) first.

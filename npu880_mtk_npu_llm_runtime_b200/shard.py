@@ -10,6 +10,8 @@ to the concatenated slices.
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import numpy as np
 
 
@@ -197,3 +199,75 @@ class RowShardedFfn:
         with self._on_ctx_stream():
             all_gather(self.o_all, self.o_send.view(-1))
         self.assemble_out(y)
+
+
+class PeerGather:
+    """The vocabulary-sharded LM head with its all-gather inside the GEMV (kq_peer_gather).
+
+    Each rank owns a region (two buffers of [M][vocab] tagged 64-bit entries and control words);
+    the regions are exchanged as IPC handles and opened by every rank.  gather(w, x) runs this
+    rank's slice and stores every logit, tagged with the step, into every rank's region over
+    NVLink; wait(out) reads (bounded) until all entries carry the step and copies the logits to out
+    (fp32 [M][vocab]).
+
+    exchange(handle) -> the handles of all ranks in rank order (e.g. torch_exchange).  For tests on
+    one device, PeerGather.emulated builds `world` ranks in this process."""
+
+    def __init__(self, ctx, rank: int, world: int, M: int, vocab: int, row_begin: int, exchange=None,
+                 regions=None, own=None):
+        from . import PeerGatherStruct
+        self.ctx, self.rank, self.world, self.M, self.vocab = ctx, rank, world, M, vocab
+        self.row_stride = vocab
+        self.opened, self.owned = [], []
+        if regions is None:
+            nbytes = ctx.peer_region_bytes(M, self.row_stride)
+            own, handle = ctx.peer_alloc(nbytes)
+            self.owned.append(own)
+            handles = exchange(handle) if world > 1 else [handle]
+            regions = []
+            for q, hq in enumerate(handles):
+                if q == rank:
+                    regions.append(own)
+                else:
+                    p = ctx.peer_open(hq)
+                    self.opened.append(p)
+                    regions.append(p)
+        elif own is not None:
+            self.owned.append(own)
+        arr = (C.c_void_p * 8)(*(list(regions) + [None] * (8 - len(regions))))
+        self.pg = PeerGatherStruct(world, rank, M, self.row_stride, row_begin, arr)
+
+    @classmethod
+    def emulated(cls, ctx, world: int, M: int, vocab: int) -> list["PeerGather"]:
+        """`world` ranks in one process on ctx's device (their regions are plain device memory of
+        this process, so no IPC)."""
+        nbytes = ctx.peer_region_bytes(M, vocab)
+        owns = [ctx.peer_alloc(nbytes)[0] for _ in range(world)]
+        out = []
+        for r in range(world):
+            row0, _ = vocab_slice(r, world, vocab)
+            out.append(cls(ctx, r, world, M, vocab, row0, regions=owns, own=owns[r]))
+        return out
+
+    def gather(self, w, x_dev):
+        self.ctx.gemm_peer_gather_async(w, x_dev, self.pg)
+
+    def wait(self, out_dev=None):
+        self.ctx.peer_gather_wait_async(self.pg, out_dev)
+
+    def close(self):
+        for p in self.opened:
+            self.ctx.peer_close(p)
+        for p in self.owned:
+            self.ctx.peer_free(p)
+        self.opened, self.owned = [], []
+
+
+def torch_exchange(handle: bytes, device) -> list[bytes]:
+    """All ranks' IPC handles through torch.distributed (an all-gather of the 64 handle bytes)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(list(handle), dtype=torch.uint8, device=device)
+    outs = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(outs, t)
+    return [bytes(o.cpu().tolist()) for o in outs]

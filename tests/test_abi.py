@@ -1,4 +1,4 @@
-"""libkq.so loads, exports exactly what include/kq.h declares, and its host-side logic works
+"""libkq.so loads, exports exactly what include/*.h declare, and its host-side logic works
 without a GPU (no compute calls here)."""
 from __future__ import annotations
 
@@ -21,9 +21,14 @@ def lib():
 
 
 def header_symbols():
-    src = open(os.path.join(ROOT, "include", "kq.h")).read()
-    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(kq_[a-z0-9_]+)\s*\(", src)))
+    """every function declared in include/*.h"""
+    names = set()
+    for h in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if h.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", h)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names |= set(re.findall(r"\b(kq_[a-z0-9_]+)\s*\(", src))
+    return sorted(names)
 
 
 def test_header_declares_the_python_export_list():
@@ -97,3 +102,28 @@ def test_synth_layouts():
             m = C.c_uint8()
             lib.kqo_get_scale_min_k4(j, packed[b].ctypes.data_as(C.c_void_p), C.byref(d), C.byref(m))
             assert (d.value, m.value) == (sc[b, j], mn[b, j])
+
+
+def test_peer_gather_struct_layout(tmp_path):
+    """kq_peer_gather as compiled by C has the field offsets of the ctypes mirror."""
+    import subprocess
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "kq.h"\nint main(void) {\n'
+                   '  printf("%zu %zu %zu %zu %zu %zu %zu\\n", offsetof(kq_peer_gather, world), offsetof(kq_peer_gather, rank),\n'
+                   '         offsetof(kq_peer_gather, M), offsetof(kq_peer_gather, row_stride),\n'
+                   '         offsetof(kq_peer_gather, row_begin), offsetof(kq_peer_gather, regions), sizeof(kq_peer_gather));\n'
+                   '  return 0;\n}\n')
+    exe = tmp_path / "layout"
+    inc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+    subprocess.check_call(["gcc", "-I", inc, str(src), "-o", str(exe)])
+    got = [int(v) for v in subprocess.check_output([str(exe)]).split()]
+    S = kq.PeerGatherStruct
+    want = [S.world.offset, S.rank.offset, S.M.offset, S.row_stride.offset, S.row_begin.offset, S.regions.offset,
+            C.sizeof(S)]
+    assert got == want
+
+
+def test_peer_region_bytes(lib):
+    """256 bytes of control words, then two buffers of [M][row_stride] 64-bit entries"""
+    assert lib.kq_peer_region_bytes(2, 151936) == 256 + 2 * 2 * 151936 * 8
+    assert lib.kq_peer_region_bytes(0, 151936) == 0
