@@ -18,11 +18,14 @@ activation is quantized to Q8_K inside the kernel and the 9728 fp32 outputs are 
   gpu_launches: kernels of this library launched inside the timed region
 
 --config lm_head runs config 1 (Q6_K LM head, N=151936, K=2560) with vocab rows
-sharded over the ranks and the logit slices all-gathered with NCCL.
+sharded over the ranks and the logit slices all-gathered with NCCL, and (record p2p_gather) with
+the gather inside the GEMV over NVLink.  --config ffn / prefill / decode run configs 2-4
+(--tokens M; --ffn-fused 0 times the FFN block's four launches instead of the persistent kernel).
 --impl reference times the reference engine's own CPU path (oracle/_ref, built from its
 sources) on this host on the same workload.
 
-python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config gemv|lm_head]
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                [--config gemv|lm_head|ffn|prefill|decode] [--tokens M]
 """
 from __future__ import annotations
 
@@ -349,18 +352,24 @@ def lm_head_sharded(ctx, args, rank, world, dev, stream, steps, warmup, want_arg
                           exchange=(lambda h: shard.torch_exchange(h, dev)) if world > 1 else None)
     p2p_out = torch.zeros((1, pg.row_stride), dtype=torch.float32, device=dev)
 
-    def step_p(i):
+    def step_p(i):  # the step completes inside the GEMV (its last CTAs collect the other ranks' rows)
+        pg.gather(Ws[i % n_copies], x, p2p_out)
+
+    def step_w(i):  # the same with a separate wait kernel
         pg.gather(Ws[i % n_copies], x)
         pg.wait(p2p_out)
 
+    dtw = graph_timed(stream, step_w, steps, warmup, world)
     dtp = graph_timed(stream, step_p, steps, warmup, world)
     torch.cuda.synchronize()
     same = bool(torch.equal(p2p_out[0, :V], gather[:V]))
     rec["p2p_gather"] = {"value": round(float(total.item()) * steps / dtp / 1e9, 1), "unit": "GB/s",
                          "ms_per_step": round(dtp / steps * 1e3, 6), "equal_to_nccl_gather": same,
                          "how": "GEMV epilogue stores each logit into every rank's buffer over NVLink as one 64-bit "
-                                "(step, fp32) entry; a bounded wait reads the entries until all carry the step and "
-                                "writes the fp32 logits out"}
+                                "(step, fp32) entry; the GEMV's last CTAs read the other ranks' entries until all carry "
+                                "the step and write the fp32 logits out",
+                         "with_wait_kernel": {"ms_per_step": round(dtw / steps * 1e3, 6),
+                                              "value": round(float(total.item()) * steps / dtw / 1e9, 1)}}
     if world > 1:
         dist.barrier()
     pg.close()
@@ -629,11 +638,13 @@ def run_stack(args, rank, world, local_rank):
         x = torch.from_numpy(x16.view(np.uint16).copy()).to(dev).view(torch.float16).view(M, HIDDEN)
         gm = torch.from_numpy(gamma.view(np.uint16).copy()).to(dev)
         out = torch.zeros((M, HIDDEN), dtype=torch.float16, device=dev)
+        ctx.set_option("ffn_fused", args.ffn_fused)
+        fused = bool(args.ffn_fused) and M <= 2  # the persistent kernel covers 1-2 tokens of these types
         if world == 1:
             def step(i):
                 g_, u_, d_ = sets[i % n_sets]
                 ctx.run_ffn_async(g_, u_, d_, M, x, gm, out)
-            launches = 4
+            launches = 1 if fused else 4
         else:
             rk = shard.RowShardedFfn(ctx, plan, rank, M, dev)
             tks = [rk.tasks(*st_, x) for st_ in sets]
@@ -690,6 +701,8 @@ def run_stack(args, rank, world, local_rank):
             "config": {"workload": f"config2: FFN block M={M}, hidden 2560, intermediate 9728"
                                    + (" (batched prefill FFN)" if M > 64 else " (tree verify)"),
                        "m": M, "weight_bytes_per_step": wbytes, "weight_bytes_per_step_per_rank": rank_wbytes,
+                       "form": ("one persistent kernel (kq_ffn_fused)" if fused and world == 1 else
+                                "RMSNorm+Q8_K, gate/up, SwiGLU+Q8_K, down+residual launches"),
                        "tops": round(ops * steps / dt / 1e12, 3),
                        "l2": f"{n_sets} rotating weight sets per rank ({n_sets * rank_wbytes / 2**20:.0f} MiB > 2x126 MB L2)",
                        "parallelism": "replicas x1" if world == 1 else f"row-shard x{world}",
@@ -995,6 +1008,8 @@ def main():
     ap.add_argument("--config", choices=["gemv", "lm_head", "ffn", "prefill", "decode"], default="gemv")
     # (not "--m": torchrun's own parser takes it for an abbreviation of its options)
     ap.add_argument("--tokens", "--m", dest="tokens", type=int, default=0, help="tokens (ffn: 8/16/32/64 or 512/2048, prefill: 512/2048)")
+    ap.add_argument("--ffn-fused", type=int, default=1, help="ffn: 1 = the persistent FFN kernel where it applies "
+                                                              "(1-2 tokens), 0 = the four launches")
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
