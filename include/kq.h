@@ -341,10 +341,15 @@ int kq_peer_free(kq_ctx *ctx, void *region_dev);
 /* Map another process's region (its handle) into this context's device. */
 int kq_peer_open(kq_ctx *ctx, const void *ipc_handle, void **region_dev);
 int kq_peer_close(kq_ctx *ctx, void *region_dev);
-/* This rank's slice: all rows of w against the fp16 activation x_dev [M][K] (K = w's cols). */
-int kq_gemm_peer_gather_async(kq_ctx *ctx, const kq_weight *w, const uint16_t *x_dev, const kq_peer_gather *pg);
-/* Wait for every rank's slice of the current step; out_dev (fp32 [M][row_stride]) receives the
- * gathered logits (NULL: wait only). */
+/* This rank's slice: all rows of w against the fp16 activation x_dev [M][K] (K = w's cols).  With
+ * out_dev (fp32 [M][row_stride]) the step completes inside this call's kernel: this rank's logits go
+ * to out_dev from the epilogue, and the kernel's last CTAs wait (bounded) for the other ranks'
+ * entries and write them to out_dev -- no wait call follows.  With out_dev NULL the step is
+ * completed by kq_peer_gather_wait_async. */
+int kq_gemm_peer_gather_async(kq_ctx *ctx, const kq_weight *w, const uint16_t *x_dev, const kq_peer_gather *pg,
+                              float *out_dev);
+/* Wait for every rank's slice of the current step (after a kq_gemm_peer_gather_async without
+ * out_dev); out_dev (fp32 [M][row_stride]) receives the gathered logits (NULL: wait only). */
 int kq_peer_gather_wait_async(kq_ctx *ctx, const kq_peer_gather *pg, float *out_dev);
 
 #ifdef __cplusplus

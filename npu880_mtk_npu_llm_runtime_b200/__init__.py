@@ -151,7 +151,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "kq_peer_free": (_i, [_vp, _vp]),
         "kq_peer_open": (_i, [_vp, _vp, C.POINTER(_vp)]),
         "kq_peer_close": (_i, [_vp, _vp]),
-        "kq_gemm_peer_gather_async": (_i, [_vp, _vp, _vp, C.POINTER(PeerGatherStruct)]),
+        "kq_gemm_peer_gather_async": (_i, [_vp, _vp, _vp, C.POINTER(PeerGatherStruct), _vp]),
         "kq_peer_gather_wait_async": (_i, [_vp, C.POINTER(PeerGatherStruct), _vp]),
         "kq_measure_int8_tops": (_i, [_i, _i, C.POINTER(C.c_double)]),
     }
@@ -428,8 +428,8 @@ class Context:
     def peer_close(self, ptr: int):
         self.check(self.L.kq_peer_close(self.handle, ptr))
 
-    def gemm_peer_gather_async(self, w: Weight, x_dev, pg: PeerGatherStruct):
-        self.check(self.L.kq_gemm_peer_gather_async(self.handle, w.handle, _dp(x_dev), C.byref(pg)))
+    def gemm_peer_gather_async(self, w: Weight, x_dev, pg: PeerGatherStruct, out_dev=None):
+        self.check(self.L.kq_gemm_peer_gather_async(self.handle, w.handle, _dp(x_dev), C.byref(pg), _dp(out_dev)))
 
     def peer_gather_wait_async(self, pg: PeerGatherStruct, out_dev=None):
         self.check(self.L.kq_peer_gather_wait_async(self.handle, C.byref(pg), _dp(out_dev)))

@@ -1285,7 +1285,7 @@ extern "C" int kq_peer_close(kq_ctx *c, void *region_dev) {
 }
 
 extern "C" int kq_gemm_peer_gather_async(kq_ctx *c, const kq_weight *w, const uint16_t *x_dev,
-                                         const kq_peer_gather *pg) {
+                                         const kq_peer_gather *pg, float *out_dev) {
     if (!c || !w || !x_dev) return fail(c, KQ_ERR_INVALID_ARGUMENT, "NULL argument");
     if (int r = check_peer_gather(c, pg)) return r;
     if (int r = check_weight_device(c, w)) return r;
@@ -1307,6 +1307,18 @@ extern "C" int kq_gemm_peer_gather_async(kq_ctx *c, const kq_weight *w, const ui
     t.w = w;
     t.row_begin = 0;
     t.rows = w->rows;
+    if (out_dev) {
+        // the step completes inside the GEMV: this rank's rows straight to out, the others' rows
+        // collected by the launch's last CTAs
+        po.out = out_dev;
+        po.rows = w->rows;
+        po.M = pg->M;
+        po.arrivals = reinterpret_cast<unsigned *>(own + 72);
+        po.tail_done = reinterpret_cast<unsigned *>(own + 80);
+        po.step_rw = reinterpret_cast<unsigned long long *>(own + 64);
+        t.dst_f32 = out_dev + pg->row_begin;
+        t.dst_f32_stride = (size_t)pg->row_stride;
+    }
     GemvExtra ex;
     ex.peer = &po;
     return run_gemv(c, &t, 1, pg->M, w->cols, reinterpret_cast<const __half *>(x_dev), w->cols, nullptr, nullptr, ex);

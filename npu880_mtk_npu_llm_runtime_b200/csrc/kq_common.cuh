@@ -306,9 +306,51 @@ struct PeerOut {
     int n = 0, rank = 0;
     unsigned long long *buf[PEER_MAX];         // every rank's entries (region + 256)
     const unsigned long long *step = nullptr;  // this rank's completed steps
-    long long row_stride = 0, buf_stride = 0;  // entries per row / per buffer
+    long long row_stride = 0, buf_stride = 0;  // entries per row (all rows) / per buffer
     int row0 = 0;                              // global row of local row 0
+    // completion inside the GEMV (out != nullptr): the launch's last CTAs wait for the other ranks'
+    // entries of this step and write them to out (this rank's rows go there from the epilogue),
+    // then the step is counted as completed
+    float *out = nullptr;                      // fp32 [M][row_stride]
+    int rows = 0, M = 0;                       // this rank's rows, tokens
+    unsigned *arrivals = nullptr, *tail_done = nullptr;  // CTA arrivals, tail CTAs finished
+    unsigned long long *step_rw = nullptr;     // the completed-steps word, written by the last tail CTA
 };
+
+// Bounded read of the tagged entries src[map(j)] for j in [jb, je), four per thread at a time,
+// into out[map(j)] (when out is set): an entry without `tag` yet is read again.  On timeout the
+// thread records DEV_ERR_TIMEOUT and sets *fail, which the other threads see and stop waiting.
+template <class Map>
+__device__ __forceinline__ void peer_collect(const unsigned long long *src, uint32_t tag, long long jb, long long je,
+                                             int tid, int nthreads, Map map, float *out, uint64_t t0,
+                                             unsigned long long timeout_ns, int *status, volatile int *fail) {
+    for (long long j0 = jb + 4ll * tid; j0 < je; j0 += 4ll * nthreads) {
+        unsigned long long e[4];
+        long long o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            o[k] = (j0 + k < je) ? map(j0 + k) : 0;
+            if (j0 + k < je) asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(e[k]) : "l"(src + o[k]) : "memory");
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (j0 + k >= je) break;
+            int polls = 0;
+            while ((uint32_t)(e[k] >> 32) != tag) {
+                if ((++polls & 63) == 0) {
+                    if (*fail) break;
+                    if (global_timer_ns() - t0 > timeout_ns) {
+                        report_error(status, DEV_ERR_TIMEOUT);
+                        *fail = 1;
+                        break;
+                    }
+                }
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(e[k]) : "l"(src + o[k]) : "memory");
+            }
+            if (out) out[o[k]] = __uint_as_float((uint32_t)e[k]);
+        }
+    }
+}
 
 // The step the current launch produces: one more than the steps this rank completed (written by
 // an earlier kernel, constant during this one: read through the read-only cache).

@@ -39,6 +39,51 @@
 
 namespace kq {
 
+// ------------------------------------------------------------------ the ranks' gather, in the GEMV
+//
+// After the CTA's outputs: count the CTA's arrival; the last PEER_TAIL_CTAS to arrive (every other
+// CTA of the grid has finished) each wait for, and write to p.peer.out, an equal share of the
+// other ranks' entries of this step -- stores of other GPUs' kernels only, never of a CTA of this
+// grid, so nothing waits for a CTA that may not be resident.  The last of them to finish clears
+// the counts and counts the step as completed.
+constexpr unsigned PEER_TAIL_CTAS = 16;
+
+__device__ __noinline__ void peer_tail(const GemvParams &p, int tid, bool aborted) {
+    __shared__ int s_tail, s_fail;
+    const PeerOut &po = p.peer;
+    const unsigned G = gridDim.x, Kt = G < PEER_TAIL_CTAS ? G : PEER_TAIL_CTAS;
+    if (tid == 0) {
+        const unsigned a = atomicAdd(po.arrivals, 1u);
+        s_tail = (a >= G - Kt) ? (int)(a - (G - Kt)) : -1;
+        s_fail = 0;
+    }
+    __syncthreads();
+    const int t = s_tail;
+    if (t < 0) return;
+    const unsigned long long st = peer_step(po);
+    const long long other = po.row_stride - po.rows, total = (long long)po.M * other;
+    if (!aborted && total > 0) {
+        const unsigned long long *src = po.buf[po.rank] + (size_t)(st & 1ull) * po.buf_stride;
+        const long long r0 = po.row0, rows = po.rows, rs = po.row_stride;
+        auto map = [=](long long j) {
+            const long long tok = j / other, c = j - tok * other;
+            return tok * rs + (c < r0 ? c : c + rows);
+        };
+        peer_collect(src, (uint32_t)st, total * t / Kt, total * (t + 1) / Kt, tid, (int)blockDim.x, map, po.out,
+                     global_timer_ns(), p.timeout_ns, p.status, &s_fail);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(po.tail_done, 1u) == Kt - 1) {
+            *reinterpret_cast<volatile unsigned *>(po.arrivals) = 0u;
+            *reinterpret_cast<volatile unsigned *>(po.tail_done) = 0u;
+            __threadfence();
+            *reinterpret_cast<volatile unsigned long long *>(po.step_rw) = st;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ the kernel
 //
 // CTA c owns row groups [rg_lo, rg_hi) = tiles [t0, t1) of the launch's tile sequence
@@ -333,6 +378,7 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
     }
     __syncthreads();
     if (p.argmax && tid < p.M && !s_abort) atomicMax(&p.argmax[tid], s_best[tid]);
+    if (p.peer.out) peer_tail(p, tid, s_abort != 0);
     // drain: a slot's most recent copy must land before the CTA exits (matters only after an
     // early stop); consumers never arrive on full barriers, so the last S issued stages are
     // exactly the outstanding candidates
@@ -622,33 +668,9 @@ __global__ void __launch_bounds__(256) kq_peer_gather_wait(const __grid_constant
     const unsigned long long s = s_step;
     const uint32_t tag = (uint32_t)s;
     const unsigned long long *src = W.buf + (size_t)(s & 1ull) * W.buf_stride;
-    const uint64_t t0 = global_timer_ns();
-    // four consecutive entries per thread, loaded together; an entry without the tag yet is polled
-    const long long stride = (long long)gridDim.x * blockDim.x * 4;
-    for (long long i0 = ((long long)blockIdx.x * blockDim.x + tid) * 4; i0 < W.n_entries; i0 += stride) {
-        unsigned long long e[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-            if (i0 + k < W.n_entries)
-                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(e[k]) : "l"(src + i0 + k) : "memory");
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            if (i0 + k >= W.n_entries) break;
-            int polls = 0;
-            while ((uint32_t)(e[k] >> 32) != tag) {
-                if ((++polls & 63) == 0) {
-                    if (*reinterpret_cast<volatile int *>(&s_fail)) break;
-                    if (global_timer_ns() - t0 > W.timeout_ns) {
-                        report_error(W.status, DEV_ERR_TIMEOUT);
-                        s_fail = 1;
-                        break;
-                    }
-                }
-                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(e[k]) : "l"(src + i0 + k) : "memory");
-            }
-            if (W.out) W.out[i0 + k] = __uint_as_float((uint32_t)e[k]);
-        }
-    }
+    // every thread of the grid: entries 4 t .. 4 t + 3, then the next 4 x (threads of the grid)
+    peer_collect(src, tag, 0, W.n_entries, (int)(blockIdx.x * blockDim.x + tid), (int)(gridDim.x * blockDim.x),
+                 [](long long j) { return j; }, W.out, global_timer_ns(), W.timeout_ns, W.status, &s_fail);
     __syncthreads();
     if (tid == 0) {
         __threadfence();

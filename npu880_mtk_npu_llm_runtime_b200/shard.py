@@ -249,8 +249,10 @@ class PeerGather:
             out.append(cls(ctx, r, world, M, vocab, row0, regions=owns, own=owns[r]))
         return out
 
-    def gather(self, w, x_dev):
-        self.ctx.gemm_peer_gather_async(w, x_dev, self.pg)
+    def gather(self, w, x_dev, out_dev=None):
+        """This rank's slice into every rank's buffer.  With out_dev the step completes inside the
+        kernel (no wait call); without, wait() completes it."""
+        self.ctx.gemm_peer_gather_async(w, x_dev, self.pg, out_dev)
 
     def wait(self, out_dev=None):
         self.ctx.peer_gather_wait_async(self.pg, out_dev)

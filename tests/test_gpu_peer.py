@@ -74,3 +74,30 @@ def test_peer_gather_wait_times_out(kqctx):
     kqctx.synchronize()
     assert np.isfinite(out.cpu().numpy()).all()
     W0.free()
+
+
+def test_peer_gather_in_kernel_completion_one_rank(kqctx):
+    """The step completed inside the GEMV (out given, no wait call): with one rank the kernel's tail
+    CTAs only count the step; over 3 steps (both buffers) out equals an unsharded GEMV, and a
+    following gather + wait pair (the other form) sees the steps counted"""
+    import torch
+    V, K, M = 1000, 512, 2
+    w = synth.gen_weights(kq.TYPE_Q6_K, V, K, seed=95)
+    W = kqctx.upload(w, kq.TYPE_Q6_K, V, K)
+    (g,) = shard.PeerGather.emulated(kqctx, 1, M, V)
+    try:
+        for step in range(4):
+            x = torch.from_numpy(synth.gen_activations(M, K, 96 + step).view(np.uint16).copy()).cuda()
+            ref = torch.zeros((M, V), dtype=torch.float32, device="cuda")
+            kqctx.gemm_multi_async(x, M, K, kqctx.make_tasks([dict(w=W, dst_f32=ref, dst_f32_stride=V)]))
+            out = torch.full((M, V), float("nan"), dtype=torch.float32, device="cuda")
+            if step < 3:
+                g.gather(W, x, out)
+            else:
+                g.gather(W, x)
+                g.wait(out)
+            kqctx.synchronize()
+            assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.cpu().numpy().view(np.uint32)), step
+    finally:
+        g.close()
+        W.free()

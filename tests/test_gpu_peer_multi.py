@@ -11,7 +11,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-V, K, M, STEPS = 151936 // 8, 2560, 2, 3
+V, K, M, STEPS = 151936 // 8, 2560, 2, 4
 
 
 def _free_port() -> int:
@@ -22,7 +22,7 @@ def _free_port() -> int:
     return port
 
 
-def _rank_main(rank: int, world: int, port: int, q):
+def _rank_main(rank: int, world: int, port: int, q, mode: str):
     import sys
     from datetime import timedelta
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -47,8 +47,11 @@ def _rank_main(rank: int, world: int, port: int, q):
             ref = torch.zeros((M, V), dtype=torch.float32, device=dev)
             ctx.gemm_multi_async(x, M, K, ctx.make_tasks([dict(w=Wf, dst_f32=ref, dst_f32_stride=V)]))
             out = torch.full((M, pg.row_stride), float("nan"), dtype=torch.float32, device=dev)
-            pg.gather(Ws, x)
-            pg.wait(out)
+            if mode == "in_kernel" or (mode == "mixed" and step % 2 == 0):
+                pg.gather(Ws, x, out)  # completed by the GEMV's last CTAs
+            else:
+                pg.gather(Ws, x)
+                pg.wait(out)
             ctx.synchronize()
             ok &= bool(np.array_equal(out[:, :V].cpu().numpy().view(np.uint32), ref.cpu().numpy().view(np.uint32)))
         dist.barrier()
@@ -61,8 +64,9 @@ def _rank_main(rank: int, world: int, port: int, q):
         q.put((rank, False, repr(e)))
 
 
+@pytest.mark.parametrize("mode", ["wait_kernel", "in_kernel", "mixed"])
 @pytest.mark.parametrize("world", [2])
-def test_peer_gather_two_processes(world):
+def test_peer_gather_two_processes(world, mode):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < world:
@@ -70,7 +74,7 @@ def test_peer_gather_two_processes(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]
