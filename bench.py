@@ -708,11 +708,12 @@ def run_stack(args, rank, world, local_rank):
                        "parallelism": "replicas x1" if world == 1 else f"row-shard x{world}",
                        "timing": "CUDA graph: warm-up steps, event, timed steps, event"
                                  + ("" if world == 1 else " (NCCL all-gathers captured); max over ranks")},
-            "roofline": {"bound": "hbm", "achieved": round(per_rank, 1), "peak": peak_hbm, "unit": "GB/s",
-                         "frac": round(per_rank / peak_hbm, 4), "peak_source": peak_kind,
-                         "traffic": ncu_traffic(f"ffn_m{M}", "dram_bytes_per_step") if world == 1 else None,
-                         "note": "weight bytes of this rank's share per step time (the whole block at 1 GPU); "
-                                 "traffic = DRAM bytes of one whole step (all its kernels) from the ncu summary"},
+            "roofline": ({"bound": "hbm", "achieved": round(per_rank, 1), "peak": peak_hbm, "unit": "GB/s",
+                          "frac": round(per_rank / peak_hbm, 4), "peak_source": peak_kind,
+                          "traffic": ncu_traffic(f"ffn_m{M}", "dram_bytes_per_step") if world == 1 else None,
+                          "note": "weight bytes of this rank's share per step time (the whole block at 1 GPU); "
+                                  "traffic = DRAM bytes of one whole step (all its kernels) from the ncu summary"}
+                         if M <= 64 else ffn_tensor_roofline(ops * steps / dt / 1e12 / world, local_rank)),
             "cpu_baseline": cpu, "clocks": clocks,
             "e2e": {"value": round(wbytes * e2e_steps / e2e_dt / 1e9, 2), "unit": "GB/s", "steps": e2e_steps,
                     "h2d_bytes_per_step": int(x16.nbytes + (gamma.nbytes if world == 1 else 0)),
@@ -941,6 +942,15 @@ def run_stack(args, rank, world, local_rank):
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+def ffn_tensor_roofline(tops_per_rank, device):
+    """Batched-prefill FFN (hundreds of tokens and more): a dense int8 contraction, so its roofline is
+    the tensor-core peak (measured live), per GPU."""
+    peak, src = measured_int8_tops(device)
+    return {"bound": "tensor", "achieved": round(tops_per_rank, 2), "peak": round(peak, 1), "unit": "TOPS",
+            "frac": round(tops_per_rank / peak, 4), "peak_source": src, "traffic": None,
+            "note": "int8 TOPS of one rank's share of the block per step time"}
 
 
 def measured_int8_tops(device):

@@ -46,7 +46,7 @@ namespace kq {
 // other ranks' entries of this step -- stores of other GPUs' kernels only, never of a CTA of this
 // grid, so nothing waits for a CTA that may not be resident.  The last of them to finish clears
 // the counts and counts the step as completed.
-constexpr unsigned PEER_TAIL_CTAS = 16;
+constexpr unsigned PEER_TAIL_CTAS = 64;
 
 __device__ __noinline__ void peer_tail(const GemvParams &p, int tid, bool aborted) {
     __shared__ int s_tail, s_fail;
