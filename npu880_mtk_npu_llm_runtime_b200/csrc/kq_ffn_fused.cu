@@ -14,14 +14,13 @@
 //     of 5 warps), normalize, quantize to Q8_K into the gate/up activation (every CTA for
 //     itself: no exchange);
 //  2. gate/up: the row groups of gate and up alternate (gate rows 16 w.., up rows 16 w.., gate
-//     rows 16 (w+1).., ...) and each CTA owns an equal range of their (row group, unit) tiles; a
-//     row group shared by two CTAs is folded by the later one in unit order (fold_shared_f);
-//     outputs go to global memory in fp16, and whichever of the pair (gate w, up w) is folded
-//     second computes SwiGLU of those 16 rows (ENG:4350-4356, the same exp table as
-//     kq_swiglu_q8k) in place of g -- each value once;
+//     rows 16 (w+1).., ...) and each CTA owns whole pairs (gate w, up w) (ffn_share); the warp
+//     completing a row group folds it in unit order; outputs go to global memory in fp16, then the
+//     CTA computes SwiGLU of its pairs (ENG:4350-4356, the same exp table as kq_swiglu_q8k) in place
+//     of g -- each value once;
 //  3. one grid-wide barrier (bounded wait; an arrival count and a generation word);
 //  4. Q8_K of all of h into the down activation (every CTA for itself);
-//  5. down + residual over an equal tile range per CTA, folded like 2.
+//  5. down + residual, shared out and folded like 2.
 // Every wait is bounded; on a timeout the kernel records DEV_ERR_TIMEOUT, stops issuing and
 // computing, drains its own copies in flight (bounded) and returns.
 #include "kq_gemv_dev.cuh"
@@ -55,31 +54,72 @@ struct FfnFusedParams {
     unsigned long long timeout_ns;
 };
 
-// This CTA's equal share of a phase's tile sequence (the GEMV's split ownership).
+// This CTA's share of a phase's tiles, as two runs done in this order:
+//  run 0: an equal range of a split space of row groups (tiles xs .. xs + xt of the phase), whose
+//         row groups neighbouring CTAs share and fold with fold_shared_f (the last to finish adds
+//         all block terms in unit order; nobody waits);
+//  run 1: whole groups of `gran` row groups.
+// Gate/up (gran 2: a pair (gate w, up w), so every SwiGLU pair is local) is whole pairs only,
+// spread as evenly as whole pairs allow (608 pairs: 4 or 5 per CTA).  Down (gran 1) gives every
+// CTA the same number of whole row groups and splits the remaining row groups (160 = 148 + 12 at
+// hidden 2,560) over all CTAs, computed first so that their folds across CTAs happen while the
+// CTA's own row groups are computed.  Splitting the 16 remaining gate/up pairs the same way was
+// slower (32.6 against 30.2 us per block at 1 token): their 10-unit row groups spread over 4-5
+// CTAs each, and the folds and pair counts across CTAs cost more than the uneven pairs.  Measured: whole row groups beat equal tile
+// ranges, whose folds through L2 sat at the end of every CTA; the 12 CTAs holding two down row
+// groups then set the end of the launch, hence the split remainder.
 struct FfnShare {
-    int t0, n;          // tiles [t0, t0 + n) of the phase
-    int rg_lo, n_lr;    // row groups touched
-    int u_first, u_end; // owned units of the first / last row group
+    long long xs, xt;   // split space: first phase tile, tiles
+    int x0, nx;         // this CTA's split tiles [x0, x0 + nx) of the space
+    int rgx_lo, nlx;    // row groups run 0 touches
+    int rg1, n1;        // whole row groups of run 1
+    int n, n_lr;        // tiles, row groups (term slots: run 0's first)
 };
 
-__device__ __forceinline__ FfnShare ffn_share(const GemvParams &p) {
+__device__ __forceinline__ FfnShare ffn_share(const GemvParams &p, int gran, bool split_rest) {
     FfnShare s;
-    const long long tl = p.total_tiles * blockIdx.x / gridDim.x;
-    const long long th = p.total_tiles * (blockIdx.x + 1) / gridDim.x;
-    s.t0 = (int)tl;
-    s.n = (int)(th - tl);
-    s.rg_lo = (int)(tl / p.nbu);
-    const int rg_hi = s.n > 0 ? (int)((th + p.nbu - 1) / p.nbu) : s.rg_lo;
-    s.n_lr = rg_hi - s.rg_lo;
-    s.u_first = (int)(tl - (long long)s.rg_lo * p.nbu);
-    s.u_end = s.n > 0 ? (int)(th - (long long)(rg_hi - 1) * p.nbu) : 0;
+    const long long groups = p.total_rg / gran, G = gridDim.x, c = blockIdx.x;
+    long long whole, g_lo;
+    if (split_rest) {
+        whole = groups / G;  // whole groups per CTA, the same for all
+        g_lo = whole * c;
+        s.xs = whole * G * gran * p.nbu;
+        s.xt = (groups - whole * G) * gran * p.nbu;
+    } else {
+        g_lo = groups * c / G;
+        whole = groups * (c + 1) / G - g_lo;
+        s.xs = 0;
+        s.xt = 0;
+    }
+    s.rg1 = (int)(g_lo * gran);
+    s.n1 = (int)(whole * gran);
+    const long long xa = s.xt * c / G, xb = s.xt * (c + 1) / G;
+    s.x0 = (int)xa;
+    s.nx = (int)(xb - xa);
+    s.rgx_lo = (int)((s.xs + xa) / p.nbu);
+    s.nlx = s.nx > 0 ? (int)((s.xs + xb + p.nbu - 1) / p.nbu) - s.rgx_lo : 0;
+    s.n = s.nx + s.n1 * p.nbu;
+    s.n_lr = s.nlx + s.n1;
     return s;
 }
 
-// owned units [ua, ub) of local row group lr
-__device__ __forceinline__ void ffn_owned(const FfnShare &s, int nbu, int lr, int &ua, int &ub) {
-    ua = (lr == 0) ? s.u_first : 0;
-    ub = (lr == s.n_lr - 1) ? s.u_end : nbu;
+// local tile i of the share -> phase tile index
+__device__ __forceinline__ long long ffn_tile(const FfnShare &s, int i, int nbu) {
+    return i < s.nx ? s.xs + s.x0 + i : (long long)s.rg1 * nbu + (i - s.nx);
+}
+
+// term slot of row group rg, and its units [ua, ub) owned by this CTA
+__device__ __forceinline__ void ffn_slot(const FfnShare &s, int nbu, int rg, bool split, int &lr, int &ua, int &ub) {
+    if (split) {
+        lr = rg - s.rgx_lo;
+        const long long b0 = (long long)rg * nbu;
+        ua = (int)max(0ll, s.xs + s.x0 - b0);
+        ub = (int)min((long long)nbu, s.xs + s.x0 + s.nx - b0);
+    } else {
+        lr = s.nlx + (rg - s.rg1);
+        ua = 0;
+        ub = nbu;
+    }
 }
 
 // Grid-wide barrier of the grid's CTAs (all resident), one thread per CTA.  Arrival is a release
@@ -172,15 +212,17 @@ __device__ __forceinline__ void ffn_phase(const FfnFusedParams &P, const GemvPar
             if (lane == 0) *reinterpret_cast<volatile int *>(s_abort) = 1;
             break;
         }
-        const int tau = sh.t0 + i, rg = tau / nbu, u = tau - rg * nbu, lr = rg - sh.rg_lo;
+        const long long tau = ffn_tile(sh, i, nbu);
+        const int rg = (int)(tau / nbu), u = (int)(tau - (long long)rg * nbu);
+        const bool split = i < sh.nx;
+        int lr, ua, ub;
+        ffn_slot(sh, nbu, rg, split, lr, ua, ub);
         const uint8_t *tile = ring + (size_t)slot * P.stage_bytes + (size_t)tt * p.tile_bytes;
         DbgOut db;
         db.si = nullptr;
         float *tb = terms + (size_t)lr * J * E;
         compute_item<TYPE, MT>(p, tile, u, smem, lane, tb + (size_t)u * E, db);
         __syncwarp();
-        int ua, ub;
-        ffn_owned(sh, nbu, lr, ua, ub);
         int last = 0;
         if (lane == 0) {
             const int n_in = min(sh.n - k * T, T);  // tiles of this stage
@@ -192,14 +234,19 @@ __device__ __forceinline__ void ffn_phase(const FfnFusedParams &P, const GemvPar
         if (last) {
             __threadfence_block();
             const bool shared = ua > 0 || ub < nbu;
+            const long long first = (long long)rg * nbu - sh.xs;  // the row group's first tile in the split space
             if (PHASE_A) {
                 bool done = true;
-                if (shared) done = fold_shared_f<MT>(p, tb, J, 1, ua, ub, rg, lane, [&](int e) { ffn_fold_a<MT>(P, tb, J, e, rg); });
+                if (shared)
+                    done = fold_shared_f<MT>(p, tb, J, 1, ua, ub, first, sh.xt, lane,
+                                             [&](int e) { ffn_fold_a<MT>(P, tb, J, e, rg); });
                 else
                     for (int e = lane; e < E; e += 32) ffn_fold_a<MT>(P, tb, J, e, rg);
                 if (done && lane == 0) s_fin[lr] = 1;  // this CTA made the row group's final fold
             } else {
-                if (shared) fold_shared<MT>(p, tasks, tb, J, 1, ua, ub, rg, lane, s_best);
+                if (shared)
+                    fold_shared_f<MT>(p, tb, J, 1, ua, ub, first, sh.xt, lane,
+                                      [&](int e) { fold_one<MT>(p, tasks, tb, J, e, rg, s_best); });
                 else
                     for (int e = lane; e < E; e += 32) fold_one<MT>(p, tasks, tb, J, e, rg, s_best);
             }
@@ -223,7 +270,7 @@ __global__ void __launch_bounds__(threads_of<MT>(), 1) kq_ffn_fused(const __grid
     uint8_t *ring = smem + P.off_stages;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P.off_bars);  // full[S], empty[S]
     float *terms = reinterpret_cast<float *>(smem + pa.off_terms);
-    const FfnShare sa = ffn_share(pa), sb = ffn_share(pb);
+    const FfnShare sa = ffn_share(pa, 2, false), sb = ffn_share(pb, 1, true);
     const int na_st = (sa.n + P.TA - 1) / P.TA, nb_st = (sb.n + P.TB - 1) / P.TB, n_st = na_st + nb_st;
 
     if (tid == 0) s_tb[0] = pb.task[0];
@@ -267,17 +314,17 @@ __global__ void __launch_bounds__(threads_of<MT>(), 1) kq_ffn_fused(const __grid
                 mbar_arrive_expect_tx(full, (uint32_t)(b - a) * p.tile_bytes);
                 int i = a;
                 while (i < b) {
-                    const int tau = sh.t0 + i, rg = tau / p.nbu;
+                    // a copy stays inside one run (split / whole) and, for gate/up, one row group
+                    const long long tau = ffn_tile(sh, i, p.nbu);
+                    const int rg = (int)(tau / p.nbu);
+                    int iend = (i < sh.nx) ? min(b, sh.nx) : b;
                     const uint8_t *src;
-                    int iend;
                     if (ph_a) {
                         // gate/up row group rg: weight row group rg / 2 of gate (even) or up (odd)
-                        src = ((rg & 1) ? P.wu : P.wg) + ((size_t)(rg >> 1) * p.nbu + (tau - rg * p.nbu)) * p.tile_bytes;
-                        iend = min(b, (rg + 1) * p.nbu - sh.t0);
+                        src = ((rg & 1) ? P.wu : P.wg) + ((size_t)(rg >> 1) * p.nbu + (size_t)(tau - (long long)rg * p.nbu)) * p.tile_bytes;
+                        iend = min(iend, i + (int)((long long)(rg + 1) * p.nbu - tau));
                     } else {
-                        const GemvTaskDev &tk = p.task[0];
-                        src = tk.w + (size_t)tau * p.tile_bytes;
-                        iend = b;
+                        src = p.task[0].w + (size_t)tau * p.tile_bytes;
                     }
                     bulk_g2s(sdst + (uint32_t)(i - a) * p.tile_bytes, src, (uint32_t)(iend - i) * p.tile_bytes, full,
                              policy);
@@ -357,8 +404,10 @@ __global__ void __launch_bounds__(threads_of<MT>(), 1) kq_ffn_fused(const __grid
         // folds were made by two CTAs is counted in P.pair[w] and computed by the second
         for (int lr = warp; lr < sa.n_lr; lr += W) {
             if (!s_fin[lr]) continue;
-            const int q = sa.rg_lo + lr, plr = (q ^ 1) - sa.rg_lo;
-            const bool local = plr >= 0 && plr < sa.n_lr && s_fin[plr];
+            const int q = lr < sa.nlx ? sa.rgx_lo + lr : sa.rg1 + (lr - sa.nlx), pq = q ^ 1;
+            const int plr = (pq >= sa.rg1 && pq < sa.rg1 + sa.n1) ? sa.nlx + (pq - sa.rg1)
+                            : (pq >= sa.rgx_lo && pq < sa.rgx_lo + sa.nlx) ? pq - sa.rgx_lo : -1;
+            const bool local = plr >= 0 && s_fin[plr];
             int mine;
             if (local) {
                 mine = (q & 1) == 0;
@@ -439,10 +488,11 @@ FfnPlan ffn_plan(int gt, int dt, int hidden, int ffn, int MT, int grid) {
                    desc = ffn_al((size_t)n_teams * RMS_MAX_SEG * 4 * 16);
     const unsigned act_a = xa + dxa + xsa, region_b = std::max(xb + dxb + xsb, rows + hs + desc);
     const long long rg_f = ffn / 16, rg_h = hidden / 16;
-    const long long tiles_a = 2 * rg_f * nbh, tiles_b = rg_h * nbf;
-    const long long per_a = (tiles_a + grid - 1) / grid, per_b = (tiles_b + grid - 1) / grid;
-    const long long rga = std::min(2 * rg_f, (per_a + nbh - 2) / nbh + 1);
-    const long long rgb = std::min(rg_h, (per_b + nbf - 2) / nbf + 1);
+    // whole pairs of gate/up row groups and whole down row groups per CTA
+    const long long rga = 2 * ((rg_f + grid - 1) / grid);  // whole gate/up pairs
+    // down: the same whole row groups everywhere, plus a range of the split remainder
+    const long long whole_b = rg_h / grid, per_x = ((rg_h - whole_b * grid) * nbf + grid - 1) / grid;
+    const long long rgb = whole_b + (per_x > 0 ? (per_x + nbf - 2) / nbf + 1 : 0);
     if (rga > kMaxTermSlots || rgb > kMaxTermSlots) return pl;
     const unsigned terms = ffn_al((size_t)std::max(rga * nbh, rgb * nbf) * 16 * MT * 4);
     const unsigned tba = (unsigned)tile_bytes(gt), tbb = (unsigned)tile_bytes(dt);

@@ -781,11 +781,13 @@ __device__ __forceinline__ void fold_one(const GemvParams &p, const GemvTaskDev 
 // copies through L2, all in flight), calls fold_e(e) for every (row, token) e of the row group
 // (which adds the J terms in block order and writes the result), clears the count for the next
 // launch and returns true.  No CTA waits for another.  One warp.
+// The split space is T tiles owned in equal ranges by the grid's CTAs; the row group's first tile
+// is tile `first` of it.
 template <int MT, class FoldE>
-__device__ __forceinline__ bool fold_shared_f(const GemvParams &p, float *tb, int J, int JU, int ua, int ub, int rg,
-                                              int lane, FoldE fold_e) {
+__device__ __forceinline__ bool fold_shared_f(const GemvParams &p, float *tb, int J, int JU, int ua, int ub,
+                                              long long first, long long T, int lane, FoldE fold_e) {
     constexpr int E = 16 * MT;  // floats per term (16 rows x MT tokens): a multiple of 4
-    const long long first = (long long)rg * p.nbu, G = gridDim.x, T = p.total_tiles;
+    const long long G = gridDim.x;
     const int c_first = (int)(((first + 1) * G - 1) / T);     // CTA owning tile `first`
     const int c_last = (int)(((first + p.nbu) * G - 1) / T);  // CTA owning the row group's last tile
     float4 *g4 = reinterpret_cast<float4 *>(p.gterms + (size_t)c_first * J * E);
@@ -813,7 +815,7 @@ __device__ __forceinline__ bool fold_shared_f(const GemvParams &p, float *tb, in
 template <int MT>
 __device__ __forceinline__ void fold_shared(const GemvParams &p, const GemvTaskDev *tasks, float *tb, int J, int JU,
                                             int ua, int ub, int rg, int lane, unsigned long long *s_best) {
-    fold_shared_f<MT>(p, tb, J, JU, ua, ub, rg, lane,
+    fold_shared_f<MT>(p, tb, J, JU, ua, ub, (long long)rg * p.nbu, p.total_tiles, lane,
                       [&](int e) { fold_one<MT>(p, tasks, tb, J, e, rg, s_best); });
 }
 
