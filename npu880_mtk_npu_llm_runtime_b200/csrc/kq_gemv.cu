@@ -23,9 +23,9 @@
 //    the epilogue: fp32 out, fp16 out with optional fp16 residual, argmax keys.
 //  * Each CTA owns whole row groups and streams them through a ring of stages.  When the terms
 //    of its whole share fit in shared memory (small launches) the warps compute all items and
-//    fold everything after one barrier (and, when the ring holds the whole share, wait for the
-//    stages once); otherwise the warp that completes a row group folds it (shared-memory
-//    counters).
+//    fold everything after one barrier (when the ring holds the whole share, every stage is
+//    probed once and, where one has not landed yet, each tile waits for its own stage only);
+//    otherwise the warp that completes a row group folds it (shared-memory counters).
 //    Under half an SM per CTA, the next kernel's CTA (programmatic dependent launch, enabled at
 //    CTA start) prefetches its weights during this one's wait and arithmetic.
 //  * Every wait is bounded (globaltimer); on timeout the kernel records DEV_ERR_TIMEOUT,
@@ -184,17 +184,8 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
         const int first = min(S, n_stages_cta);  // stages that need no free slot
         if (lane == 0)
             for (int s = 0; s < first; ++s) issue(s);
-        if (SMALL && n_stages_cta <= S && lane == 0) {
-            // the ring holds the whole share: wait for it here, while the consumers stage the
-            // activation, so they find every tile in place after the barrier below
-            for (int s = 0; s < n_stages_cta; ++s)
-                if (!mbar_wait_bounded(smem_u32(&bars[s]), 0, p.timeout_ns, p.status)) {
-                    s_abort = 1;
-                    break;
-                }
-        }
         __syncwarp();
-        __syncthreads();  // activation staged (and, all in, the weights landed)
+        __syncthreads();  // activation staged
         if (lane == 0) {
             for (int s = first; s < n_stages_cta; ++s) {
                 if (!mbar_wait_bounded(smem_u32(&bars[S + s % S]), ((s / S) - 1) & 1, p.timeout_ns, p.status)) {
@@ -220,9 +211,10 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
         const int JU = (TYPE == TYPE_Q8_0 && p.q80_exact) ? 8 : 1;  // terms per unit
         bool any_dbg = false;
         for (int k = 0; k < p.n_tasks; ++k) any_dbg |= s_task[k].dbg_sumi != nullptr;
-        // all in: the producer saw every stage land before the barrier above, so the loop has no
-        // waits; without a split each row group is folded by the warp that completes it (the
-        // row-group counters s_done), overlapping the folds with the other warps' tiles
+        // all in (the ring holds the whole share, every stage issued at CTA start): no slot is
+        // reused, so no consumer frees one; without a split each row group is folded by the warp
+        // that completes it (the row-group counters s_done), overlapping the folds with the other
+        // warps' tiles
         const bool early_fold = all_in && !SPLIT && n_lr <= kMaxTermSlots;
         if (all_in) {
             int tt = warp, sg = 0;
@@ -235,8 +227,26 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
                 u -= nbu;
                 ++lr;
             }
+            // every stage was issued at CTA start.  In a chain of launches they landed during the
+            // previous kernel (one probe each, then no waits); after a cold start (e.g. one call
+            // after a host copy) each tile waits only for its own stage, so the arithmetic starts
+            // while the later stages still stream in
+            int seen = 1;
+            if (lane == 0)
+                for (int s = 0; s < n_stages_cta; ++s) seen &= mbar_test_wait(smem_u32(&bars[s]), 0) ? 1 : 0;
+            seen = __shfl_sync(0xffffffffu, seen, 0) ? n_stages_cta : 0;
             const bool go = !*reinterpret_cast<volatile int *>(&s_abort);
             for (int i = warp; go && i < n_tiles; i += TSTEP) {
+                if (sg >= seen) {
+                    int ok = 1;
+                    if (lane == 0) ok = mbar_wait_bounded(smem_u32(&bars[sg]), 0, p.timeout_ns, p.status);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) {
+                        if (lane == 0) s_abort = 1;
+                        break;
+                    }
+                    seen = sg + 1;
+                }
                 const uint8_t *tile = ring + sg * p.stage_bytes + tt * p.tile_bytes;
                 DbgOut db;
                 db.si = nullptr;

@@ -222,6 +222,46 @@ def test_config0_shape_bitexact(kqctx, oracle):
     assert np.array_equal(bits(got), bits(ref))
 
 
+def test_dispatch_pinned_input_and_outputs(kqctx, oracle):
+    """Host input and outputs in pinned (mapped) memory: the GPU reads the input over the host
+    link (a copy kernel ahead of the product, which streams its weights meanwhile) and writes the
+    outputs in place.  Bit for bit the oracle on several calls in a row with new input each time
+    (no stale read), through an unaligned input view (byte copies) and the fp16 + residual
+    epilogue at 2 rows."""
+    import torch
+    N, K = 9728, 2560
+    w = synth.gen_weights(kq.TYPE_Q4_K, N, K, seed=301)
+    W = kqctx.upload(w, kq.TYPE_Q4_K, N, K)
+    xp = torch.zeros((1, K + 8), dtype=torch.float16).pin_memory().numpy()
+    op = torch.zeros((1, N), dtype=torch.float32).pin_memory().numpy()
+    tasks = kqctx.make_host_tasks([dict(w=W, dst_f32=op)])
+    try:
+        for step in range(4):
+            x = synth.gen_activations(1, K, seed=310 + step)
+            off = 0 if step < 3 else 1  # 2 bytes in: not 16-byte aligned
+            xp[:, off:off + K] = x
+            kqctx.sdot_gemm_multi_dispatch(xp[:, off:off + K], tasks)
+            ref = oracle.gemm(kq.TYPE_Q4_K, w, K, oracle.quantize_q8k(x))
+            assert np.array_equal(bits(op), bits(ref)), step
+    finally:
+        W.free()
+    M, N2, K2 = 2, 1000, 512
+    w2 = synth.gen_weights(kq.TYPE_Q5_K, N2, K2, seed=320)
+    W2 = kqctx.upload(w2, kq.TYPE_Q5_K, N2, K2)
+    x2p = torch.zeros((M, K2), dtype=torch.float16).pin_memory().numpy()
+    d2p = torch.zeros((M, N2), dtype=torch.float16).pin_memory().numpy()
+    res = synth.gen_activations(M, N2, seed=321)
+    try:
+        for step in range(2):
+            x2 = synth.gen_activations(M, K2, seed=322 + step)
+            x2p[:] = x2
+            kqctx.sdot_gemm_multi_dispatch(x2p, [dict(w=W2, dst=d2p, residual=res)])
+            ref = oracle.gemm(kq.TYPE_Q5_K, w2, K2, oracle.quantize_q8k(x2))
+            assert np.array_equal(bits(d2p), bits(oracle.epilogue_f16(ref, res))), step
+    finally:
+        W2.free()
+
+
 def test_quantizers_bitexact(kqctx, oracle):
     x = synth.gen_activations(6, 2560, 77).astype(np.float32)
     x[1] = 0
