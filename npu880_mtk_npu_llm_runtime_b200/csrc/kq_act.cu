@@ -117,34 +117,6 @@ cudaError_t launch_quantize(int target_type, const void *x, long long x_stride, 
     return cudaGetLastError();
 }
 
-// ------------------------------------------------------------------ host input, read by the GPU
-//
-// The dispatch's input rows from pinned, mapped host memory, read over the host link by a kernel
-// instead of a DMA copy: the product launched behind it (programmatic dependent launch) becomes
-// resident at once and streams its weights while these reads are in flight; it reads the rows
-// only after this grid has completed (griddepcontrol.wait).  Loads bypass the caches (the host
-// rewrites the buffer between calls).
-__global__ void __launch_bounds__(256) kq_copy_in(uint8_t *dst, const uint8_t *src, size_t bytes) {
-    asm volatile("griddepcontrol.launch_dependents;");
-    const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nt = (size_t)gridDim.x * blockDim.x;
-    size_t done = 0;
-    if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0) {
-        const size_t n16 = bytes / 16;
-        for (size_t i = t; i < n16; i += nt)
-            reinterpret_cast<uint4 *>(dst)[i] = __ldcv(reinterpret_cast<const uint4 *>(src) + i);
-        done = n16 * 16;
-    }
-    for (size_t i = done + t; i < bytes; i += nt) dst[i] = __ldcv(src + i);
-}
-
-cudaError_t launch_copy_in(void *dst, const void *src_mapped, size_t bytes, cudaStream_t stream) {
-    if (bytes == 0) return cudaSuccess;
-    const unsigned grid = (unsigned)std::min<size_t>(148, (bytes + 16 * 256 - 1) / (16 * 256));
-    kq_copy_in<<<grid, 256, 0, stream>>>(static_cast<uint8_t *>(dst), static_cast<const uint8_t *>(src_mapped),
-                                         bytes);
-    return cudaGetLastError();
-}
-
 // ------------------------------------------------------------------ RMSNorm (+ Q8_K)
 //
 // x_out = fp16((x * inv_rms) * gamma), inv_rms = 1 / sqrt(sum_sq * (1/K) + 1e-6), every operation

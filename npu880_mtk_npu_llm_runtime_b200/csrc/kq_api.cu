@@ -738,15 +738,7 @@ extern "C" int kq_sdot_gemm_multi_dispatch(kq_ctx *c, const uint16_t *x, int M, 
     const bool use_pending = c->pending && c->pending_M == M && c->pending_K == K;
     c->pending = false;
 
-    // a pinned, mapped input is read by a small kernel, so the products launched behind it
-    // (programmatic dependent launch) stream their weights meanwhile; other memory is copied
-    const size_t xbytes = (size_t)M * K * 2;
-    if (const void *xmap = c->pdl ? mapped_device_ptr(x) : nullptr) {
-        if (int r = ensure(c, c->x, xbytes)) return r;
-        KQ_CUDA(c, kq::launch_copy_in(c->x.p, xmap, xbytes, c->stream));
-    } else if (int r = h2d(c, c->x, x, xbytes)) {
-        return r;
-    }
+    if (int r = h2d(c, c->x, x, (size_t)M * K * 2)) return r;
     // device staging of outputs and residuals, one contiguous [M][rows] slab per task
     size_t o16 = 0, o32 = 0, ores = 0;
     std::vector<size_t> off16(n), off32(n), offr(n);

@@ -235,6 +235,7 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
             if (lane == 0)
                 for (int s = 0; s < n_stages_cta; ++s) seen &= mbar_test_wait(smem_u32(&bars[s]), 0) ? 1 : 0;
             seen = __shfl_sync(0xffffffffu, seen, 0) ? n_stages_cta : 0;
+            __syncwarp();  // lane 0 saw the stages complete: order the warp's reads after it
             const bool go = !*reinterpret_cast<volatile int *>(&s_abort);
             for (int i = warp; go && i < n_tiles; i += TSTEP) {
                 if (sg >= seen) {
@@ -245,6 +246,7 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
                         if (lane == 0) s_abort = 1;
                         break;
                     }
+                    __syncwarp();
                     seen = sg + 1;
                 }
                 const uint8_t *tile = ring + sg * p.stage_bytes + tt * p.tile_bytes;

@@ -143,9 +143,6 @@ cudaError_t launch_gather_rows(int type, int K, const uint8_t *src, const uint32
                                cudaStream_t stream);
 
 // kq_act.cu
-// Copy `bytes` from pinned, mapped host memory (its device address) to device memory with a
-// kernel that lets the next kernel launch at once (programmatic dependent launch).
-cudaError_t launch_copy_in(void *dst, const void *src_mapped, size_t bytes, cudaStream_t stream);
 cudaError_t launch_quantize(int target_type /*12 = Q8_K, 8 = Q8_0*/, const void *x, long long x_stride, int M, int K,
                             void *out, cudaStream_t stream);
 cudaError_t launch_repack(int type, const uint8_t *gguf, uint8_t *dev, int rows, int K, cudaStream_t stream);

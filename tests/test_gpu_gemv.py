@@ -223,11 +223,9 @@ def test_config0_shape_bitexact(kqctx, oracle):
 
 
 def test_dispatch_pinned_input_and_outputs(kqctx, oracle):
-    """Host input and outputs in pinned (mapped) memory: the GPU reads the input over the host
-    link (a copy kernel ahead of the product, which streams its weights meanwhile) and writes the
-    outputs in place.  Bit for bit the oracle on several calls in a row with new input each time
-    (no stale read), through an unaligned input view (byte copies) and the fp16 + residual
-    epilogue at 2 rows."""
+    """Host input and outputs in pinned (mapped) memory, the outputs written in place by the
+    kernel: bit for bit the oracle on several calls in a row with new input each time, through an
+    unaligned input view, and the fp16 + residual epilogue at 2 rows."""
     import torch
     N, K = 9728, 2560
     w = synth.gen_weights(kq.TYPE_Q4_K, N, K, seed=301)
