@@ -204,8 +204,11 @@ def graph_timed(stream, step, steps, warmup, world, per_step_launches=1):
     """Time `steps` calls of step(i) on the device, hot: one eager call configures the kernels,
     then a CUDA graph holds the `warmup` untimed steps, a timing event, the `steps` timed steps and
     a second event, so the timed steps start right after warm-up steps with the GPU busy (no idle
-    gap, no graph boundary inside the timed region).  Beyond GRAPH_MAX steps the timed steps are
-    replayed from graphs of at most GRAPH_MAX steps.  Returns seconds (max over ranks)."""
+    gap, no graph boundary inside the timed region).  The first event is recorded on a side branch
+    of the graph (it fires when the warm-up steps have completed) so that the first timed launch
+    keeps its programmatic-dependent-launch edge to the last warm-up launch, as every later one
+    does.  Beyond GRAPH_MAX steps the timed steps are replayed from graphs of at most GRAPH_MAX
+    steps.  Returns seconds (max over ranks)."""
     import torch
     import torch.distributed as dist
     with torch.cuda.stream(stream):
@@ -217,13 +220,19 @@ def graph_timed(stream, step, steps, warmup, world, per_step_launches=1):
     try:
         if steps <= GRAPH_MAX:
             g = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(device=stream.device)
+            fork, join = torch.cuda.Event(), torch.cuda.Event()
             with torch.cuda.graph(g, stream=stream):
                 for i in range(warmup):
                     step(i)
-                ev0.record()
+                fork.record(stream)
+                side.wait_event(fork)
+                ev0.record(side)
                 for i in range(steps):
                     step(warmup + i)
-                ev1.record()
+                ev1.record(stream)
+                join.record(side)
+                stream.wait_event(join)
             graphs.append(g)
             plan = [g]
         else:
