@@ -156,7 +156,9 @@ typedef struct kq_task {
  * x [M][K].  The input is quantized to Q8_K (and/or Q8_0 for Q8_0 weights) inside the kernel,
  * unless a producer (kq_rmsnorm_fp16_rows / kq_swiglu_fp16_rows) left a pre-quantized Q8_K
  * activation of the same M x K in the context, exactly like g_sdot_input_q8k_prequantized
- * (ENG:4184, ENG:4205-4218).  HOST pointers; blocking. */
+ * (ENG:4184, ENG:4205-4218).  HOST pointers; blocking.  Outputs in pinned (page-locked, mapped)
+ * host memory are written in place by the kernel; other outputs go through device staging and a
+ * copy back. */
 int kq_sdot_gemm_multi_dispatch(kq_ctx *ctx, const uint16_t *x, int M, int K, const kq_task *tasks, int n_tasks);
 /* Same with DEVICE pointers (x and every task pointer); asynchronous.  x_stride = elements
  * between rows of x (>= K). */
