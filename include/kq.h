@@ -90,6 +90,10 @@ const char *kq_last_error(const kq_ctx *ctx);
  * over the SMs give every CTA an equal range of 16-row x 256-value tiles instead; a row group
  * shared by neighbouring CTAs is summed in block order by the last of them (1, default); 0 keeps
  * whole row groups per CTA;
+ * "gemv_half" -- Q4_K / Q5_K GEMV launches of 1-2 activation rows whose row groups divide
+ * unevenly over the SMs, or whose largest share does not fit one CTA's shared memory whole, give
+ * every CTA a contiguous range of 8-row halves of row groups instead (1, default); 0 keeps whole
+ * row groups.  Results are identical either way;
  * "ffn_fused" -- kq_run_ffn / kq_run_ffn_async for 1-2 rows with Q4_K / Q5_K gate and up and a
  * Q4_K / Q5_K / Q6_K down projection run the whole block as one persistent kernel, one CTA per SM,
  * all resident at once, with one grid-wide barrier between gate/up and down (1, default); the

@@ -46,6 +46,7 @@ struct kq_ctx {
     // launches; re-cleared after a launch that stopped early)
     DevBuf gsplit, gcount;  // gcount: the split launches' arrival counts, then the fused FFN's grid barrier
     bool gemv_split = true;
+    bool gemv_half = true;  // Q4_K / Q5_K GEMV launches of 1-2 rows: 8-row halves per CTA where better
     bool ffn_fused = true;  // FFN blocks of 1-2 tokens as one persistent kernel where a plan exists
     bool split_dirty = false;
     bool graph_holds_scratch = false;  // a call of this context was captured into a CUDA graph
@@ -342,6 +343,7 @@ int run_gemv(kq_ctx *c, const kq_task *tasks, int n, int M, int K, const __half 
             L.inject_wait = c->inject_timeout ? 1 : 0;
             if (ex.peer) L.peer = *ex.peer;
             if (int r = gemv_split_scratch(c, type, K, mt, L)) return r;
+            L.half_ok = c->gemv_half;
             cudaError_t e = kq::launch_gemv(L, c->stream);
             if (e == cudaErrorInvalidConfiguration && mt > 1) {
                 // activation too large for shared memory at this tile: halve the tile
@@ -561,6 +563,10 @@ extern "C" int kq_set_option(kq_ctx *c, const char *name, long long value) {
     }
     if (!strcmp(name, "gemv_split")) {
         c->gemv_split = value != 0;
+        return KQ_OK;
+    }
+    if (!strcmp(name, "gemv_half")) {
+        c->gemv_half = value != 0;
         return KQ_OK;
     }
     if (!strcmp(name, "timeout_us")) {

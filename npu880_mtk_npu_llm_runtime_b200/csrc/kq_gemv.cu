@@ -21,7 +21,11 @@
 //  * Each (row, token) result is the sum of its block terms in block order -- the reference's
 //    `acc += term` sequence, so fp32 results equal the reference's bit for bit -- followed by
 //    the epilogue: fp32 out, fp16 out with optional fp16 residual, argmax keys.
-//  * Each CTA owns whole row groups and streams them through a ring of stages.  When the terms
+//  * Q4_K / Q5_K launches of 1-2 tokens whose shares would not fit shared memory whole or would
+//    spread unevenly (config 0: 608 row groups over 148 SMs) give each CTA 8-row halves of row
+//    groups instead: the whole share lands in one stage, the warps compute terms only, and the rows
+//    are folded after a consumer barrier, spread over the threads (HalfShare, half_walk).
+//  * Otherwise each CTA owns whole row groups and streams them through a ring of stages.  When the terms
 //    of its whole share fit in shared memory (small launches) the warps compute all items and
 //    fold everything after one barrier (when the ring holds the whole share, every stage is
 //    probed once and, where one has not landed yet, each tile waits for its own stage only);
@@ -84,6 +88,119 @@ __device__ __noinline__ void peer_tail(const GemvParams &p, int tid, bool aborte
     }
 }
 
+// ------------------------------------------------------------------ half row-group ownership
+//
+// A CTA owns the 8-row halves [h_lo, h_hi) (half h = rows 8 (h % 2).. of row group h / 2).  Its
+// ring holds exactly those rows, in one stage:
+//   [ha: the first row group's second half, units 0..nbu-1]
+//   [the full row groups' tiles, as in global memory]
+//   [hb: the last row group's first half, units 0..nbu-1]
+// (ha = h_lo odd, hb = h_hi odd); a half tile (8 rows of one unit) is half a tile's bytes.
+struct HalfShare {
+    int h_lo, h_hi, rg_lo, ha, hb, nfull, hbytes;
+
+    __device__ __forceinline__ HalfShare(int lo, int hi, int tile_bytes)
+        : h_lo(lo), h_hi(hi), rg_lo(lo >> 1), ha(lo & 1), hb(hi & 1), nfull((hi - (hi & 1) - lo - (lo & 1)) >> 1),
+          hbytes(tile_bytes / 2) {}
+
+    // owned halves of local row group lr, and the first of them (0 or 1)
+    __device__ __forceinline__ int halves(int lr) const {
+        const int n_lr = ((h_hi + 1) >> 1) - rg_lo;
+        return ((lr == 0 && ha) || (lr == n_lr - 1 && hb)) ? 1 : 2;
+    }
+    __device__ __forceinline__ int first_half(int lr) const { return (lr == 0 && ha) ? 1 : 0; }
+};
+
+// Producer lane: every copy of the share onto full barrier `bar` (one phase).
+__device__ __forceinline__ void half_issue(const GemvParams &p, const HalfShare &hs, uint8_t *ring, uint32_t bar) {
+    const int nbu = p.nbu, HB = hs.hbytes;
+    const uint64_t policy = l2_evict_first_policy();
+    const uint32_t base = smem_u32(ring);
+    auto src = [&](int rg, int u) {
+        const GemvTaskDev &tk = p.task[task_of_rg(p, rg)];
+        return tk.w + ((size_t)(tk.rg_first - tk.rg_start) * nbu + (size_t)rg * nbu + u) * p.tile_bytes;
+    };
+    mbar_arrive_expect_tx(bar, (uint32_t)((hs.h_hi - hs.h_lo) * nbu * HB));
+    if (hs.ha)
+        for (int u = 0; u < nbu; ++u) bulk_g2s(base + u * HB, src(hs.rg_lo, u) + HB, HB, bar, policy);
+    const int r0 = hs.rg_lo + hs.ha, re = r0 + hs.nfull;
+    for (int rg = r0; rg < re;) {  // whole tiles, one copy per task's run of row groups
+        const GemvTaskDev &tk = p.task[task_of_rg(p, rg)];
+        const int rend = min(re, tk.rg_start + tk.n_rg);
+        bulk_g2s(base + (hs.ha + 2 * (rg - r0)) * nbu * HB, src(rg, 0), (uint32_t)((rend - rg) * nbu) * p.tile_bytes,
+                 bar, policy);
+        rg = rend;
+    }
+    if (hs.hb)
+        for (int u = 0; u < nbu; ++u)
+            bulk_g2s(base + (hs.ha + 2 * hs.nfull) * nbu * HB + u * HB, src(re, u), HB, bar, policy);
+}
+
+// Consumers.  Warp w takes passes w, w + W, ... of the share: first the boundary passes -- with
+// both a first and a last half row group, pass u is unit u of both (lanes 0-15 the first, 16-31
+// the last); with one of them, pass j is its units 2j and 2j + 1 -- then the whole tiles of the
+// full row groups, one per pass, as in a whole-row-group launch (warp-uniform unit, two lanes per
+// row).  Terms only: the rows are folded after all passes (a fold inside the walk holds up the
+// warp that makes it, and the walk's length is the slowest warp's).
+template <int TYPE, int MT>
+__device__ __forceinline__ void half_walk(const GemvParams &p, const GemvTaskDev *s_task, const HalfShare &hs,
+                                          const uint8_t *ring, const uint8_t *smem, float *terms, int warp, int lane,
+                                          int W, bool any_dbg) {
+    const int nbu = p.nbu, J = p.terms_per_rg, tstride = 16 * MT, HB = hs.hbytes;
+    const int n_lr = ((hs.h_hi + 1) >> 1) - hs.rg_lo;
+    const int n_b = (hs.ha && hs.hb) ? nbu : (hs.ha || hs.hb) ? (nbu + 1) >> 1 : 0;
+    const int g = lane >> 4, l16 = lane & 15;
+    const int base_f = hs.ha * nbu * HB;                   // the full row groups' tiles
+    const int base_b = (hs.ha + 2 * hs.nfull) * nbu * HB;  // the last half row group
+    int j = warp;
+    for (; j < n_b; j += W) {
+        // per lane group: which half (first or last row group) and unit
+        int u, lr, hh, off;
+        if (hs.ha && hs.hb) {
+            u = j;
+            lr = g ? n_lr - 1 : 0;
+            hh = g ? 0 : 1;
+            off = (g ? base_b : 0) + u * HB;
+        } else {
+            u = min(2 * j + g, nbu - 1);  // an odd last pass: lanes 16-31 repeat lanes 0-15's unit
+            lr = hs.ha ? 0 : n_lr - 1;
+            hh = hs.ha ? 1 : 0;
+            off = (hs.ha ? 0 : base_b) + u * HB;
+        }
+        DbgOut db;
+        db.si = nullptr;
+        if (any_dbg) {
+            const GemvTaskDev &tk = s_task[task_of_rg(p, hs.rg_lo + lr)];
+            if (tk.dbg_sumi) {
+                db = make_dbg(p, tk, hs.rg_lo + lr, u, 0);
+                db.r0 += 8 * hh;
+            }
+        }
+        compute_item<TYPE, MT>(p, ring + off, u, smem, l16, terms + (lr * J + u) * tstride + 8 * hh * MT, db);
+    }
+    // whole tiles: pass n_b + t is tile t = k nbu + u of the full row groups (local row group ha + k)
+    int t = j - n_b, k = 0, u = t;
+    while (u >= nbu) {
+        u -= nbu;
+        ++k;
+    }
+    for (; t < hs.nfull * nbu; t += W) {
+        const int lr = hs.ha + k;
+        DbgOut db;
+        db.si = nullptr;
+        if (any_dbg) {
+            const GemvTaskDev &tk = s_task[task_of_rg(p, hs.rg_lo + lr)];
+            if (tk.dbg_sumi) db = make_dbg(p, tk, hs.rg_lo + lr, u, 0);
+        }
+        compute_item<TYPE, MT>(p, ring + base_f + t * 2 * HB, u, smem, lane, terms + (lr * J + u) * tstride, db);
+        u += W;
+        while (u >= nbu) {
+            u -= nbu;
+            ++k;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ the kernel
 //
 // CTA c owns row groups [rg_lo, rg_hi) = tiles [t0, t1) of the launch's tile sequence
@@ -119,6 +236,10 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
     // this CTA's tiles [t0, t0 + n_tiles) of the launch's row-group-major tile sequence: whole
     // row groups, or (SPLIT) an equal share of tiles whose first / last row group may be shared
     int rg_lo, rg_hi, t0, n_tiles, u_first = 0, u_end = nbu;
+    // half row-group ownership (GemvParams::half): halves [h_lo, h_hi)
+    constexpr bool HALF_OK = SMALL && !SPLIT && MT <= 2 && (TYPE == TYPE_Q4_K || TYPE == TYPE_Q5_K);
+    const bool half = HALF_OK && p.half;
+    int h_lo = 0, h_hi = 0;
     if (SPLIT) {
         const long long tl = p.total_tiles * blockIdx.x / gridDim.x;
         const long long th = p.total_tiles * (blockIdx.x + 1) / gridDim.x;
@@ -128,6 +249,14 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
         rg_hi = (int)((th + nbu - 1) / nbu);
         u_first = t0 - rg_lo * nbu;                         // owned units of row group rg_lo: [u_first, nbu)
         u_end = (int)(th - (long long)(rg_hi - 1) * nbu);  // owned units of row group rg_hi - 1: [0, u_end)
+    } else if (half) {
+        const long long nh = 2ll * p.total_rg;
+        h_lo = (int)(nh * blockIdx.x / gridDim.x);
+        h_hi = (int)(nh * (blockIdx.x + 1) / gridDim.x);
+        rg_lo = h_lo >> 1;
+        rg_hi = (h_hi + 1) >> 1;
+        t0 = rg_lo * nbu;
+        n_tiles = (rg_hi - rg_lo) * nbu;  // tiles touched (a half tile counted whole)
     } else {
         rg_lo = (int)((long long)p.total_rg * blockIdx.x / gridDim.x);
         rg_hi = (int)((long long)p.total_rg * (blockIdx.x + 1) / gridDim.x);
@@ -160,7 +289,16 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
     // so its weight stream overlaps this kernel's wait, activation staging and arithmetic (a chain
     // of such launches is then bound by the weight stream, not by the dependent-launch release).
     pdl_launch_dependents();
-    if (warp == W) {
+    const HalfShare hs(h_lo, h_hi, (int)p.tile_bytes);
+    if (half && warp == W) {
+        // ---------------- producer, halves: the whole share in one stage (the consumers wait for it)
+        if (lane == 0) {
+            half_issue(p, hs, ring, smem_u32(&bars[0]));
+            s_issued = 1;
+        }
+        __syncwarp();
+        __syncthreads();  // activation staged
+    } else if (warp == W) {
         // ---------------- producer: the weight stream does not depend on earlier kernels
         const uint64_t policy = l2_evict_first_policy();
         auto issue = [&](int s) {
@@ -207,7 +345,7 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
 
         // tile walk: tile i advances by W; stage/slot/phase, unit and row group incremental.
         constexpr int TSTEP = W;
-        const bool all_in = SMALL && n_stages_cta <= S;
+        const bool all_in = !half && SMALL && n_stages_cta <= S;
         const int JU = (TYPE == TYPE_Q8_0 && p.q80_exact) ? 8 : 1;  // terms per unit
         bool any_dbg = false;
         for (int k = 0; k < p.n_tasks; ++k) any_dbg |= s_task[k].dbg_sumi != nullptr;
@@ -216,6 +354,26 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
         // that completes it (the row-group counters s_done), overlapping the folds with the other
         // warps' tiles
         const bool early_fold = all_in && !SPLIT && n_lr <= kMaxTermSlots;
+        if (HALF_OK && half) {
+            // the share's one stage (landed during the previous kernel in a chain of launches)
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait_bounded(smem_u32(&bars[0]), 0, p.timeout_ns, p.status);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            __syncwarp();
+            if (!ok && lane == 0) s_abort = 1;
+            if (ok && !*reinterpret_cast<volatile int *>(&s_abort))
+                half_walk<TYPE, MT>(p, s_task, hs, ring, smem, terms, warp, lane, W, any_dbg);
+            // fold the owned rows of every row group after all passes, spread over the consumers
+            named_bar_sync(1, W * 32);
+            if (!*reinterpret_cast<volatile int *>(&s_abort)) {
+                const int E = 16 * MT;
+                for (int idx = tid; idx < n_lr * E; idx += W * 32) {
+                    const int l = idx / E, e = idx - l * E, e0 = 8 * hs.first_half(l) * MT;
+                    if (e >= e0 && e < e0 + 8 * hs.halves(l) * MT)
+                        fold_one<MT>(p, s_task, terms + (size_t)l * J * tstride, J, e, rg_lo + l, s_best);
+                }
+            }
+        }
         if (all_in) {
             int tt = warp, sg = 0;
             while (tt >= T) {
@@ -284,7 +442,7 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
                 }
             }
         }
-        int i = all_in ? n_tiles : warp;
+        int i = (all_in || half) ? n_tiles : warp;
         int tt = i, sg = 0, slot = 0, ph = 0;
         while (tt >= T) {
             tt -= T;
@@ -371,7 +529,7 @@ __global__ void __launch_bounds__(threads_of<MT>(), 2) kq_gemv(const __grid_cons
                 }
             }
         }
-        if (SMALL && !early_fold) {
+        if (SMALL && !early_fold && !half) {
             // ---------------- fold all row groups of the share
             named_bar_sync(1, W * 32);
             const int E = 16 * MT;
@@ -498,6 +656,42 @@ Plan make_plan(int type, int K, int MT, int total_rg, int num_sms, int n_warps, 
     return pl;  // smem 0: does not fit
 }
 
+// Half row-group ownership (Q4_K / Q5_K, <= 2 tokens): at most one CTA per SM, each CTA's whole
+// share of 8-row halves in one stage and the terms of every row group it touches in shared
+// memory, all within ~110 KB so that the next kernel's CTA fits beside it.  smem 0: no such plan.
+Plan make_half_plan(int type, int K, int MT, int total_rg, int num_sms) {
+    Plan pl{};
+    if (MT > 2 || (type != TYPE_Q4_K && type != TYPE_Q5_K)) return pl;
+    const int nbu = K / 256;
+    const unsigned x_bytes = align_up((unsigned)(MT * 320 * nbu), 128);
+    const unsigned dx_bytes = align_up((unsigned)(nbu * 2 * 4), 128);
+    const unsigned xs_bytes = align_up((unsigned)(MT * nbu * 8 * 4), 128);
+    const unsigned fixed = x_bytes + dx_bytes + xs_bytes;
+    const int grid = std::max(1, std::min(2 * total_rg, num_sms));
+    const int hc = (2 * total_rg + grid - 1) / grid;   // halves of the largest share
+    const int rg_cta = std::min(total_rg, hc / 2 + 1);  // row groups it can touch
+    const unsigned stage = align_up((unsigned)(hc * nbu) * (unsigned)tile_bytes(type) / 2, 128);
+    const unsigned term_bytes = align_up((unsigned)(rg_cta * nbu * 16 * MT * 4), 128);
+    const unsigned total = fixed + term_bytes + stage + 3 * 8;
+    if (total > 110u * 1024u || rg_cta > kMaxTermSlots) return pl;
+    pl.small = 1;
+    pl.T = hc * nbu;
+    pl.S = 1;
+    pl.TS = 1;
+    pl.J = nbu;
+    pl.q80_exact = 0;
+    pl.grid = grid;
+    pl.stage_bytes = stage;
+    pl.off_x = 0;
+    pl.off_dx = x_bytes;
+    pl.off_xs = x_bytes + dx_bytes;
+    pl.off_terms = fixed;
+    pl.off_stages = fixed + term_bytes;
+    pl.off_bars = pl.off_stages + stage;
+    pl.smem = pl.off_bars + 3 * 8;
+    return pl;
+}
+
 template <typename Kern>
 cudaError_t configure_smem(Kern kern) {
     static std::mutex mu;
@@ -558,8 +752,26 @@ cudaError_t launch_t(const GemvLaunch &L, cudaStream_t stream) {
         split = ps.smem != 0 && (pl.smem == 0 || sm_load(pl, false) * 10 >= sm_load(ps, true) * 14);
         if (split) pl = ps;
     }
+    // Halves where whole row groups leave the largest share partly outside shared memory (its last
+    // stages refill while the launch computes) or give its warps more tile passes: config 0's 608
+    // row groups over 148 SMs are 4 or 5 row groups per CTA (50 tiles, 40 fit), as halves 8 or 9
+    // (at most 45 tiles' rows, all resident, 3 passes per warp).
+    bool half = false;
+    if (L.half_ok && !split && pl.smem != 0 && pl.small && pl.grid <= L.num_sms) {
+        const Plan ph = make_half_plan(TYPE, L.K, MT, total_rg, L.num_sms);
+        if (ph.smem != 0) {
+            const int nbu = L.K / 256, Wn = warps_of<MT>();
+            const int tiles_whole = (total_rg + pl.grid - 1) / pl.grid * nbu;
+            const bool whole_in = (tiles_whole + pl.T - 1) / pl.T <= pl.S;
+            const int hc = (2 * total_rg + ph.grid - 1) / ph.grid;
+            const int passes_half = ((hc * nbu + 1) / 2 + Wn - 1) / Wn, passes_whole = (tiles_whole + Wn - 1) / Wn;
+            half = !whole_in || passes_half < passes_whole;
+            if (half) pl = ph;
+        }
+    }
     if (pl.smem == 0) return cudaErrorInvalidConfiguration;
     if (split && gemv_split_bytes(TYPE, L.K, L.M, L.num_sms) > L.split_terms_bytes) return cudaErrorInvalidValue;
+    p.half = half ? 1 : 0;
     p.total_tiles = (long long)total_rg * (L.K / 256);
     p.gterms = split ? L.split_terms : nullptr;
     p.gcount = split ? L.split_count : nullptr;

@@ -67,6 +67,10 @@ struct GemvParams {
     float *gterms;
     int *gcount;
     PeerOut peer;  // task 0's fp32 outputs also into every rank's gather buffer (peer.n > 0)
+    // Half row-group ownership (Q4_K / Q5_K, <= 2 tokens, the whole share in one stage): CTA c
+    // owns the 8-row halves [2 R c / G, 2 R (c + 1) / G) of the launch's R row groups, so no CTA
+    // holds more than one half above the mean and no row is shared between CTAs.
+    int half;
 };
 
 

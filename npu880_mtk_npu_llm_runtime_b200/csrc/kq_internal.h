@@ -60,6 +60,8 @@ struct GemvLaunch {
     float *split_terms = nullptr;
     size_t split_terms_bytes = 0;
     int *split_count = nullptr;
+    // Half row-group ownership allowed (Q4_K / Q5_K, 1-2 rows, where the plan finds it better)
+    bool half_ok = true;
     PeerOut peer;  // n > 0: task 0's fp32 outputs also into every rank's gather buffer
 };
 
