@@ -127,3 +127,14 @@ def test_peer_region_bytes(lib):
     """256 bytes of control words, then two buffers of [M][row_stride] 64-bit entries"""
     assert lib.kq_peer_region_bytes(2, 151936) == 256 + 2 * 2 * 151936 * 8
     assert lib.kq_peer_region_bytes(0, 151936) == 0
+
+
+def test_every_option_is_documented():
+    """each option name kq_set_option accepts is described in the header's option list"""
+    api = open(os.path.join(ROOT, "npu880_mtk_npu_llm_runtime_b200", "csrc", "kq_api.cu")).read()
+    accepted = set(re.findall(r'strcmp\(name, "([a-z0-9_]+)"\)', api))
+    header = open(os.path.join(ROOT, "include", "kq.h")).read()
+    doc = header[header.index("/* Options:"):header.index("int kq_set_option(")]
+    assert accepted, "no option names found"
+    missing = sorted(o for o in accepted if f'"{o}"' not in doc)
+    assert not missing, f"options accepted but not documented in kq.h: {missing}"
